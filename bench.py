@@ -1,0 +1,291 @@
+"""Headline benchmark: stage-1 engram training throughput of the 31B-class Gemma-style hybrid
+decoder at seq 8192, on N GPUs of one node.
+
+  python bench.py --gpus N --steps K --warmup W          (N=1)
+  torchrun --nproc-per-node N bench.py --gpus N ...       (N>1, one rank per GPU)
+  python bench.py --impl reference ...                    (the unmodified reference)
+
+Config: 60 layers, d 5376, FFN 21504, 32 q heads, sliding-1024 layers (16 KV heads, head_dim
+256) interleaved 5:1 with global layers (4 KV heads, head_dim 512, v = k), vocab 262144 tied
+with final softcap 30; frozen random-init bf16 base; one engram at layer 0 with 2/3/4-gram
+tables {1572864, 4194304, 4194304} x 8 heads x dim 64 (scalar_sqrt gate, rowwise_adam, bf16 +
+stochastic rounding); seq 8192, micro-batch 1, grad accumulation 3, per-layer activation
+checkpointing + activation offloading; synthetic packed Zipf(1.1) token documents of uniform
+length 256-4096 (weak scaling: every GPU trains its own micro-batches).
+
+Timing: W untimed warm-up steps, then K steps bracketed by a barrier + synchronize, timed with
+CUDA events on the launching stream, max over ranks. Each step streams the ~61 GB base through
+the GPU several times, far more than the 126 MB L2, so no flush is needed between steps.
+`value` is the device-timed step (inputs staged on the device beforehand); `e2e` repeats the
+K steps through the public `Trainer.train_step` API, which collates each step's micro-batches
+on the host, copies them from pinned memory and reads the loss back.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+METRIC = "train tokens/s (31B-class, seq 8192)"
+MODEL = "31B-class Gemma-style hybrid decoder (60L, d5376, FFN 21504, 32q heads, sliding hd256x16kv / global hd512x4kv 5:1, V=262144), stage-1 engram"
+SEQ, MBS, GA = 8192, 1, 3
+TABLES = {2: 1572864, 3: 4194304, 4: 4194304}
+BASELINE_VALUE = None  # the reference publishes no tokens/s figure
+
+
+def base_config_31b():
+    return {
+        "architectures": ["Gemma4ForCausalLM"], "model_type": "gemma4_text",
+        "vocab_size": 262144, "hidden_size": 5376, "intermediate_size": 21504, "num_hidden_layers": 60,
+        "num_attention_heads": 32, "num_key_value_heads": 16, "head_dim": 256, "global_head_dim": 512,
+        "num_global_key_value_heads": 4, "attention_k_eq_v": True, "sliding_window": 1024,
+        "final_logit_softcapping": 30.0, "rms_norm_eps": 1e-6, "pad_token_id": 0, "eos_token_id": 1,
+        "bos_token_id": 2, "tie_word_embeddings": True, "hidden_size_per_layer_input": 0,
+        "layer_types": ["sliding_attention" if (i + 1) % 6 else "full_attention" for i in range(60)],
+        "rope_parameters": {"sliding_attention": {"rope_type": "default", "rope_theta": 10000.0},
+                            "full_attention": {"rope_type": "proportional", "partial_rotary_factor": 0.25,
+                                               "rope_theta": 1000000.0}},
+    }
+
+
+def synthetic_samples(n_bins, vocab, seed=1234, min_len=256, max_len=4096, seq=SEQ):
+    """Zipf(1.1) token documents of uniform length min_len-max_len, enough for n_bins bins of seq."""
+    import numpy as np
+
+    from micro_engram.train.data import Samples
+
+    rng = np.random.default_rng(seed)
+    ranks = np.arange(1, vocab + 1, dtype=np.float64)
+    p = ranks ** -1.1
+    cdf = np.cumsum(p / p.sum())
+    items, total = [], 0
+    need = n_bins * seq * 1.15
+    while total < need:
+        n = int(rng.integers(min_len, max_len + 1))
+        ids = np.searchsorted(cdf, rng.random(n)).astype(np.int32)
+        items.append((ids, None))
+        total += n
+    return Samples.from_list(items)
+
+
+def bench_config(tmp, steps):
+    base = os.path.join(tmp, "base")
+    os.makedirs(base, exist_ok=True)
+    with open(os.path.join(base, "config.json"), "w") as f:
+        json.dump(base_config_31b(), f)
+    return {
+        "base_model": base, "base_init": "random",
+        "datasets": [{"path": os.path.join(tmp, "unused.jsonl"), "type": "completion"}],
+        "output_dir": os.path.join(tmp, "out"), "sequence_len": SEQ,
+        "micro_batch_size": MBS, "gradient_accumulation_steps": GA, "max_steps": steps,
+        "micro_engram_layer": 0, "micro_engram_table_size": 2097152, "micro_engram_table_sizes": TABLES,
+        "micro_engram_dim": 64, "micro_engram_heads": 8, "micro_engram_gate": "scalar_sqrt",
+        "micro_engram_dtype": "bf16", "micro_engram_optimizer": "rowwise_adam",
+        "learning_rate": 5e-3, "micro_engram_dense_lr": 1e-3, "max_grad_norm": 2.0, "warmup_steps": 0,
+        "gradient_checkpointing": True, "activation_offloading": True, "micro_engram_stats_steps": 0,
+        "seed": 42,
+    }
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx = float(parts[2])
+                except ValueError:
+                    continue
+                for name, val in zip(names, parts[5:9]):
+                    if val.lower() == "active":
+                        reasons.add(name)
+        os.unlink(self.path)
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def count_launches(trainer, micro):
+    """Kernels of our extension launched by one step (profiled outside the timed region)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    ours = ("hash_kernel", "gather_kernel", "scatter_grad_kernel", "touched_sqnorm_kernel", "clip_coef_kernel",
+            "adam_touched_kernel", "adam_dense_kernel", "gate_fwd_kernel", "gate_bwd_kernel", "rmsnorm_fwd_kernel",
+            "rmsnorm_bwd_kernel", "post_norm_add_kernel", "post_norm_add_bwd_kernel", "qkv_norm_rope_kernel",
+            "qkv_norm_rope_bwd_kernel", "geglu_fwd_kernel", "geglu_bwd_kernel", "ce_fwd_kernel", "ce_bwd_kernel",
+            "attn_fwd_kernel", "attn_bwd_pre_kernel", "attn_bwd_dkdv_kernel", "attn_bwd_dq_kernel",
+            "me_gemm", "allreduce_p2p")
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        trainer.train_step(micro)
+        torch.cuda.synchronize()
+    n_ours, n_all = 0, 0
+    for ev in prof.events():
+        if ev.device_type == torch.autograd.DeviceType.CUDA:
+            n_all += 1
+            if any(k in ev.name for k in ours):
+                n_ours += 1
+    return n_ours, n_all
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from micro_engram.train.config import load_config
+    from micro_engram.train.data import collate
+    from micro_engram.train.loop import Trainer
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    steps_total = args.warmup + 2 * args.steps + 1
+    tmp = tempfile.mkdtemp(prefix="me_bench_")
+    cfg = load_config(bench_config(tmp, steps_total))
+    trainer = Trainer(cfg)
+    rank, device = trainer.rank, trainer.device
+    n_bins = steps_total * GA * MBS * world + 8
+    samples = synthetic_samples(n_bins, 262144)
+    trainer.build(samples=samples, tokenizer=None)
+    plan = trainer.plan
+
+    def sync():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    step_idx = 0
+
+    def next_micro():
+        nonlocal step_idx
+        m = plan.micro_batches(0, step_idx, rank)
+        step_idx += 1
+        return m
+
+    for _ in range(args.warmup):
+        trainer.train_step(next_micro())
+    n_ours, n_all = count_launches(trainer, next_micro())
+
+    # device-timed: inputs staged on the GPU before the timed region
+    staged = []
+    for _ in range(args.steps):
+        micro = next_micro()
+        staged.append((micro, [{k: v.to(device) for k, v in collate(trainer.samples, b, SEQ, trainer.pad_id).items()}
+                               for b in micro]))
+    clocks = Clocks(int(os.environ.get("LOCAL_RANK", 0)))
+    sync()
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    tokens = 0
+    t0.record()
+    for micro, batches in staged:
+        trainer.train_step(micro, batches=batches)
+        tokens += SEQ * MBS * GA
+    t1.record()
+    sync()
+    clk = clocks.stop()
+    dev_ms = t0.elapsed_time(t1)
+
+    # end to end through the public API: host collate + pinned H2D + loss readback each step
+    sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        trainer.train_step(next_micro())
+    e1.record()
+    sync()
+    e2e_ms = e0.elapsed_time(e1)
+
+    vals = torch.tensor([dev_ms, e2e_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    dev_ms, e2e_ms = vals.tolist()
+    ms_step = dev_ms / args.steps
+    value = tokens * world / (dev_ms / 1e3)
+    e2e_value = tokens * world / (e2e_ms / 1e3)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 2),
+            "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None if not BASELINE_VALUE else round(value / BASELINE_VALUE, 4),
+            "dtype": "bf16", "data": "synthetic (Zipf(1.1) packed docs 256-4096, random-init weights)",
+            "config": {"model": MODEL, "global_batch": MBS * GA * world, "seq_len": SEQ,
+                       "parallelism": f"dp{world} (replicated frozen base, row-sharded engram, vocab-parallel head)",
+                       "engram": "layer 0, tables {2:1572864,3:4194304,4:4194304} x8 heads x dim 64, "
+                                 "scalar_sqrt, rowwise_adam bf16+SR",
+                       "activation_checkpointing": "per-layer", "activation_offloading": True,
+                       "l2": "inputs larger than L2 (61 GB base streamed per step), no flush"},
+            "clocks": clk,
+            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": GA * 3 * SEQ * MBS * 8, "d2h_bytes_per_step": 16},
+            "gpu_launches": n_ours * args.steps,
+            "gpu_launches_all_per_step": n_all,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    try:
+        from micro_engram_fork_b200.baseline_ref import run as ref_run
+    except ImportError as e:
+        print(json.dumps({"impl": "reference", "unavailable": f"reference arm not wired ({e})"}))
+        return
+    return ref_run(args)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        print("bench: at least 3 warm-up steps", file=sys.stderr)
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    main()

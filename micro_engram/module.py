@@ -1,0 +1,458 @@
+"""MicroEngram: a hashed n-gram memory injected into the residual stream of a frozen decoder.
+
+Public surface and math match the reference (micro_engram/module.py:1-393): order-major
+table layout, hashing `(sum_i tok[t-i] * mult[k,i]) % (2^31-1) % rows_k` with the canon map
+and position_ids document boundaries, the scalar / scalar_sqrt / ple gates with a zero-init
+output projection (exact no-op at step 0), delta-stored norm scales, row sharding and the
+attachment hooks.
+
+B200 path: on CUDA the hash is one kernel, row-sharded tables live in a RowStore (peer
+memory over NVLink when world > 1) and are fetched by a gather kernel that reads the
+owner's shard directly, and the scalar gates run as one fused forward / backward kernel.
+The PyTorch code below is the CPU path and the oracle.
+"""
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from micro_engram_fork_b200.ops import use_native
+
+_PRIME = 2_147_483_647  # 2^31 - 1
+
+
+def resolve_order_sizes(table_size, orders=(2, 3), table_sizes=None):
+    """{order: rows per table}, sorted by order.
+
+    Each order of `orders` starts with `table_size` rows; `table_sizes` (int or string keys,
+    as from JSON/YAML) overrides or adds orders. Orders whose size is 0 or None are dropped.
+    """
+    merged = {int(n): table_size for n in orders}
+    merged.update({int(n): v for n, v in (table_sizes or {}).items()})
+    sizes = {n: int(merged[n]) for n in sorted(merged) if merged[n]}
+    if not sizes:
+        raise ValueError("micro_engram: every n-gram order has size 0/None: nothing left to hash")
+    if min(sizes) < 1 or min(sizes.values()) < 1:
+        raise ValueError(f"micro_engram: bad orders/sizes {sizes}")
+    return sizes
+
+
+class MicroEngram(nn.Module):
+    """Hashed n-gram memory (Engram-style) with a learned gate into the hidden state.
+
+    At position t, the 2-, 3- (optionally 4-) grams ending at t are hashed into `num_heads`
+    tables per order; the rows are concatenated into `mem` [.., n_tables*engram_dim].
+
+    Gates:
+      scalar       alpha = sigmoid(<rms(h), rms(key(mem))> / sqrt(d)); h += alpha * value(mem)
+      scalar_sqrt  as scalar with a signed square root on the score and learnable norm
+                   scales q_scale / k_scale (stored as delta from 1)
+      ple          g = gelu_tanh(down(rms(h))); h += up(g * mem)
+    """
+
+    GATES = ("scalar", "ple", "scalar_sqrt")
+    SCALAR_GATES = ("scalar", "scalar_sqrt")
+    DELTA_SCALES = ("q_scale", "k_scale")
+
+    # row sharding state: plain attributes, outside parameters()/state_dict()
+    row_shards = None
+    row_info = None
+    row_store = None
+    row_lookup_fn = None  # a server's own lookup for row-sharded tables (vLLM tensor parallel)
+
+    def __init__(self, model_dim, table_size=65_536, engram_dim=128, num_heads=4, orders=(2, 3), pad_id=0,
+                 seed=0, vocab_size=262_144, canon=None, gate="scalar", build_tables=True, table_sizes=None):
+        super().__init__()
+        if gate not in self.GATES:
+            raise ValueError(f"gate must be one of {self.GATES}, got {gate!r}")
+        self.gate = gate
+        self.order_sizes = resolve_order_sizes(table_size, orders, table_sizes)
+        self.orders = tuple(self.order_sizes)
+        self.engram_dim = engram_dim
+        self.seed = seed
+        self.pad_id = pad_id
+        self._table_orders = [n for n in self.orders for _ in range(num_heads)]
+        self.table_rows = [self.order_sizes[n] for n in self._table_orders]
+        self.table_size = self.table_rows[0] if len(set(self.table_rows)) == 1 else None
+        n_tables = len(self._table_orders)
+
+        if build_tables:
+            self.tables = nn.ModuleList(nn.Embedding(r, engram_dim) for r in self.table_rows)
+            for t in self.tables:
+                nn.init.normal_(t.weight, std=0.02)
+
+        mem_dim = engram_dim * n_tables
+        if gate in self.SCALAR_GATES:
+            self.key = nn.Linear(mem_dim, model_dim, bias=False)
+            self.value = nn.Linear(mem_dim, model_dim, bias=False)
+            nn.init.zeros_(self.value.weight)  # exact no-op at step 0
+            if gate == "scalar_sqrt":
+                # scale = 1 + delta: an Adam step near 1.0 would round away in bf16 (spacing 1/128)
+                self.q_scale = nn.Parameter(torch.zeros(model_dim))
+                self.k_scale = nn.Parameter(torch.zeros(model_dim))
+        else:
+            self.down = nn.Linear(model_dim, mem_dim, bias=False)
+            self.up = nn.Linear(mem_dim, model_dim, bias=False)
+            nn.init.zeros_(self.up.weight)
+
+        # hash multipliers: deterministic from the seed (a CPU generator, whatever the default device)
+        gen = torch.Generator().manual_seed(seed)
+        mults = torch.randint(1, _PRIME, (n_tables, max(self.orders)), generator=gen, device="cpu") | 1
+        self.register_buffer("mults", mults)
+        if canon is None:
+            canon = torch.arange(vocab_size)
+        else:
+            canon = torch.as_tensor(canon).long().clone()
+            if canon.shape != (vocab_size,):
+                raise ValueError(f"canon must have shape ({vocab_size},), got {tuple(canon.shape)}")
+        self.register_buffer("canon", canon)
+        self._dev_consts = {}
+
+    # ------------------------------------------------------------------ row sharding
+    def shard_rows(self, rank, world, device=None, dtype=None, requires_grad=True, empty=False, pin_memory=False,
+                   group=None):
+        """Keep only this rank's rows of every table (ceil(rows/world) per rank).
+
+        Rows come from the loaded tables when they exist, else a fresh N(0, 0.02) init with
+        the per-rank seed `seed*1_000_003 + rank`, or stay uninitialised with `empty=True`
+        (a server that loads the real rows next). On a CUDA device the rows live in a
+        RowStore (peer-mapped when world > 1) that the fused lookup reads directly.
+        """
+        from .rows import row_range
+
+        spans = [row_range(rows, rank, world) for rows in self.table_rows]
+        pers = [-(-rows // world) for rows in self.table_rows]
+        device = torch.device(device) if device is not None else None
+        src = None
+        if "tables" in self._modules:
+            src = [t.weight.detach()[a:a + c] for t, (a, c) in zip(self.tables, spans)]
+            dtype = dtype or src[0].dtype
+            del self.tables
+        dtype = dtype or torch.float32
+        on_cuda = device is not None and device.type == "cuda" and not pin_memory
+        if on_cuda:
+            from micro_engram_fork_b200.parallel.row_store import RowStore
+
+            store = RowStore(self.table_rows, self.engram_dim, dtype, rank, world, device, group=group)
+            shards = []
+            gen = None
+            for k, (_a, c) in enumerate(spans):
+                view = store.shard(k)
+                if src is not None:
+                    view.copy_(src[k])
+                elif not empty:
+                    if gen is None:  # device generator: tables of tens of GB initialise in place
+                        gen = torch.Generator(device=device).manual_seed(self.seed * 1_000_003 + rank)
+                    view.copy_(torch.randn(c, self.engram_dim, generator=gen, device=device) * 0.02)
+                shards.append(nn.Parameter(view, requires_grad=requires_grad))
+            self.__dict__["row_store"] = store
+        else:
+            if src is None and empty:
+                pin = pin_memory and torch.cuda.is_available()
+                src = [torch.empty(c, self.engram_dim, device=None if pin else device, dtype=dtype, pin_memory=pin)
+                       for _, c in spans]
+                shards = [nn.Parameter(t, requires_grad=requires_grad) for t in src]
+            else:
+                if src is None:
+                    gen = torch.Generator().manual_seed(self.seed * 1_000_003 + rank)
+                    src = [torch.randn(c, self.engram_dim, generator=gen) * 0.02 for _, c in spans]
+                shards = [nn.Parameter(t.to(device=device, dtype=dtype).clone(), requires_grad=requires_grad)
+                          for t in src]
+            self.__dict__["row_store"] = None
+        self.__dict__["row_shards"] = shards
+        self.__dict__["row_info"] = (rank, world, [a for a, _ in spans], pers)
+        return shards
+
+    def all_parameters(self):
+        """Registered parameters plus this rank's table rows when row-sharded."""
+        return list(self.parameters()) + list(self.row_shards or [])
+
+    def lookup(self, idx):
+        """Table rows for the hashed ids `idx` (one tensor per table)."""
+        if self.row_shards is not None:
+            if self.row_lookup_fn is not None:
+                return self.row_lookup_fn(self, idx)
+            from .rows import row_lookup
+
+            return row_lookup(self, idx)
+        return [tab(i) for tab, i in zip(self.tables, idx)]
+
+    # ------------------------------------------------------------------ delta scales
+    def norm_scales(self):
+        """(q scale, k scale) in fp32: 1 + delta, with the delta made fp32 first."""
+        return 1 + self.q_scale.float(), 1 + self.k_scale.float()
+
+    def _save_to_state_dict(self, destination, prefix, keep_vars):
+        super()._save_to_state_dict(destination, prefix, keep_vars)
+        for name in self.DELTA_SCALES:
+            key = prefix + name
+            if key in destination:
+                destination[key] = destination[key].detach().float() + 1
+
+    def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
+                              error_msgs):
+        for name in self.DELTA_SCALES:
+            key = prefix + name
+            if key in state_dict:
+                state_dict[key] = state_dict[key].float() - 1
+        super()._load_from_state_dict(state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
+                                      error_msgs)
+
+    # ------------------------------------------------------------------ hashing
+    def _consts(self, device):
+        """Device copies of the hash constants (built once per device)."""
+        key = str(device)
+        c = self._dev_consts.get(key)
+        if c is None or c[0].device != device:
+            c = (self.canon.to(device=device, dtype=torch.long).contiguous(),
+                 self.mults.to(device=device, dtype=torch.long).contiguous(),
+                 torch.tensor(self._table_orders, dtype=torch.int32, device=device),
+                 torch.tensor(self.table_rows, dtype=torch.long, device=device))
+            self._dev_consts[key] = c
+        return c
+
+    def _apply(self, fn, *args, **kwargs):
+        self._dev_consts = {}
+        return super()._apply(fn, *args, **kwargs)
+
+    def hash_ids(self, input_ids, position_ids=None):
+        """One [B, T] tensor of row ids per table, for token ids [B, T]."""
+        ids = input_ids.long()
+        if use_native(ids):
+            from micro_engram_fork_b200.ops.engram import hash_ids as _hash
+
+            canon, mults, orders, rows = self._consts(ids.device)
+            pos = position_ids.to(ids.device) if position_ids is not None else None
+            out = _hash(ids, pos, canon, mults, orders, rows, self.pad_id)
+            return list(out.reshape(len(self.table_rows), *ids.shape).unbind(0))
+        canon = self.canon.to(ids.device)
+        ids = canon[ids.clamp(0, canon.numel() - 1)]
+        T = ids.shape[-1]
+        max_n = max(self.orders)
+        padded = F.pad(ids, (max_n - 1, 0), value=self.pad_id)
+        # back[i][:, t] = token t - i (the pad id before the row start)
+        back = [padded[..., max_n - 1 - i: max_n - 1 - i + T] for i in range(max_n)]
+        if position_ids is not None:
+            pos = position_ids.to(ids.device).expand_as(ids)
+            back = [b if i == 0 else torch.where(pos >= i, b, torch.full_like(b, self.pad_id))
+                    for i, b in enumerate(back)]
+        mults = self.mults.to(ids.device)
+        out = []
+        for k, n in enumerate(self._table_orders):
+            x = back[0] * mults[k, 0]
+            for i in range(1, n):
+                x = x + back[i] * mults[k, i]
+            out.append((x % _PRIME) % self.table_rows[k])
+        return out
+
+    def hash_prev(self, ids):
+        """Hashes from [N, max_order] histories: column i = token at t-i, -1 = none."""
+        ids = ids.long()
+        if use_native(ids):
+            from micro_engram_fork_b200.ops.engram import hash_prev as _hash_prev
+
+            canon, mults, orders, rows = self._consts(ids.device)
+            return list(_hash_prev(ids.contiguous(), canon, mults, orders, rows, self.pad_id).unbind(0))
+        canon = self.canon.to(ids.device)
+        merged = canon[ids.clamp(0, canon.numel() - 1)]
+        merged = torch.where(ids >= 0, merged, torch.full_like(merged, self.pad_id))
+        mults = self.mults.to(ids.device)
+        out = []
+        for k, n in enumerate(self._table_orders):
+            x = merged[:, 0] * mults[k, 0]
+            for i in range(1, n):
+                x = x + merged[:, i] * mults[k, i]
+            out.append((x % _PRIME) % self.table_rows[k])
+        return out
+
+    # ------------------------------------------------------------------ injection
+    def _fused_ok(self, hidden):
+        store = self.row_store
+        return (store is not None and self.row_lookup_fn is None and use_native(hidden)
+                and self.gate in self.SCALAR_GATES and hidden.dtype == torch.bfloat16
+                and self.key.weight.dtype == torch.bfloat16 and self.value.weight.dtype == torch.bfloat16)
+
+    def inject(self, hidden, idx, keep=None):
+        """Add the gated memory for hashed rows `idx` to `hidden`.
+
+        keep: optional [n_tokens] bool; False tokens get no memory (media placeholders)."""
+        if self._fused_ok(hidden):
+            return self._inject_fused(hidden, idx, keep)
+        mem = torch.cat(self.lookup(idx), dim=-1)
+        if self.row_shards is not None:
+            reader = self.key if self.gate in self.SCALAR_GATES else self.up
+            mem = mem.to(reader.weight.dtype)
+        d = hidden.shape[-1]
+        if self.gate in self.SCALAR_GATES:
+            if (use_native(hidden) and hidden.dtype == torch.bfloat16 and mem.dtype == torch.bfloat16
+                    and self.key.weight.dtype == torch.bfloat16):
+                k = self.key(mem)
+                v = self.value(mem)
+                return self._gate_native(hidden, k, v, keep)
+            if self.gate == "scalar_sqrt":
+                qs, ks = self.norm_scales()
+                h = F.rms_norm(hidden.float(), (d,), weight=qs)
+                k = F.rms_norm(self.key(mem).float(), (d,), weight=ks)
+            else:
+                h = F.rms_norm(hidden.float(), (d,))
+                k = F.rms_norm(self.key(mem).float(), (d,))
+            s = (h * k).sum(-1, keepdim=True) / d ** 0.5
+            if self.gate == "scalar_sqrt":
+                s = s.sign() * s.abs().clamp_min(1e-6).sqrt()
+            alpha = torch.sigmoid(s)
+            if self.training:
+                self._record_gate(alpha)
+            out = alpha * self.value(mem).float()
+        else:
+            h = F.rms_norm(hidden.float(), (d,))
+            g = F.gelu(self.down(h.to(self.down.weight.dtype)), approximate="tanh")
+            out = self.up(g * mem).float()
+        if keep is not None:
+            out = out * keep.reshape(*out.shape[:-1], 1).to(out.dtype)
+        return hidden + out.to(hidden.dtype)
+
+    def _gate_native(self, hidden, k, v, keep):
+        from micro_engram_fork_b200.ops.engram import gate
+
+        sqrt_gate = self.gate == "scalar_sqrt"
+        acc = self._gate_acc(hidden.device) if self.training else None
+        qd = self.q_scale if sqrt_gate else None
+        kd = self.k_scale if sqrt_gate else None
+        shape = hidden.shape
+        d = shape[-1]
+        out = gate(hidden.reshape(-1, d), k.reshape(-1, d), v.reshape(-1, d), qd, kd, keep, sqrt_gate, acc)
+        return out.reshape(shape)
+
+    def _inject_fused(self, hidden, idx, keep):
+        from micro_engram_fork_b200.ops.engram import gather_rows
+
+        flat = torch.stack([i.reshape(-1) for i in idx]) if isinstance(idx, (list, tuple)) else idx
+        flat = flat.reshape(len(self.table_rows), -1).to(hidden.device).contiguous()
+        mem = gather_rows(flat, self.row_store, torch.bfloat16, self.row_shards)
+        k = F.linear(mem, self.key.weight)
+        v = F.linear(mem, self.value.weight)
+        return self._gate_native(hidden, k, v, keep)
+
+    def forward(self, hidden, input_ids, position_ids=None):
+        idx = self.hash_ids(input_ids.to(hidden.device), position_ids)
+        return self.inject(hidden, idx)
+
+    # ------------------------------------------------------------------ gate statistics
+    def _gate_acc(self, device):
+        acc = getattr(self, "_gate_stats", None)
+        if acc is None or acc.device != device:
+            acc = torch.zeros(3, device=device)
+            self._gate_stats = acc
+        return acc
+
+    def _record_gate(self, alpha):
+        a = alpha.detach().float()
+        acc = self._gate_acc(a.device)
+        acc += torch.stack([a.sum(), torch.tensor(float(a.numel()), device=a.device), (a > 0.99).float().sum()])
+
+    def pop_gate_stats(self):
+        """(mean gate, share of tokens with gate > 0.99) since the last call, or None."""
+        stats = getattr(self, "_gate_stats", None)
+        self._gate_stats = None
+        if stats is None:
+            return None
+        s, n, sat = stats.tolist()
+        if n == 0:
+            return None
+        return s / n, sat / n
+
+
+def find_text_layers(model):
+    """(name, ModuleList) of the language model's decoder layers (not a vision/audio tower)."""
+    cands = [(n, m) for n, m in model.named_modules() if isinstance(m, nn.ModuleList) and n.endswith("layers")]
+    for n, m in cands:
+        if "language_model" in n:
+            return n, m
+    for n, m in cands:
+        if "vision" not in n and "audio" not in n:
+            return n, m
+    raise RuntimeError("Could not find text decoder layers; print(model) and set the path by hand.")
+
+
+def engram_from_spec(spec, model_dim, vocab_size, pad_default=0, canon=None, build_tables=True):
+    """A MicroEngram from one engram spec (see weights.engram_specs); the seed fixes the hash."""
+    return MicroEngram(
+        model_dim=model_dim,
+        table_size=spec["table_size"],
+        table_sizes=spec.get("table_sizes"),
+        engram_dim=spec["engram_dim"],
+        num_heads=spec["num_heads"],
+        orders=tuple(spec.get("orders") or (2, 3)),
+        pad_id=spec["pad_id"] if spec.get("pad_id") is not None else pad_default,
+        seed=spec.get("seed") or 0,
+        vocab_size=vocab_size,
+        canon=canon,
+        gate=spec.get("gate") or "scalar",
+        build_tables=build_tables,
+    )
+
+
+def check_loaded(engram, sd, where):
+    """Strictly load `sd` into `engram`. `mults` may be absent (rebuilt from the seed) but,
+    when present, must equal the seed's: a different one means a wrong seed."""
+    if "mults" in sd and not torch.equal(sd["mults"].to(engram.mults.device).long(), engram.mults.long()):
+        raise ValueError(f"[micro_engram] {where}: the saved hash multipliers differ from the ones this engram's "
+                         f"seed gives; the seed is wrong for these weights")
+    result = engram.load_state_dict(sd, strict=False)
+    problems = [k for k in result.missing_keys if k != "mults"] + list(result.unexpected_keys)
+    if problems:
+        raise ValueError(f"[micro_engram] {where} does not match the engram settings: {problems[:10]}")
+    return result
+
+
+_QUANTIZED_PARAMS = ("Params4bit", "Int8Params", "NF4Weight")
+
+
+def layer_device_dtype(layer):
+    """(device, compute dtype) for an engram placed in `layer`: the first real floating-point
+    weight, else a quantized module's compute dtype, else bf16."""
+    params = list(layer.parameters())
+    if not params:
+        raise RuntimeError("decoder layer has no parameters")
+    for p in params:
+        if p.is_floating_point() and type(p).__name__ not in _QUANTIZED_PARAMS:
+            return p.device, p.dtype
+    for m in layer.modules():
+        cd = getattr(m, "compute_dtype", None)
+        if isinstance(cd, torch.dtype) and cd.is_floating_point:
+            return params[0].device, cd
+    return params[0].device, torch.bfloat16
+
+
+def attach_engram(model, engram, layer_idx, dtype=None, get_ids=None):
+    """Nest `engram` in decoder layer `layer_idx` and inject it into that layer's output.
+
+    get_ids: optional callable -> (input_ids, position_ids) for the current forward; by
+    default a pre-hook on `model` captures them from its forward kwargs.
+    Returns (the layer's module name, [hook handles]).
+    """
+    name, layers = find_text_layers(model)
+    target = layers[layer_idx]
+    device, layer_dtype = layer_device_dtype(target)
+    engram.to(device=device, dtype=dtype or layer_dtype)
+    target.add_module("micro_engram", engram)
+    seen = {}
+
+    def capture(_mod, args, kwargs):
+        ids = kwargs.get("input_ids")
+        if ids is None and args:
+            ids = args[0]
+        seen["input_ids"] = ids
+        seen["position_ids"] = kwargs.get("position_ids")
+
+    def inject(_mod, _args, output):
+        ids, pos = get_ids() if get_ids is not None else (seen.get("input_ids"), seen.get("position_ids"))
+        if ids is None:
+            return output
+        if isinstance(output, tuple):
+            return (engram(output[0], ids, pos),) + tuple(output[1:])
+        return engram(output, ids, pos)
+
+    handles = [target.register_forward_hook(inject)]
+    if get_ids is None:
+        handles.append(model.register_forward_pre_hook(capture, with_kwargs=True))
+    return f"{name}.{layer_idx}", handles

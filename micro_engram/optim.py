@@ -1,0 +1,180 @@
+"""LazyAdamW and stochastic bf16 rounding (semantics of micro_engram/optim.py:1-133).
+
+AdamW with decoupled weight decay and a global step count, state names as
+torch.optim.AdamW (step, exp_avg, exp_avg_sq). Per parameter group:
+
+  lazy=True      a row whose gradient is all zero is left exactly as it is (weight and both
+                 moments), like SparseAdam, also on dense gradients
+  rowwise=True   ONE fp32 second moment per row, the running mean of the row's g^2 (FBGEMM /
+                 TorchRec partial row-wise Adam); kept fp32 whatever the weight dtype, since a
+                 bf16 v = 0.999 v + 0.001 g^2 stops moving once v has grown
+
+bf16 weights and states are written back with stochastic rounding when enabled.
+
+On CUDA the update runs in the sm_100a kernels: row-sharded tables with a RowStore are
+updated on their touched rows only (one warp per row, Philox4x32-10 rounding bits, the
+accumulator cleared in the same pass); other CUDA parameters use a fused elementwise AdamW.
+"""
+import torch
+
+from micro_engram_fork_b200.ops import use_native
+
+
+def _local(t):
+    to_local = getattr(t, "to_local", None)
+    return to_local() if to_local is not None else t
+
+
+def stochastic_bf16(x):
+    """fp32 -> bf16 with stochastic rounding: 16 random bits are added below the kept mantissa
+    and cut off, so a value rounds up with probability equal to the dropped fraction. The
+    sign is its own bit, so this is unbiased for both signs; inf/nan pass through."""
+    x = x.float().contiguous()
+    noise = torch.randint(0, 1 << 16, x.shape, dtype=torch.int32, device=x.device)
+    bits = (x.view(torch.int32) + noise) & -65536
+    out = torch.where(torch.isfinite(x), bits.view(torch.float32), x)
+    return out.to(torch.bfloat16)
+
+
+_SEED_BASE = 0x5EED
+
+
+class LazyAdamW(torch.optim.Optimizer):
+    def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, lazy=False, rowwise=False,
+                 stochastic_rounding=True):
+        super().__init__(params, dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay, lazy=lazy,
+                                      rowwise=rowwise, stochastic_rounding=stochastic_rounding))
+
+    @staticmethod
+    def init_state(state, p, group):
+        """Fresh state: exp_avg like p; exp_avg_sq like p, or [rows] fp32 when row-wise."""
+        state["step"] = torch.zeros((), dtype=torch.float32)
+        state["exp_avg"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+        if group.get("rowwise") and p.dim() >= 2:
+            state["exp_avg_sq"] = torch.zeros(p.shape[0], dtype=torch.float32, device=p.device)
+        else:
+            state["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        stores = []
+        for group in self.param_groups:
+            for p in group["params"]:
+                rs = getattr(p, "_row_store", None)
+                if rs is not None:
+                    self._step_store(p, group)
+                    if rs[0] not in stores:
+                        stores.append(rs[0])
+                else:
+                    self._step_param(p, group)
+        for store in stores:  # every touched row was consumed (and cleared) by the kernels
+            store.pending = False
+            store.coef = None
+        return loss
+
+    # ------------------------------------------------------------------ row-store tables (CUDA)
+    def _step_store(self, p, group):
+        store, k = p._row_store
+        if not store.pending:
+            return
+        state = self.state[p]
+        if not state:
+            self.init_state(state, p, group)
+        state["step"] += 1
+        step = float(state["step"])
+        beta1, beta2 = group["betas"]
+        lr, eps, wd = group["lr"], group["eps"], group["weight_decay"]
+        bc1, bc2 = 1 - beta1 ** step, 1 - beta2 ** step
+        sr = bool(group.get("stochastic_rounding", True))
+        seed = (_SEED_BASE + 7919 * store.rank + 104729 * getattr(store, "salt", 0)) & 0x7FFFFFFF
+        from micro_engram_fork_b200.ops.engram import adam_dense, adam_touched
+
+        coef = getattr(store, "coef", None)
+        if group["lazy"]:
+            adam_touched(p.data, state["exp_avg"], state["exp_avg_sq"], store.acc[k], store.bits[k],
+                         store.list[k], store.count[k], coef, lr, beta1, beta2, eps, wd, bc1, bc2, sr, seed,
+                         int(step), k)
+        else:
+            n = p.shape[0]
+            g = store.acc[k][:n]
+            if coef is not None:
+                g.mul_(coef)
+            adam_dense(p.data, g, state["exp_avg"], state["exp_avg_sq"], lr, beta1, beta2, eps, wd, bc1, bc2,
+                       1.0, sr, seed, int(step))
+            store.acc[k].zero_()
+            store.bits[k].zero_()
+        store.count[k].zero_()
+
+    # ------------------------------------------------------------------ everything else
+    def _step_param(self, p, group):
+        sparse = getattr(p, "sparse_grad", None)
+        if p.grad is None and sparse is None:
+            return
+        state = self.state[p]
+        if not state:
+            self.init_state(state, p, group)
+        state["step"] += 1
+        step = float(state["step"])
+        beta1, beta2 = group["betas"]
+        lr, eps, wd = group["lr"], group["eps"], group["weight_decay"]
+        bc1, bc2 = 1 - beta1 ** step, 1 - beta2 ** step
+        sr = group.get("stochastic_rounding", True)
+        P = _local(p)
+        M, V = _local(state["exp_avg"]), _local(state["exp_avg_sq"])
+        if (sparse is None and not group["lazy"] and use_native(P) and M.dim() == V.dim()
+                and P.dtype in (torch.bfloat16, torch.float32) and P.is_contiguous()):
+            from micro_engram_fork_b200.ops.engram import adam_dense
+
+            G = _local(p.grad)
+            if G.dtype not in (torch.float32, P.dtype):
+                G = G.float()
+            adam_dense(P, G.contiguous(), M, V, lr, beta1, beta2, eps, wd, bc1, bc2, 1.0,
+                       bool(sr) and P.dtype == torch.bfloat16, _SEED_BASE ^ (id(p) & 0xFFFF), int(step))
+            return
+        rows = None
+        if sparse is not None:
+            if not group["lazy"]:
+                raise ValueError("sparse row gradients need lazy=True")
+            rows, g = sparse
+            keep = (g != 0).flatten(1).any(dim=1)
+            rows, g = rows[keep], g[keep]
+            if rows.numel() == 0:
+                return
+            pw = P.index_select(0, rows).float()
+            m, v = M.index_select(0, rows).float(), V.index_select(0, rows).float()
+        elif group["lazy"] and P.dim() >= 2:
+            G = _local(p.grad)
+            rows = (G != 0).flatten(1).any(dim=1).nonzero().squeeze(1)
+            if rows.numel() == 0:
+                return
+            pw, g = P.index_select(0, rows).float(), G.index_select(0, rows).float()
+            m, v = M.index_select(0, rows).float(), V.index_select(0, rows).float()
+        else:
+            G = _local(p.grad)
+            pw, g, m, v = P.float(), G.float(), M.float(), V.float()
+        if wd:
+            pw.mul_(1 - lr * wd)
+        m.mul_(beta1).add_(g, alpha=1 - beta1)
+        if v.dim() < g.dim():
+            v.mul_(beta2).add_(g.pow(2).flatten(1).mean(dim=1), alpha=1 - beta2)
+            denom = (v.sqrt() / bc2 ** 0.5).add_(eps).reshape(-1, *([1] * (g.dim() - 1)))
+        else:
+            v.mul_(beta2).addcmul_(g, g, value=1 - beta2)
+            denom = (v.sqrt() / bc2 ** 0.5).add_(eps)
+        pw.addcdiv_(m, denom, value=-lr / bc1)
+
+        def cast(x, dtype):
+            return stochastic_bf16(x) if sr and dtype == torch.bfloat16 else x.to(dtype)
+
+        if rows is None:
+            P.copy_(cast(pw, P.dtype))
+            M.copy_(cast(m, M.dtype))
+            V.copy_(cast(v, V.dtype))
+        else:
+            P.index_copy_(0, rows, cast(pw, P.dtype))
+            M.index_copy_(0, rows, cast(m, M.dtype))
+            V.index_copy_(0, rows, cast(v, V.dtype))

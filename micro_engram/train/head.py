@@ -1,0 +1,261 @@
+"""Vocab-parallel tied embedding and chunked softcapped loss (full logits never exist).
+
+Each rank keeps row_range(V) of the tied embedding / output head (outside the base):
+
+  embed  every rank fetches its tokens' rows from their owners and scales by sqrt(d) (in
+         the weight dtype, like Gemma4TextScaledWordEmbedding). CUDA: one gather kernel reads
+         the owners' rows straight from their peer-mapped shards. CPU: the row all_to_all.
+  loss   per chunk of tokens, the chunk's hidden states are gathered from all ranks, each rank
+         computes logits against its own vocab rows (bf16 GEMM, fp32 softcap), and the
+         per-row (max, sum-exp, target logit) partials are combined across ranks into the LSE.
+         CUDA: one row kernel produces the partials in a single pass over the bf16 logits,
+         and the backward overwrites the recomputed logits in place with
+         (softmax - onehot) * w * softcap' before the dH GEMM and the reduce-scatter.
+
+Every rank runs the same chunk count: the chunk size comes from ceil(V/world), never from
+this rank's own row count (micro_engram/train/head.py:38-42 of the reference). Loss terms
+are sums; the trainer divides by the step's trained-token count.
+"""
+import torch
+import torch.distributed as dist
+
+from micro_engram_fork_b200.ops import use_native
+
+from ..rows import _group, _RowLookup, row_range
+
+IGNORE = -100
+
+
+class VocabShard:
+    def __init__(self, weight, rank, world, embed_scale=None, softcap=None, chunk_tokens=2048,
+                 chunk_bytes=256 << 20, device=None, dtype=None):
+        self.V, self.d = int(weight.shape[0]), int(weight.shape[1])
+        self.rank, self.world = rank, world
+        self.start, self.rows = row_range(self.V, rank, world)
+        self.per = -(-self.V // world)
+        device = torch.device(device) if device is not None else weight.device
+        dtype = dtype or weight.dtype
+        self._buf = None
+        local = weight[self.start:self.start + self.rows].detach()
+        if device.type == "cuda" and world > 1 and use_native(torch.empty(0, device=device)):
+            # peer-mapped shard (padded to `per` rows, same layout on every rank)
+            from micro_engram_fork_b200.parallel.symm import SymmBuffer
+
+            esz = torch.empty((), dtype=dtype).element_size()
+            self._buf = SymmBuffer(self.per * self.d * esz, device, _group(world))
+            full = self._buf.view(0, (self.per, self.d), dtype)
+            full[:self.rows].copy_(local.to(device=device, dtype=dtype))
+            self.weight = full[:self.rows]
+            self._ptrs = torch.tensor(self._buf.ptrs, dtype=torch.int64, device=device)
+        else:
+            self.weight = local.to(device=device, dtype=dtype).clone()
+            self._ptrs = None
+        self._per_t = None
+        self.embed_scale = embed_scale
+        self.softcap = softcap
+        fit = max(64, chunk_bytes // max(1, world * self.per * 4))
+        self.chunk = max(1, min(chunk_tokens, fit))
+
+    @property
+    def group(self):
+        return _group(self.world)
+
+    @torch.no_grad()
+    def embed(self, ids):
+        """[*ids.shape, d] embeddings (frozen, no autograd), times sqrt(d) in the weight dtype."""
+        flat = ids.reshape(-1).to(self.weight.device)
+        if use_native(flat):
+            from micro_engram_fork_b200 import native
+
+            if self._ptrs is None:
+                out = self.weight.index_select(0, flat)
+            else:
+                if self._per_t is None:
+                    self._per_t = torch.tensor([self.per], dtype=torch.int64, device=flat.device)
+                src = 0 if self.weight.dtype == torch.bfloat16 else 1
+                out = native().engram_gather(flat.long().reshape(1, -1).contiguous(), self._ptrs, self._per_t,
+                                             self.world, self.d, src, self.weight.dtype, None)
+        else:
+            out = _RowLookup.apply(flat, ([0, self.V], [self.per], self.rank, self.world), self.weight)
+        out = out.reshape(*ids.shape, self.d)
+        if self.embed_scale is not None:
+            out = out * torch.tensor(self.embed_scale, dtype=self.weight.dtype, device=out.device)
+        return out
+
+    def loss_sum(self, hidden, labels):
+        """(sum of this rank's token losses, its trained-token count). hidden [N, d] requires
+        grad; labels [N] with -100 untrained. Collective: every rank calls it with the same N."""
+        count = (labels != IGNORE).sum()
+        labels = labels.to(hidden.device)
+        if use_native(hidden) and self.weight.dtype == torch.bfloat16:
+            total = _FusedVocabCE.apply(hidden, labels, self)
+        else:
+            total = _VocabParallelCE.apply(hidden, labels, self)
+        return total, count
+
+
+def _gather(x, group, world):
+    if world == 1:
+        return x
+    out = x.new_empty((world * x.shape[0],) + tuple(x.shape[1:]))
+    dist.all_gather_into_tensor(out, x.contiguous(), group=group)
+    return out
+
+
+def _reduce_scatter(x, n, d, group, world):
+    if world == 1:
+        return x
+    out = torch.empty(n, d, dtype=x.dtype, device=x.device)
+    dist.reduce_scatter_tensor(out, x.contiguous(), group=group)
+    return out
+
+
+def _chunk_logits(h, w, softcap):
+    z = (h @ w.t()).float()
+    if softcap:
+        z.div_(softcap).tanh_().mul_(softcap)
+    return z
+
+
+class _VocabParallelCE(torch.autograd.Function):
+    """PyTorch path (CPU/gloo and the oracle)."""
+
+    @staticmethod
+    def forward(ctx, hidden, labels, shard):
+        world, group, w = shard.world, shard.group, shard.weight
+        N, c = hidden.shape[0], shard.chunk
+        h = hidden.detach().to(w.dtype)
+        lses, total = [], torch.zeros((), dtype=torch.float32, device=hidden.device)
+        for a in range(0, N, c):
+            b = min(N, a + c)
+            H = _gather(h[a:b], group, world)
+            L = _gather(labels[a:b].contiguous(), group, world)
+            z = _chunk_logits(H, w, shard.softcap)
+            m = z.max(dim=1).values
+            loc = L - shard.start
+            mine = (L != IGNORE) & (loc >= 0) & (loc < shard.rows)
+            tgt = torch.zeros_like(m)
+            idx = mine.nonzero().squeeze(1)
+            if idx.numel():
+                tgt[idx] = z[idx, loc[idx]]
+            if world > 1:
+                dist.all_reduce(m, op=dist.ReduceOp.MAX, group=group)
+            s = z.sub_(m[:, None]).exp_().sum(dim=1)
+            if world > 1:
+                st = torch.stack([s, tgt])
+                dist.all_reduce(st, group=group)
+                s, tgt = st[0], st[1]
+            lse = m + torch.log(s)
+            n = b - a
+            own = slice(shard.rank * n, (shard.rank + 1) * n)
+            valid = L[own] != IGNORE
+            total = total + torch.where(valid, lse[own] - tgt[own], torch.zeros_like(lse[own])).sum()
+            lses.append(lse)
+        ctx.shard = shard
+        ctx.save_for_backward(hidden.detach(), labels, *lses)
+        return total
+
+    @staticmethod
+    def backward(ctx, g):
+        shard = ctx.shard
+        hidden, labels, *lses = ctx.saved_tensors
+        world, group, w = shard.world, shard.group, shard.weight
+        N, c = hidden.shape[0], shard.chunk
+        gs = _gather(g.detach().float().reshape(1), group, world)
+        h = hidden.to(w.dtype)
+        grad = torch.empty(N, shard.d, dtype=hidden.dtype, device=hidden.device)
+        for k, a in enumerate(range(0, N, c)):
+            b = min(N, a + c)
+            n = b - a
+            H = _gather(h[a:b], group, world)
+            L = _gather(labels[a:b].contiguous(), group, world)
+            p = _chunk_logits(H, w, shard.softcap)
+            cap = (p / shard.softcap).pow_(2).neg_().add_(1) if shard.softcap else None
+            p.sub_(lses[k][:, None]).exp_()
+            loc = L - shard.start
+            mine = (L != IGNORE) & (loc >= 0) & (loc < shard.rows)
+            idx = mine.nonzero().squeeze(1)
+            if idx.numel():
+                p[idx, loc[idx]] -= 1
+            p.mul_((gs.repeat_interleave(n) * (L != IGNORE).float())[:, None])
+            if cap is not None:
+                p.mul_(cap)
+            dH = (p.to(w.dtype) @ w).float()
+            grad[a:b] = _reduce_scatter(dH, n, shard.d, group, world).to(grad.dtype)
+        return grad, None, None
+
+
+class _FusedVocabCE(torch.autograd.Function):
+    """CUDA path: bf16 logits GEMM + one-pass softcap/LSE row kernel; in-place gradient."""
+
+    @staticmethod
+    def forward(ctx, hidden, labels, shard):
+        from micro_engram_fork_b200 import native
+
+        C = native()
+        world, group, w = shard.world, shard.group, shard.weight
+        N, c = hidden.shape[0], shard.chunk
+        cap = float(shard.softcap or 0.0)
+        h = hidden.detach().to(w.dtype)
+        lses, total = [], torch.zeros((), dtype=torch.float32, device=hidden.device)
+        for a in range(0, N, c):
+            b = min(N, a + c)
+            H = _gather(h[a:b], group, world)
+            L = _gather(labels[a:b].contiguous(), group, world)
+            z = H @ w.t()
+            m, s, tgt = C.ce_fwd(z, L, shard.start, cap)
+            del z
+            if world > 1:
+                M = m.clone()
+                dist.all_reduce(M, op=dist.ReduceOp.MAX, group=group)
+                st = torch.stack([s * torch.exp(m - M), tgt])
+                dist.all_reduce(st, group=group)
+                m, s, tgt = M, st[0], st[1]
+            lse = m + torch.log(s)
+            n = b - a
+            own = slice(shard.rank * n, (shard.rank + 1) * n)
+            valid = L[own] != IGNORE
+            total = total + torch.where(valid, lse[own] - tgt[own], torch.zeros_like(lse[own])).sum()
+            lses.append(lse)
+        ctx.shard = shard
+        ctx.save_for_backward(hidden.detach(), labels, *lses)
+        return total
+
+    @staticmethod
+    def backward(ctx, g):
+        from micro_engram_fork_b200 import native
+
+        C = native()
+        shard = ctx.shard
+        hidden, labels, *lses = ctx.saved_tensors
+        world, group, w = shard.world, shard.group, shard.weight
+        N, c = hidden.shape[0], shard.chunk
+        cap = float(shard.softcap or 0.0)
+        gs = _gather(g.detach().float().reshape(1), group, world)
+        h = hidden.to(w.dtype)
+        grad = torch.empty(N, shard.d, dtype=hidden.dtype, device=hidden.device)
+        for k, a in enumerate(range(0, N, c)):
+            b = min(N, a + c)
+            n = b - a
+            H = _gather(h[a:b], group, world)
+            L = _gather(labels[a:b].contiguous(), group, world)
+            z = H @ w.t()
+            w_row = gs.repeat_interleave(n) * (L != IGNORE).float()
+            C.ce_bwd_inplace(z, L, shard.start, cap, lses[k], w_row)
+            if world > 1:
+                dH = torch.matmul(z, w).float()
+                grad[a:b] = _reduce_scatter(dH, n, shard.d, group, world).to(grad.dtype)
+            else:
+                grad[a:b] = torch.matmul(z, w).to(grad.dtype)
+        return grad, None, None
+
+
+def reference_loss_sum(hidden, labels, weight, softcap=None):
+    """Plain full-logit loss sum (tests)."""
+    z = (hidden.to(weight.dtype) @ weight.t()).float()
+    if softcap:
+        z = torch.tanh(z / softcap) * softcap
+    valid = labels != IGNORE
+    lse = torch.logsumexp(z, dim=-1)
+    tgt = z.gather(1, labels.clamp_min(0)[:, None]).squeeze(1)
+    return torch.where(valid, lse - tgt, torch.zeros_like(lse)).sum()

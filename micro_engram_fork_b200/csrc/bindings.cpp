@@ -1,0 +1,100 @@
+// Python bindings of the sm_100a extension (micro_engram_fork_b200._C).
+#include <torch/extension.h>
+
+// engram.cu
+torch::Tensor engram_hash(torch::Tensor ids, c10::optional<torch::Tensor> pos, torch::Tensor canon,
+                          torch::Tensor mults, torch::Tensor orders, torch::Tensor rows, int64_t pad_id);
+torch::Tensor engram_hash_prev(torch::Tensor ids, torch::Tensor canon, torch::Tensor mults, torch::Tensor orders,
+                               torch::Tensor rows, int64_t pad_id);
+torch::Tensor engram_gather(torch::Tensor idx, torch::Tensor ptrs, torch::Tensor per, int64_t world, int64_t dim,
+                            int64_t src_dtype, torch::ScalarType out_dtype, c10::optional<torch::Tensor> status);
+void engram_scatter_grad(torch::Tensor g, torch::Tensor idx, torch::Tensor acc_ptrs, torch::Tensor bit_ptrs,
+                         torch::Tensor list_ptrs, torch::Tensor cnt_ptrs, torch::Tensor per, int64_t world,
+                         double scale, c10::optional<torch::Tensor> status);
+void engram_touched_sqnorm(torch::Tensor acc_ptrs, torch::Tensor list_ptrs, torch::Tensor cnt_ptrs, int64_t dim,
+                           torch::Tensor sq);
+void engram_clip_coef(torch::Tensor sq, double max_norm, torch::Tensor coef, torch::Tensor norm);
+void engram_adam_touched(torch::Tensor p, torch::Tensor m, torch::Tensor v, torch::Tensor acc, torch::Tensor bits,
+                         torch::Tensor list, torch::Tensor cnt, c10::optional<torch::Tensor> coef, double lr,
+                         double beta1, double beta2, double eps, double wd, double bc1, double bc2, bool sr,
+                         int64_t seed, int64_t step, int64_t table_id);
+void adam_dense(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, double lr, double beta1,
+                double beta2, double eps, double wd, double bc1, double bc2, double gscale, bool sr, int64_t seed,
+                int64_t step);
+std::vector<torch::Tensor> engram_gate_fwd(torch::Tensor h, torch::Tensor k, torch::Tensor v,
+                                           c10::optional<torch::Tensor> qs, c10::optional<torch::Tensor> ks,
+                                           c10::optional<torch::Tensor> keep, bool sqrt_gate,
+                                           c10::optional<torch::Tensor> gate_acc);
+std::vector<torch::Tensor> engram_gate_bwd(torch::Tensor g, torch::Tensor h, torch::Tensor k, torch::Tensor v,
+                                           c10::optional<torch::Tensor> qs, c10::optional<torch::Tensor> ks,
+                                           c10::optional<torch::Tensor> keep, torch::Tensor stats, bool sqrt_gate);
+// norm.cu
+std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, c10::optional<torch::Tensor> w, double eps);
+torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, c10::optional<torch::Tensor> w, torch::Tensor rstd,
+                          c10::optional<torch::Tensor> dx_add);
+std::vector<torch::Tensor> post_norm_add(torch::Tensor r, torch::Tensor a, torch::Tensor w_post,
+                                         c10::optional<torch::Tensor> ls, c10::optional<torch::Tensor> w_next,
+                                         double eps);
+std::vector<torch::Tensor> post_norm_add_bwd(c10::optional<torch::Tensor> dxo, c10::optional<torch::Tensor> dh,
+                                             torch::Tensor a, torch::Tensor x, torch::Tensor w_post,
+                                             c10::optional<torch::Tensor> ls, c10::optional<torch::Tensor> w_next,
+                                             torch::Tensor rstd_a, c10::optional<torch::Tensor> rstd_x);
+std::vector<torch::Tensor> qkv_norm_rope(torch::Tensor qkv, torch::Tensor qw, torch::Tensor kw,
+                                         torch::Tensor inv_freq, torch::Tensor pos, int64_t Hq, int64_t Hk, int64_t D,
+                                         bool kv_shared, double eps);
+torch::Tensor qkv_norm_rope_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor qkv,
+                                torch::Tensor qw, torch::Tensor kw, torch::Tensor inv_freq, torch::Tensor pos,
+                                torch::Tensor rstd, int64_t Hq, int64_t Hk, int64_t D, bool kv_shared);
+torch::Tensor geglu_fwd(torch::Tensor gu);
+torch::Tensor geglu_bwd(torch::Tensor dm, torch::Tensor gu);
+// ce.cu
+std::vector<torch::Tensor> ce_fwd(torch::Tensor z, torch::Tensor labels, int64_t start, double softcap);
+void ce_bwd_inplace(torch::Tensor z, torch::Tensor labels, int64_t start, double softcap, torch::Tensor lse,
+                    torch::Tensor w_row);
+// attention.cu
+std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor doc_start,
+                                    int64_t window, double scale);
+std::vector<torch::Tensor> attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                    torch::Tensor o, torch::Tensor lse, torch::Tensor doc_start, int64_t window,
+                                    double scale);
+// symm.cpp
+int64_t symm_alloc(int64_t nbytes, int64_t device);
+void symm_free(int64_t ptr, int64_t device);
+py::bytes symm_export(int64_t ptr, int64_t device);
+int64_t symm_import(py::bytes handle, int64_t device);
+void symm_close(int64_t ptr, int64_t device);
+torch::Tensor symm_view(int64_t ptr, std::vector<int64_t> shape, torch::ScalarType dtype, int64_t device);
+bool can_access_peer(int64_t dev, int64_t peer);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "micro_engram_fork_b200 sm_100a kernels";
+  m.def("engram_hash", &engram_hash);
+  m.def("engram_hash_prev", &engram_hash_prev);
+  m.def("engram_gather", &engram_gather);
+  m.def("engram_scatter_grad", &engram_scatter_grad);
+  m.def("engram_touched_sqnorm", &engram_touched_sqnorm);
+  m.def("engram_clip_coef", &engram_clip_coef);
+  m.def("engram_adam_touched", &engram_adam_touched);
+  m.def("adam_dense", &adam_dense);
+  m.def("engram_gate_fwd", &engram_gate_fwd);
+  m.def("engram_gate_bwd", &engram_gate_bwd);
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("post_norm_add", &post_norm_add);
+  m.def("post_norm_add_bwd", &post_norm_add_bwd);
+  m.def("qkv_norm_rope", &qkv_norm_rope);
+  m.def("qkv_norm_rope_bwd", &qkv_norm_rope_bwd);
+  m.def("geglu_fwd", &geglu_fwd);
+  m.def("geglu_bwd", &geglu_bwd);
+  m.def("ce_fwd", &ce_fwd);
+  m.def("ce_bwd_inplace", &ce_bwd_inplace);
+  m.def("attn_fwd", &attn_fwd);
+  m.def("attn_bwd", &attn_bwd);
+  m.def("symm_alloc", &symm_alloc);
+  m.def("symm_free", &symm_free);
+  m.def("symm_export", &symm_export);
+  m.def("symm_import", &symm_import);
+  m.def("symm_close", &symm_close);
+  m.def("symm_view", &symm_view);
+  m.def("can_access_peer", &can_access_peer);
+}

@@ -1,0 +1,816 @@
+// Engram kernels for sm_100a: n-gram hashing, table-row gather from the row owners (local
+// or NVLink peer memory), the gated residual injection (forward and backward), the push of
+// row gradients into the owners' accumulators, and the touched-row AdamW with stochastic
+// rounding.
+//
+// Behaviour mirrors the reference PyTorch engram (micro_engram/module.py:183-265 for hash
+// and gate, micro_engram/rows.py:76-147 for the row exchange, micro_engram/optim.py:65-133
+// for the optimizer); the B200 design replaces the all_to_all + host sync exchange with
+// direct peer loads/stores/atomics through a table of per-rank base pointers, so no host
+// round trip sits inside the step.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+using namespace me;
+
+namespace {
+
+constexpr int64_t kPrime = 2147483647LL;  // 2^31 - 1
+
+ME_DEVICE int64_t floor_mod(int64_t x, int64_t m) {
+  int64_t r = x % m;
+  return r < 0 ? r + m : r;
+}
+
+// ------------------------------------------------------------------------------ hash
+// ids [B, T]; pos [B, T] or null. out [n_tables, B*T].
+// token t-i of the n-gram: canon[clamp(ids[t-i])], or the RAW pad id when t-i < 0 or the
+// document started after it (pos[t] < i).
+__global__ void hash_kernel(const int64_t* __restrict__ ids, const int64_t* __restrict__ pos,
+                            int64_t B, int64_t T, const int64_t* __restrict__ canon, int64_t V,
+                            const int64_t* __restrict__ mults, int n_tables, int max_order,
+                            const int* __restrict__ orders, const int64_t* __restrict__ rows,
+                            int64_t pad_id, int64_t* __restrict__ out) {
+  const int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= B * T) return;
+  const int64_t b = n / T, t = n % T;
+  int64_t tok[8];
+  const int64_t p = pos ? pos[n] : INT64_MAX;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if (i >= max_order) break;
+    if (t - i < 0 || (i > 0 && p < i)) {
+      tok[i] = pad_id;
+    } else {
+      int64_t id = ids[b * T + t - i];
+      id = id < 0 ? 0 : (id >= V ? V - 1 : id);
+      tok[i] = canon[id];
+    }
+  }
+  for (int k = 0; k < n_tables; ++k) {
+    const int ord = orders[k];
+    int64_t x = 0;
+    for (int i = 0; i < ord; ++i) x += tok[i] * mults[k * max_order + i];
+    out[(int64_t)k * B * T + n] = floor_mod(floor_mod(x, kPrime), rows[k]);
+  }
+}
+
+// ids [N, max_order]: column i is the token at t-i, -1 where there is none.
+__global__ void hash_prev_kernel(const int64_t* __restrict__ ids, int64_t N,
+                                 const int64_t* __restrict__ canon, int64_t V,
+                                 const int64_t* __restrict__ mults, int n_tables, int max_order,
+                                 const int* __restrict__ orders, const int64_t* __restrict__ rows,
+                                 int64_t pad_id, int64_t* __restrict__ out) {
+  const int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  int64_t tok[8];
+  for (int i = 0; i < max_order && i < 8; ++i) {
+    int64_t id = ids[n * max_order + i];
+    if (id < 0) {
+      tok[i] = pad_id;
+    } else {
+      id = id >= V ? V - 1 : id;
+      tok[i] = canon[id];
+    }
+  }
+  for (int k = 0; k < n_tables; ++k) {
+    const int ord = orders[k];
+    int64_t x = 0;
+    for (int i = 0; i < ord; ++i) x += tok[i] * mults[k * max_order + i];
+    out[(int64_t)k * N + n] = floor_mod(floor_mod(x, kPrime), rows[k]);
+  }
+}
+
+// ------------------------------------------------------------------------------ gather
+// mem[n, k*dim + c] = table_k[idx[k, n], c], read from the owner of the row:
+// owner = row / per[k], local = row - owner*per[k], base = ptrs[owner*n_tables + k].
+// One thread per 8 output elements (one 16-byte store).
+template <typename Tin, typename Tout>
+__global__ void gather_kernel(const int64_t* __restrict__ idx, int64_t N, int n_tables, int dim,
+                              const int64_t* __restrict__ ptrs, const int64_t* __restrict__ per,
+                              int world, Tout* __restrict__ mem, int* status) {
+  const int chunks = dim / 8;
+  const int64_t total = N * n_tables * chunks;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % chunks);
+    const int64_t nk = i / chunks;
+    const int k = (int)(nk % n_tables);
+    const int64_t n = nk / n_tables;
+    const int64_t row = idx[(int64_t)k * N + n];
+    const int64_t pk = per[k];
+    int owner = (int)(row / pk);
+    const int64_t local = row - (int64_t)owner * pk;
+#ifdef ME_BOUNDS_CHECK
+    if (row < 0 || owner >= world) {
+      report(status, ME_ERR_BOUNDS, (int)k);
+      continue;
+    }
+#endif
+    const Tin* src = reinterpret_cast<const Tin*>(ptrs[owner * n_tables + k]) + local * dim + c * 8;
+    float v[8];
+    if constexpr (sizeof(Tin) == 2) {
+      BF16x8 x;
+      x.u = *reinterpret_cast<const uint4*>(src);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = bf2f(x.h[j]);
+    } else {
+      F32x4 a, b;
+      a.v = *reinterpret_cast<const float4*>(src);
+      b.v = *reinterpret_cast<const float4*>(src + 4);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[j] = a.f[j];
+        v[4 + j] = b.f[j];
+      }
+    }
+    Tout* dst = mem + n * (int64_t)n_tables * dim + (int64_t)k * dim + c * 8;
+    if constexpr (sizeof(Tout) == 2) {
+      BF16x8 y;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) y.h[j] = f2bf(v[j]);
+      *reinterpret_cast<uint4*>(dst) = y.u;
+    } else {
+      F32x4 a, b;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        a.f[j] = v[j];
+        b.f[j] = v[4 + j];
+      }
+      *reinterpret_cast<float4*>(dst) = a.v;
+      *reinterpret_cast<float4*>(dst + 4) = b.v;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------ row grads
+// Backward of the gather: every looked-up row's gradient (scaled by `scale`, 1/world as the
+// reference's owner-side average) is added into the owner's fp32 accumulator with float4
+// atomics (peer memory over NVLink when the owner is another GPU), and the row is marked
+// touched in the owner's bitmap; the first toucher appends it to the owner's touched list.
+// State pointer table layout, per (rank, table): acc [per, dim] fp32, bits [ceil(per/32)]
+// u32, list [per] i32, count [1] i32.
+template <typename Tg>
+__global__ void scatter_grad_kernel(const Tg* __restrict__ g, const int64_t* __restrict__ idx,
+                                    int64_t N, int n_tables, int dim,
+                                    const int64_t* __restrict__ acc_ptrs,
+                                    const int64_t* __restrict__ bit_ptrs,
+                                    const int64_t* __restrict__ list_ptrs,
+                                    const int64_t* __restrict__ cnt_ptrs,
+                                    const int64_t* __restrict__ per, int world, float scale,
+                                    int* status) {
+  const int chunks = dim / 4;
+  const int64_t total = N * n_tables * chunks;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % chunks);
+    const int64_t nk = i / chunks;
+    const int k = (int)(nk % n_tables);
+    const int64_t n = nk / n_tables;
+    const int64_t row = idx[(int64_t)k * N + n];
+    const int64_t pk = per[k];
+    const int owner = (int)(row / pk);
+    const int64_t local = row - (int64_t)owner * pk;
+#ifdef ME_BOUNDS_CHECK
+    if (row < 0 || owner >= world) {
+      report(status, ME_ERR_BOUNDS, (int)k);
+      continue;
+    }
+#endif
+    const Tg* src = g + n * (int64_t)n_tables * dim + (int64_t)k * dim + c * 4;
+    float4 v;
+    if constexpr (sizeof(Tg) == 2) {
+      const __nv_bfloat162* s2 = reinterpret_cast<const __nv_bfloat162*>(src);
+      const float2 a = __bfloat1622float2(s2[0]), b = __bfloat1622float2(s2[1]);
+      v = make_float4(a.x * scale, a.y * scale, b.x * scale, b.y * scale);
+    } else {
+      const float4 a = *reinterpret_cast<const float4*>(src);
+      v = make_float4(a.x * scale, a.y * scale, a.z * scale, a.w * scale);
+    }
+    const int slot = owner * n_tables + k;
+    float* acc = reinterpret_cast<float*>(acc_ptrs[slot]) + local * dim + c * 4;
+    atomicAdd(reinterpret_cast<float4*>(acc), v);
+    if (c == 0) {
+      uint32_t* bits = reinterpret_cast<uint32_t*>(bit_ptrs[slot]);
+      const uint32_t bit = 1u << (local & 31);
+      const uint32_t old = atomicOr(bits + (local >> 5), bit);
+      if (!(old & bit)) {
+        int* cnt = reinterpret_cast<int*>(cnt_ptrs[slot]);
+        const int pos = atomicAdd(cnt, 1);
+        if (pos < pk) {
+          reinterpret_cast<int*>(list_ptrs[slot])[pos] = (int)local;
+        } else {
+          report(status, ME_ERR_CAPACITY, k);
+        }
+      }
+    }
+  }
+}
+
+// Sum of squares of the touched rows' accumulated gradients (every row lives on exactly one
+// rank, so the sum over ranks is the global table norm^2). counts are read on the device.
+__global__ void touched_sqnorm_kernel(const int64_t* __restrict__ acc_ptrs,
+                                      const int64_t* __restrict__ list_ptrs,
+                                      const int64_t* __restrict__ cnt_ptrs, int n_tables, int dim,
+                                      float* __restrict__ out) {
+  __shared__ float scratch[64];
+  float local_sum = 0.f;
+  const int lane = threadIdx.x & 31;
+  const int warps_total = gridDim.x * (blockDim.x >> 5);
+  const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  for (int k = 0; k < n_tables; ++k) {
+    const int cnt = *reinterpret_cast<const int*>(cnt_ptrs[k]);
+    const int* list = reinterpret_cast<const int*>(list_ptrs[k]);
+    const float* acc = reinterpret_cast<const float*>(acc_ptrs[k]);
+    for (int r = wid; r < cnt; r += warps_total) {
+      const float* a = acc + (int64_t)list[r] * dim;
+      for (int j = lane; j < dim; j += 32) local_sum += a[j] * a[j];
+    }
+  }
+  const float s = block_sum(local_sum, scratch);
+  if (threadIdx.x == 0) atomicAdd(out, s);
+}
+
+// coef = min(1, max_norm / (sqrt(sq) + 1e-6)); also stores the norm.
+__global__ void clip_coef_kernel(const float* sq, float max_norm, float* coef, float* norm) {
+  const float n = sqrtf(*sq);
+  *norm = n;
+  *coef = max_norm > 0.f ? fminf(1.f, max_norm / (n + 1e-6f)) : 1.f;
+}
+
+// AdamW on the touched rows of one table shard (micro_engram/optim.py:65-133 semantics):
+// rows whose gradient is all zero are left alone; rowwise keeps ONE fp32 second moment per
+// row (mean of g^2 over the row); bf16 weights/moments are written back with stochastic
+// rounding (Philox4x32-10 keyed by seed/step, counter = row, column block). The
+// accumulator row and its touched bit are cleared for the next step. One warp per row.
+template <typename Tp, typename Tm>
+__global__ void adam_touched_kernel(Tp* __restrict__ p, Tm* __restrict__ m, float* __restrict__ v_row,
+                                    Tm* __restrict__ v_val, float* __restrict__ acc,
+                                    uint32_t* __restrict__ bits, const int* __restrict__ list,
+                                    const int* __restrict__ cnt_ptr, int dim, const float* coef_ptr,
+                                    float lr, float beta1, float beta2, float eps, float wd, float bc1,
+                                    float bc2_sqrt, int sr, uint32_t seed, uint32_t step,
+                                    uint32_t table_id) {
+  const int lane = threadIdx.x & 31;
+  const int warps_total = gridDim.x * (blockDim.x >> 5);
+  const int cnt = *cnt_ptr;
+  const float coef = coef_ptr ? *coef_ptr : 1.f;
+  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < cnt; r += warps_total) {
+    const int64_t row = list[r];
+    float* a = acc + row * dim;
+    // gradient of this row (dim <= 256: at most 8 per lane)
+    float g[8];
+    bool nz = false;
+    float gsq = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int j = lane + q * 32;
+      g[q] = 0.f;
+      if (j < dim) {
+        g[q] = a[j] * coef;
+        nz |= (a[j] != 0.f);
+        gsq += g[q] * g[q];
+        a[j] = 0.f;
+      }
+    }
+    if (lane == 0) atomicAnd(bits + (row >> 5), ~(1u << (row & 31)));
+    if (!__any_sync(0xffffffffu, nz)) continue;
+    float vr = 0.f;
+    if (v_row) {
+      const float mean_g2 = warp_sum(gsq) / (float)dim;
+      vr = v_row[row] * beta2 + (1.f - beta2) * mean_g2;
+    }
+    const Philox4 rnd0 = philox4x32_10((uint32_t)row, table_id, (uint32_t)lane, 0u, seed, step);
+    const Philox4 rnd1 = philox4x32_10((uint32_t)row, table_id, (uint32_t)lane, 1u, seed, step);
+    const uint32_t rbits[8] = {rnd0.c[0], rnd0.c[1], rnd0.c[2], rnd0.c[3],
+                               rnd1.c[0], rnd1.c[1], rnd1.c[2], rnd1.c[3]};
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int j = lane + q * 32;
+      if (j >= dim) break;
+      const int64_t o = row * dim + j;
+      float pw = to_f(p[o]);
+      float mw = to_f(m[o]);
+      if (wd != 0.f) pw *= (1.f - lr * wd);
+      mw = mw * beta1 + (1.f - beta1) * g[q];
+      float denom;
+      float vv = 0.f;
+      if (v_row) {
+        denom = sqrtf(vr) / bc2_sqrt + eps;
+      } else {
+        vv = to_f(v_val[o]) * beta2 + (1.f - beta2) * g[q] * g[q];
+        denom = sqrtf(vv) / bc2_sqrt + eps;
+      }
+      pw = pw + (-lr / bc1) * mw / denom;
+      // write back (stochastic rounding for bf16 when enabled)
+      const uint32_t rb = rbits[q];
+      if constexpr (sizeof(Tp) == 2) {
+        p[o] = sr ? sr_bf16(pw, rb) : f2bf(pw);
+      } else {
+        p[o] = pw;
+      }
+      if constexpr (sizeof(Tm) == 2) {
+        m[o] = sr ? sr_bf16(mw, rb >> 16) : f2bf(mw);
+        if (!v_row) v_val[o] = sr ? sr_bf16(vv, rb * 2654435761u) : f2bf(vv);
+      } else {
+        m[o] = mw;
+        if (!v_row) v_val[o] = vv;
+      }
+    }
+    if (v_row && lane == 0) v_row[row] = vr;
+  }
+}
+
+// Plain AdamW over a whole tensor (the replicated dense engram parameters, and tables
+// trained with the non-lazy optimizer). g is fp32 or the param dtype.
+template <typename Tp, typename Tg>
+__global__ void adam_dense_kernel(Tp* __restrict__ p, const Tg* __restrict__ g, Tp* __restrict__ m,
+                                  Tp* __restrict__ v, int64_t n, float lr, float beta1, float beta2,
+                                  float eps, float wd, float bc1, float bc2_sqrt, float gscale, int sr,
+                                  uint32_t seed, uint32_t step) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float gr = to_f(g[i]) * gscale;
+    float pw = to_f(p[i]), mw = to_f(m[i]), vw = to_f(v[i]);
+    if (wd != 0.f) pw *= (1.f - lr * wd);
+    mw = mw * beta1 + (1.f - beta1) * gr;
+    vw = vw * beta2 + (1.f - beta2) * gr * gr;
+    pw = pw + (-lr / bc1) * mw / (sqrtf(vw) / bc2_sqrt + eps);
+    if constexpr (sizeof(Tp) == 2) {
+      const Philox4 r = philox4x32_10((uint32_t)i, (uint32_t)(i >> 32), 0x5eedu, 0u, seed, step);
+      p[i] = sr ? sr_bf16(pw, r.c[0]) : f2bf(pw);
+      m[i] = sr ? sr_bf16(mw, r.c[1]) : f2bf(mw);
+      v[i] = sr ? sr_bf16(vw, r.c[2]) : f2bf(vw);
+    } else {
+      p[i] = pw;
+      m[i] = mw;
+      v[i] = vw;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------ gate
+// The scalar / scalar_sqrt gate (micro_engram/module.py:239-261), one block per row:
+//   hn = rms(h) * qs, kn = rms(k) * ks   (fp32, torch's default eps = FLT_EPSILON)
+//   s  = <hn, kn> / sqrt(d);  sqrt gate: s = sign(s) sqrt(max(|s|, 1e-6))
+//   a  = sigmoid(s);  out = h + bf16(a * v) * keep
+// stats[n] = (rh, rk, s_raw, a) for the backward. gate_acc += (sum a, count, count a>0.99).
+constexpr float kEps = 1.1920928955078125e-07f;
+
+template <int VPT>
+__global__ void gate_fwd_kernel(const __nv_bfloat16* __restrict__ h, const __nv_bfloat16* __restrict__ k,
+                                const __nv_bfloat16* __restrict__ v, const float* __restrict__ qs,
+                                const float* __restrict__ ks, const uint8_t* __restrict__ keep,
+                                int64_t N, int d, int sqrt_gate, __nv_bfloat16* __restrict__ out,
+                                float* __restrict__ stats, float* __restrict__ gate_acc) {
+  __shared__ float scratch[64];
+  const float inv_sqrt_d = rsqrtf((float)d);
+  float acc_a = 0.f, acc_n = 0.f, acc_sat = 0.f;
+  for (int64_t n = blockIdx.x; n < N; n += gridDim.x) {
+    const __nv_bfloat16* hr = h + n * d;
+    const __nv_bfloat16* kr = k + n * d;
+    float hv[VPT], kv[VPT];
+    float sh = 0.f, sk = 0.f;
+#pragma unroll
+    for (int q = 0; q < VPT; ++q) {
+      const int j = threadIdx.x + q * blockDim.x;
+      hv[q] = j < d ? bf2f(hr[j]) : 0.f;
+      kv[q] = j < d ? bf2f(kr[j]) : 0.f;
+      sh += hv[q] * hv[q];
+      sk += kv[q] * kv[q];
+    }
+    const float2 ss = block_sum2(sh, sk, scratch);
+    const float rh = rsqrtf(ss.x / d + kEps), rk = rsqrtf(ss.y / d + kEps);
+    float dot = 0.f;
+#pragma unroll
+    for (int q = 0; q < VPT; ++q) {
+      const int j = threadIdx.x + q * blockDim.x;
+      if (j < d) {
+        const float a = hv[q] * rh * (qs ? qs[j] : 1.f);
+        const float b = kv[q] * rk * (ks ? ks[j] : 1.f);
+        dot += a * b;
+      }
+    }
+    const float s_raw = block_sum(dot, scratch) * inv_sqrt_d;
+    float s = s_raw;
+    if (sqrt_gate) {
+      const float sg = s_raw > 0.f ? 1.f : (s_raw < 0.f ? -1.f : 0.f);
+      s = sg * sqrtf(fmaxf(fabsf(s_raw), 1e-6f));
+    }
+    const float alpha = 1.f / (1.f + expf(-s));
+    const float kp = keep ? (keep[n] ? 1.f : 0.f) : 1.f;
+    const __nv_bfloat16* vr = v + n * d;
+    __nv_bfloat16* orow = out + n * d;
+#pragma unroll
+    for (int q = 0; q < VPT; ++q) {
+      const int j = threadIdx.x + q * blockDim.x;
+      if (j < d) {
+        const float add = bf2f(f2bf(alpha * bf2f(vr[j]) * kp));
+        orow[j] = f2bf(hv[q] + add);
+      }
+    }
+    if (threadIdx.x == 0) {
+      stats[n * 4 + 0] = rh;
+      stats[n * 4 + 1] = rk;
+      stats[n * 4 + 2] = s_raw;
+      stats[n * 4 + 3] = alpha;
+      acc_a += alpha;
+      acc_n += 1.f;
+      acc_sat += alpha > 0.99f ? 1.f : 0.f;
+    }
+  }
+  if (gate_acc && threadIdx.x == 0) {
+    atomicAdd(gate_acc + 0, acc_a);
+    atomicAdd(gate_acc + 1, acc_n);
+    atomicAdd(gate_acc + 2, acc_sat);
+  }
+}
+
+// Backward of the gate. g: grad of out. Produces dh (= g + the gate's grad through rms(h)),
+// dk, dv (bf16, as autograd casts them back to the bf16 projections), and per-column
+// partial sums for d(q_scale), d(k_scale) (fp32, atomically added once per block).
+template <int VPT>
+__global__ void gate_bwd_kernel(const __nv_bfloat16* __restrict__ g, const __nv_bfloat16* __restrict__ h,
+                                const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
+                                const float* __restrict__ qs, const float* __restrict__ ks,
+                                const uint8_t* __restrict__ keep, const float* __restrict__ stats,
+                                int64_t N, int d, int sqrt_gate, __nv_bfloat16* __restrict__ dh,
+                                __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv,
+                                float* __restrict__ dqs, float* __restrict__ dks) {
+  __shared__ float scratch[64];
+  const float inv_sqrt_d = rsqrtf((float)d);
+  float pq[VPT], pk[VPT];
+#pragma unroll
+  for (int q = 0; q < VPT; ++q) pq[q] = pk[q] = 0.f;
+  for (int64_t n = blockIdx.x; n < N; n += gridDim.x) {
+    const float rh = stats[n * 4 + 0], rk = stats[n * 4 + 1], s_raw = stats[n * 4 + 2],
+                alpha = stats[n * 4 + 3];
+    const float kp = keep ? (keep[n] ? 1.f : 0.f) : 1.f;
+    float gv[VPT], hv[VPT], kv[VPT];
+    float da = 0.f;
+#pragma unroll
+    for (int q = 0; q < VPT; ++q) {
+      const int j = threadIdx.x + q * blockDim.x;
+      if (j < d) {
+        gv[q] = bf2f(g[n * d + j]);
+        hv[q] = bf2f(h[n * d + j]);
+        kv[q] = bf2f(k[n * d + j]);
+        const float vj = bf2f(v[n * d + j]);
+        da += gv[q] * kp * vj;
+        dv[n * d + j] = f2bf(alpha * gv[q] * kp);
+      } else {
+        gv[q] = hv[q] = kv[q] = 0.f;
+      }
+    }
+    da = block_sum(da, scratch);
+    // through sigmoid and the signed square root
+    float ds = da * alpha * (1.f - alpha);
+    if (sqrt_gate) {
+      const float c = fabsf(s_raw);
+      ds = (c >= 1e-6f && s_raw != 0.f) ? ds * 0.5f / sqrtf(c) : 0.f;
+    }
+    ds *= inv_sqrt_d;  // s = dot / sqrt(d)
+    // dhn_j = ds * kn_j, dkn_j = ds * hn_j; rms-norm backward with weights qs / ks
+    float sum_h = 0.f, sum_k = 0.f;
+#pragma unroll
+    for (int q = 0; q < VPT; ++q) {
+      const int j = threadIdx.x + q * blockDim.x;
+      if (j < d) {
+        const float wq = qs ? qs[j] : 1.f, wk = ks ? ks[j] : 1.f;
+        const float hn0 = hv[q] * rh, kn0 = kv[q] * rk;  // before the scales
+        const float dhn = ds * kn0 * wk, dkn = ds * hn0 * wq;
+        sum_h += hv[q] * wq * dhn;
+        sum_k += kv[q] * wk * dkn;
+        pq[q] += dhn * hn0;
+        pk[q] += dkn * kn0;
+      }
+    }
+    const float2 sums = block_sum2(sum_h, sum_k, scratch);
+    const float ch = rh * rh * rh * sums.x / d, ck = rk * rk * rk * sums.y / d;
+#pragma unroll
+    for (int q = 0; q < VPT; ++q) {
+      const int j = threadIdx.x + q * blockDim.x;
+      if (j < d) {
+        const float wq = qs ? qs[j] : 1.f, wk = ks ? ks[j] : 1.f;
+        const float hn0 = hv[q] * rh, kn0 = kv[q] * rk;
+        const float dhn = ds * kn0 * wk, dkn = ds * hn0 * wq;
+        const float dhg = rh * wq * dhn - ch * hv[q];
+        const float dkg = rk * wk * dkn - ck * kv[q];
+        dh[n * d + j] = f2bf(gv[q] + bf2f(f2bf(dhg)));
+        dk[n * d + j] = f2bf(dkg);
+      }
+    }
+  }
+  if (dqs) {
+#pragma unroll
+    for (int q = 0; q < VPT; ++q) {
+      const int j = threadIdx.x + q * blockDim.x;
+      if (j < d) {
+        atomicAdd(dqs + j, pq[q]);
+        atomicAdd(dks + j, pk[q]);
+      }
+    }
+  }
+}
+
+int sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+int grid_for(int64_t work, int threads, int per_sm = 8) {
+  const int64_t need = (work + threads - 1) / threads;
+  return (int)std::max<int64_t>(1, std::min<int64_t>(need, (int64_t)sm_count() * per_sm));
+}
+
+void check_cuda(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+}
+
+}  // namespace
+
+// ================================================================================ bindings
+torch::Tensor engram_hash(torch::Tensor ids, c10::optional<torch::Tensor> pos, torch::Tensor canon,
+                          torch::Tensor mults, torch::Tensor orders, torch::Tensor rows,
+                          int64_t pad_id) {
+  check_cuda(ids, "ids");
+  TORCH_CHECK(ids.dim() == 2, "ids must be [B, T]");
+  const at::cuda::CUDAGuard guard(ids.device());
+  const int64_t B = ids.size(0), T = ids.size(1);
+  const int nt = (int)mults.size(0), mo = (int)mults.size(1);
+  TORCH_CHECK(mo <= 8, "n-gram orders above 8 are not supported");
+  auto ids64 = ids.to(torch::kLong).contiguous();
+  torch::Tensor pos64;
+  if (pos.has_value()) pos64 = pos->to(torch::kLong).expand({B, T}).contiguous();
+  auto out = torch::empty({nt, B, T}, ids.options().dtype(torch::kLong));
+  const int threads = 256;
+  const int64_t n = B * T;
+  if (n == 0) return out;
+  hash_kernel<<<(n + threads - 1) / threads, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      ids64.data_ptr<int64_t>(), pos.has_value() ? pos64.data_ptr<int64_t>() : nullptr, B, T,
+      canon.data_ptr<int64_t>(), canon.numel(), mults.data_ptr<int64_t>(), nt, mo,
+      orders.data_ptr<int>(), rows.data_ptr<int64_t>(), pad_id, out.data_ptr<int64_t>());
+  return out;
+}
+
+torch::Tensor engram_hash_prev(torch::Tensor ids, torch::Tensor canon, torch::Tensor mults,
+                               torch::Tensor orders, torch::Tensor rows, int64_t pad_id) {
+  check_cuda(ids, "ids");
+  const at::cuda::CUDAGuard guard(ids.device());
+  const int nt = (int)mults.size(0), mo = (int)mults.size(1);
+  TORCH_CHECK(ids.dim() == 2 && ids.size(1) == mo, "ids must be [N, max_order]");
+  auto ids64 = ids.to(torch::kLong).contiguous();
+  const int64_t N = ids.size(0);
+  auto out = torch::empty({nt, N}, ids.options().dtype(torch::kLong));
+  if (N == 0) return out;
+  const int threads = 256;
+  hash_prev_kernel<<<(N + threads - 1) / threads, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      ids64.data_ptr<int64_t>(), N, canon.data_ptr<int64_t>(), canon.numel(), mults.data_ptr<int64_t>(),
+      nt, mo, orders.data_ptr<int>(), rows.data_ptr<int64_t>(), pad_id, out.data_ptr<int64_t>());
+  return out;
+}
+
+// idx [n_tables, N] int64 (global rows per table); ptrs [world*n_tables] int64 device
+// addresses (this rank's and its peers' shards); per [n_tables] rows per rank.
+torch::Tensor engram_gather(torch::Tensor idx, torch::Tensor ptrs, torch::Tensor per, int64_t world,
+                            int64_t dim, int64_t src_dtype, torch::ScalarType out_dtype,
+                            c10::optional<torch::Tensor> status) {
+  check_cuda(idx, "idx");
+  const at::cuda::CUDAGuard guard(idx.device());
+  const int nt = (int)idx.size(0);
+  const int64_t N = idx.size(1);
+  TORCH_CHECK(dim % 8 == 0, "engram dim must be a multiple of 8");
+  auto mem = torch::empty({N, nt * dim}, idx.options().dtype(out_dtype));
+  if (N == 0) return mem;
+  const int threads = 256;
+  const int64_t work = N * nt * (dim / 8);
+  const int grid = grid_for(work, threads);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  int* st = status.has_value() ? status->data_ptr<int>() : nullptr;
+  const int64_t* ip = idx.data_ptr<int64_t>();
+  const int64_t* pp = ptrs.data_ptr<int64_t>();
+  const int64_t* pe = per.data_ptr<int64_t>();
+  const bool in_bf16 = src_dtype == 0;
+  if (out_dtype == torch::kBFloat16) {
+    auto* o = reinterpret_cast<__nv_bfloat16*>(mem.data_ptr());
+    if (in_bf16)
+      gather_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, threads, 0, stream>>>(ip, N, nt, dim, pp, pe, world, o, st);
+    else
+      gather_kernel<float, __nv_bfloat16><<<grid, threads, 0, stream>>>(ip, N, nt, dim, pp, pe, world, o, st);
+  } else {
+    TORCH_CHECK(out_dtype == torch::kFloat32, "gather output must be bf16 or fp32");
+    auto* o = mem.data_ptr<float>();
+    if (in_bf16)
+      gather_kernel<__nv_bfloat16, float><<<grid, threads, 0, stream>>>(ip, N, nt, dim, pp, pe, world, o, st);
+    else
+      gather_kernel<float, float><<<grid, threads, 0, stream>>>(ip, N, nt, dim, pp, pe, world, o, st);
+  }
+  return mem;
+}
+
+void engram_scatter_grad(torch::Tensor g, torch::Tensor idx, torch::Tensor acc_ptrs, torch::Tensor bit_ptrs,
+                         torch::Tensor list_ptrs, torch::Tensor cnt_ptrs, torch::Tensor per, int64_t world,
+                         double scale, c10::optional<torch::Tensor> status) {
+  check_cuda(g, "g");
+  check_cuda(idx, "idx");
+  const at::cuda::CUDAGuard guard(g.device());
+  const int nt = (int)idx.size(0);
+  const int64_t N = idx.size(1);
+  if (N == 0) return;
+  const int dim = (int)(g.size(1) / nt);
+  TORCH_CHECK(dim % 4 == 0, "engram dim must be a multiple of 4");
+  const int threads = 256;
+  const int grid = grid_for(N * nt * (dim / 4), threads);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  int* st = status.has_value() ? status->data_ptr<int>() : nullptr;
+  if (g.scalar_type() == torch::kBFloat16) {
+    scatter_grad_kernel<__nv_bfloat16><<<grid, threads, 0, stream>>>(
+        reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), idx.data_ptr<int64_t>(), N, nt, dim,
+        acc_ptrs.data_ptr<int64_t>(), bit_ptrs.data_ptr<int64_t>(), list_ptrs.data_ptr<int64_t>(),
+        cnt_ptrs.data_ptr<int64_t>(), per.data_ptr<int64_t>(), world, (float)scale, st);
+  } else {
+    TORCH_CHECK(g.scalar_type() == torch::kFloat32, "row grads must be bf16 or fp32");
+    scatter_grad_kernel<float><<<grid, threads, 0, stream>>>(
+        g.data_ptr<float>(), idx.data_ptr<int64_t>(), N, nt, dim, acc_ptrs.data_ptr<int64_t>(),
+        bit_ptrs.data_ptr<int64_t>(), list_ptrs.data_ptr<int64_t>(), cnt_ptrs.data_ptr<int64_t>(),
+        per.data_ptr<int64_t>(), world, (float)scale, st);
+  }
+}
+
+// sq (fp32 [1], accumulated into) += sum over the local touched rows of acc^2.
+void engram_touched_sqnorm(torch::Tensor acc_ptrs, torch::Tensor list_ptrs, torch::Tensor cnt_ptrs,
+                           int64_t dim, torch::Tensor sq) {
+  const at::cuda::CUDAGuard guard(sq.device());
+  const int nt = (int)acc_ptrs.numel();
+  touched_sqnorm_kernel<<<sm_count() * 2, 512, 0, at::cuda::getCurrentCUDAStream()>>>(
+      acc_ptrs.data_ptr<int64_t>(), list_ptrs.data_ptr<int64_t>(), cnt_ptrs.data_ptr<int64_t>(), nt,
+      (int)dim, sq.data_ptr<float>());
+}
+
+void engram_clip_coef(torch::Tensor sq, double max_norm, torch::Tensor coef, torch::Tensor norm) {
+  const at::cuda::CUDAGuard guard(sq.device());
+  clip_coef_kernel<<<1, 1, 0, at::cuda::getCurrentCUDAStream()>>>(
+      sq.data_ptr<float>(), (float)max_norm, coef.data_ptr<float>(), norm.data_ptr<float>());
+}
+
+void engram_adam_touched(torch::Tensor p, torch::Tensor m, torch::Tensor v, torch::Tensor acc,
+                         torch::Tensor bits, torch::Tensor list, torch::Tensor cnt,
+                         c10::optional<torch::Tensor> coef, double lr, double beta1, double beta2,
+                         double eps, double wd, double bc1, double bc2, bool sr, int64_t seed,
+                         int64_t step, int64_t table_id) {
+  check_cuda(p, "p");
+  const at::cuda::CUDAGuard guard(p.device());
+  const int dim = (int)p.size(1);
+  TORCH_CHECK(dim <= 256, "engram dim above 256 is not supported by the touched-row Adam");
+  TORCH_CHECK(m.scalar_type() == p.scalar_type(), "exp_avg must have the weight dtype");
+  const bool rowwise = v.dim() == 1;
+  TORCH_CHECK(rowwise ? v.scalar_type() == torch::kFloat32 : v.scalar_type() == p.scalar_type(),
+              "exp_avg_sq dtype");
+  const int threads = 256;
+  const int grid = sm_count() * 4;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const float* cp = coef.has_value() ? coef->data_ptr<float>() : nullptr;
+  const float bc2s = (float)std::sqrt(bc2);
+  float* vrow = rowwise ? v.data_ptr<float>() : nullptr;
+  if (p.scalar_type() == torch::kBFloat16) {
+    adam_touched_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, threads, 0, stream>>>(
+        reinterpret_cast<__nv_bfloat16*>(p.data_ptr()), reinterpret_cast<__nv_bfloat16*>(m.data_ptr()), vrow,
+        rowwise ? nullptr : reinterpret_cast<__nv_bfloat16*>(v.data_ptr()), acc.data_ptr<float>(),
+        reinterpret_cast<uint32_t*>(bits.data_ptr<int32_t>()), list.data_ptr<int>(), cnt.data_ptr<int>(), dim,
+        cp, (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd, (float)bc1, bc2s, sr ? 1 : 0,
+        (uint32_t)seed, (uint32_t)step, (uint32_t)table_id);
+  } else {
+    TORCH_CHECK(p.scalar_type() == torch::kFloat32, "tables must be bf16 or fp32");
+    adam_touched_kernel<float, float><<<grid, threads, 0, stream>>>(
+        p.data_ptr<float>(), m.data_ptr<float>(), vrow, rowwise ? nullptr : v.data_ptr<float>(),
+        acc.data_ptr<float>(), reinterpret_cast<uint32_t*>(bits.data_ptr<int32_t>()), list.data_ptr<int>(),
+        cnt.data_ptr<int>(), dim, cp, (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd,
+        (float)bc1, bc2s, 0, (uint32_t)seed, (uint32_t)step, (uint32_t)table_id);
+  }
+}
+
+void adam_dense(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, double lr,
+                double beta1, double beta2, double eps, double wd, double bc1, double bc2, double gscale,
+                bool sr, int64_t seed, int64_t step) {
+  check_cuda(p, "p");
+  check_cuda(g, "g");
+  const at::cuda::CUDAGuard guard(p.device());
+  const int64_t n = p.numel();
+  if (n == 0) return;
+  const int threads = 256;
+  const int grid = grid_for(n, threads, 4);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const float bc2s = (float)std::sqrt(bc2);
+  TORCH_CHECK(m.scalar_type() == p.scalar_type() && v.scalar_type() == p.scalar_type(), "moment dtype");
+  if (p.scalar_type() == torch::kBFloat16) {
+    auto* pp = reinterpret_cast<__nv_bfloat16*>(p.data_ptr());
+    auto* mp = reinterpret_cast<__nv_bfloat16*>(m.data_ptr());
+    auto* vp = reinterpret_cast<__nv_bfloat16*>(v.data_ptr());
+    if (g.scalar_type() == torch::kFloat32)
+      adam_dense_kernel<__nv_bfloat16, float><<<grid, threads, 0, stream>>>(
+          pp, g.data_ptr<float>(), mp, vp, n, (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd,
+          (float)bc1, bc2s, (float)gscale, sr ? 1 : 0, (uint32_t)seed, (uint32_t)step);
+    else
+      adam_dense_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, threads, 0, stream>>>(
+          pp, reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), mp, vp, n, (float)lr, (float)beta1,
+          (float)beta2, (float)eps, (float)wd, (float)bc1, bc2s, (float)gscale, sr ? 1 : 0, (uint32_t)seed,
+          (uint32_t)step);
+  } else {
+    TORCH_CHECK(p.scalar_type() == torch::kFloat32 && g.scalar_type() == torch::kFloat32, "fp32 adam");
+    adam_dense_kernel<float, float><<<grid, threads, 0, stream>>>(
+        p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), n, (float)lr,
+        (float)beta1, (float)beta2, (float)eps, (float)wd, (float)bc1, bc2s, (float)gscale, 0, (uint32_t)seed,
+        (uint32_t)step);
+  }
+}
+
+// stats [N, 4] fp32 out; gate_acc [3] fp32 (accumulated) or None.
+std::vector<torch::Tensor> engram_gate_fwd(torch::Tensor h, torch::Tensor k, torch::Tensor v,
+                                           c10::optional<torch::Tensor> qs, c10::optional<torch::Tensor> ks,
+                                           c10::optional<torch::Tensor> keep, bool sqrt_gate,
+                                           c10::optional<torch::Tensor> gate_acc) {
+  check_cuda(h, "hidden");
+  check_cuda(k, "key");
+  check_cuda(v, "value");
+  TORCH_CHECK(h.scalar_type() == torch::kBFloat16 && k.scalar_type() == torch::kBFloat16 &&
+                  v.scalar_type() == torch::kBFloat16,
+              "the fused gate runs on bf16 hidden/key/value");
+  const at::cuda::CUDAGuard guard(h.device());
+  const int d = (int)h.size(-1);
+  const int64_t N = h.numel() / d;
+  auto out = torch::empty_like(h);
+  auto stats = torch::empty({N, 4}, h.options().dtype(torch::kFloat32));
+  if (N == 0) return {out, stats};
+  const int threads = 256;
+  const int vpt = (d + threads - 1) / threads;
+  TORCH_CHECK(vpt <= 32, "hidden size above 8192 is not supported by the fused gate");
+  const int grid = (int)std::min<int64_t>(N, (int64_t)sm_count() * 8);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto* hp = reinterpret_cast<const __nv_bfloat16*>(h.data_ptr());
+  auto* kp = reinterpret_cast<const __nv_bfloat16*>(k.data_ptr());
+  auto* vp = reinterpret_cast<const __nv_bfloat16*>(v.data_ptr());
+  const float* qsp = qs.has_value() ? qs->data_ptr<float>() : nullptr;
+  const float* ksp = ks.has_value() ? ks->data_ptr<float>() : nullptr;
+  const uint8_t* kpp = keep.has_value() ? keep->data_ptr<uint8_t>() : nullptr;
+  float* gap = gate_acc.has_value() ? gate_acc->data_ptr<float>() : nullptr;
+  auto* op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+#define ME_GATE_FWD(V)                                                                                  \
+  gate_fwd_kernel<V><<<grid, threads, 0, stream>>>(hp, kp, vp, qsp, ksp, kpp, N, d, sqrt_gate ? 1 : 0, op, \
+                                                   stats.data_ptr<float>(), gap)
+  if (vpt <= 8) ME_GATE_FWD(8);
+  else if (vpt <= 16) ME_GATE_FWD(16);
+  else if (vpt <= 24) ME_GATE_FWD(24);
+  else ME_GATE_FWD(32);
+#undef ME_GATE_FWD
+  return {out, stats};
+}
+
+std::vector<torch::Tensor> engram_gate_bwd(torch::Tensor g, torch::Tensor h, torch::Tensor k, torch::Tensor v,
+                                           c10::optional<torch::Tensor> qs, c10::optional<torch::Tensor> ks,
+                                           c10::optional<torch::Tensor> keep, torch::Tensor stats,
+                                           bool sqrt_gate) {
+  check_cuda(g, "grad");
+  const at::cuda::CUDAGuard guard(h.device());
+  auto gc = g.contiguous();
+  const int d = (int)h.size(-1);
+  const int64_t N = h.numel() / d;
+  auto dh = torch::empty_like(h), dk = torch::empty_like(k), dv = torch::empty_like(v);
+  torch::Tensor dqs, dks;
+  if (qs.has_value()) {
+    dqs = torch::zeros({d}, h.options().dtype(torch::kFloat32));
+    dks = torch::zeros({d}, h.options().dtype(torch::kFloat32));
+  }
+  if (N == 0) return {dh, dk, dv, dqs, dks};
+  const int threads = 256;
+  const int vpt = (d + threads - 1) / threads;
+  TORCH_CHECK(vpt <= 32, "hidden size above 8192 is not supported by the fused gate");
+  const int grid = (int)std::min<int64_t>(N, (int64_t)sm_count() * 4);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const float* qsp = qs.has_value() ? qs->data_ptr<float>() : nullptr;
+  const float* ksp = ks.has_value() ? ks->data_ptr<float>() : nullptr;
+  const uint8_t* kpp = keep.has_value() ? keep->data_ptr<uint8_t>() : nullptr;
+#define BF(t) reinterpret_cast<__nv_bfloat16*>(t.data_ptr())
+#define CBF(t) reinterpret_cast<const __nv_bfloat16*>(t.data_ptr())
+#define ME_GATE_BWD(V)                                                                                   \
+  gate_bwd_kernel<V><<<grid, threads, 0, stream>>>(CBF(gc), CBF(h), CBF(k), CBF(v), qsp, ksp, kpp,         \
+                                                   stats.data_ptr<float>(), N, d, sqrt_gate ? 1 : 0, BF(dh), \
+                                                   BF(dk), BF(dv), qs.has_value() ? dqs.data_ptr<float>() : nullptr, \
+                                                   qs.has_value() ? dks.data_ptr<float>() : nullptr)
+  if (vpt <= 8) ME_GATE_BWD(8);
+  else if (vpt <= 16) ME_GATE_BWD(16);
+  else if (vpt <= 24) ME_GATE_BWD(24);
+  else ME_GATE_BWD(32);
+#undef ME_GATE_BWD
+#undef BF
+#undef CBF
+  return {dh, dk, dv, dqs, dks};
+}

@@ -1,0 +1,159 @@
+"""Device storage of one engram's row-sharded tables on one rank (CUDA path).
+
+Every rank holds ceil(rows/world) rows of each table (the DTensor Shard(0) split of
+micro_engram/rows.py:39-44; the last ranks hold fewer real rows but the same padded
+layout), in ONE buffer laid out identically on every rank so a peer's row is at
+`ptr[owner] + offset(table) + local_row * row_bytes`:
+
+    per table k:  weight [per_k, dim]  (table dtype)   read by peers' gathers
+                  acc    [per_k, dim]  fp32            peers' row gradients land here
+                  bits   [ceil(per_k/32)] u32          touched bitmap
+                  list   [per_k] i32                   touched rows, in arrival order
+                  count  [4] i32                       number of touched rows
+
+With world > 1 the buffer is a SymmBuffer (CUDA IPC over NVLink); kernels index it
+through device tables of per-rank addresses. The optimizer moments live in ordinary local
+memory (only the owner touches them).
+"""
+import torch
+
+from .. import native
+
+_ALIGN = 256
+
+
+def _align(n):
+    return (n + _ALIGN - 1) // _ALIGN * _ALIGN
+
+
+class RowStore:
+    _created = 0
+
+    def __init__(self, table_rows, dim, dtype, rank, world, device, group=None):
+        RowStore._created += 1
+        self.salt = RowStore._created  # decorrelates the rounding bits of different engrams
+        self.coef = None  # device clip coefficient for the next optimizer step
+        self.table_rows = [int(r) for r in table_rows]
+        self.dim = int(dim)
+        self.dtype = dtype
+        self.rank, self.world = int(rank), int(world)
+        self.device = torch.device(device)
+        self.nt = len(self.table_rows)
+        self.per = [-(-r // self.world) for r in self.table_rows]
+        self.counts = []
+        for r, p in zip(self.table_rows, self.per):
+            start = min(self.rank * p, r)
+            self.counts.append(max(0, min(p, r - start)))
+        esz = torch.empty((), dtype=dtype).element_size()
+        self.layout = []  # per table: dict of byte offsets
+        off = 0
+        for p in self.per:
+            ent = {}
+            ent["weight"] = off
+            off = _align(off + p * self.dim * esz)
+            ent["acc"] = off
+            off = _align(off + p * self.dim * 4)
+            ent["bits"] = off
+            off = _align(off + (-(-p // 32)) * 4)
+            ent["list"] = off
+            off = _align(off + p * 4)
+            ent["count"] = off
+            off = _align(off + 16)
+            self.layout.append(ent)
+        self.nbytes = off
+        if self.world > 1:
+            from .symm import SymmBuffer
+
+            self.buf = SymmBuffer(self.nbytes, self.device, group)
+            base_ptrs = self.buf.ptrs
+
+            def view(o, shape, dt):
+                return self.buf.view(o, shape, dt)
+        else:
+            self.buf = None
+            self._raw = torch.zeros(self.nbytes, dtype=torch.uint8, device=self.device)
+            base_ptrs = [self._raw.data_ptr()]
+
+            def view(o, shape, dt):
+                n = 1
+                for s in shape:
+                    n *= s
+                nb = n * torch.empty((), dtype=dt).element_size()
+                return self._raw[o:o + nb].view(dt).view(*shape)
+        self.weights, self.acc, self.bits, self.list, self.count = [], [], [], [], []
+        for k, (p, ent) in enumerate(zip(self.per, self.layout)):
+            self.weights.append(view(ent["weight"], (p, self.dim), dtype))
+            self.acc.append(view(ent["acc"], (p, self.dim), torch.float32))
+            self.bits.append(view(ent["bits"], (-(-p // 32),), torch.int32))
+            self.list.append(view(ent["list"], (p,), torch.int32))
+            self.count.append(view(ent["count"], (4,), torch.int32))
+
+        def table(kind):
+            return torch.tensor([base_ptrs[r] + self.layout[k][kind] for r in range(self.world)
+                                 for k in range(self.nt)], dtype=torch.int64, device=self.device)
+
+        self.w_ptrs = table("weight")
+        self.acc_ptrs = table("acc")
+        self.bit_ptrs = table("bits")
+        self.list_ptrs = table("list")
+        self.cnt_ptrs = table("count")
+        # this rank's own entries (for the optimizer and the norm)
+        own = slice(self.rank * self.nt, (self.rank + 1) * self.nt)
+        self.own_acc_ptrs = self.acc_ptrs[own].contiguous()
+        self.own_list_ptrs = self.list_ptrs[own].contiguous()
+        self.own_cnt_ptrs = self.cnt_ptrs[own].contiguous()
+        self.per_t = torch.tensor(self.per, dtype=torch.int64, device=self.device)
+        self.status = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self.pending = False  # row gradients were pushed since the last optimizer step
+
+    # ---------------------------------------------------------------- views
+    def shard(self, k):
+        """This rank's real rows of table k (a view; the Parameter wraps it)."""
+        return self.weights[k][:self.counts[k]]
+
+    def touched(self, k):
+        """(local rows, fp32 grads) of table k's touched rows: one host sync (tests/logging)."""
+        n = int(self.count[k][0])
+        rows = self.list[k][:n].long()
+        return rows, self.acc[k].index_select(0, rows)
+
+    # ---------------------------------------------------------------- kernels
+    def gather(self, idx, out_dtype):
+        """idx [n_tables, N] global rows -> mem [N, n_tables*dim] from the owners' shards."""
+        src = 0 if self.dtype == torch.bfloat16 else 1
+        return native().engram_gather(idx, self.w_ptrs, self.per_t, self.world, self.dim, src, out_dtype,
+                                      self.status)
+
+    def push_grads(self, g, idx, scale):
+        """Row gradients g [N, n_tables*dim] of the looked-up rows -> the owners' accumulators."""
+        native().engram_scatter_grad(g.contiguous(), idx, self.acc_ptrs, self.bit_ptrs, self.list_ptrs,
+                                     self.cnt_ptrs, self.per_t, self.world, float(scale), self.status)
+        self.pending = True
+
+    def sqnorm_into(self, sq):
+        native().engram_touched_sqnorm(self.own_acc_ptrs, self.own_list_ptrs, self.own_cnt_ptrs, self.dim, sq)
+
+    def clear_counts(self):
+        for c in self.count:
+            c.zero_()
+        self.pending = False
+
+    def zero_grads(self):
+        """Drop pending gradients (zero_grad without a step): clears only the touched rows."""
+        for k in range(self.nt):
+            n = int(self.count[k][0])
+            if n:
+                rows = self.list[k][:n].long()
+                self.acc[k].index_fill_(0, rows, 0.0)
+                self.bits[k].zero_()
+        self.clear_counts()
+
+    def check_status(self):
+        st = self.status.tolist()
+        if st[0] != 0:
+            raise RuntimeError(f"[micro_engram] row store kernel error code {st[0]} (detail {st[1]})")
+
+    def close(self):
+        if self.buf is not None:
+            self.buf.close()
+            self.buf = None
