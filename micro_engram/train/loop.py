@@ -45,6 +45,14 @@ def _log0(msg):
 
 def setup_dist(timeout_s=None):
     rank, world = dist_rank_world()
+    if world == 1 and "MASTER_ADDR" not in os.environ:  # single process without a launcher
+        import socket
+
+        with socket.socket() as s:
+            s.bind(("127.0.0.1", 0))
+            port = s.getsockname()[1]
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", str(port))
     local = int(os.environ.get("LOCAL_RANK", 0))
     cuda = torch.cuda.is_available() and os.environ.get("MICRO_ENGRAM_CPU") != "1"
     if cuda:

@@ -57,6 +57,9 @@ std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Ten
 std::vector<torch::Tensor> attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                     torch::Tensor o, torch::Tensor lse, torch::Tensor doc_start, int64_t window,
                                     double scale);
+// gemm.cu
+torch::Tensor gemm_tc(torch::Tensor A, torch::Tensor B, int64_t block_n);
+torch::Tensor gemm_status(int64_t device);
 // symm.cpp
 int64_t symm_alloc(int64_t nbytes, int64_t device);
 void symm_free(int64_t ptr, int64_t device);
@@ -90,6 +93,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_bwd_inplace", &ce_bwd_inplace);
   m.def("attn_fwd", &attn_fwd);
   m.def("attn_bwd", &attn_bwd);
+  m.def("gemm_tc", &gemm_tc, py::arg("A"), py::arg("B"), py::arg("block_n") = 256);
+  m.def("gemm_status", &gemm_status);
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_free", &symm_free);
   m.def("symm_export", &symm_export);

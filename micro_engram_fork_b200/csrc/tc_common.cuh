@@ -1,0 +1,143 @@
+// Blackwell (sm_100a) building blocks shared by the tcgen05 kernels: mbarriers with bounded
+// waits, TMA tile loads, tensor memory (TMEM) allocation, UMMA shared-memory / instruction
+// descriptors, tcgen05.mma issue/commit and tcgen05.ld.
+//
+// Descriptor bit layouts follow the PTX ISA's tcgen05 "shared memory descriptor" and
+// "instruction descriptor" tables (as also encoded by CUTLASS's cute/arch/mma_sm100_desc.hpp).
+// Operand tiles are K-major with the 128-byte swizzle that TMA writes: rows of 64 bf16
+// (128 B), 8-row atoms of 1024 B, so SBO = 1024 B and the K=16 sub-steps of one 64-wide
+// K block advance the descriptor start address by 32 B.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace me {
+namespace tc {
+
+ME_DEVICE uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// ------------------------------------------------------------------ mbarrier
+ME_DEVICE void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+}
+ME_DEVICE void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+ME_DEVICE void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+ME_DEVICE void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+ME_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for the phase with `parity` to complete, for at most `limit_ns`. On timeout the
+// status word gets ME_ERR_TIMEOUT (detail = `where`), `*abort` is raised, and false returns.
+ME_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int where, volatile int* abort,
+                         uint64_t limit_ns = 2000000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0) {
+      if (abort && *abort) return false;
+      if (globaltimer_ns() - t0 > limit_ns) {
+        report(status, ME_ERR_TIMEOUT, where);
+        if (abort) *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ TMA
+ME_DEVICE void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+ME_DEVICE void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ------------------------------------------------------------------ TMEM
+// One warp allocates `ncols` (power of two >= 32) columns; the address lands in *slot.
+ME_DEVICE void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot)),
+               "r"(ncols));
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+}
+ME_DEVICE void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+ME_DEVICE void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+ME_DEVICE void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// ------------------------------------------------------------------ descriptors
+// K-major, 128-byte swizzle, version 1 (Blackwell), SBO = 1024 B.
+ME_DEVICE uint64_t desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFF) >> 4);          // start address [0,14)
+  d |= (uint64_t)1 << 16;                           // LBO (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;                 // SBO [32,46)
+  d |= (uint64_t)1 << 46;                           // version = 1 [46,48)
+  d |= (uint64_t)2 << 61;                           // layout: SWIZZLE_128B [61,64)
+  return d;
+}
+
+// kind::f16 instruction descriptor: bf16 A/B, fp32 D, both K-major, M=128, N=n.
+ME_HOST_DEVICE uint32_t idesc_bf16(int m, int n) {
+  return (1u << 4)                      // D format F32
+         | (1u << 7)                    // A format BF16
+         | (1u << 10)                   // B format BF16
+         | ((uint32_t)(n >> 3) << 17)   // N >> 3
+         | ((uint32_t)(m >> 4) << 24);  // M >> 4
+}
+
+ME_DEVICE void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+// Arrive on `bar` once every tcgen05.mma issued so far by this thread has completed.
+ME_DEVICE void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+// 32 lanes x 32 consecutive fp32 columns: thread t gets row (lane base + t), columns c..c+31.
+ME_DEVICE void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+}  // namespace tc
+}  // namespace me

@@ -6,6 +6,30 @@ import torch
 import torch.multiprocessing as mp
 
 
+def _pack(x):
+    """Tensors travel between processes by value (numpy), not through shared-memory handles that
+    die with the worker."""
+    if isinstance(x, torch.Tensor):
+        return ("__tensor__", x.detach().cpu().float().numpy() if x.dtype == torch.bfloat16 else x.detach().cpu().numpy(),
+                str(x.dtype))
+    if isinstance(x, (list, tuple)):
+        return type(x)(_pack(v) for v in x)
+    if isinstance(x, dict):
+        return {k: _pack(v) for k, v in x.items()}
+    return x
+
+
+def _unpack(x):
+    if isinstance(x, tuple) and len(x) == 3 and x[0] == "__tensor__":
+        t = torch.from_numpy(x[1])
+        return t.to(getattr(torch, x[2].split(".")[-1]))
+    if isinstance(x, (list, tuple)):
+        return type(x)(_unpack(v) for v in x)
+    if isinstance(x, dict):
+        return {k: _unpack(v) for k, v in x.items()}
+    return x
+
+
 def _worker(rank, world, port, fn, args, q):
     import torch.distributed as dist
 
@@ -14,7 +38,7 @@ def _worker(rank, world, port, fn, args, q):
     try:
         dist.init_process_group("gloo", rank=rank, world_size=world)
         out = fn(rank, world, *args)
-        q.put((rank, "ok", out))
+        q.put((rank, "ok", _pack(out)))
     except Exception:  # noqa: BLE001
         q.put((rank, "err", traceback.format_exc()))
     finally:
@@ -36,7 +60,7 @@ def run_dist(fn, world, *args, timeout=300):
     for _ in range(world):
         rank, status, out = q.get(timeout=timeout)
         if status == "ok":
-            results[rank] = out
+            results[rank] = _unpack(out)
         else:
             errors.append(f"rank {rank}:\n{out}")
     for p in procs:

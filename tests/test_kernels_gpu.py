@@ -155,7 +155,7 @@ def test_adam_touched_matches_reference():
     opt = LazyAdamW([{"params": [p], "lazy": True, "rowwise": True}], lr=1e-2)
     opt.step()
     torch.testing.assert_close(st.shard(0).cpu(), p.detach(), rtol=1e-5, atol=1e-6)
-    torch.testing.assert_close(v.cpu(), opt.state[p]["exp_avg_sq"], rtol=1e-5, atol=1e-9)
+    torch.testing.assert_close(v.cpu(), opt.state[p]["exp_avg_sq"], rtol=1e-4, atol=1e-9)
     assert float(st.acc[0].abs().sum()) == 0.0 and int(st.bits[0].abs().sum()) == 0
 
 
@@ -350,17 +350,44 @@ def test_decoder_native_vs_torch(checkpoint):
     y = text(x, pos)
     g = torch.randn_like(y)
     y.backward(g)
-    # plain PyTorch path on the same GPU weights
     import os
 
-    os.environ["MICRO_ENGRAM_REFERENCE_OPS"] = "1"
-    try:
-        xr = x.detach().clone().requires_grad_()
-        yr = text(xr, pos)
-        yr.backward(g)
-    finally:
-        os.environ.pop("MICRO_ENGRAM_REFERENCE_OPS")
-    rel = (y.float() - yr.float()).norm() / yr.float().norm()
-    assert rel < 3e-2, rel
-    relg = (x.grad.float() - xr.grad.float()).norm() / xr.grad.float().norm()
-    assert relg < 5e-2, relg
+    def torch_path(model_dtype):
+        m = G.GemmaForCausalLM(cfg).to(_dev())
+        m.load_state_dict(model.state_dict())
+        G.cast_projections_(m, model_dtype)
+        xr = x.detach().to(model_dtype).clone().requires_grad_()
+        os.environ["MICRO_ENGRAM_REFERENCE_OPS"] = "1"
+        try:
+            yr = m.model(xr, pos)
+            yr.backward(g.to(model_dtype))
+        finally:
+            os.environ.pop("MICRO_ENGRAM_REFERENCE_OPS")
+        return yr, xr.grad
+
+    y32, gx32 = torch_path(torch.float32)   # fp32 oracle on the same (bf16-valued) weights
+    yb, gxb = torch_path(torch.bfloat16)    # plain PyTorch in bf16: the noise floor
+
+    def rel(a, b):
+        return float((a.float() - b.float()).norm() / b.float().norm())
+
+    assert rel(y, y32) <= 1.5 * rel(yb, y32) + 2e-3, (rel(y, y32), rel(yb, y32))
+    assert rel(x.grad, gx32) <= 1.5 * rel(gxb, gx32) + 2e-3, (rel(x.grad, gx32), rel(gxb, gx32))
+
+
+# ----------------------------------------------------------------------------- tcgen05 GEMM
+@cuda
+@pytest.mark.parametrize("M,N,K,bn", [(128, 256, 64, 256), (300, 520, 200, 256), (1024, 1536, 4096, 256),
+                                      (257, 384, 1536, 128), (8192, 5376, 1536, 256)])
+def test_tcgen05_gemm(M, N, K, bn):
+    import micro_engram_fork_b200 as me
+
+    torch.manual_seed(0)
+    A = torch.randn(M, K, device=_dev()).to(torch.bfloat16)
+    B = (torch.randn(N, K, device=_dev()) / K ** 0.5).to(torch.bfloat16)
+    C = me.native().gemm_tc(A, B, bn)
+    torch.cuda.synchronize()
+    assert int(me.native().gemm_status(0)[0]) == 0, "tcgen05 GEMM reported a timeout"
+    ref32 = A.float() @ B.float().t()
+    plain = A @ B.t()
+    noise_floor_check(C, ref32, plain, rel=1.5, eps=1e-2, name=f"gemm {M}x{N}x{K}")
