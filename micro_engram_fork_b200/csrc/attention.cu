@@ -627,3 +627,108 @@ std::vector<torch::Tensor> attn_bwd(torch::Tensor dout, torch::Tensor q, torch::
                                      stream));
   return {dq, dk, dv};
 }
+
+// =============================================================================== no-alloc entry
+// Allocation-free variant of attn_bwd for callers that cannot allocate device memory (see
+// noalloc.h). Its scratch is the file-scope array below; host code only ever passes the
+// device address looked up with cudaGetSymbolAddress, never the array's name.
+#include <mutex>
+
+#include "noalloc.h"
+
+namespace {
+
+static __device__ __align__(256) unsigned char g_attn_bwd_scratch[ME_ATTN_BWD_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kNoAllocMaxDevices = 64;
+void* g_scratch_addr[kNoAllocMaxDevices] = {nullptr};
+std::mutex g_scratch_mu;
+thread_local const char* g_noalloc_err = "no error";
+
+size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+
+// doc_end[s] = last token of s's document: each document's last token writes its range.
+__global__ void doc_end_from_start_kernel(const int* __restrict__ ds, int T, int* __restrict__ de) {
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < T; t += gridDim.x * blockDim.x) {
+    if (t == T - 1 || ds[t + 1] == t + 1) {
+      for (int s = ds[t]; s <= t; ++s) de[s] = t;
+    }
+  }
+}
+
+// Device address of the scratch array on the current device (looked up once per device).
+void* scratch_on_current_device(int* err) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) {
+    *err = ME_NOALLOC_ERR_SETUP;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_bwd_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      *err = ME_NOALLOC_ERR_SETUP;
+      return nullptr;
+    }
+    g_scratch_addr[dev] = p;
+  }
+  return g_scratch_addr[dev];
+}
+
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) const char* me_noalloc_last_error(void) { return g_noalloc_err; }
+
+extern "C" __attribute__((visibility("default"))) int me_attn_bwd_noalloc(
+    const void* dout, const void* q, const void* k, const void* v, const void* o, const float* lse,
+    const int* doc_start, int T, int Hq, int Hk, int D, int window, float scale, void* dq, void* dk, void* dv,
+    cudaStream_t stream) {
+  if (!dout || !q || !k || !v || !o || !lse || !doc_start || !dq || !dk || !dv || T <= 0 || Hq <= 0 || Hk <= 0 ||
+      Hq % Hk != 0 || !(D == 64 || D == 128 || D == 256 || D == 512)) {
+    g_noalloc_err = "me_attn_bwd_noalloc: null pointer, non-positive size, Hq not a multiple of Hk, or head_dim "
+                    "not in {64, 128, 256, 512}";
+    return ME_NOALLOC_ERR_ARGS;
+  }
+  const size_t delta_bytes = align256((size_t)Hq * (size_t)T * sizeof(float));
+  const size_t need = delta_bytes + align256((size_t)T * sizeof(int));
+  if (need > (size_t)ME_ATTN_BWD_NOALLOC_SCRATCH_BYTES) {
+    g_noalloc_err = "me_attn_bwd_noalloc: Hq*T*4 + T*4 bytes of scratch exceed the fixed 8 MiB array "
+                    "(ME_ATTN_BWD_NOALLOC_SCRATCH_BYTES); use attn_bwd for this size";
+    return ME_NOALLOC_ERR_TOO_LARGE;
+  }
+  int err = ME_NOALLOC_OK;
+  unsigned char* scratch = static_cast<unsigned char*>(scratch_on_current_device(&err));
+  if (scratch == nullptr) {
+    g_noalloc_err = "me_attn_bwd_noalloc: cudaGetSymbolAddress of the scratch array failed on this device";
+    return err;
+  }
+  float* delta = reinterpret_cast<float*>(scratch);
+  int* doc_end = reinterpret_cast<int*>(scratch + delta_bytes);
+  {
+    const int64_t rows = (int64_t)T * Hq;
+    const int grid = (int)std::min<int64_t>((rows + 7) / 8, 148 * 32);
+    attn_bwd_pre_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const bf16*>(o), reinterpret_cast<const bf16*>(dout),
+                                                  T, Hq, D, delta);
+    doc_end_from_start_kernel<<<(T + 255) / 256, 256, 0, stream>>>(doc_start, T, doc_end);
+  }
+  const bf16* qp = reinterpret_cast<const bf16*>(q);
+  const bf16* kp = reinterpret_cast<const bf16*>(k);
+  const bf16* vp = reinterpret_cast<const bf16*>(v);
+  const bf16* gp = reinterpret_cast<const bf16*>(dout);
+  bf16* dqp = reinterpret_cast<bf16*>(dq);
+  bf16* dkp = reinterpret_cast<bf16*>(dk);
+  bf16* dvp = reinterpret_cast<bf16*>(dv);
+  switch (D) {
+    case 64: launch_bwd<64>(qp, kp, vp, gp, lse, delta, doc_start, doc_end, T, Hq, Hk, window, scale, dqp, dkp, dvp, stream); break;
+    case 128: launch_bwd<128>(qp, kp, vp, gp, lse, delta, doc_start, doc_end, T, Hq, Hk, window, scale, dqp, dkp, dvp, stream); break;
+    case 256: launch_bwd<256>(qp, kp, vp, gp, lse, delta, doc_start, doc_end, T, Hq, Hk, window, scale, dqp, dkp, dvp, stream); break;
+    default: launch_bwd<512>(qp, kp, vp, gp, lse, delta, doc_start, doc_end, T, Hq, Hk, window, scale, dqp, dkp, dvp, stream); break;
+  }
+  if (cudaGetLastError() != cudaSuccess) {
+    g_noalloc_err = "me_attn_bwd_noalloc: a kernel launch failed";
+    return ME_NOALLOC_ERR_LAUNCH;
+  }
+  g_noalloc_err = "no error";
+  return ME_NOALLOC_OK;
+}
