@@ -315,8 +315,10 @@ def run_reference(args):
     for k in ("base_init",):
         c.pop(k)
     # the reference's recommended B200-runnable kernel settings (README example config)
+    # (fused_attn_kernel off: that patch's shared-KV side channel is None under the installed
+    # transformers and the stock layer then fails; its unfused path is the reference's own option)
     c.update({"gemma4_hybrid_attn_impl": True, "large_head_attention": "auto", "liger_rms_norm": True,
-              "liger_glu_activation": True, "attn_implementation": "sdpa"})
+              "liger_glu_activation": True, "attn_implementation": "sdpa", "fused_attn_kernel": False})
     try:
         import flash_attn  # noqa: F401
         from flash_attn import flash_attn_func
