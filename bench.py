@@ -85,6 +85,7 @@ def bench_config(tmp, steps):
         "micro_engram_dtype": "bf16", "micro_engram_optimizer": "rowwise_adam",
         "learning_rate": 5e-3, "micro_engram_dense_lr": 1e-3, "max_grad_norm": 2.0, "warmup_steps": 0,
         "gradient_checkpointing": True, "activation_offloading": True, "micro_engram_stats_steps": 0,
+        "gradient_checkpointing_policy": os.environ.get("ME_BENCH_AC", "selective"),
         "seed": 42,
     }
 
@@ -247,7 +248,10 @@ def run_ours(args):
                        "parallelism": f"dp{world} (replicated frozen base, row-sharded engram, vocab-parallel head)",
                        "engram": "layer 0, tables {2:1572864,3:4194304,4:4194304} x8 heads x dim 64, "
                                  "scalar_sqrt, rowwise_adam bf16+SR",
-                       "activation_checkpointing": "per-layer", "activation_offloading": True,
+                       "activation_checkpointing": f"per-layer, policy {trainer.cfg.gradient_checkpointing_policy}"
+                                                   " (selective: each layer's q/k/v projection, attention output"
+                                                   " and o-proj kept on the GPU, norms/RoPE/MLP recomputed)",
+                       "activation_offloading": "layer inputs to pinned host memory, prefetched in the backward",
                        "l2": "inputs larger than L2 (61 GB base streamed per step), no flush"},
             "clocks": clk,
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
@@ -312,7 +316,7 @@ def run_reference(args):
 
     tmp = tempfile.mkdtemp(prefix="me_ref_")
     c = bench_config(tmp, args.warmup + 2 * args.steps + 2)
-    for k in ("base_init",):
+    for k in ("base_init", "gradient_checkpointing_policy"):  # keys the reference does not have
         c.pop(k)
     # the reference's recommended B200-runnable kernel settings (README example config)
     # (fused_attn_kernel off: that patch's shared-KV side channel is None under the installed

@@ -14,6 +14,9 @@ Keys this framework adds (all optional, defaults keep the reference's behaviour)
                        replicated when it fits in HBM
   kernels              "native" (sm_100a kernels, the default on CUDA) or "reference"
                        (plain PyTorch ops; oracle runs)
+  gradient_checkpointing_policy
+                       "full" (default: keep each layer's input) or "selective" (also keep
+                       the attention half of each layer on the GPU; recompute only the MLP)
 """
 import logging
 import os
@@ -127,6 +130,9 @@ class TrainConfig(MicroEngramArgs):
     seed: int = 42
     gradient_checkpointing: bool = True
     gradient_checkpointing_kwargs: Optional[Dict[str, Any]] = None
+    # full: keep only each layer's input (the reference's behaviour); selective: also keep the
+    # q/k/v projection, attention output + LSE and o-proj output on the GPU, recompute the rest
+    gradient_checkpointing_policy: Literal["full", "selective"] = "full"
     activation_offloading: bool = False
     no_grad_prefix: bool = True
     sharded_vocab: bool = True

@@ -140,7 +140,7 @@ def checkpointing(model, text, cfg, no_grad_upto):
     """Per-layer activation checkpointing (only the layer input is kept), off for the prefix."""
     if not cfg.gradient_checkpointing:
         return
-    text.gradient_checkpointing_enable(upto=no_grad_upto)
+    text.gradient_checkpointing_enable(upto=no_grad_upto, policy=cfg.gradient_checkpointing_policy)
 
 
 def base_bytes(text):

@@ -17,6 +17,7 @@ class ActivationOffload:
         self.device = device
         self.pool = {}
         self.in_use = []
+        self.order = []  # packed entries of this micro-batch, in forward order
         self.stream = torch.cuda.Stream(device) if device.type == "cuda" else None
 
     def _buffer(self, t):
@@ -36,14 +37,39 @@ class ActivationOffload:
             ev = torch.cuda.Event()
             ev.record(self.stream)
         t.record_stream(self.stream)
-        return (buf, t.shape, t.device, ev)
+        entry = {"buf": buf, "shape": t.shape, "device": t.device, "ev": ev, "dev": None, "ready": None}
+        self.order.append(entry)
+        return entry
+
+    def _fetch(self, e):
+        """Start the host->device copy of entry e on the side stream (once)."""
+        if e["dev"] is not None:
+            return
+        self.stream.wait_event(e["ev"])
+        with torch.cuda.stream(self.stream):
+            e["dev"] = e["buf"].to(e["device"], non_blocking=True)
+            e["ready"] = torch.cuda.Event()
+            e["ready"].record(self.stream)
 
     def unpack(self, packed):
         if isinstance(packed, torch.Tensor):
             return packed
-        buf, shape, device, ev = packed
-        torch.cuda.current_stream(device).wait_event(ev)
-        return buf.to(device, non_blocking=True).view(shape)
+        e = packed
+        self._fetch(e)
+        # the backward visits layers in reverse: start copying the previous layer's input now,
+        # so it overlaps this layer's backward
+        try:
+            i = next(j for j in range(len(self.order) - 1, -1, -1) if self.order[j] is e)
+        except StopIteration:
+            i = -1
+        if i > 0:
+            self._fetch(self.order[i - 1])
+        cur = torch.cuda.current_stream(e["device"])
+        cur.wait_event(e["ready"])
+        out = e["dev"]
+        out.record_stream(cur)
+        e["dev"] = None  # the caller owns it now
+        return out.view(e["shape"])
 
     def context(self):
         return torch.autograd.graph.saved_tensors_hooks(self.pack, self.unpack)
@@ -55,6 +81,7 @@ class ActivationOffload:
         for key, buf in self.in_use:
             self.pool[key].append(buf)
         self.in_use = []
+        self.order = []
 
     def pinned_bytes(self):
         return (sum(b.numel() * b.element_size() for bs in self.pool.values() for b in bs)

@@ -255,7 +255,8 @@ class GemmaLayer(nn.Module):
         """x [T, d] (one packed row), pos [T], doc_start [T] int32 -> [T, d]."""
         if use_native(x):
             if torch.is_grad_enabled() and x.requires_grad:
-                return _LayerFn.apply(x, pos, doc_start, self, bool(self.gradient_checkpointing))
+                ck = self.gradient_checkpointing
+                return _LayerFn.apply(x, pos, doc_start, self, ck if ck == "selective" else bool(ck))
             with torch.no_grad():
                 return _layer_fwd(self, x, pos, doc_start)[0]
         if self.gradient_checkpointing and torch.is_grad_enabled() and x.requires_grad:
@@ -323,16 +324,43 @@ def _layer_fwd(layer, x, pos, doc_start, keep=False):
 
 
 _SAVE_KEYS = ("r_in", "qkv", "q", "k", "v", "r_qkv", "a", "lse", "o", "x2", "r_o", "r_x2", "gu", "dn", "r_dn")
+# selective checkpointing keeps the expensive-to-recompute attention half of the layer on the GPU
+_SELECTIVE_KEYS = ("qkv", "a", "lse", "o")
+
+
+def _recompute_selective(layer, x, pos, kept):
+    """Rebuild a layer's saved state from its input and the kept attention tensors: norms,
+    RoPE and the MLP are recomputed; the q/k/v and o projections and attention are not."""
+    eps = layer.cfg.rms_norm_eps
+    att = layer.self_attn
+    _, r_in = N.rmsnorm(x, layer.input_layernorm.weight, eps)
+    q, k, v, r_qkv = N.qkv_norm_rope(kept["qkv"], att.q_norm.weight, att.k_norm.weight, layer.inv_freq, pos,
+                                     layer.n_q, layer.n_kv, layer.head_dim, layer.kv_eq, eps)
+    x2, h2, r_o, r_x2 = N.post_norm_add(x, kept["o"], layer.post_attention_layernorm.weight, None,
+                                        layer.pre_feedforward_layernorm.weight, eps)
+    gu = F.linear(h2, layer.gate_up_weight)
+    dn = F.linear(N.geglu(gu), layer.mlp.down_proj.weight)
+    _, _, r_dn, _ = N.post_norm_add(x2, dn, layer.post_feedforward_layernorm.weight, _ls(layer), None, eps)
+    return dict(r_in=r_in, qkv=kept["qkv"], q=q, k=k, v=v, r_qkv=r_qkv, a=kept["a"], lse=kept["lse"], o=kept["o"],
+                x2=x2, r_o=r_o, r_x2=r_x2, gu=gu, dn=dn, r_dn=r_dn)
 
 
 class _LayerFn(torch.autograd.Function):
-    """One decoder layer on the sm_100a kernels with a hand-written dX-only backward."""
+    """One decoder layer on the sm_100a kernels with a hand-written dX-only backward.
+
+    checkpoint: False (save everything), "full"/True (save only the input; recompute the
+    layer), "selective" (save the input plus the q/k/v projection, attention output + LSE and
+    o-proj output, kept on the GPU outside the saved-tensor hooks so activation offloading
+    moves only the layer input; recompute norms, RoPE and the MLP)."""
 
     @staticmethod
     def forward(ctx, x, pos, doc_start, layer, checkpoint):
         ctx.layer, ctx.checkpoint = layer, checkpoint
-        out, saved = _layer_fwd(layer, x, pos, doc_start, keep=not checkpoint)
-        if checkpoint:
+        out, saved = _layer_fwd(layer, x, pos, doc_start, keep=checkpoint in (False, "selective"))
+        if checkpoint == "selective":
+            ctx.save_for_backward(x, pos, doc_start)
+            ctx.kept = {k: saved[k] for k in _SELECTIVE_KEYS}
+        elif checkpoint:
             ctx.save_for_backward(x, pos, doc_start)
         else:
             ctx.save_for_backward(x, pos, doc_start, *[saved[k] for k in _SAVE_KEYS])
@@ -347,7 +375,11 @@ class _LayerFn(torch.autograd.Function):
         att = layer.self_attn
         tensors = ctx.saved_tensors
         x, pos, doc_start = tensors[:3]
-        if ctx.checkpoint:
+        if ctx.checkpoint == "selective":
+            with torch.no_grad():
+                s = _recompute_selective(layer, x, pos, ctx.kept)
+            ctx.kept = None
+        elif ctx.checkpoint:
             with torch.no_grad():
                 _, s = _layer_fwd(layer, x, pos, doc_start, keep=True)
         else:
@@ -385,9 +417,12 @@ class GemmaTextModel(nn.Module):
     def embed_scale(self):
         return float(self.config.hidden_size) ** 0.5
 
-    def gradient_checkpointing_enable(self, upto=None):
+    def gradient_checkpointing_enable(self, upto=None, policy="full"):
+        """Per-layer checkpointing for the layers after `upto` (the no-grad prefix needs none).
+        policy: "full" (keep only the layer input) or "selective" (also keep the attention half)."""
         for i, layer in enumerate(self.layers):
-            layer.gradient_checkpointing = upto is None or i > upto
+            on = upto is None or i > upto
+            layer.gradient_checkpointing = ("selective" if policy == "selective" else True) if on else False
 
     def forward(self, inputs_embeds, position_ids):
         """inputs_embeds [1, T, d] or [T, d]; position_ids [1, T] or [T] -> final hidden [T, d]."""

@@ -332,7 +332,7 @@ def test_attention(D, Hq, Hk, window):
 
 # ----------------------------------------------------------------------------- decoder layer
 @cuda
-@pytest.mark.parametrize("checkpoint", [False, True])
+@pytest.mark.parametrize("checkpoint", [False, "full", "selective"])
 def test_decoder_native_vs_torch(checkpoint):
     from micro_engram_fork_b200.models import gemma as G
     from micro_engram_fork_b200.ops.attention import doc_starts
@@ -343,7 +343,8 @@ def test_decoder_native_vs_torch(checkpoint):
     G.init_random_(model, seed=3)
     G.cast_projections_(model, torch.bfloat16)
     text = model.model
-    text.gradient_checkpointing_enable() if checkpoint else None
+    if checkpoint:
+        text.gradient_checkpointing_enable(policy=checkpoint)
     T = 300
     pos = torch.cat([torch.arange(100), torch.arange(200)]).to(_dev())
     x = (torch.randn(T, cfg.hidden_size, device=_dev())).to(torch.bfloat16).requires_grad_()
