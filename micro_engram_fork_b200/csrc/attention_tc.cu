@@ -1,0 +1,398 @@
+// tcgen05 (5th-gen tensor core) packed-varlen attention forward for sm_100a.
+//
+// One CTA = 128 queries of one head (M = 128 TMEM lanes) x DV output columns, looping over
+// key blocks of 64. Warp roles (192 threads):
+//   warp 0     TMA producer: Q once (D/64 chunks of 128x64, 128B swizzle), K in 64x64 chunks
+//              through a KS-deep ring, V in 64-key x DV blocks through a VS-deep ring (3-D
+//              tensor maps over [T, H, D]; no multicast)
+//   warp 1     TMEM owner + single-thread MMA issuer:
+//                S_j = Q K_j^T  into one of two 64-column S buffers  (A, B K-major)
+//                O  += P_j V_j  into a DV-column O accumulator       (B = V, N-contiguous)
+//              tcgen05.commit releases K/V stages and signals S-ready / PV-done
+//   warps 2-5  softmax: each thread owns one query row = one TMEM lane; reads its 64 scores
+//              (tcgen05.ld), applies the document / causal / sliding-window mask, keeps a
+//              running max with lazy rescaling (O in TMEM is rescaled only when the max grows
+//              by more than 2^8, warp-uniformly), writes P (bf16) into shared memory for the PV
+//              MMA, and finally normalises O out of TMEM and writes O and the LSE.
+// Every wait is bounded (2 s); a timeout records ME_ERR_TIMEOUT in the status word and the
+// kernel frees TMEM and returns.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "tc_common.cuh"
+
+using namespace me;
+using namespace me::tc;
+
+namespace {
+using bf16 = __nv_bfloat16;
+
+template <int D, int DV, int KS, int VS>
+struct AttnLayout {
+  static constexpr int BM = 128, BN = 64, NC = D / 64;
+  static constexpr int Q_BYTES = BM * D * 2;
+  static constexpr int KCH_BYTES = BN * 64 * 2;
+  static constexpr int V_BYTES = BN * DV * 2;
+  static constexpr int P_BYTES = BM * BN * 2;
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = Q_OFF + Q_BYTES;
+  static constexpr int V_OFF = K_OFF + KS * KCH_BYTES;
+  static constexpr int P_OFF = V_OFF + VS * V_BYTES;
+  static constexpr int BAR_OFF = P_OFF + P_BYTES;
+  static constexpr int N_BARS = 1 + 2 * KS + 2 * VS + 2 + 2 + 1 + 1 + 1;
+  static constexpr int BYTES = BAR_OFF + N_BARS * 8 + 16 + 1024;
+  static constexpr uint32_t TMEM_COLS = (128 + DV) <= 256 ? 256 : 512;
+  static constexpr int O_COL = 128;
+};
+
+ME_DEVICE float warp_any_f(bool p) { return __any_sync(0xffffffffu, p) ? 1.f : 0.f; }
+
+template <int D, int DV, int KS, int VS>
+__global__ void __launch_bounds__(192, 1)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                       const __grid_constant__ CUtensorMap tv, const int* __restrict__ doc_start, int T, int Hq,
+                       int Hk, int window, float scale, bf16* __restrict__ o, float* __restrict__ lse, int* status) {
+  using L = AttnLayout<D, DV, KS, VS>;
+  constexpr int BM = L::BM, BN = L::BN, NC = L::NC;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + L::Q_OFF;
+  uint8_t* sK = smem + L::K_OFF;
+  uint8_t* sV = smem + L::V_OFF;
+  uint8_t* sP = smem + L::P_OFF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + KS;
+  uint64_t* v_full = k_empty + KS;
+  uint64_t* v_empty = v_full + VS;
+  uint64_t* s_full = v_empty + VS;
+  uint64_t* s_free = s_full + 2;
+  uint64_t* p_full = s_free + 2;
+  uint64_t* pv_done = p_full + 1;
+  uint64_t* o_final = pv_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q0 = blockIdx.x * BM, h = blockIdx.y, hk = h / (Hq / Hk), dv0 = blockIdx.z * DV;
+  const int qlast = min(q0 + BM - 1, T - 1);
+  int kstart = doc_start[q0];
+  if (window > 0) kstart = max(kstart, q0 - window + 1);
+  const int kb_first = (kstart / BN) * BN;
+  const int nkb = (qlast - kb_first) / BN + 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < KS; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < VS; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(pv_done, 1);
+    mbar_init(o_final, 1);
+    *abort = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tq);
+    prefetch_tmap(&tk);
+    prefetch_tmap(&tv);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, L::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------------- producer
+      mbar_expect_tx(q_full, L::Q_BYTES);
+      for (int c = 0; c < NC; ++c) tma_load_3d(sQ + c * (BM * 128), &tq, q_full, c * 64, h, q0);
+      int issued_k = 0, issued_v = 0;
+      bool ok = true;
+      auto load_k = [&](int j) {
+        for (int c = 0; c < NC && ok; ++c) {
+          const int g = j * NC + c, st = g % KS, r = g / KS;
+          if (r > 0 && !mbar_wait(&k_empty[st], (r - 1) & 1, status, 11, abort)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&k_full[st], L::KCH_BYTES);
+          tma_load_3d(sK + st * L::KCH_BYTES, &tk, &k_full[st], c * 64, hk, kb_first + j * BN);
+          issued_k = g + 1;
+        }
+      };
+      auto load_v = [&](int j) {
+        const int b = j % VS, r = j / VS;
+        if (r > 0 && !mbar_wait(&v_empty[b], (r - 1) & 1, status, 12, abort)) {
+          ok = false;
+          return;
+        }
+        mbar_expect_tx(&v_full[b], L::V_BYTES);
+        for (int vc = 0; vc < DV / 64; ++vc)
+          tma_load_3d(sV + b * L::V_BYTES + vc * (BN * 128), &tv, &v_full[b], dv0 + vc * 64, hk, kb_first + j * BN);
+        issued_v = j + 1;
+      };
+      load_k(0);
+      for (int j = 0; j < nkb && ok; ++j) {
+        if (j + 1 < nkb) load_k(j + 1);
+        if (ok) load_v(j);
+      }
+      // drain every copy still in flight before the CTA may exit
+      mbar_wait(q_full, 0, status, 19, nullptr);
+      for (int g = max(0, issued_k - KS); g < issued_k; ++g) mbar_wait(&k_full[g % KS], (g / KS) & 1, status, 19, nullptr);
+      for (int j = max(0, issued_v - VS); j < issued_v; ++j) mbar_wait(&v_full[j % VS], (j / VS) & 1, status, 19, nullptr);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------------------------------------------------------- MMA issuer
+      const uint32_t id_s = idesc_bf16(BM, BN);
+      const uint32_t id_o = idesc_bf16(BM, DV, true);
+      const uint32_t aQ = smem_addr(sQ), aK = smem_addr(sK), aV = smem_addr(sV), aP = smem_addr(sP);
+      bool ok = mbar_wait(q_full, 0, status, 20, abort);
+      auto issue_pv = [&](int i) {
+        if (!ok) return;
+        const int vb = i % VS;
+        if (!mbar_wait(p_full, i & 1, status, 21, abort) || !mbar_wait(&v_full[vb], (i / VS) & 1, status, 22, abort)) {
+          ok = false;
+          return;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          umma_bf16(tmem + L::O_COL, desc_sw128(aP + kk * 32),
+                    desc_mn_sw128(aV + vb * L::V_BYTES + kk * 16 * 128, BN * 128, 1024), id_o, (i > 0 || kk > 0));
+        umma_commit(&v_empty[vb]);
+        umma_commit(pv_done);
+      };
+      for (int j = 0; j < nkb && ok; ++j) {
+        const int b = j & 1;
+        if (j >= 2 && !mbar_wait(&s_free[b], ((j - 2) >> 1) & 1, status, 23, abort)) {
+          ok = false;
+          break;
+        }
+        for (int c = 0; c < NC; ++c) {
+          const int g = j * NC + c, st = g % KS;
+          if (!mbar_wait(&k_full[st], (g / KS) & 1, status, 24, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16(tmem + b * BN, desc_sw128(aQ + c * (BM * 128) + kk * 32),
+                      desc_sw128(aK + st * L::KCH_BYTES + kk * 32), id_s, (c | kk) != 0);
+          umma_commit(&k_empty[st]);
+        }
+        if (!ok) break;
+        umma_commit(&s_full[b]);
+        if (j >= 1) issue_pv(j - 1);
+      }
+      if (ok) issue_pv(nkb - 1);
+      if (ok) umma_commit(o_final);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax + epilogue
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const int t = q0 + r;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    const int ds_t = t < T ? doc_start[t] : 0;
+    const int lo = window > 0 ? max(ds_t, t - window + 1) : ds_t;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkb && ok; ++j) {
+      const int b = j & 1, kb = kb_first + j * BN;
+      if (!mbar_wait(&s_full[b], (j >> 1) & 1, status, 30, abort)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[BN];
+      tmem_ld32(tmem + lane_base + b * BN, *reinterpret_cast<float(*)[32]>(&s[0]));
+      tmem_ld32(tmem + lane_base + b * BN + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
+      tc_fence_before();
+      mbar_arrive(&s_free[b]);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) {
+        const int sc = kb + c;
+        float x = s[c] * scale;
+        if (t >= T || sc > t || sc < lo || sc >= T) x = -INFINITY;
+        s[c] = x;
+        mx = fmaxf(mx, x);
+      }
+      float m_new = m_used, alpha = 1.f;
+      bool resc = false;
+      if (mx > -INFINITY) {
+        if (m_used == -INFINITY) {
+          m_new = mx;
+          alpha = 0.f;  // nothing accumulated yet (l = 0, O rows are zero)
+        } else if (mx > m_used + 8.f) {
+          m_new = mx;
+          alpha = __expf(m_used - m_new);
+          resc = true;
+        }
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) {
+        const float p = (s[c] == -INFINITY) ? 0.f : __expf(s[c] - m_new);
+        s[c] = p;
+        sum += p;
+      }
+      l = l * alpha + sum;
+      m_used = m_new;
+      // PV_{j-1} must be done: the P buffer is reused and O may be rescaled
+      if (j >= 1 && !mbar_wait(pv_done, (j - 1) & 1, status, 31, abort)) {
+        ok = false;
+        break;
+      }
+      if (j >= 1 && __any_sync(0xffffffffu, resc)) {
+        tc_fence_after();
+        const float f = resc ? alpha : 1.f;
+#pragma unroll 1
+        for (int cc = 0; cc < DV / 32; ++cc) {
+          float v[32];
+          tmem_ld32(tmem + lane_base + L::O_COL + cc * 32, v);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] *= f;
+          tmem_st32(tmem + lane_base + L::O_COL + cc * 32, v);
+        }
+        tmem_st_wait();
+      }
+      // P row r: 64 bf16 = 8 swizzled 16-byte chunks
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) {
+        BF16x8 pk;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) pk.h[e] = f2bf(s[c8 * 8 + e]);
+        const uint32_t addr = smem_addr(sP) + r * 128 + ((c8 ^ (r & 7)) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk.u.x), "r"(pk.u.y), "r"(pk.u.z),
+                     "r"(pk.u.w)
+                     : "memory");
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && mbar_wait(o_final, 0, status, 32, abort)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int64_t ldo = (int64_t)Hq * D;
+#pragma unroll 1
+      for (int cc = 0; cc < DV / 32; ++cc) {
+        float v[32];
+        tmem_ld32(tmem + lane_base + L::O_COL + cc * 32, v);
+        if (t < T) {
+          bf16* dst = o + (int64_t)t * ldo + (int64_t)h * D + dv0 + cc * 32;
+#pragma unroll
+          for (int j8 = 0; j8 < 4; ++j8) {
+            BF16x8 ov;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ov.h[e] = f2bf(v[j8 * 8 + e] * inv);
+            *reinterpret_cast<uint4*>(dst + j8 * 8) = ov.u;
+          }
+        }
+      }
+      if (blockIdx.z == 0 && t < T) lse[(int64_t)h * T + t] = m_used + logf(l);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TMEM_COLS);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  TORCH_CHECK(fn != nullptr, "cuTensorMapEncodeTiled is unavailable");
+  return fn;
+}
+
+// [T, H, D] bf16 -> 3-D map with box {64 (D), 1 (head), rows (tokens)}, 128B swizzle.
+CUtensorMap make_tmap_thd(const void* ptr, int64_t T, int64_t H, int64_t D, int rows) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(ptr) % 16 == 0, "attention operand must be 16-byte aligned");
+  CUtensorMap map;
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T};
+  cuuint64_t strides[2] = {(cuuint64_t)(D * 2), (cuuint64_t)(H * D * 2)};
+  cuuint32_t box[3] = {64, 1, (cuuint32_t)rows};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (attention) failed: ", (int)r);
+  return map;
+}
+
+template <int D, int DV, int KS, int VS>
+void launch_fwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const int* ds, int window,
+                   float scale, torch::Tensor& o, torch::Tensor& lse, int* status, cudaStream_t stream) {
+  using L = AttnLayout<D, DV, KS, VS>;
+  const int T = (int)q.size(0), Hq = (int)q.size(1), Hk = (int)k.size(1);
+  const CUtensorMap tq = make_tmap_thd(q.data_ptr(), T, Hq, D, 128);
+  const CUtensorMap tk = make_tmap_thd(k.data_ptr(), T, Hk, D, 64);
+  const CUtensorMap tv = make_tmap_thd(v.data_ptr(), T, Hk, D, 64);
+  auto kern = attn_fwd_tc_kernel<D, DV, KS, VS>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
+  dim3 grid((T + 127) / 128, Hq, D / DV);
+  kern<<<grid, 192, L::BYTES, stream>>>(tq, tk, tv, ds, T, Hq, Hk, window, scale,
+                                        reinterpret_cast<bf16*>(o.data_ptr()), lse.data_ptr<float>(), status);
+}
+
+torch::Tensor& attn_status(int dev) {
+  static torch::Tensor bufs[64];
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!bufs[dev].defined())
+    bufs[dev] = torch::zeros({2}, torch::TensorOptions().dtype(torch::kInt32).device(torch::kCUDA, dev));
+  return bufs[dev];
+}
+
+}  // namespace
+
+std::vector<torch::Tensor> attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor doc_start,
+                                       int64_t window, double scale) {
+  TORCH_CHECK(q.is_cuda() && q.is_contiguous() && k.is_contiguous() && v.is_contiguous(), "attn_fwd_tc: contiguous CUDA");
+  TORCH_CHECK(q.scalar_type() == torch::kBFloat16, "attn_fwd_tc: bf16");
+  const at::cuda::CUDAGuard guard(q.device());
+  const int T = (int)q.size(0), Hq = (int)q.size(1), D = (int)q.size(2);
+  auto o = torch::empty_like(q);
+  auto lse = torch::empty({Hq, T}, q.options().dtype(torch::kFloat32));
+  if (T == 0) return {o, lse};
+  auto ds = doc_start.to(torch::kInt32).contiguous();
+  auto stream = at::cuda::getCurrentCUDAStream();
+  int* st = attn_status(q.get_device()).data_ptr<int>();
+  switch (D) {
+    case 64: launch_fwd_tc<64, 64, 8, 2>(q, k, v, ds.data_ptr<int>(), (int)window, (float)scale, o, lse, st, stream); break;
+    case 128: launch_fwd_tc<128, 128, 8, 2>(q, k, v, ds.data_ptr<int>(), (int)window, (float)scale, o, lse, st, stream); break;
+    case 256: launch_fwd_tc<256, 256, 8, 2>(q, k, v, ds.data_ptr<int>(), (int)window, (float)scale, o, lse, st, stream); break;
+    case 512: launch_fwd_tc<512, 256, 4, 1>(q, k, v, ds.data_ptr<int>(), (int)window, (float)scale, o, lse, st, stream); break;
+    default: TORCH_CHECK(false, "attn_fwd_tc: head_dim must be 64, 128, 256 or 512");
+  }
+  return {o, lse};
+}
+
+torch::Tensor attn_tc_status(int64_t device) { return attn_status((int)device); }

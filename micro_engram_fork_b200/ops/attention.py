@@ -69,7 +69,13 @@ def attention_torch(q, k, v, doc_start, window=None, scale=1.0):
 
 
 def attention_fwd(q, k, v, doc_start, window=None, scale=1.0):
-    """(o [T, Hq, D] bf16, lse [Hq, T] fp32) on the sm_100a kernel."""
+    """(o [T, Hq, D] bf16, lse [Hq, T] fp32) on the tcgen05 kernel (csrc/attention_tc.cu):
+    S and O accumulate in tensor memory, Q/K/V arrive by TMA."""
+    return native().attn_fwd_tc(q, k, v, doc_start, int(window or 0), float(scale))
+
+
+def attention_fwd_mma(q, k, v, doc_start, window=None, scale=1.0):
+    """The first-generation warp-level mma.sync forward (kept for comparison and tests)."""
     return native().attn_fwd(q, k, v, doc_start, int(window or 0), float(scale))
 
 

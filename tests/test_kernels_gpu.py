@@ -392,3 +392,32 @@ def test_tcgen05_gemm(M, N, K, bn):
     ref32 = A.float() @ B.float().t()
     plain = A @ B.t()
     noise_floor_check(C, ref32, plain, rel=1.5, eps=1e-2, name=f"gemm {M}x{N}x{K}")
+
+
+# ----------------------------------------------------------------------------- tcgen05 attention forward
+@cuda
+@pytest.mark.parametrize("D,Hq,Hk,window,lens", [
+    (64, 4, 2, 48, [37, 120, 1, 80, 77]),
+    (128, 4, 1, None, [300, 2, 211]),
+    (256, 4, 2, 100, [37, 260, 1, 80, 140]),
+    (512, 8, 2, None, [700, 33, 290]),
+])
+def test_attention_fwd_tcgen05(D, Hq, Hk, window, lens):
+    import micro_engram_fork_b200 as me
+    from micro_engram_fork_b200.ops.attention import attention_ref, doc_starts
+
+    torch.manual_seed(0)
+    T = sum(lens)
+    pos = torch.cat([torch.arange(n) for n in lens]).to(_dev())
+    ds = doc_starts(pos)
+    q = torch.randn(T, Hq, D, device=_dev()).to(torch.bfloat16)
+    k = torch.randn(T, Hk, D, device=_dev()).to(torch.bfloat16)
+    v = torch.randn(T, Hk, D, device=_dev()).to(torch.bfloat16)
+    scale = 1.0 / math.sqrt(D)
+    o, lse = me.native().attn_fwd_tc(q, k, v, ds, window or 0, scale)
+    torch.cuda.synchronize()
+    assert int(me.native().attn_tc_status(0)[0]) == 0, "tcgen05 attention reported a timeout"
+    o32, lse32 = attention_ref(q.float(), k.float(), v.float(), ds, window, scale)
+    ob, _ = attention_ref(q, k, v, ds, window, scale)
+    noise_floor_check(o, o32, ob.to(torch.bfloat16), rel=2.0, eps=2e-3, name="attn tc out")
+    torch.testing.assert_close(lse, lse32, rtol=1e-3, atol=1e-3)
