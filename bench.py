@@ -85,7 +85,7 @@ def bench_config(tmp, steps):
         "micro_engram_dtype": "bf16", "micro_engram_optimizer": "rowwise_adam",
         "learning_rate": 5e-3, "micro_engram_dense_lr": 1e-3, "max_grad_norm": 2.0, "warmup_steps": 0,
         "gradient_checkpointing": True, "activation_offloading": True, "micro_engram_stats_steps": 0,
-        "gradient_checkpointing_policy": os.environ.get("ME_BENCH_AC", "selective"),
+        "gradient_checkpointing_policy": os.environ.get("ME_BENCH_AC", "auto"),
         "seed": 42,
     }
 
@@ -249,8 +249,10 @@ def run_ours(args):
                        "engram": "layer 0, tables {2:1572864,3:4194304,4:4194304} x8 heads x dim 64, "
                                  "scalar_sqrt, rowwise_adam bf16+SR",
                        "activation_checkpointing": f"per-layer, policy {trainer.cfg.gradient_checkpointing_policy}"
-                                                   " (selective: each layer's q/k/v projection, attention output"
-                                                   " and o-proj kept on the GPU, norms/RoPE/MLP recomputed)",
+                                                   " (HBM-budgeted: selective = q/k/v projection, attention output"
+                                                   " and o-proj kept on the GPU, norms/RoPE/MLP recomputed; none ="
+                                                   " nothing recomputed)",
+                       "activation_checkpointing_plan": getattr(trainer, "ckpt_plan", None),
                        "activation_offloading": "layer inputs to pinned host memory, prefetched in the backward",
                        "l2": "inputs larger than L2 (61 GB base streamed per step), no flush"},
             "clocks": clk,

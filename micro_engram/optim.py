@@ -56,6 +56,15 @@ class LazyAdamW(torch.optim.Optimizer):
             state["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.preserve_format)
 
     @torch.no_grad()
+    def materialize_state(self):
+        """Create every parameter's state now (instead of at the first step), so memory
+        planning sees the optimizer's full footprint."""
+        for group in self.param_groups:
+            for p in group["params"]:
+                if not self.state[p]:
+                    self.init_state(self.state[p], p, group)
+
+    @torch.no_grad()
     def step(self, closure=None):
         loss = None
         if closure is not None:

@@ -132,7 +132,8 @@ class TrainConfig(MicroEngramArgs):
     gradient_checkpointing_kwargs: Optional[Dict[str, Any]] = None
     # full: keep only each layer's input (the reference's behaviour); selective: also keep the
     # q/k/v projection, attention output + LSE and o-proj output on the GPU, recompute the rest
-    gradient_checkpointing_policy: Literal["full", "selective"] = "full"
+    # auto: selective where it fits in HBM, plus no recompute at all for as many layers as still fit
+    gradient_checkpointing_policy: Literal["full", "selective", "auto"] = "full"
     activation_offloading: bool = False
     no_grad_prefix: bool = True
     sharded_vocab: bool = True

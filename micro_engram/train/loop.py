@@ -177,11 +177,33 @@ class Trainer:
                               sparse_grads=bool(cfg.sparse_row_grads and opt in ("lazy_adam", "rowwise_adam")))
         if cfg.optimizer and not str(cfg.optimizer).startswith("adamw"):
             _log0(f"[micro_engram] optimizer: {cfg.optimizer} is not used; key/value/scales use AdamW")
+        if self.device.type == "cuda" and self.rows.optimizer is not None:
+            self.rows.optimizer.materialize_state()  # the tables' Adam state counts in memory planning
+        if cfg.gradient_checkpointing and cfg.gradient_checkpointing_policy == "auto" and self.device.type == "cuda":
+            self._plan_checkpointing(no_grad_upto)
         self.total_steps = self._count_steps()
         self.scheduler = self._scheduler()
         self.offload = ActivationOffload(self.device) if (cfg.activation_offloading and self.device.type == "cuda") \
             else None
         self._report()
+
+    def _plan_checkpointing(self, no_grad_upto):
+        """HBM-budgeted checkpointing plan (gradient_checkpointing_policy: auto): the free memory
+        after setup, minus headroom for one layer's backward working set, the loss chunks and
+        the allocator, decides which layers keep what. Identical on every rank (min over ranks)."""
+        torch.cuda.synchronize(self.device)
+        free, total = torch.cuda.mem_get_info(self.device)
+        cached = torch.cuda.memory_reserved(self.device) - torch.cuda.memory_allocated(self.device)
+        budget = torch.tensor([float(free + cached - (16 << 30) - 0.08 * total)], device=self.device)
+        if self.world > 1:
+            dist.all_reduce(budget, op=dist.ReduceOp.MIN)
+        tokens = self.cfg.micro_batch_size * self.cfg.sequence_len
+        plan = self.text.plan_checkpointing(tokens, max(0.0, float(budget)), upto=no_grad_upto)
+        counts = {m: sum(1 for v in plan.values() if v == m) for m in ("none", "selective", "full")}
+        _log0(f"[micro_engram] activation checkpointing plan ({float(budget) / 2**30:.1f} GiB budget): "
+              f"{counts['none']} layers keep everything, {counts['selective']} keep the attention half, "
+              f"{counts['full']} keep only their input")
+        self.ckpt_plan = counts
 
     def _place_engrams(self):
         """Dense engram params/buffers on this GPU, identical on every rank (rank 0's)."""

@@ -256,7 +256,8 @@ class GemmaLayer(nn.Module):
         if use_native(x):
             if torch.is_grad_enabled() and x.requires_grad:
                 ck = self.gradient_checkpointing
-                return _LayerFn.apply(x, pos, doc_start, self, ck if ck == "selective" else bool(ck))
+                mode = ck if ck in ("selective", "none", "full") else ("full" if ck else False)
+                return _LayerFn.apply(x, pos, doc_start, self, mode)
             with torch.no_grad():
                 return _layer_fwd(self, x, pos, doc_start)[0]
         if self.gradient_checkpointing and torch.is_grad_enabled() and x.requires_grad:
@@ -356,10 +357,14 @@ class _LayerFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, pos, doc_start, layer, checkpoint):
         ctx.layer, ctx.checkpoint = layer, checkpoint
-        out, saved = _layer_fwd(layer, x, pos, doc_start, keep=checkpoint in (False, "selective"))
+        out, saved = _layer_fwd(layer, x, pos, doc_start, keep=checkpoint in (False, "selective", "none"))
         if checkpoint == "selective":
             ctx.save_for_backward(x, pos, doc_start)
             ctx.kept = {k: saved[k] for k in _SELECTIVE_KEYS}
+        elif checkpoint == "none":
+            # everything except q/k/v (cheap to rebuild from qkv), kept on the GPU
+            ctx.save_for_backward(x, pos, doc_start)
+            ctx.kept = {k: v for k, v in saved.items() if k not in ("q", "k", "v")}
         elif checkpoint:
             ctx.save_for_backward(x, pos, doc_start)
         else:
@@ -379,6 +384,13 @@ class _LayerFn(torch.autograd.Function):
             with torch.no_grad():
                 s = _recompute_selective(layer, x, pos, ctx.kept)
             ctx.kept = None
+        elif ctx.checkpoint == "none":
+            s = ctx.kept
+            ctx.kept = None
+            with torch.no_grad():
+                s["q"], s["k"], s["v"], _ = N.qkv_norm_rope(
+                    s["qkv"], att.q_norm.weight, att.k_norm.weight, layer.inv_freq, pos, layer.n_q, layer.n_kv,
+                    layer.head_dim, layer.kv_eq, cfg.rms_norm_eps)
         elif ctx.checkpoint:
             with torch.no_grad():
                 _, s = _layer_fwd(layer, x, pos, doc_start, keep=True)
@@ -419,10 +431,45 @@ class GemmaTextModel(nn.Module):
 
     def gradient_checkpointing_enable(self, upto=None, policy="full"):
         """Per-layer checkpointing for the layers after `upto` (the no-grad prefix needs none).
-        policy: "full" (keep only the layer input) or "selective" (also keep the attention half)."""
+        policy: "full" (keep only the layer input), "selective" (also keep the attention half),
+        "auto" (selective now; plan_checkpointing() later upgrades layers that fit in HBM)."""
+        mode = {"auto": "selective", "selective": "selective", "none": "none"}.get(policy, "full")
         for i, layer in enumerate(self.layers):
-            on = upto is None or i > upto
-            layer.gradient_checkpointing = ("selective" if policy == "selective" else True) if on else False
+            layer.gradient_checkpointing = mode if (upto is None or i > upto) else False
+
+    @staticmethod
+    def layer_saved_bytes(layer, tokens):
+        """(selective, none) bytes a layer keeps on the GPU between its forward and backward."""
+        cfg = layer.cfg
+        d, f, hd = cfg.hidden_size, cfg.intermediate_size, layer.head_dim
+        qkv_w = (layer.n_q + (1 if layer.kv_eq else 2) * layer.n_kv) * hd
+        sel = tokens * (qkv_w * 2 + layer.n_q * hd * 2 + d * 2 + layer.n_q * 4 + (layer.n_q + 2 * layer.n_kv) * 4)
+        mlp = tokens * (d * 2 + 2 * f * 2 + d * 2 + 4 * 4)
+        return sel, sel + mlp
+
+    def plan_checkpointing(self, tokens, budget_bytes, upto=None):
+        """HBM-budgeted checkpointing: with `budget_bytes` free for saved activations, every
+        trained layer keeps its attention half (selective) when that fits, and as many layers
+        as then still fit keep their MLP activations too (no recompute at all). Returns the
+        per-layer plan. The math is identical under every plan; only recompute vs memory moves."""
+        layers = [l for i, l in enumerate(self.layers) if upto is None or i > upto]
+        costs = [self.layer_saved_bytes(l, tokens) for l in layers]
+        sel_total = sum(c[0] for c in costs)
+        plan = {}
+        if sel_total > budget_bytes:
+            for l in layers:
+                l.gradient_checkpointing = "full"
+                plan[l.idx] = "full"
+            return plan
+        left = budget_bytes - sel_total
+        for l, (sel, none) in zip(layers, costs):
+            if none - sel <= left:
+                l.gradient_checkpointing = "none"
+                left -= none - sel
+            else:
+                l.gradient_checkpointing = "selective"
+            plan[l.idx] = l.gradient_checkpointing
+        return plan
 
     def forward(self, inputs_embeds, position_ids):
         """inputs_embeds [1, T, d] or [T, d]; position_ids [1, T] or [T] -> final hidden [T, d]."""

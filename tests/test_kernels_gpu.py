@@ -332,7 +332,7 @@ def test_attention(D, Hq, Hk, window):
 
 # ----------------------------------------------------------------------------- decoder layer
 @cuda
-@pytest.mark.parametrize("checkpoint", [False, "full", "selective"])
+@pytest.mark.parametrize("checkpoint", [False, "full", "selective", "none"])
 def test_decoder_native_vs_torch(checkpoint):
     from micro_engram_fork_b200.models import gemma as G
     from micro_engram_fork_b200.ops.attention import doc_starts

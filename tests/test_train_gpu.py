@@ -49,6 +49,7 @@ def test_checkpoint_policies_and_offload_agree(dist_env):
         "full": _step(tmp, "full", False),
         "full+offload": _step(tmp, "full", True),
         "selective+offload": _step(tmp, "selective", True),
+        "auto+offload": _step(tmp, "auto", True),
     }
     ref = runs["none"]
     assert ref["table_grad_norm"] > 0 and ref["grad_norm"] > 0
