@@ -10,7 +10,7 @@ torch::Tensor engram_gather(torch::Tensor idx, torch::Tensor ptrs, torch::Tensor
                             int64_t src_dtype, torch::ScalarType out_dtype, c10::optional<torch::Tensor> status);
 void engram_scatter_grad(torch::Tensor g, torch::Tensor idx, torch::Tensor acc_ptrs, torch::Tensor bit_ptrs,
                          torch::Tensor list_ptrs, torch::Tensor cnt_ptrs, torch::Tensor per, int64_t world,
-                         double scale, c10::optional<torch::Tensor> status);
+                         double scale, c10::optional<torch::Tensor> status, int64_t my_rank);
 void engram_touched_sqnorm(torch::Tensor acc_ptrs, torch::Tensor list_ptrs, torch::Tensor cnt_ptrs, int64_t dim,
                            torch::Tensor sq);
 void engram_clip_coef(torch::Tensor sq, double max_norm, torch::Tensor coef, torch::Tensor norm);

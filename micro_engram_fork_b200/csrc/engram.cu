@@ -161,7 +161,7 @@ __global__ void scatter_grad_kernel(const Tg* __restrict__ g, const int64_t* __r
                                     const int64_t* __restrict__ list_ptrs,
                                     const int64_t* __restrict__ cnt_ptrs,
                                     const int64_t* __restrict__ per, int world, float scale,
-                                    int* status) {
+                                    int* status, int my_rank) {
   const int chunks = dim / 4;
   const int64_t total = N * n_tables * chunks;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -192,7 +192,14 @@ __global__ void scatter_grad_kernel(const Tg* __restrict__ g, const int64_t* __r
     }
     const int slot = owner * n_tables + k;
     float* acc = reinterpret_cast<float*>(acc_ptrs[slot]) + local * dim + c * 4;
-    atomicAdd(reinterpret_cast<float4*>(acc), v);
+    if (owner == my_rank) {
+      atomicAdd(reinterpret_cast<float4*>(acc), v);  // local memory: one 16-byte vector atomic
+    } else {  // a peer's memory over NVLink: plain fp32 atomics
+      atomicAdd(acc + 0, v.x);
+      atomicAdd(acc + 1, v.y);
+      atomicAdd(acc + 2, v.z);
+      atomicAdd(acc + 3, v.w);
+    }
     if (c == 0) {
       uint32_t* bits = reinterpret_cast<uint32_t*>(bit_ptrs[slot]);
       const uint32_t bit = 1u << (local & 31);
@@ -619,7 +626,7 @@ torch::Tensor engram_gather(torch::Tensor idx, torch::Tensor ptrs, torch::Tensor
 
 void engram_scatter_grad(torch::Tensor g, torch::Tensor idx, torch::Tensor acc_ptrs, torch::Tensor bit_ptrs,
                          torch::Tensor list_ptrs, torch::Tensor cnt_ptrs, torch::Tensor per, int64_t world,
-                         double scale, c10::optional<torch::Tensor> status) {
+                         double scale, c10::optional<torch::Tensor> status, int64_t my_rank) {
   check_cuda(g, "g");
   check_cuda(idx, "idx");
   const at::cuda::CUDAGuard guard(g.device());
@@ -636,13 +643,13 @@ void engram_scatter_grad(torch::Tensor g, torch::Tensor idx, torch::Tensor acc_p
     scatter_grad_kernel<__nv_bfloat16><<<grid, threads, 0, stream>>>(
         reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), idx.data_ptr<int64_t>(), N, nt, dim,
         acc_ptrs.data_ptr<int64_t>(), bit_ptrs.data_ptr<int64_t>(), list_ptrs.data_ptr<int64_t>(),
-        cnt_ptrs.data_ptr<int64_t>(), per.data_ptr<int64_t>(), world, (float)scale, st);
+        cnt_ptrs.data_ptr<int64_t>(), per.data_ptr<int64_t>(), world, (float)scale, st, (int)my_rank);
   } else {
     TORCH_CHECK(g.scalar_type() == torch::kFloat32, "row grads must be bf16 or fp32");
     scatter_grad_kernel<float><<<grid, threads, 0, stream>>>(
         g.data_ptr<float>(), idx.data_ptr<int64_t>(), N, nt, dim, acc_ptrs.data_ptr<int64_t>(),
         bit_ptrs.data_ptr<int64_t>(), list_ptrs.data_ptr<int64_t>(), cnt_ptrs.data_ptr<int64_t>(),
-        per.data_ptr<int64_t>(), world, (float)scale, st);
+        per.data_ptr<int64_t>(), world, (float)scale, st, (int)my_rank);
   }
 }
 

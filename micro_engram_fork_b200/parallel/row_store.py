@@ -127,7 +127,7 @@ class RowStore:
     def push_grads(self, g, idx, scale):
         """Row gradients g [N, n_tables*dim] of the looked-up rows -> the owners' accumulators."""
         native().engram_scatter_grad(g.contiguous(), idx, self.acc_ptrs, self.bit_ptrs, self.list_ptrs,
-                                     self.cnt_ptrs, self.per_t, self.world, float(scale), self.status)
+                                     self.cnt_ptrs, self.per_t, self.world, float(scale), self.status, self.rank)
         self.pending = True
 
     def sqnorm_into(self, sq):
