@@ -1,0 +1,158 @@
+"""Kernel microbenchmarks of the sm_100a kernels on the 31B-class shapes, timed with CUDA
+events (warm-up, synchronize on both sides) and reported against the measured roofline
+(MEASURED_PEAKS.json: cuBLAS bf16 burst TFLOP/s and copy bandwidth; the recipe's fallback
+figures otherwise). Also the workload that the committed ncu summaries in profiles/ capture.
+
+  python -m micro_engram_fork_b200.utils.kernel_bench [--case all|gemm|attn_fwd|attn_bwd|gate|ce] [--iters N]
+"""
+import argparse
+import json
+import os
+
+import torch
+
+_FALLBACK = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
+
+
+def peaks():
+    here = os.path.dirname(os.path.abspath(__file__))
+    path = os.path.join(here, "..", "..", "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {"bf16_tflops": float(d["bf16_tflops"]), "hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {**_FALLBACK, "source": "fallback"}
+
+
+def _time(fn, iters):
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def _docs(T, dev, lens=(2000, 3000, 1192, 2000)):
+    from ..ops.attention import doc_starts
+
+    pos = torch.cat([torch.arange(n) for n in lens])[:T].to(dev)
+    return doc_starts(pos)
+
+
+def case_gemm(C, dev, it, pk):
+    """Engram key projection shape: [8192 tokens x 1536] x [5376 x 1536]^T."""
+    A = torch.randn(8192, 1536, device=dev).to(torch.bfloat16)
+    B = (torch.randn(5376, 1536, device=dev) / 40).to(torch.bfloat16)
+    flops = 2 * 8192 * 5376 * 1536
+    out = {}
+    for name, fn in (("tcgen05 gemm_tc", lambda: C.gemm_tc(A, B, 256)), ("cuBLAS (torch.matmul)", lambda: A @ B.t())):
+        ms = _time(fn, it)
+        out[name] = {"ms": round(ms, 4), "tflops": round(flops / ms / 1e9, 1),
+                     "frac_of_peak": round(flops / ms / 1e9 / pk["bf16_tflops"], 3)}
+    return out
+
+
+def _attn_inputs(dev, D, Hk, T=8192, Hq=32):
+    q = torch.randn(T, Hq, D, device=dev).to(torch.bfloat16)
+    k = torch.randn(T, Hk, D, device=dev).to(torch.bfloat16)
+    v = torch.randn(T, Hk, D, device=dev).to(torch.bfloat16)
+    return q, k, v
+
+
+def _attn_flops(ds, W, D, Hq):
+    T = ds.numel()
+    t = torch.arange(T, device=ds.device)
+    lo = ds.long()
+    if W:
+        lo = torch.maximum(lo, t - W + 1)
+    return 4.0 * float((t - lo + 1).double().sum()) * D * Hq
+
+
+def case_attn_fwd(C, dev, it, pk):
+    out = {}
+    ds = _docs(8192, dev)
+    for (D, Hk, W) in ((256, 16, 1024), (512, 4, 0)):
+        q, k, v = _attn_inputs(dev, D, Hk)
+        fl = _attn_flops(ds, W, D, 32)
+        for name, fn in (("tcgen05", lambda: C.attn_fwd_tc(q, k, v, ds, W, 1.0)),
+                         ("mma.sync", lambda: C.attn_fwd(q, k, v, ds, W, 1.0))):
+            ms = _time(fn, it)
+            out[f"hd{D} {name}"] = {"ms": round(ms, 4), "useful_tflops": round(fl / ms / 1e9, 1),
+                                    "frac_of_peak": round(fl / ms / 1e9 / pk["bf16_tflops"], 3)}
+    return out
+
+
+def case_attn_bwd(C, dev, it, pk):
+    out = {}
+    ds = _docs(8192, dev)
+    for (D, Hk, W) in ((256, 16, 1024), (512, 4, 0)):
+        q, k, v = _attn_inputs(dev, D, Hk)
+        o, lse = C.attn_fwd_tc(q, k, v, ds, W, 1.0)
+        do = torch.randn_like(o)
+        fl = 2.5 * _attn_flops(ds, W, D, 32)
+        ms = _time(lambda: C.attn_bwd(do, q, k, v, o, lse, ds, W, 1.0), it)
+        out[f"hd{D} bwd"] = {"ms": round(ms, 4), "useful_tflops": round(fl / ms / 1e9, 1),
+                             "frac_of_peak": round(fl / ms / 1e9 / pk["bf16_tflops"], 3)}
+    return out
+
+
+def case_gate(C, dev, it, pk):
+    """Fused scalar_sqrt gate at the microbenchmark size: 65536 tokens x d 5376."""
+    N, d = 65536, 5376
+    h = torch.randn(N, d, device=dev).to(torch.bfloat16)
+    k = torch.randn_like(h)
+    v = torch.randn_like(h) * 0.1
+    s = torch.ones(d, device=dev)
+    fwd_bytes = 4 * N * d * 2           # read h, k, v; write out
+    bwd_bytes = 7 * N * d * 2           # read g, h, k, v; write dh, dk, dv
+    out, st = C.engram_gate_fwd(h, k, v, s, s, None, True, None)
+    r = {}
+    ms = _time(lambda: C.engram_gate_fwd(h, k, v, s, s, None, True, None), it)
+    r["gate fwd"] = {"ms": round(ms, 4), "gbs": round(fwd_bytes / ms / 1e6, 1),
+                     "frac_of_hbm": round(fwd_bytes / ms / 1e6 / pk["hbm_gbs"], 3)}
+    ms = _time(lambda: C.engram_gate_bwd(out, h, k, v, s, s, None, st, True), it)
+    r["gate bwd"] = {"ms": round(ms, 4), "gbs": round(bwd_bytes / ms / 1e6, 1),
+                     "frac_of_hbm": round(bwd_bytes / ms / 1e6 / pk["hbm_gbs"], 3)}
+    return r
+
+
+def case_ce(C, dev, it, pk):
+    """One loss chunk: 256 tokens x 262144 vocab logits (bf16) -> softcapped LSE partials."""
+    z = torch.randn(2048, 262144, device=dev).to(torch.bfloat16)
+    lab = torch.randint(0, 262144, (2048,), device=dev)
+    nbytes = z.numel() * 2
+    ms = _time(lambda: C.ce_fwd(z, lab, 0, 30.0), it)
+    return {"ce_fwd 2048x262144": {"ms": round(ms, 4), "gbs": round(nbytes / ms / 1e6, 1),
+                                   "frac_of_hbm": round(nbytes / ms / 1e6 / pk["hbm_gbs"], 3)}}
+
+
+CASES = {"gemm": case_gemm, "attn_fwd": case_attn_fwd, "attn_bwd": case_attn_bwd, "gate": case_gate, "ce": case_ce}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--case", default="all", choices=["all"] + list(CASES))
+    ap.add_argument("--iters", type=int, default=10)
+    args = ap.parse_args(argv)
+    from .. import native
+
+    C = native()
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    pk = peaks()
+    res = {"peaks": pk}
+    for name, fn in CASES.items():
+        if args.case in ("all", name):
+            res[name] = fn(C, dev, args.iters, pk)
+    res["status"] = {"gemm": C.gemm_status(0).tolist(), "attn_tc": C.attn_tc_status(0).tolist()}
+    print(json.dumps(res, indent=1))
+
+
+if __name__ == "__main__":
+    main()
