@@ -25,6 +25,8 @@ def _load():
     if _C is not None or _C_ERROR is not None:
         return _C
     try:
+        import torch  # noqa: F401 - loads libc10/libtorch the extension links against
+
         _C = importlib.import_module("micro_engram_fork_b200._C")
     except ImportError as e:  # not built (CPU-only checkout): CUDA ops raise on use
         _C_ERROR = e

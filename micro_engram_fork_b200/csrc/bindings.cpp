@@ -28,6 +28,9 @@ std::vector<torch::Tensor> engram_gate_fwd(torch::Tensor h, torch::Tensor k, tor
 std::vector<torch::Tensor> engram_gate_bwd(torch::Tensor g, torch::Tensor h, torch::Tensor k, torch::Tensor v,
                                            c10::optional<torch::Tensor> qs, c10::optional<torch::Tensor> ks,
                                            c10::optional<torch::Tensor> keep, torch::Tensor stats, bool sqrt_gate);
+void engram_fill_ids(torch::Tensor out, torch::Tensor input_ids, torch::Tensor positions, torch::Tensor idx_mapping,
+                     torch::Tensor qsl, torch::Tensor all_ids, int64_t num_reqs, int64_t num_tokens,
+                     int64_t num_padded);
 // norm.cu
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, c10::optional<torch::Tensor> w, double eps);
 torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, c10::optional<torch::Tensor> w, torch::Tensor rstd,
@@ -85,6 +88,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adam_dense", &adam_dense);
   m.def("engram_gate_fwd", &engram_gate_fwd);
   m.def("engram_gate_bwd", &engram_gate_bwd);
+  m.def("engram_fill_ids", &engram_fill_ids);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("post_norm_add", &post_norm_add);

@@ -523,6 +523,203 @@ __global__ void gate_bwd_kernel(const __nv_bfloat16* __restrict__ g, const __nv_
   }
 }
 
+// Vectorised gate (16-byte loads, one block per row, NCH chunks of 8 bf16 per thread).
+// The rms and dot products collapse into one pass: with D = sum_j h_j k_j qs_j ks_j,
+//   s_raw = rh rk D / sqrt(d);   backward: sum_j h_j qs_j dhn_j = ds rk D, sum_j k_j ks_j dkn_j = ds rh D,
+//   d qs_j = ks_j S_j, d ks_j = qs_j S_j with S_j = sum_n ds_n rh_n rk_n h_nj k_nj,
+// so k is never held across a reduction in the forward and the column partials need one array.
+// Requires d % 8 == 0 and 16-byte aligned rows; the scalar kernels above take the rest.
+ME_DEVICE float3 block_sum3(float a, float b, float c, float* scratch) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  a = warp_sum(a);
+  b = warp_sum(b);
+  c = warp_sum(c);
+  __syncthreads();
+  if (lane == 0) {
+    scratch[wid] = a;
+    scratch[32 + wid] = b;
+    scratch[64 + wid] = c;
+  }
+  __syncthreads();
+  float ra = lane < nw ? scratch[lane] : 0.f, rb = lane < nw ? scratch[32 + lane] : 0.f,
+        rc = lane < nw ? scratch[64 + lane] : 0.f;
+  return make_float3(warp_sum(ra), warp_sum(rb), warp_sum(rc));
+}
+
+ME_DEVICE void load_scale8(const float* __restrict__ s, int c, float* out) {
+  if (s) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(s) + 2 * c);
+    const float4 b = __ldg(reinterpret_cast<const float4*>(s) + 2 * c + 1);
+    out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+    out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) out[e] = 1.f;
+  }
+}
+
+template <int NCH>
+__global__ void __launch_bounds__(256) gate_fwd_vec_kernel(
+    const uint4* __restrict__ h, const uint4* __restrict__ k, const uint4* __restrict__ v,
+    const float* __restrict__ qs, const float* __restrict__ ks, const uint8_t* __restrict__ keep, int64_t N,
+    int d, int sqrt_gate, uint4* __restrict__ out, float* __restrict__ stats, float* __restrict__ gate_acc) {
+  __shared__ float scratch[96];
+  const int nc = d >> 3;
+  const float inv_sqrt_d = rsqrtf((float)d);
+  float acc_a = 0.f, acc_n = 0.f, acc_sat = 0.f;
+  for (int64_t n = blockIdx.x; n < N; n += gridDim.x) {
+    BF16x8 hv[NCH];
+    float sh = 0.f, sk = 0.f, dot = 0.f;
+#pragma unroll
+    for (int q = 0; q < NCH; ++q) {
+      const int c = threadIdx.x + q * blockDim.x;
+      BF16x8 kv;
+      if (c < nc) {
+        hv[q].u = __ldcs(h + n * nc + c);
+        kv.u = __ldcs(k + n * nc + c);
+        float w[8], u[8];
+        load_scale8(qs, c, w);
+        load_scale8(ks, c, u);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float a = bf2f(hv[q].h[e]), b = bf2f(kv.h[e]);
+          sh += a * a;
+          sk += b * b;
+          dot += a * b * w[e] * u[e];
+        }
+      }
+    }
+    const float3 r3 = block_sum3(sh, sk, dot, scratch);
+    const float rh = rsqrtf(r3.x / d + kEps), rk = rsqrtf(r3.y / d + kEps);
+    const float s_raw = rh * rk * r3.z * inv_sqrt_d;
+    float s = s_raw;
+    if (sqrt_gate) {
+      const float sg = s_raw > 0.f ? 1.f : (s_raw < 0.f ? -1.f : 0.f);
+      s = sg * sqrtf(fmaxf(fabsf(s_raw), 1e-6f));
+    }
+    const float alpha = 1.f / (1.f + expf(-s));
+    const float kp = keep ? (keep[n] ? 1.f : 0.f) : 1.f;
+#pragma unroll
+    for (int q = 0; q < NCH; ++q) {
+      const int c = threadIdx.x + q * blockDim.x;
+      if (c < nc) {
+        BF16x8 vv, o;
+        vv.u = __ldcs(v + n * nc + c);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float add = bf2f(f2bf(alpha * bf2f(vv.h[e]) * kp));
+          o.h[e] = f2bf(bf2f(hv[q].h[e]) + add);
+        }
+        out[n * nc + c] = o.u;
+      }
+    }
+    if (threadIdx.x == 0) {
+      reinterpret_cast<float4*>(stats)[n] = make_float4(rh, rk, s_raw, alpha);
+      acc_a += alpha;
+      acc_n += 1.f;
+      acc_sat += alpha > 0.99f ? 1.f : 0.f;
+    }
+  }
+  if (gate_acc && threadIdx.x == 0) {
+    atomicAdd(gate_acc + 0, acc_a);
+    atomicAdd(gate_acc + 1, acc_n);
+    atomicAdd(gate_acc + 2, acc_sat);
+  }
+}
+
+template <int NCH>
+__global__ void __launch_bounds__(256) gate_bwd_vec_kernel(
+    const uint4* __restrict__ g, const uint4* __restrict__ h, const uint4* __restrict__ k,
+    const uint4* __restrict__ v, const float* __restrict__ qs, const float* __restrict__ ks,
+    const uint8_t* __restrict__ keep, const float* __restrict__ stats, int64_t N, int d, int sqrt_gate,
+    uint4* __restrict__ dh, uint4* __restrict__ dk, uint4* __restrict__ dv, float* __restrict__ dqs,
+    float* __restrict__ dks) {
+  __shared__ float scratch[96];
+  const int nc = d >> 3;
+  const float inv_sqrt_d = rsqrtf((float)d);
+  float S[NCH][8];
+#pragma unroll
+  for (int q = 0; q < NCH; ++q)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) S[q][e] = 0.f;
+  for (int64_t n = blockIdx.x; n < N; n += gridDim.x) {
+    const float4 st = reinterpret_cast<const float4*>(stats)[n];
+    const float rh = st.x, rk = st.y, s_raw = st.z, alpha = st.w;
+    const float kp = keep ? (keep[n] ? 1.f : 0.f) : 1.f;
+    BF16x8 gv[NCH], hv[NCH], kv[NCH];
+    float da = 0.f, dot = 0.f;
+#pragma unroll
+    for (int q = 0; q < NCH; ++q) {
+      const int c = threadIdx.x + q * blockDim.x;
+      if (c < nc) {
+        gv[q].u = __ldcs(g + n * nc + c);
+        hv[q].u = __ldcs(h + n * nc + c);
+        kv[q].u = __ldcs(k + n * nc + c);
+        BF16x8 vv, o;
+        vv.u = __ldcs(v + n * nc + c);
+        float w[8], u[8];
+        load_scale8(qs, c, w);
+        load_scale8(ks, c, u);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float gg = bf2f(gv[q].h[e]);
+          da += gg * kp * bf2f(vv.h[e]);
+          dot += bf2f(hv[q].h[e]) * bf2f(kv[q].h[e]) * w[e] * u[e];
+          o.h[e] = f2bf(alpha * gg * kp);
+        }
+        __stcs(dv + n * nc + c, o.u);
+      }
+    }
+    const float2 r2 = block_sum2(da, dot, scratch);
+    float ds = r2.x * alpha * (1.f - alpha);
+    if (sqrt_gate) {
+      const float c = fabsf(s_raw);
+      ds = (c >= 1e-6f && s_raw != 0.f) ? ds * 0.5f / sqrtf(c) : 0.f;
+    }
+    ds *= inv_sqrt_d;
+    const float ch = rh * rh * rh * ds * rk * r2.y / d, ck = rk * rk * rk * ds * rh * r2.y / d;
+    const float cn = ds * rh * rk;
+#pragma unroll
+    for (int q = 0; q < NCH; ++q) {
+      const int c = threadIdx.x + q * blockDim.x;
+      if (c < nc) {
+        float w[8], u[8];
+        load_scale8(qs, c, w);
+        load_scale8(ks, c, u);
+        BF16x8 oh, ok;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float hh = bf2f(hv[q].h[e]), kk = bf2f(kv[q].h[e]);
+          const float hk = cn * w[e] * u[e];
+          const float dhg = hk * kk - ch * hh;
+          const float dkg = hk * hh - ck * kk;
+          oh.h[e] = f2bf(bf2f(gv[q].h[e]) + bf2f(f2bf(dhg)));
+          ok.h[e] = f2bf(dkg);
+          S[q][e] += cn * hh * kk;
+        }
+        __stcs(dh + n * nc + c, oh.u);
+        __stcs(dk + n * nc + c, ok.u);
+      }
+    }
+  }
+  if (dqs) {
+#pragma unroll
+    for (int q = 0; q < NCH; ++q) {
+      const int c = threadIdx.x + q * blockDim.x;
+      if (c < nc) {
+        float w[8], u[8];
+        load_scale8(qs, c, w);
+        load_scale8(ks, c, u);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          atomicAdd(dqs + 8 * c + e, u[e] * S[q][e]);
+          atomicAdd(dks + 8 * c + e, w[e] * S[q][e]);
+        }
+      }
+    }
+  }
+}
+
 int sm_count() {
   static int n = 0;
   if (n == 0) {
@@ -740,6 +937,25 @@ void adam_dense(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor
   }
 }
 
+// A persistent grid: as many blocks as fit on every SM at once, at most one per row.
+template <typename K>
+static int occupancy_grid(K kernel, int threads, int64_t rows) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  return (int)std::max<int64_t>(1, std::min<int64_t>(rows, (int64_t)sm_count() * per_sm));
+}
+
+// The vectorised gate wants 8-element (16-byte) chunks: d % 8 == 0, 16-byte aligned rows and
+// scales, hidden size at most 8192 (4 chunks of 8 per thread at 256 threads).
+static bool gate_vec_ok(int d, std::initializer_list<const void*> rows, const float* qs, const float* ks) {
+  if (d % 8 != 0 || d > 8192) return false;
+  for (const void* p : rows)
+    if (reinterpret_cast<uintptr_t>(p) % 16 != 0) return false;
+  if ((qs && reinterpret_cast<uintptr_t>(qs) % 16) || (ks && reinterpret_cast<uintptr_t>(ks) % 16)) return false;
+  return true;
+}
+
 // stats [N, 4] fp32 out; gate_acc [3] fp32 (accumulated) or None.
 std::vector<torch::Tensor> engram_gate_fwd(torch::Tensor h, torch::Tensor k, torch::Tensor v,
                                            c10::optional<torch::Tensor> qs, c10::optional<torch::Tensor> ks,
@@ -757,6 +973,28 @@ std::vector<torch::Tensor> engram_gate_fwd(torch::Tensor h, torch::Tensor k, tor
   auto out = torch::empty_like(h);
   auto stats = torch::empty({N, 4}, h.options().dtype(torch::kFloat32));
   if (N == 0) return {out, stats};
+  const float* qsp0 = qs.has_value() ? qs->data_ptr<float>() : nullptr;
+  const float* ksp0 = ks.has_value() ? ks->data_ptr<float>() : nullptr;
+  if (gate_vec_ok(d, {h.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), stats.data_ptr()}, qsp0, ksp0)) {
+    const int nch = (d / 8 + 255) / 256;
+    const int threads = ((d / 8 + nch - 1) / nch + 31) / 32 * 32;
+    auto stream = at::cuda::getCurrentCUDAStream();
+    auto U = [](const torch::Tensor& t) { return reinterpret_cast<const uint4*>(t.data_ptr()); };
+    const uint8_t* kpp0 = keep.has_value() ? keep->data_ptr<uint8_t>() : nullptr;
+    float* gap0 = gate_acc.has_value() ? gate_acc->data_ptr<float>() : nullptr;
+#define ME_GATE_FWD_VEC(C)                                                                                  \
+  const int grid = occupancy_grid(gate_fwd_vec_kernel<C>, threads, N);                                      \
+  gate_fwd_vec_kernel<C><<<grid, threads, 0, stream>>>(U(h), U(k), U(v), qsp0, ksp0, kpp0, N, d, sqrt_gate ? 1 : 0, \
+                                                       reinterpret_cast<uint4*>(out.data_ptr()),            \
+                                                       stats.data_ptr<float>(), gap0)
+    if (nch == 1) { ME_GATE_FWD_VEC(1); }
+    else if (nch == 2) { ME_GATE_FWD_VEC(2); }
+    else if (nch == 3) { ME_GATE_FWD_VEC(3); }
+    else { ME_GATE_FWD_VEC(4); }
+#undef ME_GATE_FWD_VEC
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return {out, stats};
+  }
   const int threads = 256;
   const int vpt = (d + threads - 1) / threads;
   TORCH_CHECK(vpt <= 32, "hidden size above 8192 is not supported by the fused gate");
@@ -797,6 +1035,34 @@ std::vector<torch::Tensor> engram_gate_bwd(torch::Tensor g, torch::Tensor h, tor
     dks = torch::zeros({d}, h.options().dtype(torch::kFloat32));
   }
   if (N == 0) return {dh, dk, dv, dqs, dks};
+  {
+    const float* qsp0 = qs.has_value() ? qs->data_ptr<float>() : nullptr;
+    const float* ksp0 = ks.has_value() ? ks->data_ptr<float>() : nullptr;
+    if (gate_vec_ok(d, {gc.data_ptr(), h.data_ptr(), k.data_ptr(), v.data_ptr(), dh.data_ptr(), dk.data_ptr(),
+                        dv.data_ptr(), stats.data_ptr()}, qsp0, ksp0) &&
+        stats.is_contiguous() && stats.scalar_type() == torch::kFloat32) {
+      const int nch = (d / 8 + 255) / 256;
+      const int threads = ((d / 8 + nch - 1) / nch + 31) / 32 * 32;
+      auto stream = at::cuda::getCurrentCUDAStream();
+      auto U = [](const torch::Tensor& t) { return reinterpret_cast<const uint4*>(t.data_ptr()); };
+      auto W = [](torch::Tensor& t) { return reinterpret_cast<uint4*>(t.data_ptr()); };
+      const uint8_t* kpp0 = keep.has_value() ? keep->data_ptr<uint8_t>() : nullptr;
+      float* dq0 = qs.has_value() ? dqs.data_ptr<float>() : nullptr;
+      float* dk0 = qs.has_value() ? dks.data_ptr<float>() : nullptr;
+#define ME_GATE_BWD_VEC(C)                                                                                   \
+  const int grid = occupancy_grid(gate_bwd_vec_kernel<C>, threads, N);                                       \
+  gate_bwd_vec_kernel<C><<<grid, threads, 0, stream>>>(U(gc), U(h), U(k), U(v), qsp0, ksp0, kpp0,              \
+                                                       stats.data_ptr<float>(), N, d, sqrt_gate ? 1 : 0, W(dh), \
+                                                       W(dk), W(dv), dq0, dk0)
+      if (nch == 1) { ME_GATE_BWD_VEC(1); }
+      else if (nch == 2) { ME_GATE_BWD_VEC(2); }
+      else if (nch == 3) { ME_GATE_BWD_VEC(3); }
+      else { ME_GATE_BWD_VEC(4); }
+#undef ME_GATE_BWD_VEC
+      C10_CUDA_KERNEL_LAUNCH_CHECK();
+      return {dh, dk, dv, dqs, dks};
+    }
+  }
   const int threads = 256;
   const int vpt = (d + threads - 1) / threads;
   TORCH_CHECK(vpt <= 32, "hidden size above 8192 is not supported by the fused gate");
@@ -820,4 +1086,67 @@ std::vector<torch::Tensor> engram_gate_bwd(torch::Tensor g, torch::Tensor h, tor
 #undef BF
 #undef CBF
   return {dh, dk, dv, dqs, dks};
+}
+
+// ------------------------------------------------------------------------------ serving histories
+// For every token a serving step runs, its n-gram history: out[t, i] = token at position p_t - i
+// of the same request, -1 before the request's first token; rows [num_tokens, num_padded) = -1.
+// Tokens from the step's own chunk come from input_ids (t - i), earlier ones from the request's
+// row of all_ids (micro_engram_vllm/ids.py:10-59 of the reference states the same rule as torch
+// ops). One thread per (token, i); the request of token t is found by binary search over the
+// request offsets `qsl`. Index tensors may be int32 or int64 (is64 flags per tensor).
+ME_DEVICE int64_t ld_index(const void* p, int is64, int64_t i) {
+  return is64 ? reinterpret_cast<const int64_t*>(p)[i] : (int64_t)reinterpret_cast<const int32_t*>(p)[i];
+}
+
+__global__ void fill_ids_kernel(int32_t* __restrict__ out, int max_order, const void* input_ids, int ids64,
+                                const void* positions, int pos64, const void* idx_mapping, int map64,
+                                const void* qsl, int qsl64, const void* all_ids, int all64, int64_t all_stride,
+                                int num_reqs, int num_tokens, int num_padded) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= (int64_t)num_padded * max_order) return;
+  const int t = (int)(e / max_order), i = (int)(e % max_order);
+  if (t >= num_tokens) {
+    out[e] = -1;
+    return;
+  }
+  int lo = 0, hi = num_reqs - 1;  // last request whose first token is <= t
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (ld_index(qsl, qsl64, mid) <= t) lo = mid;
+    else hi = mid - 1;
+  }
+  const int64_t first = ld_index(qsl, qsl64, lo);
+  const int64_t chunk_start = ld_index(positions, pos64, first);
+  const int64_t q = ld_index(positions, pos64, t) - i;
+  int64_t v;
+  if (q < 0) v = -1;
+  else if (q >= chunk_start) v = ld_index(input_ids, ids64, t - i);
+  else v = ld_index(all_ids, all64, ld_index(idx_mapping, map64, lo) * all_stride + q);
+  out[e] = (int32_t)v;
+}
+
+void engram_fill_ids(torch::Tensor out, torch::Tensor input_ids, torch::Tensor positions, torch::Tensor idx_mapping,
+                     torch::Tensor qsl, torch::Tensor all_ids, int64_t num_reqs, int64_t num_tokens,
+                     int64_t num_padded) {
+  check_cuda(out, "out");
+  TORCH_CHECK(out.scalar_type() == torch::kInt32 && out.dim() == 2 && out.is_contiguous(),
+              "out must be a contiguous [max_tokens, max_order] int32 buffer");
+  TORCH_CHECK(num_padded <= out.size(0) && num_tokens <= num_padded, "more tokens than the buffer holds");
+  TORCH_CHECK(all_ids.dim() == 2 && all_ids.stride(1) == 1, "all_token_ids must be [max_reqs, max_len] row-major");
+  auto is64 = [](const torch::Tensor& x) {
+    TORCH_CHECK(x.scalar_type() == torch::kInt32 || x.scalar_type() == torch::kInt64, "index tensors are int32/int64");
+    TORCH_CHECK(x.dim() == 2 || x.stride(0) == 1, "index vectors must be contiguous");
+    return x.scalar_type() == torch::kInt64 ? 1 : 0;
+  };
+  const at::cuda::CUDAGuard guard(out.device());
+  const int64_t n = num_padded * out.size(1);
+  if (n == 0) return;
+  if (num_tokens > 0) TORCH_CHECK(num_reqs > 0, "tokens without requests");
+  const int threads = 256;
+  fill_ids_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      out.data_ptr<int32_t>(), (int)out.size(1), input_ids.data_ptr(), is64(input_ids), positions.data_ptr(),
+      is64(positions), idx_mapping.data_ptr(), is64(idx_mapping), qsl.data_ptr(), is64(qsl), all_ids.data_ptr(),
+      is64(all_ids), all_ids.stride(0), (int)num_reqs, (int)num_tokens, (int)num_padded);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
