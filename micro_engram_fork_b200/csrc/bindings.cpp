@@ -67,6 +67,9 @@ torch::Tensor attn_tc_status(int64_t device);
 // gemm.cu
 torch::Tensor gemm_tc(torch::Tensor A, torch::Tensor B, int64_t block_n);
 torch::Tensor gemm_status(int64_t device);
+// nf4.cu
+std::vector<torch::Tensor> nf4_quantize(torch::Tensor w);
+void nf4_dequant(torch::Tensor codes, torch::Tensor absmax, torch::Tensor out);
 // symm.cpp
 int64_t symm_alloc(int64_t nbytes, int64_t device);
 void symm_free(int64_t ptr, int64_t device);
@@ -105,6 +108,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_tc_status", &attn_tc_status);
   m.def("gemm_tc", &gemm_tc, py::arg("A"), py::arg("B"), py::arg("block_n") = 256);
   m.def("gemm_status", &gemm_status);
+  m.def("nf4_quantize", &nf4_quantize);
+  m.def("nf4_dequant", &nf4_dequant);
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_free", &symm_free);
   m.def("symm_export", &symm_export);

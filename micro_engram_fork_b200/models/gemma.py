@@ -238,6 +238,12 @@ class GemmaLayer(nn.Module):
         self._relink()
         return out
 
+    def __setstate__(self, state):
+        # copy.deepcopy / pickle rebuild the fused buffers and the HF-named weights as separate
+        # tensors; make the names views of the buffers again
+        super().__setstate__(state)
+        self._relink()
+
     def _relink(self):
         nq = self.n_q * self.head_dim
         nk = self.n_kv * self.head_dim
@@ -270,6 +276,7 @@ class GemmaLayer(nn.Module):
         return N.rmsnorm_ref(x, None if w_none else norm.weight, self.cfg.rms_norm_eps)
 
     def _forward_torch(self, x, pos, doc_start):
+        _materialize(self)
         cfg, att = self.cfg, self.self_attn
         T = x.shape[0]
         hd = self.head_dim
@@ -296,10 +303,19 @@ def _ls(layer):
     return layer.layer_scalar.float().reshape(1).contiguous()
 
 
+def _materialize(layer):
+    """NF4 base: expand this layer's weights into the shared bf16 buffer before they are read."""
+    if getattr(layer, "_nf4", None) is not None:
+        from .nf4 import materialize
+
+        materialize(layer)
+
+
 def _layer_fwd(layer, x, pos, doc_start, keep=False):
     """Native forward of one layer; returns (out, saved dict or None)."""
     from ..ops.attention import attention_fwd
 
+    _materialize(layer)
     cfg = layer.cfg
     eps = cfg.rms_norm_eps
     T = x.shape[0]
@@ -332,6 +348,7 @@ _SELECTIVE_KEYS = ("qkv", "a", "lse", "o")
 def _recompute_selective(layer, x, pos, kept):
     """Rebuild a layer's saved state from its input and the kept attention tensors: norms,
     RoPE and the MLP are recomputed; the q/k/v and o projections and attention are not."""
+    _materialize(layer)
     eps = layer.cfg.rms_norm_eps
     att = layer.self_attn
     _, r_in = N.rmsnorm(x, layer.input_layernorm.weight, eps)
@@ -376,6 +393,7 @@ class _LayerFn(torch.autograd.Function):
         from ..ops.attention import attention_bwd
 
         layer = ctx.layer
+        _materialize(layer)
         cfg = layer.cfg
         att = layer.self_attn
         tensors = ctx.saved_tensors
