@@ -396,3 +396,428 @@ std::vector<torch::Tensor> attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::
 }
 
 torch::Tensor attn_tc_status(int64_t device) { return attn_status((int)device); }
+
+// =============================================================================== backward
+// tcgen05 packed-varlen attention backward, three kernels from one template (head_dim <= 256):
+//   MODE_DQ  one CTA = 128 queries of one head (resident Q and dO); per key block of BC keys:
+//            S = Q K^T, dP = dO V^T (TMEM), dS = P * (dP - delta_row) -> smem, dQ += dS K
+//   MODE_DK  one CTA = 128 keys of one kv head (resident K and V); per (query head of the GQA
+//            group, block of BC queries): S^T = K Q^T, dP^T = V dO^T, dS^T = P^T * (dP^T - delta_col)
+//            -> smem, dK += dS^T Q
+//   MODE_DV  resident K; S^T = K Q^T, P^T -> smem, dV += P^T dO
+// with P = exp(scale * S - LSE) from the forward's LSE. dK and dV sum over the GQA group inside
+// the CTA (no atomics); dQ and dK carry the softmax scale. TMEM: two S buffers, two dP
+// buffers, one D-column accumulator. Warp roles as in the forward: warp 0 TMA producer (Q/K/V/dO
+// tiles by 3-D tensor maps; per-query LSE, delta and document starts by untiled bulk copies),
+// warp 1 TMEM owner + MMA issuer, warps 2-5 one row (TMEM lane) per thread. Every wait is
+// bounded; a timeout records ME_ERR_TIMEOUT and the kernel frees TMEM and returns.
+namespace {
+
+enum { MODE_DQ = 0, MODE_DK = 1, MODE_DV = 2 };
+
+template <int D, int BC, int MODE>
+struct BwdLayout {
+  static constexpr bool TWO = MODE != MODE_DV;    // a second product (dP) and resident R2
+  static constexpr bool COLS = MODE != MODE_DQ;   // per-column (query) LSE / delta / doc start
+  static constexpr int NC = D / 64;
+  static constexpr int R_BYTES = 128 * D * 2;
+  static constexpr int C_BYTES = BC * D * 2;      // one streamed tile (D/64 chunks of BC x 128 B)
+  static constexpr int COL_BYTES = COLS ? 3 * BC * 4 : 0;
+  // stage starts stay 1024-byte aligned: the 128-byte-swizzle atoms of TMA and UMMA need it
+  static constexpr int STAGE_BYTES = (2 * C_BYTES + COL_BYTES + 1023) / 1024 * 1024;
+  static constexpr int R_OFF = 0;
+  static constexpr int R2_OFF = R_OFF + R_BYTES;
+  static constexpr int ST_OFF = R2_OFF + (TWO ? R_BYTES : 0);
+  static constexpr int W_OFF = ST_OFF + 2 * STAGE_BYTES;
+  static constexpr int BAR_OFF = W_OFF + 128 * 128;
+  static constexpr int N_BARS = 1 + 2 + 2 + 2 + 2 + 1 + 1 + 1;
+  static constexpr int BYTES = BAR_OFF + N_BARS * 8 + 16 + 1024;
+  static constexpr int S_COL = 0, DP_COL = 2 * BC, ACC_COL = TWO ? 4 * BC : 2 * BC;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static_assert(ACC_COL + D <= 512, "TMEM columns");
+  static_assert(BYTES <= 232448, "shared memory");
+};
+
+template <int D, int BC, int MODE>
+__global__ void __launch_bounds__(192, 1)
+    attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tr, const __grid_constant__ CUtensorMap tr2,
+                       const __grid_constant__ CUtensorMap tc1, const __grid_constant__ CUtensorMap tc2,
+                       const float* __restrict__ lse, const float* __restrict__ delta, const int* __restrict__ ds,
+                       const int* __restrict__ de, int T, int Tp, int Hq, int Hk, int window, float scale,
+                       bf16* __restrict__ out, int* status) {
+  using L = BwdLayout<D, BC, MODE>;
+  constexpr int NC = L::NC;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sR = smem + L::R_OFF;
+  uint8_t* sR2 = smem + L::R2_OFF;
+  uint8_t* sW = smem + L::W_OFF;
+  auto stage_c1 = [&](int st) { return smem + L::ST_OFF + st * L::STAGE_BYTES; };
+  auto stage_c2 = [&](int st) { return smem + L::ST_OFF + st * L::STAGE_BYTES + L::C_BYTES; };
+  auto stage_cols = [&](int st) {
+    return reinterpret_cast<float*>(smem + L::ST_OFF + st * L::STAGE_BYTES + 2 * L::C_BYTES);
+  };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* r_full = bars;
+  uint64_t* c_full = r_full + 1;
+  uint64_t* c_empty = c_full + 2;
+  uint64_t* s_full = c_empty + 2;
+  uint64_t* s_free = s_full + 2;
+  uint64_t* w_full = s_free + 2;
+  uint64_t* acc_done = w_full + 1;
+  uint64_t* acc_final = acc_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_final + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = Hq / Hk;
+  const int r0 = blockIdx.x * 128;  // first resident row (query for DQ, key otherwise)
+  const int head = blockIdx.y;      // query head (DQ) or kv head
+  const int rlast = min(r0 + 127, T - 1);
+  // the streamed blocks this CTA visits
+  int first, nblk, nit;
+  if (MODE == MODE_DQ) {
+    int kstart = ds[r0];
+    if (window > 0) kstart = max(kstart, r0 - window + 1);
+    first = (kstart / BC) * BC;
+    nblk = (rlast - first) / BC + 1;
+    nit = nblk;
+  } else {
+    int tmax = de[rlast];
+    if (window > 0) tmax = min(tmax, rlast + window - 1);
+    tmax = min(tmax, T - 1);
+    first = (r0 / BC) * BC;
+    nblk = (tmax - first) / BC + 1;
+    nit = G * nblk;
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(r_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&c_full[i], 1);
+      mbar_init(&c_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+    }
+    mbar_init(w_full, 128);
+    mbar_init(acc_done, 1);
+    mbar_init(acc_final, 1);
+    *abort = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tr);
+    if (L::TWO) prefetch_tmap(&tr2);
+    prefetch_tmap(&tc1);
+    prefetch_tmap(&tc2);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, L::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // streamed block of iteration i: (row start, head of the streamed operands)
+  auto blk = [&](int i, int& start, int& shead) {
+    if (MODE == MODE_DQ) {
+      start = first + i * BC;
+      shead = head / G;
+    } else {
+      start = first + (i % nblk) * BC;
+      shead = head * G + i / nblk;
+    }
+  };
+
+  if (warp == 0) {
+    if (lane == 0 && nit > 0) {
+      // ------------------------------------------------------------------ producer
+      const int rhead = MODE == MODE_DQ ? head : head;  // resident operands' head
+      mbar_expect_tx(r_full, (L::TWO ? 2 : 1) * L::R_BYTES);
+      for (int c = 0; c < NC; ++c) {
+        tma_load_3d(sR + c * (128 * 128), &tr, r_full, c * 64, rhead, r0);
+        if (L::TWO) tma_load_3d(sR2 + c * (128 * 128), &tr2, r_full, c * 64, rhead, r0);
+      }
+      int issued = 0;
+      for (int i = 0; i < nit; ++i) {
+        const int st = i & 1;
+        if (i >= 2 && !mbar_wait(&c_empty[st], ((i - 2) >> 1) & 1, status, 41, abort)) break;
+        int start, shead;
+        blk(i, start, shead);
+        mbar_expect_tx(&c_full[st], 2 * L::C_BYTES + L::COL_BYTES);
+        for (int c = 0; c < NC; ++c) {
+          tma_load_3d(stage_c1(st) + c * (BC * 128), &tc1, &c_full[st], c * 64, shead, start);
+          tma_load_3d(stage_c2(st) + c * (BC * 128), &tc2, &c_full[st], c * 64, shead, start);
+        }
+        if (L::COLS) {
+          float* cols = stage_cols(st);
+          bulk_load(cols, lse + (int64_t)shead * Tp + start, BC * 4, &c_full[st]);
+          bulk_load(cols + BC, delta + (int64_t)shead * Tp + start, BC * 4, &c_full[st]);
+          bulk_load(cols + 2 * BC, ds + start, BC * 4, &c_full[st]);
+        }
+        issued = i + 1;
+      }
+      // drain the copies in flight before the CTA may exit
+      mbar_wait(r_full, 0, status, 49, nullptr);
+      for (int i = max(0, issued - 2); i < issued; ++i) mbar_wait(&c_full[i & 1], (i >> 1) & 1, status, 49, nullptr);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && nit > 0) {
+      // ------------------------------------------------------------------ MMA issuer
+      const uint32_t id_s = idesc_bf16(128, BC);
+      const uint32_t id_acc = idesc_bf16(128, D, true);
+      const uint32_t aR = smem_addr(sR), aR2 = smem_addr(sR2), aW = smem_addr(sW);
+      bool ok = mbar_wait(r_full, 0, status, 50, abort);
+      auto issue_acc = [&](int i) {
+        if (!ok) return;
+        if (!mbar_wait(w_full, i & 1, status, 51, abort)) {
+          ok = false;
+          return;
+        }
+        tc_fence_after();
+        const int st = i & 1;
+        const uint32_t aX = smem_addr(MODE == MODE_DV ? stage_c2(st) : stage_c1(st));
+#pragma unroll
+        for (int kk = 0; kk < BC / 16; ++kk)
+          umma_bf16(tmem + L::ACC_COL, desc_sw128(aW + kk * 32), desc_mn_sw128(aX + kk * 16 * 128, BC * 128, 1024),
+                    id_acc, (i > 0 || kk > 0));
+        umma_commit(&c_empty[st]);
+        umma_commit(acc_done);
+      };
+      for (int i = 0; i < nit && ok; ++i) {
+        const int b = i & 1, st = i & 1;
+        if (i >= 2 && !mbar_wait(&s_free[b], ((i - 2) >> 1) & 1, status, 52, abort)) {
+          ok = false;
+          break;
+        }
+        if (!mbar_wait(&c_full[st], (i >> 1) & 1, status, 53, abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t aC1 = smem_addr(stage_c1(st)), aC2 = smem_addr(stage_c2(st));
+        for (int c = 0; c < NC; ++c) {
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            umma_bf16(tmem + L::S_COL + b * BC, desc_sw128(aR + c * (128 * 128) + kk * 32),
+                      desc_sw128(aC1 + c * (BC * 128) + kk * 32), id_s, (c | kk) != 0);
+            if (L::TWO)
+              umma_bf16(tmem + L::DP_COL + b * BC, desc_sw128(aR2 + c * (128 * 128) + kk * 32),
+                        desc_sw128(aC2 + c * (BC * 128) + kk * 32), id_s, (c | kk) != 0);
+          }
+        }
+        umma_commit(&s_full[b]);
+        if (i >= 1) issue_acc(i - 1);
+      }
+      if (ok) issue_acc(nit - 1);
+      if (ok) umma_commit(acc_final);
+    }
+  } else {
+    // ------------------------------------------------------------------ elementwise + epilogue
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const int row = r0 + r;  // this thread's resident row
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    // own-row constants: DQ rows are queries (LSE, delta, document bounds); key rows need none
+    float lse_r = 0.f, delta_r = 0.f;
+    int lo_r = 0;
+    if (MODE == MODE_DQ && row < T) {
+      lse_r = lse[(int64_t)head * Tp + row];
+      delta_r = delta[(int64_t)head * Tp + row];
+      lo_r = ds[row];
+      if (window > 0) lo_r = max(lo_r, row - window + 1);
+    }
+    bool ok = true;
+    for (int i = 0; i < nit && ok; ++i) {
+      const int b = i & 1, st = i & 1;
+      int start, shead;
+      blk(i, start, shead);
+      if (!mbar_wait(&s_full[b], (i >> 1) & 1, status, 60, abort)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[BC], dp[L::TWO ? BC : 1];
+#pragma unroll
+      for (int c = 0; c < BC; c += 32)
+        tmem_ld32(tmem + lane_base + L::S_COL + b * BC + c, *reinterpret_cast<float(*)[32]>(&s[c]));
+      if (L::TWO) {
+#pragma unroll
+        for (int c = 0; c < BC; c += 32)
+          tmem_ld32(tmem + lane_base + L::DP_COL + b * BC + c, *reinterpret_cast<float(*)[32]>(&dp[c]));
+      }
+      tc_fence_before();
+      mbar_arrive(&s_free[b]);
+      const float* cols = nullptr;
+      if (L::COLS) {
+        if (!mbar_wait(&c_full[st], (i >> 1) & 1, status, 61, abort)) {  // already complete: visibility
+          ok = false;
+          break;
+        }
+        cols = stage_cols(st);
+      }
+#pragma unroll
+      for (int c = 0; c < BC; ++c) {
+        float p;
+        if (MODE == MODE_DQ) {
+          const int key = start + c;
+          const bool valid = row < T && key < T && key <= row && key >= lo_r;
+          p = valid ? __expf(s[c] * scale - lse_r) : 0.f;
+          s[c] = p * (dp[c] - delta_r);
+        } else {
+          const int t = start + c;
+          const int dst = __float_as_int(cols[2 * BC + c]);
+          const bool valid = row < T && t < T && t >= row && row >= dst && (window <= 0 || row > t - window);
+          p = valid ? __expf(s[c] * scale - cols[c]) : 0.f;
+          s[c] = MODE == MODE_DK ? p * (dp[L::TWO ? c : 0] - cols[BC + c]) : p;
+        }
+      }
+      if (i >= 1 && !mbar_wait(acc_done, (i - 1) & 1, status, 62, abort)) {
+        ok = false;
+        break;
+      }
+      // row r of W: BC bf16 = BC/8 swizzled 16-byte chunks of a 128-byte row
+#pragma unroll
+      for (int c8 = 0; c8 < BC / 8; ++c8) {
+        BF16x8 pk;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) pk.h[e] = f2bf(s[c8 * 8 + e]);
+        const uint32_t addr = smem_addr(sW) + r * 128 + ((c8 ^ (r & 7)) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk.u.x), "r"(pk.u.y), "r"(pk.u.z),
+                     "r"(pk.u.w)
+                     : "memory");
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(w_full);
+    }
+    const int64_t ld_out = (int64_t)(MODE == MODE_DQ ? Hq : Hk) * D;
+    bf16* dst = out + (int64_t)row * ld_out + (int64_t)head * D;
+    const float f = MODE == MODE_DV ? 1.f : scale;
+    if (nit == 0) {
+      if (row < T)
+        for (int e = 0; e < D; e += 8) *reinterpret_cast<uint4*>(dst + e) = make_uint4(0, 0, 0, 0);
+    } else if (ok && mbar_wait(acc_final, 0, status, 63, abort)) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int cc = 0; cc < D / 32; ++cc) {
+        float v[32];
+        tmem_ld32(tmem + lane_base + L::ACC_COL + cc * 32, v);
+        if (row < T) {
+#pragma unroll
+          for (int j8 = 0; j8 < 4; ++j8) {
+            BF16x8 ov;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ov.h[e] = f2bf(v[j8 * 8 + e] * f);
+            *reinterpret_cast<uint4*>(dst + cc * 32 + j8 * 8) = ov.u;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TMEM_COLS);
+  }
+}
+
+// delta[h * Tp + t] = sum_d dO[t, h, d] * O[t, h, d]  (one warp per (t, h))
+__global__ void attn_delta_kernel(const bf16* __restrict__ o, const bf16* __restrict__ dout, int T, int Hq, int D,
+                                  int Tp, float* __restrict__ delta) {
+  const int lane = threadIdx.x & 31;
+  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (w >= (int64_t)T * Hq) return;
+  const int t = (int)(w / Hq), h = (int)(w % Hq);
+  const bf16* a = o + w * D;
+  const bf16* b = dout + w * D;
+  float acc = 0.f;
+  for (int d = lane * 8; d < D; d += 256) {
+    BF16x8 x, y;
+    x.u = *reinterpret_cast<const uint4*>(a + d);
+    y.u = *reinterpret_cast<const uint4*>(b + d);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc += bf2f(x.h[e]) * bf2f(y.h[e]);
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) delta[(int64_t)h * Tp + t] = acc;
+}
+
+template <int D, int BC, int MODE>
+void launch_bwd_tc(const CUtensorMap& tr, const CUtensorMap& tr2, const CUtensorMap& tc1, const CUtensorMap& tc2,
+                   const float* lse, const float* delta, const int* ds, const int* de, int T, int Tp, int Hq, int Hk,
+                   int window, float scale, bf16* out, int* status, cudaStream_t stream) {
+  using L = BwdLayout<D, BC, MODE>;
+  auto kern = attn_bwd_tc_kernel<D, BC, MODE>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
+  dim3 grid((T + 127) / 128, MODE == MODE_DQ ? Hq : Hk, 1);
+  kern<<<grid, 192, L::BYTES, stream>>>(tr, tr2, tc1, tc2, lse, delta, ds, de, T, Tp, Hq, Hk, window, scale, out,
+                                        status);
+}
+
+template <int D>
+void bwd_tc_all(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const torch::Tensor& dout,
+                const float* lse, const float* delta, const int* ds, const int* de, int T, int Tp, int window,
+                float scale, torch::Tensor& dq, torch::Tensor& dk, torch::Tensor& dv, int* status, cudaStream_t s) {
+  const int Hq = (int)q.size(1), Hk = (int)k.size(1);
+  constexpr int BQ = 32, BV = 64;
+  // dQ: resident Q, dO (128 rows); streamed K, V (BQ rows)
+  launch_bwd_tc<D, BQ, MODE_DQ>(make_tmap_thd(q.data_ptr(), T, Hq, D, 128), make_tmap_thd(dout.data_ptr(), T, Hq, D, 128),
+                                make_tmap_thd(k.data_ptr(), T, Hk, D, BQ), make_tmap_thd(v.data_ptr(), T, Hk, D, BQ),
+                                lse, delta, ds, de, T, Tp, Hq, Hk, window, scale,
+                                reinterpret_cast<bf16*>(dq.data_ptr()), status, s);
+  // dK: resident K, V; streamed Q, dO
+  launch_bwd_tc<D, BQ, MODE_DK>(make_tmap_thd(k.data_ptr(), T, Hk, D, 128), make_tmap_thd(v.data_ptr(), T, Hk, D, 128),
+                                make_tmap_thd(q.data_ptr(), T, Hq, D, BQ), make_tmap_thd(dout.data_ptr(), T, Hq, D, BQ),
+                                lse, delta, ds, de, T, Tp, Hq, Hk, window, scale,
+                                reinterpret_cast<bf16*>(dk.data_ptr()), status, s);
+  // dV: resident K; streamed Q (for S^T) and dO (accumulated)
+  const CUtensorMap tk = make_tmap_thd(k.data_ptr(), T, Hk, D, 128);
+  launch_bwd_tc<D, BV, MODE_DV>(tk, tk, make_tmap_thd(q.data_ptr(), T, Hq, D, BV),
+                                make_tmap_thd(dout.data_ptr(), T, Hq, D, BV), lse, delta, ds, de, T, Tp, Hq, Hk, window,
+                                scale, reinterpret_cast<bf16*>(dv.data_ptr()), status, s);
+}
+
+}  // namespace
+
+// dq, dk, dv of the packed-varlen attention (head_dim 64 / 128 / 256) from the forward's o, lse.
+std::vector<torch::Tensor> attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                       torch::Tensor o, torch::Tensor lse, torch::Tensor doc_start, int64_t window,
+                                       double scale) {
+  TORCH_CHECK(q.is_cuda() && q.is_contiguous() && k.is_contiguous() && v.is_contiguous() && o.is_contiguous(),
+              "attn_bwd_tc: contiguous CUDA tensors");
+  TORCH_CHECK(q.scalar_type() == torch::kBFloat16 && k.scalar_type() == torch::kBFloat16, "attn_bwd_tc: bf16");
+  const at::cuda::CUDAGuard guard(q.device());
+  const int T = (int)q.size(0), Hq = (int)q.size(1), Hk = (int)k.size(1), D = (int)q.size(2);
+  TORCH_CHECK(Hq % Hk == 0 && v.size(1) == Hk && v.size(2) == D, "attn_bwd_tc: GQA shapes");
+  auto dq = torch::empty_like(q), dk = torch::empty_like(k), dv = torch::empty_like(v);
+  if (T == 0) return {dq, dk, dv};
+  auto doc = dout.contiguous();
+  const int Tp = (T + 63) / 64 * 64 + 64;  // padded rows: the bulk copies read whole BC-blocks
+  auto opts_i = doc_start.options().dtype(torch::kInt32);
+  auto ds32 = doc_start.to(torch::kInt32);
+  auto ds = torch::full({Tp}, T, opts_i);
+  ds.slice(0, 0, T).copy_(ds32);
+  // doc_end[t] = last token of t's document (reverse cumulative min of the next starts)
+  auto idx = torch::arange(T, opts_i);
+  auto nxt = torch::where(ds32.eq(idx), idx, torch::full_like(idx, T));
+  auto shifted = torch::cat({nxt.slice(0, 1), torch::full({1}, T, opts_i)});
+  auto de = (std::get<0>(torch::cummin(shifted.flip(0), 0)).flip(0) - 1).to(torch::kInt32).contiguous();
+  auto lse_p = torch::zeros({Hq, Tp}, lse.options());
+  lse_p.slice(1, 0, T).copy_(lse);
+  auto delta = torch::zeros({Hq, Tp}, lse.options());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  {
+    const int64_t warps = (int64_t)T * Hq;
+    attn_delta_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, stream>>>(
+        reinterpret_cast<const bf16*>(o.data_ptr()), reinterpret_cast<const bf16*>(doc.data_ptr()), T, Hq, D, Tp,
+        delta.data_ptr<float>());
+  }
+  int* st = attn_status(q.get_device()).data_ptr<int>();
+  switch (D) {
+    case 64: bwd_tc_all<64>(q, k, v, doc, lse_p.data_ptr<float>(), delta.data_ptr<float>(), ds.data_ptr<int>(), de.data_ptr<int>(), T, Tp, (int)window, (float)scale, dq, dk, dv, st, stream); break;
+    case 128: bwd_tc_all<128>(q, k, v, doc, lse_p.data_ptr<float>(), delta.data_ptr<float>(), ds.data_ptr<int>(), de.data_ptr<int>(), T, Tp, (int)window, (float)scale, dq, dk, dv, st, stream); break;
+    case 256: bwd_tc_all<256>(q, k, v, doc, lse_p.data_ptr<float>(), delta.data_ptr<float>(), ds.data_ptr<int>(), de.data_ptr<int>(), T, Tp, (int)window, (float)scale, dq, dk, dv, st, stream); break;
+    default: TORCH_CHECK(false, "attn_bwd_tc: head_dim must be 64, 128 or 256");
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {dq, dk, dv};
+}

@@ -78,6 +78,13 @@ ME_DEVICE void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
+// Untiled bulk copy global -> shared (no multicast): both addresses 16-byte aligned, bytes % 16 == 0.
+ME_DEVICE void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_addr(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
+}
 // Generic-proxy shared-memory writes (st.shared) -> visible to the tensor cores' async proxy.
 ME_DEVICE void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 ME_DEVICE void prefetch_tmap(const CUtensorMap* map) {

@@ -80,5 +80,8 @@ def attention_fwd_mma(q, k, v, doc_start, window=None, scale=1.0):
 
 
 def attention_bwd(do, q, k, v, o, lse, doc_start, window=None, scale=1.0):
-    """(dq, dk, dv) on the sm_100a kernels."""
+    """(dq, dk, dv) on the sm_100a kernels: the tcgen05/TMEM backward for head_dim <= 256, the
+    warp-level mma.sync backward for head_dim 512 (whose resident tiles exceed shared memory)."""
+    if q.shape[-1] <= 256:
+        return native().attn_bwd_tc(do, q, k, v, o, lse, doc_start, int(window or 0), float(scale))
     return native().attn_bwd(do, q, k, v, o, lse, doc_start, int(window or 0), float(scale))

@@ -96,9 +96,13 @@ def case_attn_bwd(C, dev, it, pk):
         o, lse = C.attn_fwd_tc(q, k, v, ds, W, 1.0)
         do = torch.randn_like(o)
         fl = 2.5 * _attn_flops(ds, W, D, 32)
-        ms = _time(lambda: C.attn_bwd(do, q, k, v, o, lse, ds, W, 1.0), it)
-        out[f"hd{D} bwd"] = {"ms": round(ms, 4), "useful_tflops": round(fl / ms / 1e9, 1),
-                             "frac_of_peak": round(fl / ms / 1e9 / pk["bf16_tflops"], 3)}
+        runs = [("mma.sync", lambda: C.attn_bwd(do, q, k, v, o, lse, ds, W, 1.0))]
+        if D <= 256:
+            runs.append(("tcgen05", lambda: C.attn_bwd_tc(do, q, k, v, o, lse, ds, W, 1.0)))
+        for name, fn in runs:
+            ms = _time(fn, it)
+            out[f"hd{D} bwd {name}"] = {"ms": round(ms, 4), "useful_tflops": round(fl / ms / 1e9, 1),
+                                        "frac_of_peak": round(fl / ms / 1e9 / pk["bf16_tflops"], 3)}
     return out
 
 
