@@ -417,6 +417,7 @@ enum { MODE_DQ = 0, MODE_DK = 1, MODE_DV = 2 };
 
 template <int D, int BC, int MODE>
 struct BwdLayout {
+  static_assert(BC == 32, "W is double-buffered in the two 64-byte halves of 128-byte rows");
   static constexpr bool TWO = MODE != MODE_DV;    // a second product (dP) and resident R2
   static constexpr bool COLS = MODE != MODE_DQ;   // per-column (query) LSE / delta / doc start
   static constexpr int NC = D / 64;
@@ -430,23 +431,25 @@ struct BwdLayout {
   static constexpr int ST_OFF = R2_OFF + (TWO ? R_BYTES : 0);
   static constexpr int W_OFF = ST_OFF + 2 * STAGE_BYTES;
   static constexpr int BAR_OFF = W_OFF + 128 * 128;
-  static constexpr int N_BARS = 1 + 2 + 2 + 2 + 2 + 1 + 1 + 1;
+  static constexpr int N_BARS = 1 + 2 + 2 + 2 + 2 + 2 + 2 + 1;
   static constexpr int BYTES = BAR_OFF + N_BARS * 8 + 16 + 1024;
   static constexpr int S_COL = 0, DP_COL = 2 * BC, ACC_COL = TWO ? 4 * BC : 2 * BC;
   static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr int THREADS = 320;  // warp 0 producer, warp 1 MMA, warps 2-9 elementwise
+  static constexpr int NCOMP = 256;
   static_assert(ACC_COL + D <= 512, "TMEM columns");
   static_assert(BYTES <= 232448, "shared memory");
 };
 
 template <int D, int BC, int MODE>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tr, const __grid_constant__ CUtensorMap tr2,
                        const __grid_constant__ CUtensorMap tc1, const __grid_constant__ CUtensorMap tc2,
                        const float* __restrict__ lse, const float* __restrict__ delta, const int* __restrict__ ds,
                        const int* __restrict__ de, int T, int Tp, int Hq, int Hk, int window, float scale,
                        bf16* __restrict__ out, int* status) {
   using L = BwdLayout<D, BC, MODE>;
-  constexpr int NC = L::NC;
+  constexpr int NC = L::NC, HB = BC / 2;  // each elementwise thread owns half of a row's columns
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sR = smem + L::R_OFF;
@@ -464,8 +467,8 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* s_full = c_empty + 2;
   uint64_t* s_free = s_full + 2;
   uint64_t* w_full = s_free + 2;
-  uint64_t* acc_done = w_full + 1;
-  uint64_t* acc_final = acc_done + 1;
+  uint64_t* acc_done = w_full + 2;
+  uint64_t* acc_final = acc_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_final + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -497,10 +500,10 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&c_full[i], 1);
       mbar_init(&c_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 128);
+      mbar_init(&s_free[i], L::NCOMP);
+      mbar_init(&w_full[i], L::NCOMP);
+      mbar_init(&acc_done[i], 1);
     }
-    mbar_init(w_full, 128);
-    mbar_init(acc_done, 1);
     mbar_init(acc_final, 1);
     *abort = 0;
     fence_barrier_init();
@@ -529,11 +532,10 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) {
     if (lane == 0 && nit > 0) {
       // ------------------------------------------------------------------ producer
-      const int rhead = MODE == MODE_DQ ? head : head;  // resident operands' head
       mbar_expect_tx(r_full, (L::TWO ? 2 : 1) * L::R_BYTES);
       for (int c = 0; c < NC; ++c) {
-        tma_load_3d(sR + c * (128 * 128), &tr, r_full, c * 64, rhead, r0);
-        if (L::TWO) tma_load_3d(sR2 + c * (128 * 128), &tr2, r_full, c * 64, rhead, r0);
+        tma_load_3d(sR + c * (128 * 128), &tr, r_full, c * 64, head, r0);
+        if (L::TWO) tma_load_3d(sR2 + c * (128 * 128), &tr2, r_full, c * 64, head, r0);
       }
       int issued = 0;
       for (int i = 0; i < nit; ++i) {
@@ -567,7 +569,8 @@ __global__ void __launch_bounds__(192, 1)
       bool ok = mbar_wait(r_full, 0, status, 50, abort);
       auto issue_acc = [&](int i) {
         if (!ok) return;
-        if (!mbar_wait(w_full, i & 1, status, 51, abort)) {
+        const int wb = i & 1;
+        if (!mbar_wait(&w_full[wb], (i >> 1) & 1, status, 51, abort)) {
           ok = false;
           return;
         }
@@ -576,10 +579,10 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t aX = smem_addr(MODE == MODE_DV ? stage_c2(st) : stage_c1(st));
 #pragma unroll
         for (int kk = 0; kk < BC / 16; ++kk)
-          umma_bf16(tmem + L::ACC_COL, desc_sw128(aW + kk * 32), desc_mn_sw128(aX + kk * 16 * 128, BC * 128, 1024),
-                    id_acc, (i > 0 || kk > 0));
+          umma_bf16(tmem + L::ACC_COL, desc_sw128(aW + wb * 64 + kk * 32),
+                    desc_mn_sw128(aX + kk * 16 * 128, BC * 128, 1024), id_acc, (i > 0 || kk > 0));
         umma_commit(&c_empty[st]);
-        umma_commit(acc_done);
+        umma_commit(&acc_done[wb]);
       };
       for (int i = 0; i < nit && ok; ++i) {
         const int b = i & 1, st = i & 1;
@@ -611,11 +614,11 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ------------------------------------------------------------------ elementwise + epilogue
-    const int q = warp & 3;
+    // warps 2-9: TMEM lane quarter (warp & 3), column half (warp - 2) / 4 of each BC block
+    const int q = warp & 3, half = (warp - 2) >> 2;
     const int r = q * 32 + lane;
     const int row = r0 + r;  // this thread's resident row
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    // own-row constants: DQ rows are queries (LSE, delta, document bounds); key rows need none
     float lse_r = 0.f, delta_r = 0.f;
     int lo_r = 0;
     if (MODE == MODE_DQ && row < T) {
@@ -629,20 +632,15 @@ __global__ void __launch_bounds__(192, 1)
       const int b = i & 1, st = i & 1;
       int start, shead;
       blk(i, start, shead);
+      start += half * HB;
       if (!mbar_wait(&s_full[b], (i >> 1) & 1, status, 60, abort)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float s[BC], dp[L::TWO ? BC : 1];
-#pragma unroll
-      for (int c = 0; c < BC; c += 32)
-        tmem_ld32(tmem + lane_base + L::S_COL + b * BC + c, *reinterpret_cast<float(*)[32]>(&s[c]));
-      if (L::TWO) {
-#pragma unroll
-        for (int c = 0; c < BC; c += 32)
-          tmem_ld32(tmem + lane_base + L::DP_COL + b * BC + c, *reinterpret_cast<float(*)[32]>(&dp[c]));
-      }
+      float s[HB], dp[L::TWO ? HB : 1];
+      tmem_ld16(tmem + lane_base + L::S_COL + b * BC + half * HB, s);
+      if (L::TWO) tmem_ld16(tmem + lane_base + L::DP_COL + b * BC + half * HB, *reinterpret_cast<float(*)[16]>(dp));
       tc_fence_before();
       mbar_arrive(&s_free[b]);
       const float* cols = nullptr;
@@ -651,10 +649,10 @@ __global__ void __launch_bounds__(192, 1)
           ok = false;
           break;
         }
-        cols = stage_cols(st);
+        cols = stage_cols(st) + half * HB;
       }
 #pragma unroll
-      for (int c = 0; c < BC; ++c) {
+      for (int c = 0; c < HB; ++c) {
         float p;
         if (MODE == MODE_DQ) {
           const int key = start + c;
@@ -669,37 +667,38 @@ __global__ void __launch_bounds__(192, 1)
           s[c] = MODE == MODE_DK ? p * (dp[L::TWO ? c : 0] - cols[BC + c]) : p;
         }
       }
-      if (i >= 1 && !mbar_wait(acc_done, (i - 1) & 1, status, 62, abort)) {
+      // W buffer b (64-byte half b of each 128-byte row) is free once ACC(i - 2) is done
+      if (i >= 2 && !mbar_wait(&acc_done[b], ((i - 2) >> 1) & 1, status, 62, abort)) {
         ok = false;
         break;
       }
-      // row r of W: BC bf16 = BC/8 swizzled 16-byte chunks of a 128-byte row
 #pragma unroll
-      for (int c8 = 0; c8 < BC / 8; ++c8) {
+      for (int c8 = 0; c8 < HB / 8; ++c8) {
         BF16x8 pk;
 #pragma unroll
         for (int e = 0; e < 8; ++e) pk.h[e] = f2bf(s[c8 * 8 + e]);
-        const uint32_t addr = smem_addr(sW) + r * 128 + ((c8 ^ (r & 7)) << 4);
+        const int chunk = b * 4 + half * (HB / 8) + c8;
+        const uint32_t addr = smem_addr(sW) + r * 128 + ((chunk ^ (r & 7)) << 4);
         asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk.u.x), "r"(pk.u.y), "r"(pk.u.z),
                      "r"(pk.u.w)
                      : "memory");
       }
       fence_async_smem();
       tc_fence_before();
-      mbar_arrive(w_full);
+      mbar_arrive(&w_full[b]);
     }
     const int64_t ld_out = (int64_t)(MODE == MODE_DQ ? Hq : Hk) * D;
-    bf16* dst = out + (int64_t)row * ld_out + (int64_t)head * D;
+    bf16* dst = out + (int64_t)row * ld_out + (int64_t)head * D + half * (D / 2);
     const float f = MODE == MODE_DV ? 1.f : scale;
     if (nit == 0) {
       if (row < T)
-        for (int e = 0; e < D; e += 8) *reinterpret_cast<uint4*>(dst + e) = make_uint4(0, 0, 0, 0);
+        for (int e = 0; e < D / 2; e += 8) *reinterpret_cast<uint4*>(dst + e) = make_uint4(0, 0, 0, 0);
     } else if (ok && mbar_wait(acc_final, 0, status, 63, abort)) {
       tc_fence_after();
 #pragma unroll 1
-      for (int cc = 0; cc < D / 32; ++cc) {
+      for (int cc = 0; cc < D / 64; ++cc) {
         float v[32];
-        tmem_ld32(tmem + lane_base + L::ACC_COL + cc * 32, v);
+        tmem_ld32(tmem + lane_base + L::ACC_COL + half * (D / 2) + cc * 32, v);
         if (row < T) {
 #pragma unroll
           for (int j8 = 0; j8 < 4; ++j8) {
@@ -749,8 +748,8 @@ void launch_bwd_tc(const CUtensorMap& tr, const CUtensorMap& tr2, const CUtensor
   auto kern = attn_bwd_tc_kernel<D, BC, MODE>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
   dim3 grid((T + 127) / 128, MODE == MODE_DQ ? Hq : Hk, 1);
-  kern<<<grid, 192, L::BYTES, stream>>>(tr, tr2, tc1, tc2, lse, delta, ds, de, T, Tp, Hq, Hk, window, scale, out,
-                                        status);
+  kern<<<grid, L::THREADS, L::BYTES, stream>>>(tr, tr2, tc1, tc2, lse, delta, ds, de, T, Tp, Hq, Hk, window, scale,
+                                               out, status);
 }
 
 template <int D>
@@ -758,7 +757,7 @@ void bwd_tc_all(const torch::Tensor& q, const torch::Tensor& k, const torch::Ten
                 const float* lse, const float* delta, const int* ds, const int* de, int T, int Tp, int window,
                 float scale, torch::Tensor& dq, torch::Tensor& dk, torch::Tensor& dv, int* status, cudaStream_t s) {
   const int Hq = (int)q.size(1), Hk = (int)k.size(1);
-  constexpr int BQ = 32, BV = 64;
+  constexpr int BQ = 32, BV = 32;
   // dQ: resident Q, dO (128 rows); streamed K, V (BQ rows)
   launch_bwd_tc<D, BQ, MODE_DQ>(make_tmap_thd(q.data_ptr(), T, Hq, D, 128), make_tmap_thd(dout.data_ptr(), T, Hq, D, 128),
                                 make_tmap_thd(k.data_ptr(), T, Hk, D, BQ), make_tmap_thd(v.data_ptr(), T, Hk, D, BQ),
