@@ -48,6 +48,7 @@ struct AttnLayout {
   static constexpr int BYTES = BAR_OFF + N_BARS * 8 + 16 + 1024;
   static constexpr uint32_t TMEM_COLS = (128 + DV) <= 256 ? 256 : 512;
   static constexpr int O_COL = 128;
+  static_assert(BYTES <= 232448, "shared memory");
 };
 
 ME_DEVICE float warp_any_f(bool p) { return __any_sync(0xffffffffu, p) ? 1.f : 0.f; }
@@ -386,9 +387,9 @@ std::vector<torch::Tensor> attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::
   auto stream = at::cuda::getCurrentCUDAStream();
   int* st = attn_status(q.get_device()).data_ptr<int>();
   switch (D) {
-    case 64: launch_fwd_tc<64, 64, 8, 2>(q, k, v, ds.data_ptr<int>(), (int)window, (float)scale, o, lse, st, stream); break;
-    case 128: launch_fwd_tc<128, 128, 8, 2>(q, k, v, ds.data_ptr<int>(), (int)window, (float)scale, o, lse, st, stream); break;
-    case 256: launch_fwd_tc<256, 256, 8, 2>(q, k, v, ds.data_ptr<int>(), (int)window, (float)scale, o, lse, st, stream); break;
+    case 64: launch_fwd_tc<64, 64, 8, 4>(q, k, v, ds.data_ptr<int>(), (int)window, (float)scale, o, lse, st, stream); break;
+    case 128: launch_fwd_tc<128, 128, 8, 4>(q, k, v, ds.data_ptr<int>(), (int)window, (float)scale, o, lse, st, stream); break;
+    case 256: launch_fwd_tc<256, 256, 6, 3>(q, k, v, ds.data_ptr<int>(), (int)window, (float)scale, o, lse, st, stream); break;
     case 512: launch_fwd_tc<512, 256, 4, 1>(q, k, v, ds.data_ptr<int>(), (int)window, (float)scale, o, lse, st, stream); break;
     default: TORCH_CHECK(false, "attn_fwd_tc: head_dim must be 64, 128, 256 or 512");
   }
@@ -415,28 +416,35 @@ namespace {
 
 enum { MODE_DQ = 0, MODE_DK = 1, MODE_DV = 2 };
 
+// Streamed tiles live in two rings. Ring A holds the tile that is still needed by the
+// accumulating MMA at the end of an iteration (DQ: K_j, DK: Q_j, DV: dO_j) plus the per-query
+// columns the elementwise warps read; it is released only when that MMA completes, so it gets
+// SA stages. Ring B holds the tile that only the S or dP product reads (DQ: V_j, DK: dO_j,
+// DV: Q_j) and is released as soon as those MMAs complete.
 template <int D, int BC, int MODE>
 struct BwdLayout {
   static_assert(BC == 32, "W is double-buffered in the two 64-byte halves of 128-byte rows");
   static constexpr bool TWO = MODE != MODE_DV;    // a second product (dP) and resident R2
   static constexpr bool COLS = MODE != MODE_DQ;   // per-column (query) LSE / delta / doc start
   static constexpr int NC = D / 64;
+  static constexpr int SA = MODE == MODE_DV ? 4 : 3, SB = 2;
   static constexpr int R_BYTES = 128 * D * 2;
   static constexpr int C_BYTES = BC * D * 2;      // one streamed tile (D/64 chunks of BC x 128 B)
-  static constexpr int COL_BYTES = COLS ? 3 * BC * 4 : 0;
-  // stage starts stay 1024-byte aligned: the 128-byte-swizzle atoms of TMA and UMMA need it
-  static constexpr int STAGE_BYTES = (2 * C_BYTES + COL_BYTES + 1023) / 1024 * 1024;
+  static constexpr int COL_FLOATS = 3 * BC;
   static constexpr int R_OFF = 0;
   static constexpr int R2_OFF = R_OFF + R_BYTES;
-  static constexpr int ST_OFF = R2_OFF + (TWO ? R_BYTES : 0);
-  static constexpr int W_OFF = ST_OFF + 2 * STAGE_BYTES;
-  static constexpr int BAR_OFF = W_OFF + 128 * 128;
-  static constexpr int N_BARS = 1 + 2 + 2 + 2 + 2 + 2 + 2 + 1;
+  static constexpr int A_OFF = R2_OFF + (TWO ? R_BYTES : 0);
+  static constexpr int B_OFF = A_OFF + SA * C_BYTES;
+  static constexpr int W_OFF = B_OFF + SB * C_BYTES;
+  static constexpr int COL_OFF = W_OFF + 128 * 128;
+  static constexpr int BAR_OFF = COL_OFF + (COLS ? SA * COL_FLOATS * 4 : 0);
+  static constexpr int N_BARS = 1 + 2 * SA + 2 * SB + 2 + 2 + 2 + 2 + 1;
   static constexpr int BYTES = BAR_OFF + N_BARS * 8 + 16 + 1024;
   static constexpr int S_COL = 0, DP_COL = 2 * BC, ACC_COL = TWO ? 4 * BC : 2 * BC;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr int THREADS = 320;  // warp 0 producer, warp 1 MMA, warps 2-9 elementwise
   static constexpr int NCOMP = 256;
+  static_assert(C_BYTES % 1024 == 0, "tiles keep the 1024-byte alignment of the swizzle atoms");
   static_assert(ACC_COL + D <= 512, "TMEM columns");
   static_assert(BYTES <= 232448, "shared memory");
 };
@@ -444,27 +452,27 @@ struct BwdLayout {
 template <int D, int BC, int MODE>
 __global__ void __launch_bounds__(320, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tr, const __grid_constant__ CUtensorMap tr2,
-                       const __grid_constant__ CUtensorMap tc1, const __grid_constant__ CUtensorMap tc2,
+                       const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                        const float* __restrict__ lse, const float* __restrict__ delta, const int* __restrict__ ds,
                        const int* __restrict__ de, int T, int Tp, int Hq, int Hk, int window, float scale,
                        bf16* __restrict__ out, int* status) {
   using L = BwdLayout<D, BC, MODE>;
-  constexpr int NC = L::NC, HB = BC / 2;  // each elementwise thread owns half of a row's columns
+  constexpr int NC = L::NC, HB = BC / 2, SA = L::SA, SB = L::SB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sR = smem + L::R_OFF;
   uint8_t* sR2 = smem + L::R2_OFF;
   uint8_t* sW = smem + L::W_OFF;
-  auto stage_c1 = [&](int st) { return smem + L::ST_OFF + st * L::STAGE_BYTES; };
-  auto stage_c2 = [&](int st) { return smem + L::ST_OFF + st * L::STAGE_BYTES + L::C_BYTES; };
-  auto stage_cols = [&](int st) {
-    return reinterpret_cast<float*>(smem + L::ST_OFF + st * L::STAGE_BYTES + 2 * L::C_BYTES);
-  };
+  auto tile_a = [&](int st) { return smem + L::A_OFF + st * L::C_BYTES; };
+  auto tile_b = [&](int st) { return smem + L::B_OFF + st * L::C_BYTES; };
+  auto cols_of = [&](int st) { return reinterpret_cast<float*>(smem + L::COL_OFF) + st * L::COL_FLOATS; };
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
   uint64_t* r_full = bars;
-  uint64_t* c_full = r_full + 1;
-  uint64_t* c_empty = c_full + 2;
-  uint64_t* s_full = c_empty + 2;
+  uint64_t* a_full = r_full + 1;
+  uint64_t* a_empty = a_full + SA;
+  uint64_t* b_full = a_empty + SA;
+  uint64_t* b_empty = b_full + SB;
+  uint64_t* s_full = b_empty + SB;
   uint64_t* s_free = s_full + 2;
   uint64_t* w_full = s_free + 2;
   uint64_t* acc_done = w_full + 2;
@@ -477,7 +485,6 @@ __global__ void __launch_bounds__(320, 1)
   const int r0 = blockIdx.x * 128;  // first resident row (query for DQ, key otherwise)
   const int head = blockIdx.y;      // query head (DQ) or kv head
   const int rlast = min(r0 + 127, T - 1);
-  // the streamed blocks this CTA visits
   int first, nblk, nit;
   if (MODE == MODE_DQ) {
     int kstart = ds[r0];
@@ -496,9 +503,15 @@ __global__ void __launch_bounds__(320, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(r_full, 1);
+    for (int i = 0; i < SA; ++i) {
+      mbar_init(&a_full[i], 1);
+      mbar_init(&a_empty[i], 1);
+    }
+    for (int i = 0; i < SB; ++i) {
+      mbar_init(&b_full[i], 1);
+      mbar_init(&b_empty[i], 1);
+    }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&c_full[i], 1);
-      mbar_init(&c_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], L::NCOMP);
       mbar_init(&w_full[i], L::NCOMP);
@@ -509,8 +522,8 @@ __global__ void __launch_bounds__(320, 1)
     fence_barrier_init();
     prefetch_tmap(&tr);
     if (L::TWO) prefetch_tmap(&tr2);
-    prefetch_tmap(&tc1);
-    prefetch_tmap(&tc2);
+    prefetch_tmap(&ta);
+    prefetch_tmap(&tb);
   }
   if (warp == 1) tmem_alloc(tmem_slot, L::TMEM_COLS);
   tc_fence_before();
@@ -539,26 +552,31 @@ __global__ void __launch_bounds__(320, 1)
       }
       int issued = 0;
       for (int i = 0; i < nit; ++i) {
-        const int st = i & 1;
-        if (i >= 2 && !mbar_wait(&c_empty[st], ((i - 2) >> 1) & 1, status, 41, abort)) break;
+        const int sa = i % SA, sb = i % SB;
         int start, shead;
         blk(i, start, shead);
-        mbar_expect_tx(&c_full[st], 2 * L::C_BYTES + L::COL_BYTES);
-        for (int c = 0; c < NC; ++c) {
-          tma_load_3d(stage_c1(st) + c * (BC * 128), &tc1, &c_full[st], c * 64, shead, start);
-          tma_load_3d(stage_c2(st) + c * (BC * 128), &tc2, &c_full[st], c * 64, shead, start);
-        }
+        if (i >= SA && !mbar_wait(&a_empty[sa], ((i / SA) - 1) & 1, status, 41, abort)) break;
+        mbar_expect_tx(&a_full[sa], L::C_BYTES + (L::COLS ? L::COL_FLOATS * 4 : 0));
+        for (int c = 0; c < NC; ++c) tma_load_3d(tile_a(sa) + c * (BC * 128), &ta, &a_full[sa], c * 64, shead, start);
         if (L::COLS) {
-          float* cols = stage_cols(st);
-          bulk_load(cols, lse + (int64_t)shead * Tp + start, BC * 4, &c_full[st]);
-          bulk_load(cols + BC, delta + (int64_t)shead * Tp + start, BC * 4, &c_full[st]);
-          bulk_load(cols + 2 * BC, ds + start, BC * 4, &c_full[st]);
+          float* cols = cols_of(sa);
+          bulk_load(cols, lse + (int64_t)shead * Tp + start, BC * 4, &a_full[sa]);
+          bulk_load(cols + BC, delta + (int64_t)shead * Tp + start, BC * 4, &a_full[sa]);
+          bulk_load(cols + 2 * BC, ds + start, BC * 4, &a_full[sa]);
         }
+        if (i >= SB && !mbar_wait(&b_empty[sb], ((i / SB) - 1) & 1, status, 42, abort)) {
+          issued = -(i + 1);  // A of iteration i is in flight, B is not
+          break;
+        }
+        mbar_expect_tx(&b_full[sb], L::C_BYTES);
+        for (int c = 0; c < NC; ++c) tma_load_3d(tile_b(sb) + c * (BC * 128), &tb, &b_full[sb], c * 64, shead, start);
         issued = i + 1;
       }
       // drain the copies in flight before the CTA may exit
+      const int na = issued < 0 ? -issued : issued, nb = issued < 0 ? -issued - 1 : issued;
       mbar_wait(r_full, 0, status, 49, nullptr);
-      for (int i = max(0, issued - 2); i < issued; ++i) mbar_wait(&c_full[i & 1], (i >> 1) & 1, status, 49, nullptr);
+      for (int i = max(0, na - SA); i < na; ++i) mbar_wait(&a_full[i % SA], (i / SA) & 1, status, 49, nullptr);
+      for (int i = max(0, nb - SB); i < nb; ++i) mbar_wait(&b_full[i % SB], (i / SB) & 1, status, 49, nullptr);
     }
   } else if (warp == 1) {
     if (lane == 0 && nit > 0) {
@@ -575,38 +593,40 @@ __global__ void __launch_bounds__(320, 1)
           return;
         }
         tc_fence_after();
-        const int st = i & 1;
-        const uint32_t aX = smem_addr(MODE == MODE_DV ? stage_c2(st) : stage_c1(st));
+        const uint32_t aX = smem_addr(tile_a(i % SA));
 #pragma unroll
         for (int kk = 0; kk < BC / 16; ++kk)
           umma_bf16(tmem + L::ACC_COL, desc_sw128(aW + wb * 64 + kk * 32),
                     desc_mn_sw128(aX + kk * 16 * 128, BC * 128, 1024), id_acc, (i > 0 || kk > 0));
-        umma_commit(&c_empty[st]);
+        umma_commit(&a_empty[i % SA]);
         umma_commit(&acc_done[wb]);
       };
       for (int i = 0; i < nit && ok; ++i) {
-        const int b = i & 1, st = i & 1;
+        const int b = i & 1, sa = i % SA, sb = i % SB;
         if (i >= 2 && !mbar_wait(&s_free[b], ((i - 2) >> 1) & 1, status, 52, abort)) {
           ok = false;
           break;
         }
-        if (!mbar_wait(&c_full[st], (i >> 1) & 1, status, 53, abort)) {
+        if (!mbar_wait(&a_full[sa], (i / SA) & 1, status, 53, abort) ||
+            !mbar_wait(&b_full[sb], (i / SB) & 1, status, 54, abort)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t aC1 = smem_addr(stage_c1(st)), aC2 = smem_addr(stage_c2(st));
+        // S's streamed operand: Q_j / K_j in ring A (DQ, DK) or Q_j in ring B (DV); dP's is ring B
+        const uint32_t aS = smem_addr(MODE == MODE_DV ? tile_b(sb) : tile_a(sa)), aP = smem_addr(tile_b(sb));
         for (int c = 0; c < NC; ++c) {
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             umma_bf16(tmem + L::S_COL + b * BC, desc_sw128(aR + c * (128 * 128) + kk * 32),
-                      desc_sw128(aC1 + c * (BC * 128) + kk * 32), id_s, (c | kk) != 0);
+                      desc_sw128(aS + c * (BC * 128) + kk * 32), id_s, (c | kk) != 0);
             if (L::TWO)
               umma_bf16(tmem + L::DP_COL + b * BC, desc_sw128(aR2 + c * (128 * 128) + kk * 32),
-                        desc_sw128(aC2 + c * (BC * 128) + kk * 32), id_s, (c | kk) != 0);
+                        desc_sw128(aP + c * (BC * 128) + kk * 32), id_s, (c | kk) != 0);
           }
         }
         umma_commit(&s_full[b]);
+        umma_commit(&b_empty[sb]);
         if (i >= 1) issue_acc(i - 1);
       }
       if (ok) issue_acc(nit - 1);
@@ -629,7 +649,7 @@ __global__ void __launch_bounds__(320, 1)
     }
     bool ok = true;
     for (int i = 0; i < nit && ok; ++i) {
-      const int b = i & 1, st = i & 1;
+      const int b = i & 1, sa = i % SA;
       int start, shead;
       blk(i, start, shead);
       start += half * HB;
@@ -645,11 +665,11 @@ __global__ void __launch_bounds__(320, 1)
       mbar_arrive(&s_free[b]);
       const float* cols = nullptr;
       if (L::COLS) {
-        if (!mbar_wait(&c_full[st], (i >> 1) & 1, status, 61, abort)) {  // already complete: visibility
+        if (!mbar_wait(&a_full[sa], (i / SA) & 1, status, 61, abort)) {  // already complete: visibility
           ok = false;
           break;
         }
-        cols = stage_cols(st) + half * HB;
+        cols = cols_of(sa) + half * HB;
       }
 #pragma unroll
       for (int c = 0; c < HB; ++c) {
@@ -757,22 +777,20 @@ void bwd_tc_all(const torch::Tensor& q, const torch::Tensor& k, const torch::Ten
                 const float* lse, const float* delta, const int* ds, const int* de, int T, int Tp, int window,
                 float scale, torch::Tensor& dq, torch::Tensor& dk, torch::Tensor& dv, int* status, cudaStream_t s) {
   const int Hq = (int)q.size(1), Hk = (int)k.size(1);
-  constexpr int BQ = 32, BV = 32;
-  // dQ: resident Q, dO (128 rows); streamed K, V (BQ rows)
-  launch_bwd_tc<D, BQ, MODE_DQ>(make_tmap_thd(q.data_ptr(), T, Hq, D, 128), make_tmap_thd(dout.data_ptr(), T, Hq, D, 128),
-                                make_tmap_thd(k.data_ptr(), T, Hk, D, BQ), make_tmap_thd(v.data_ptr(), T, Hk, D, BQ),
-                                lse, delta, ds, de, T, Tp, Hq, Hk, window, scale,
+  constexpr int BC = 32;
+  const CUtensorMap q128 = make_tmap_thd(q.data_ptr(), T, Hq, D, 128), o128 = make_tmap_thd(dout.data_ptr(), T, Hq, D, 128);
+  const CUtensorMap k128 = make_tmap_thd(k.data_ptr(), T, Hk, D, 128), v128 = make_tmap_thd(v.data_ptr(), T, Hk, D, 128);
+  const CUtensorMap qc = make_tmap_thd(q.data_ptr(), T, Hq, D, BC), oc = make_tmap_thd(dout.data_ptr(), T, Hq, D, BC);
+  const CUtensorMap kc = make_tmap_thd(k.data_ptr(), T, Hk, D, BC), vc = make_tmap_thd(v.data_ptr(), T, Hk, D, BC);
+  // dQ: resident Q, dO; ring A = K_j (S and the accumulation), ring B = V_j (dP)
+  launch_bwd_tc<D, BC, MODE_DQ>(q128, o128, kc, vc, lse, delta, ds, de, T, Tp, Hq, Hk, window, scale,
                                 reinterpret_cast<bf16*>(dq.data_ptr()), status, s);
-  // dK: resident K, V; streamed Q, dO
-  launch_bwd_tc<D, BQ, MODE_DK>(make_tmap_thd(k.data_ptr(), T, Hk, D, 128), make_tmap_thd(v.data_ptr(), T, Hk, D, 128),
-                                make_tmap_thd(q.data_ptr(), T, Hq, D, BQ), make_tmap_thd(dout.data_ptr(), T, Hq, D, BQ),
-                                lse, delta, ds, de, T, Tp, Hq, Hk, window, scale,
+  // dK: resident K, V; ring A = Q_j (S and the accumulation), ring B = dO_j (dP)
+  launch_bwd_tc<D, BC, MODE_DK>(k128, v128, qc, oc, lse, delta, ds, de, T, Tp, Hq, Hk, window, scale,
                                 reinterpret_cast<bf16*>(dk.data_ptr()), status, s);
-  // dV: resident K; streamed Q (for S^T) and dO (accumulated)
-  const CUtensorMap tk = make_tmap_thd(k.data_ptr(), T, Hk, D, 128);
-  launch_bwd_tc<D, BV, MODE_DV>(tk, tk, make_tmap_thd(q.data_ptr(), T, Hq, D, BV),
-                                make_tmap_thd(dout.data_ptr(), T, Hq, D, BV), lse, delta, ds, de, T, Tp, Hq, Hk, window,
-                                scale, reinterpret_cast<bf16*>(dv.data_ptr()), status, s);
+  // dV: resident K; ring A = dO_j (the accumulation), ring B = Q_j (S)
+  launch_bwd_tc<D, BC, MODE_DV>(k128, k128, oc, qc, lse, delta, ds, de, T, Tp, Hq, Hk, window, scale,
+                                reinterpret_cast<bf16*>(dv.data_ptr()), status, s);
 }
 
 }  // namespace
