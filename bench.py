@@ -86,6 +86,7 @@ def bench_config(tmp, steps):
         "learning_rate": 5e-3, "micro_engram_dense_lr": 1e-3, "max_grad_norm": 2.0, "warmup_steps": 0,
         "gradient_checkpointing": True, "activation_offloading": True, "micro_engram_stats_steps": 0,
         "gradient_checkpointing_policy": os.environ.get("ME_BENCH_AC", "auto"),
+        "gradient_checkpointing_reserve_gib": float(os.environ.get("ME_BENCH_AC_RESERVE", "23")),
         "seed": 42,
     }
 
@@ -253,6 +254,7 @@ def run_ours(args):
                                                    " and o-proj kept on the GPU, norms/RoPE/MLP recomputed; none ="
                                                    " nothing recomputed)",
                        "activation_checkpointing_plan": getattr(trainer, "ckpt_plan", None),
+                       "peak_hbm_reserved_gib": round(torch.cuda.max_memory_reserved() / 2 ** 30, 1),
                        "activation_offloading": "layer inputs to pinned host memory, prefetched in the backward",
                        "l2": "inputs larger than L2 (61 GB base streamed per step), no flush"},
             "clocks": clk,
@@ -318,7 +320,7 @@ def run_reference(args):
 
     tmp = tempfile.mkdtemp(prefix="me_ref_")
     c = bench_config(tmp, args.warmup + 2 * args.steps + 2)
-    for k in ("base_init", "gradient_checkpointing_policy"):  # keys the reference does not have
+    for k in ("base_init", "gradient_checkpointing_policy", "gradient_checkpointing_reserve_gib"):  # not reference keys
         c.pop(k)
     # the reference's recommended B200-runnable kernel settings (README example config)
     # (fused_attn_kernel off: that patch's shared-KV side channel is None under the installed

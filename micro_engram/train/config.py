@@ -17,6 +17,10 @@ Keys this framework adds (all optional, defaults keep the reference's behaviour)
   gradient_checkpointing_policy
                        "full" (default: keep each layer's input) or "selective" (also keep
                        the attention half of each layer on the GPU; recompute only the MLP)
+                       or "auto" (HBM-budgeted mix of no recompute and selective)
+  gradient_checkpointing_reserve_gib
+                       HBM the auto plan leaves free for the backward's working set, the loss
+                       chunks and the allocator (plus 4% of the GPU's memory)
 """
 import logging
 import os
@@ -134,6 +138,7 @@ class TrainConfig(MicroEngramArgs):
     # q/k/v projection, attention output + LSE and o-proj output on the GPU, recompute the rest
     # auto: selective where it fits in HBM, plus no recompute at all for as many layers as still fit
     gradient_checkpointing_policy: Literal["full", "selective", "auto"] = "full"
+    gradient_checkpointing_reserve_gib: float = 23.0
     activation_offloading: bool = False
     no_grad_prefix: bool = True
     sharded_vocab: bool = True

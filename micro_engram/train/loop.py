@@ -194,7 +194,8 @@ class Trainer:
         torch.cuda.synchronize(self.device)
         free, total = torch.cuda.mem_get_info(self.device)
         cached = torch.cuda.memory_reserved(self.device) - torch.cuda.memory_allocated(self.device)
-        budget = torch.tensor([float(free + cached - (16 << 30) - 0.08 * total)], device=self.device)
+        reserve = float(self.cfg.gradient_checkpointing_reserve_gib) * 2 ** 30 + 0.04 * total
+        budget = torch.tensor([float(free + cached - reserve)], device=self.device)
         if self.world > 1:
             dist.all_reduce(budget, op=dist.ReduceOp.MIN)
         tokens = self.cfg.micro_batch_size * self.cfg.sequence_len
