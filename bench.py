@@ -23,6 +23,7 @@ on the host, copies them from pinned memory and reads the loss back.
 import argparse
 import json
 import os
+import re
 import subprocess
 import sys
 import tempfile
@@ -147,20 +148,27 @@ def count_launches(trainer, micro):
     import torch
     from torch.profiler import ProfilerActivity, profile
 
-    ours = ("hash_kernel", "gather_kernel", "scatter_grad_kernel", "touched_sqnorm_kernel", "clip_coef_kernel",
-            "adam_touched_kernel", "adam_dense_kernel", "gate_fwd_kernel", "gate_bwd_kernel", "rmsnorm_fwd_kernel",
+    ours = ("hash_kernel", "hash_prev_kernel", "gather_kernel", "scatter_grad_kernel", "touched_sqnorm_kernel",
+            "clip_coef_kernel", "adam_touched_kernel", "adam_dense_kernel", "gate_fwd_kernel", "gate_bwd_kernel",
+            "gate_fwd_vec_kernel", "gate_bwd_vec_kernel", "fill_ids_kernel", "rmsnorm_fwd_kernel",
             "rmsnorm_bwd_kernel", "post_norm_add_kernel", "post_norm_add_bwd_kernel", "qkv_norm_rope_kernel",
             "qkv_norm_rope_bwd_kernel", "geglu_fwd_kernel", "geglu_bwd_kernel", "ce_fwd_kernel", "ce_bwd_kernel",
-            "attn_fwd_kernel", "attn_bwd_pre_kernel", "attn_bwd_dkdv_kernel", "attn_bwd_dq_kernel",
-            "me_gemm", "allreduce_p2p")
+            "attn_fwd_kernel", "attn_fwd_tc_kernel", "attn_bwd_pre_kernel", "attn_bwd_dkdv_kernel",
+            "attn_bwd_dq_kernel", "attn_bwd_tc_kernel", "attn_delta_kernel", "doc_end_from_start_kernel",
+            "gemm_tc_kernel", "nf4_dequant_kernel", "nf4_quantize_kernel")
+    pat = re.compile(r"\b(" + "|".join(ours) + r")\b")
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         trainer.train_step(micro)
         torch.cuda.synchronize()
+    dump = os.environ.get("ME_BENCH_KERNEL_TABLE")
+    if dump:  # per-kernel device time of this one (untimed) step, for finding the next target
+        with open(dump, "w") as f:
+            f.write(prof.key_averages().table(sort_by="device_time_total", row_limit=60, max_name_column_width=90))
     n_ours, n_all = 0, 0
     for ev in prof.events():
         if ev.device_type == torch.autograd.DeviceType.CUDA:
             n_all += 1
-            if any(k in ev.name for k in ours):
+            if pat.search(ev.name):
                 n_ours += 1
     return n_ours, n_all
 

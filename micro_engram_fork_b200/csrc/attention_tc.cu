@@ -793,6 +793,30 @@ void bwd_tc_all(const torch::Tensor& q, const torch::Tensor& k, const torch::Ten
                                 reinterpret_cast<bf16*>(dv.data_ptr()), status, s);
 }
 
+// Per-call inputs of both backward paths: document starts padded to Tp rows (value T), the
+// forward's LSE and delta = rowsum(dO * O), both [Hq, Tp] fp32 (the bulk copies read whole blocks).
+struct BwdPrep {
+  torch::Tensor ds, lse, delta;
+  int Tp;
+};
+
+BwdPrep bwd_prep(const torch::Tensor& o, const torch::Tensor& doc, const torch::Tensor& lse,
+                 const torch::Tensor& doc_start, int T, int Hq, int D) {
+  BwdPrep p;
+  p.Tp = (T + 63) / 64 * 64 + 64;
+  auto opts_i = doc_start.options().dtype(torch::kInt32);
+  p.ds = torch::full({p.Tp}, T, opts_i);
+  p.ds.slice(0, 0, T).copy_(doc_start.to(torch::kInt32));
+  p.lse = torch::zeros({Hq, p.Tp}, lse.options());
+  p.lse.slice(1, 0, T).copy_(lse);
+  p.delta = torch::zeros({Hq, p.Tp}, lse.options());
+  const int64_t warps = (int64_t)T * Hq;
+  attn_delta_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const bf16*>(o.data_ptr()), reinterpret_cast<const bf16*>(doc.data_ptr()), T, Hq, D, p.Tp,
+      p.delta.data_ptr<float>());
+  return p;
+}
+
 }  // namespace
 
 // dq, dk, dv of the packed-varlen attention (head_dim 64 / 128 / 256) from the forward's o, lse.
@@ -808,32 +832,524 @@ std::vector<torch::Tensor> attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torc
   auto dq = torch::empty_like(q), dk = torch::empty_like(k), dv = torch::empty_like(v);
   if (T == 0) return {dq, dk, dv};
   auto doc = dout.contiguous();
-  const int Tp = (T + 63) / 64 * 64 + 64;  // padded rows: the bulk copies read whole BC-blocks
+  BwdPrep prep = bwd_prep(o, doc, lse, doc_start, T, Hq, D);
+  const int Tp = prep.Tp;
   auto opts_i = doc_start.options().dtype(torch::kInt32);
   auto ds32 = doc_start.to(torch::kInt32);
-  auto ds = torch::full({Tp}, T, opts_i);
-  ds.slice(0, 0, T).copy_(ds32);
   // doc_end[t] = last token of t's document (reverse cumulative min of the next starts)
   auto idx = torch::arange(T, opts_i);
   auto nxt = torch::where(ds32.eq(idx), idx, torch::full_like(idx, T));
   auto shifted = torch::cat({nxt.slice(0, 1), torch::full({1}, T, opts_i)});
   auto de = (std::get<0>(torch::cummin(shifted.flip(0), 0)).flip(0) - 1).to(torch::kInt32).contiguous();
-  auto lse_p = torch::zeros({Hq, Tp}, lse.options());
-  lse_p.slice(1, 0, T).copy_(lse);
-  auto delta = torch::zeros({Hq, Tp}, lse.options());
+  auto ds = prep.ds, lse_p = prep.lse, delta = prep.delta;
   auto stream = at::cuda::getCurrentCUDAStream();
-  {
-    const int64_t warps = (int64_t)T * Hq;
-    attn_delta_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, stream>>>(
-        reinterpret_cast<const bf16*>(o.data_ptr()), reinterpret_cast<const bf16*>(doc.data_ptr()), T, Hq, D, Tp,
-        delta.data_ptr<float>());
-  }
   int* st = attn_status(q.get_device()).data_ptr<int>();
   switch (D) {
     case 64: bwd_tc_all<64>(q, k, v, doc, lse_p.data_ptr<float>(), delta.data_ptr<float>(), ds.data_ptr<int>(), de.data_ptr<int>(), T, Tp, (int)window, (float)scale, dq, dk, dv, st, stream); break;
     case 128: bwd_tc_all<128>(q, k, v, doc, lse_p.data_ptr<float>(), delta.data_ptr<float>(), ds.data_ptr<int>(), de.data_ptr<int>(), T, Tp, (int)window, (float)scale, dq, dk, dv, st, stream); break;
     case 256: bwd_tc_all<256>(q, k, v, doc, lse_p.data_ptr<float>(), delta.data_ptr<float>(), ds.data_ptr<int>(), de.data_ptr<int>(), T, Tp, (int)window, (float)scale, dq, dk, dv, st, stream); break;
     default: TORCH_CHECK(false, "attn_bwd_tc: head_dim must be 64, 128 or 256");
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {dq, dk, dv};
+}
+
+// =============================================================================== backward, tiles in HBM
+// Backward for wide heads (head_dim 512: a 128x512 fp32 accumulator fills all of TMEM, and a
+// resident 128-row Q + dO pair no longer fits shared memory, so the fused kernels above cannot
+// hold it). The 128x128 tiles of P and dS are materialised in HBM as bf16 and the three
+// gradients become block-sparse GEMMs without any recomputation:
+//   1. attn_bwd_sdp_kernel  one CTA per (query block i, head): for each key block j the
+//      document / window allows, S = Q_i K_j^T and dP = dO_i V_j^T (TMEM, double-buffered,
+//      K = head_dim streamed in 64-column chunks), then P = exp(scale S - LSE) and
+//      dS = P (dP - delta) are written as bf16 tiles in the UMMA K-major 128-byte-swizzled
+//      layout (two 128 x 64 chunks per tile), so the next kernel copies them verbatim.
+//   2. attn_bwd_acc_kernel  one CTA per (output block, head, 256-column half) of
+//      dV = sum P^T dO, dK = scale sum dS^T Q (A operand M-major from the same tiles, summed
+//      over the GQA group and every query block that sees the key block) and
+//      dQ = scale sum dS K (A K-major); 64-row K slices through a 4-stage TMA / bulk-copy ring.
+// Tiles of one head are indexed by off[i] + (j - jlo[i]) (attn_tiles_kernel). Heads are
+// processed in passes of whole GQA groups so the tile buffers stay within a byte budget.
+// FLOPs: 5 products per tile (the minimum), against 8 in the fused kernels' three passes.
+namespace {
+
+constexpr int MT = 128;               // tile rows (queries) = tile columns (keys)
+constexpr int TILE_BYTES = MT * MT * 2;  // one bf16 tile: two 128-row x 64-column chunks
+
+// jlo[i]: first key block of query block i; off[i]: index of tile (i, jlo[i]) among one head's
+// tiles (exclusive prefix sum of i - jlo[i] + 1), off[nb] = tiles per head; ihi[j]: last query
+// block that sees key block j. One block of 1024 threads.
+__global__ void attn_tiles_kernel(const int* __restrict__ ds, int nb, int window, int* __restrict__ jlo,
+                                  int* __restrict__ off, int* __restrict__ ihi) {
+  __shared__ int wsum[32];
+  __shared__ int carry;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (int base = 0; base < nb; base += blockDim.x) {
+    const int i = base + threadIdx.x;
+    int cnt = 0;
+    if (i < nb) {
+      int ks = ds[i * MT];
+      if (window > 0) ks = max(ks, i * MT - window + 1);
+      jlo[i] = ks / MT;
+      cnt = i - ks / MT + 1;
+    }
+    int x = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      int w = lane < nw ? wsum[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      wsum[lane] = w;
+    }
+    __syncthreads();
+    const int excl = carry + (warp > 0 ? wsum[warp - 1] : 0) + x - cnt;
+    if (i < nb) off[i] = excl;
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = excl + cnt;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) off[nb] = carry;
+  __syncthreads();
+  for (int j = threadIdx.x; j < nb; j += blockDim.x) {  // jlo is non-decreasing and jlo[i] <= i
+    int lo = j, hi = nb - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (jlo[mid] <= j) lo = mid;
+      else hi = mid - 1;
+    }
+    ihi[j] = lo;
+  }
+}
+
+template <int D>
+struct SdpLayout {
+  static constexpr int NC = D / 64, NS = 3;
+  static constexpr int CH = MT * 128;  // one 128-row x 64-column chunk (16 KB)
+  static constexpr int STAGE = 4 * CH;  // Q_i, dO_i, K_j, V_j chunks
+  static constexpr int BAR_OFF = NS * STAGE;
+  static constexpr int N_BARS = 2 * NS + 2 + 2;
+  static constexpr int BYTES = BAR_OFF + N_BARS * 8 + 16 + 1024;
+  static constexpr int THREADS = 320, NEPI = 256;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+  static_assert(BYTES <= 232448, "shared memory");
+};
+
+template <int D>
+__global__ void __launch_bounds__(320, 1)
+    attn_bwd_sdp_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap to,
+                        const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                        const float* __restrict__ lse, const float* __restrict__ delta, const int* __restrict__ ds,
+                        const int* __restrict__ jlo_a, const int* __restrict__ off_a, int T, int Tp, int nb, int G,
+                        int h0, int64_t ntmax, int window, float scale, uint8_t* __restrict__ pbuf,
+                        uint8_t* __restrict__ dsbuf, int* status) {
+  using L = SdpLayout<D>;
+  constexpr int NC = L::NC, NS = L::NS;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* full = bars;
+  uint64_t* empty = full + NS;
+  uint64_t* s_full = empty + NS;
+  uint64_t* s_free = s_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_free + 2);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i = blockIdx.x, hl = blockIdx.y, h = h0 + hl, g = h / G;
+  const int jlo = jlo_a[i];
+  int ntile = i - jlo + 1;
+  const int64_t tbase = (int64_t)hl * ntmax + off_a[i];
+  if (off_a[nb] > ntmax) {  // the host's bound on tiles per head does not hold: write nothing
+    if (threadIdx.x == 0) report(status, ME_ERR_BOUNDS, 70);
+    ntile = 0;
+  }
+  const int nit = ntile * NC;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_free[b], L::NEPI);
+    }
+    *abort = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tq);
+    prefetch_tmap(&to);
+    prefetch_tmap(&tk);
+    prefetch_tmap(&tv);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0 && nit > 0) {
+      // ------------------------------------------------------------------ producer
+      int issued = 0;
+      for (int it = 0; it < nit; ++it) {
+        const int s = it % NS, c = it % NC, j = jlo + it / NC;
+        if (it >= NS && !mbar_wait(&empty[s], ((it / NS) - 1) & 1, status, 71, abort)) break;
+        uint8_t* st = smem + s * L::STAGE;
+        mbar_expect_tx(&full[s], L::STAGE);
+        tma_load_3d(st, &tq, &full[s], c * 64, h, i * MT);
+        tma_load_3d(st + L::CH, &to, &full[s], c * 64, h, i * MT);
+        tma_load_3d(st + 2 * L::CH, &tk, &full[s], c * 64, g, j * MT);
+        tma_load_3d(st + 3 * L::CH, &tv, &full[s], c * 64, g, j * MT);
+        issued = it + 1;
+      }
+      for (int it = max(0, issued - NS); it < issued; ++it)  // drain copies in flight
+        mbar_wait(&full[it % NS], (it / NS) & 1, status, 79, nullptr);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && nit > 0) {
+      // ------------------------------------------------------------------ MMA issuer
+      const uint32_t id = idesc_bf16(128, 128);
+      bool ok = true;
+      for (int it = 0; it < nit && ok; ++it) {
+        const int s = it % NS, c = it % NC, tt = it / NC, b = tt & 1;
+        if (c == 0 && tt >= 2 && !mbar_wait(&s_free[b], ((tt - 2) >> 1) & 1, status, 72, abort)) {
+          ok = false;
+          break;
+        }
+        if (!mbar_wait(&full[s], (it / NS) & 1, status, 73, abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a = smem_addr(smem + s * L::STAGE);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          umma_bf16(tmem + b * 256, desc_sw128(a + kk * 32), desc_sw128(a + 2 * L::CH + kk * 32), id, (c | kk) != 0);
+          umma_bf16(tmem + b * 256 + 128, desc_sw128(a + L::CH + kk * 32), desc_sw128(a + 3 * L::CH + kk * 32), id,
+                    (c | kk) != 0);
+        }
+        umma_commit(&empty[s]);
+        if (c == NC - 1) umma_commit(&s_full[b]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ P / dS epilogue
+    // warps 2-9: TMEM lane quarter (warp & 3), key half (warp - 2) / 4 = stored chunk
+    const int qq = warp & 3, half = (warp - 2) >> 2;
+    const int r = qq * 32 + lane, row = i * MT + r;
+    const uint32_t lane_base = (uint32_t)(qq * 32) << 16;
+    float lse_r = 0.f, delta_r = 0.f;
+    int lo_r = 0;
+    if (row < T) {
+      lse_r = lse[(int64_t)h * Tp + row];
+      delta_r = delta[(int64_t)h * Tp + row];
+      lo_r = ds[row];
+      if (window > 0) lo_r = max(lo_r, row - window + 1);
+    }
+    for (int tt = 0; tt < ntile; ++tt) {
+      const int b = tt & 1, j = jlo + tt;
+      if (!mbar_wait(&s_full[b], (tt >> 1) & 1, status, 74, abort)) break;
+      tc_fence_after();
+      const int64_t tile = tbase + tt;
+      uint8_t* prow = pbuf + tile * TILE_BYTES + half * (TILE_BYTES / 2) + r * 128;
+      uint8_t* drow = dsbuf + tile * TILE_BYTES + half * (TILE_BYTES / 2) + r * 128;
+#pragma unroll
+      for (int sub = 0; sub < 2; ++sub) {
+        float sv[32], dp[32];
+        tmem_ld32(tmem + lane_base + b * 256 + half * 64 + sub * 32, sv);
+        tmem_ld32(tmem + lane_base + b * 256 + 128 + half * 64 + sub * 32, dp);
+#pragma unroll
+        for (int u4 = 0; u4 < 4; ++u4) {
+          BF16x8 pk, dk;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int cidx = u4 * 8 + e;
+            const int key = j * MT + half * 64 + sub * 32 + cidx;
+            const bool valid = row < T && key <= row && key >= lo_r;
+            const float p = valid ? __expf(sv[cidx] * scale - lse_r) : 0.f;
+            pk.h[e] = f2bf(p);
+            dk.h[e] = f2bf(p * (dp[cidx] - delta_r));
+          }
+          const int u = sub * 4 + u4;
+          const int pos = (u ^ (r & 7)) << 4;
+          *reinterpret_cast<uint4*>(prow + pos) = pk.u;
+          *reinterpret_cast<uint4*>(drow + pos) = dk.u;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&s_free[b]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int D>
+struct AccLayout {
+  static constexpr int DN = D < 256 ? D : 256, NH = D / DN, NS = 4;
+  static constexpr int A_BYTES = 128 * 128;  // 128 M x 64 K (K-major) or 64 K x 128 M (two 8 KB pieces)
+  static constexpr int B_BYTES = 64 * DN * 2;  // 64 K rows x DN columns: DN / 64 boxes of 8 KB
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int BAR_OFF = NS * STAGE;
+  static constexpr int N_BARS = 2 * NS + 1;
+  static constexpr int BYTES = BAR_OFF + N_BARS * 8 + 16 + 1024;
+  static constexpr uint32_t TMEM_COLS = DN;
+  static constexpr int THREADS = 192;  // warp 0 loads, warp 1 MMA, warps 2-5 epilogue
+  static_assert(STAGE % 1024 == 0, "stages keep the 1024-byte alignment of the swizzle atoms");
+  static_assert(BYTES <= 232448, "shared memory");
+};
+
+// Job list of one pass: first the dV / dK blocks (kvh kv heads x key blocks x {dV, dK} x NH
+// column halves; the longest jobs), then the dQ blocks (kvh * G query heads x query blocks x NH).
+template <int D>
+__global__ void __launch_bounds__(192, 1)
+    attn_bwd_acc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap to,
+                        const __grid_constant__ CUtensorMap tk, const int* __restrict__ jlo_a,
+                        const int* __restrict__ off_a, const int* __restrict__ ihi_a, int T, int nb, int Hq, int Hk,
+                        int G, int g0, int kvh, int64_t ntmax, float scale, const uint8_t* __restrict__ pbuf,
+                        const uint8_t* __restrict__ dsbuf, bf16* __restrict__ dq, bf16* __restrict__ dk,
+                        bf16* __restrict__ dv, int* status) {
+  using L = AccLayout<D>;
+  constexpr int NS = L::NS, DN = L::DN, NH = L::NH;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* full = bars;
+  uint64_t* empty = full + NS;
+  uint64_t* acc_final = empty + NS;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_final + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // ---- job
+  int64_t x = blockIdx.x;
+  const int64_t J1 = (int64_t)nb * kvh * 2 * NH;
+  int kind, half, blk, hsel;  // kind 0 dV, 1 dK, 2 dQ; hsel: kv head (dV/dK) or query head (dQ) in the pass
+  if (x < J1) {
+    half = (int)(x % NH);
+    x /= NH;
+    kind = (int)(x % 2);
+    x /= 2;
+    hsel = (int)(x % kvh);
+    blk = (int)(x / kvh);
+  } else {
+    x -= J1;
+    half = (int)(x % NH);
+    x /= NH;
+    hsel = (int)(x % (kvh * G));
+    blk = (int)(x / (kvh * G));
+    kind = 2;
+  }
+  const int n_i = kind == 2 ? 0 : ihi_a[blk] - blk + 1;        // query blocks per head (dV / dK)
+  const int jlo_b = kind == 2 ? jlo_a[blk] : 0;
+  int ntile = kind == 2 ? blk - jlo_b + 1 : G * n_i;
+  if (off_a[nb] > ntmax) {  // every tile index is below off[nb]; past the buffer: zeros out
+    if (threadIdx.x == 0) report(status, ME_ERR_BOUNDS, 80);
+    ntile = 0;
+  }
+  const int nit = 2 * ntile;  // two 64-row K slices per tile
+  const uint8_t* abuf = kind == 0 ? pbuf : dsbuf;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_final, 1);
+    *abort = 0;
+    fence_barrier_init();
+    prefetch_tmap(kind == 0 ? &to : kind == 1 ? &tq : &tk);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, L::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------------ loads
+      int issued = 0;
+      for (int it = 0; it < nit; ++it) {
+        const int s = it % NS, sl = it & 1, t = it >> 1;
+        int64_t tile;
+        int brow, bhead;
+        const CUtensorMap* bm;
+        if (kind == 2) {  // dQ: tile (i = blk, j = jlo + t) of query head hsel; B = K_j rows
+          const int j = jlo_b + t;
+          tile = (int64_t)hsel * ntmax + off_a[blk] + t;
+          brow = j * MT + sl * 64;
+          bhead = g0 + hsel / G;
+          bm = &tk;
+        } else {  // dV / dK: tile (i, j = blk) of query head hl of the group; B = dO_i / Q_i rows
+          const int hl = t / n_i, i = blk + t % n_i;
+          const int qh = hsel * G + hl;
+          tile = (int64_t)qh * ntmax + off_a[i] + (blk - jlo_a[i]);
+          brow = i * MT + sl * 64;
+          bhead = g0 * G + qh;
+          bm = kind == 0 ? &to : &tq;
+        }
+        if (it >= NS && !mbar_wait(&empty[s], ((it / NS) - 1) & 1, status, 81, abort)) break;
+        uint8_t* st = smem + s * L::STAGE;
+        mbar_expect_tx(&full[s], L::STAGE);
+        const uint8_t* src = abuf + tile * TILE_BYTES;
+        if (kind == 2) {
+          bulk_load(st, src + sl * (TILE_BYTES / 2), TILE_BYTES / 2, &full[s]);
+        } else {
+          bulk_load(st, src + sl * (TILE_BYTES / 4), TILE_BYTES / 4, &full[s]);
+          bulk_load(st + TILE_BYTES / 4, src + TILE_BYTES / 2 + sl * (TILE_BYTES / 4), TILE_BYTES / 4, &full[s]);
+        }
+#pragma unroll
+        for (int cb = 0; cb < DN / 64; ++cb)
+          tma_load_3d(st + L::A_BYTES + cb * 8192, bm, &full[s], half * DN + cb * 64, bhead, brow);
+        issued = it + 1;
+      }
+      for (int it = max(0, issued - NS); it < issued; ++it)
+        mbar_wait(&full[it % NS], (it / NS) & 1, status, 89, nullptr);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && nit > 0) {
+      // ------------------------------------------------------------------ MMA issuer
+      const uint32_t id = idesc_bf16(128, DN, true, kind != 2);
+      bool ok = true;
+      for (int it = 0; it < nit; ++it) {
+        const int s = it % NS;
+        if (!mbar_wait(&full[s], (it / NS) & 1, status, 82, abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a = smem_addr(smem + s * L::STAGE), bq = a + L::A_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t ad = kind == 2 ? desc_sw128(a + kk * 32) : desc_mn_sw128(a + kk * 2048, 8192, 1024);
+          umma_bf16(tmem, ad, desc_mn_sw128(bq + kk * 2048, 8192, 1024), id, (it | kk) != 0);
+        }
+        umma_commit(&empty[s]);
+      }
+      if (ok) umma_commit(acc_final);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue: one row per thread
+    const int qq = warp & 3;
+    const int r = qq * 32 + lane, row = blk * MT + r;
+    const uint32_t lane_base = (uint32_t)(qq * 32) << 16;
+    bf16* dst;
+    if (kind == 2) dst = dq + (int64_t)row * Hq * D + (int64_t)(g0 * G + hsel) * D + half * DN;
+    else dst = (kind == 0 ? dv : dk) + (int64_t)row * Hk * D + (int64_t)(g0 + hsel) * D + half * DN;
+    const float f = kind == 0 ? 1.f : scale;
+    if (nit == 0) {
+      if (row < T)
+        for (int e = 0; e < DN; e += 8) *reinterpret_cast<uint4*>(dst + e) = make_uint4(0, 0, 0, 0);
+    } else if (mbar_wait(acc_final, 0, status, 83, abort)) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int cc = 0; cc < DN / 32; ++cc) {
+        float v[32];
+        tmem_ld32(tmem + lane_base + cc * 32, v);
+        if (row < T) {
+#pragma unroll
+          for (int j8 = 0; j8 < 4; ++j8) {
+            BF16x8 ov;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ov.h[e] = f2bf(v[j8 * 8 + e] * f);
+            *reinterpret_cast<uint4*>(dst + cc * 32 + j8 * 8) = ov.u;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TMEM_COLS);
+  }
+}
+
+template <int D>
+void bwd_mat_all(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const torch::Tensor& dout,
+                 const float* lse, const float* delta, const int* ds, int T, int Tp, int window, float scale,
+                 int64_t budget, torch::Tensor& dq, torch::Tensor& dk, torch::Tensor& dv, int* status,
+                 cudaStream_t stream) {
+  const int Hq = (int)q.size(1), Hk = (int)k.size(1), G = Hq / Hk;
+  const int nb = (T + MT - 1) / MT;
+  auto opts_i = q.options().dtype(torch::kInt32);
+  auto meta = torch::empty({3 * nb + 1}, opts_i);
+  int* jlo = meta.data_ptr<int>();
+  int* off = jlo + nb;  // nb + 1 entries
+  int* ihi = off + nb + 1;
+  attn_tiles_kernel<<<1, 1024, 0, stream>>>(ds, nb, window, jlo, off, ihi);
+  // tiles per head, bounded on the host: every query block sees at most (window + 127) / 128 + 1
+  // key blocks (all of 0..i without a window)
+  const int64_t per_i = window > 0 ? std::min<int64_t>(nb, (window + MT - 1) / MT + 1) : nb;
+  const int64_t ntmax = window > 0 ? nb * per_i : (int64_t)nb * (nb + 1) / 2;
+  const int64_t group_bytes = (int64_t)G * ntmax * TILE_BYTES * 2;
+  const int kvh = (int)std::max<int64_t>(1, std::min<int64_t>(Hk, budget / std::max<int64_t>(group_bytes, 1)));
+  auto buf = torch::empty({(int64_t)kvh * G * ntmax * TILE_BYTES * 2}, q.options().dtype(torch::kUInt8));
+  uint8_t* pbuf = buf.data_ptr<uint8_t>();
+  uint8_t* dsbuf = pbuf + (int64_t)kvh * G * ntmax * TILE_BYTES;
+  const CUtensorMap q128 = make_tmap_thd(q.data_ptr(), T, Hq, D, 128), o128 = make_tmap_thd(dout.data_ptr(), T, Hq, D, 128);
+  const CUtensorMap k128 = make_tmap_thd(k.data_ptr(), T, Hk, D, 128), v128 = make_tmap_thd(v.data_ptr(), T, Hk, D, 128);
+  const CUtensorMap q64 = make_tmap_thd(q.data_ptr(), T, Hq, D, 64), o64 = make_tmap_thd(dout.data_ptr(), T, Hq, D, 64);
+  const CUtensorMap k64 = make_tmap_thd(k.data_ptr(), T, Hk, D, 64);
+  using LS = SdpLayout<D>;
+  using LA = AccLayout<D>;
+  auto ks = attn_bwd_sdp_kernel<D>;
+  auto ka = attn_bwd_acc_kernel<D>;
+  cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, LS::BYTES);
+  cudaFuncSetAttribute(ka, cudaFuncAttributeMaxDynamicSharedMemorySize, LA::BYTES);
+  bf16* pdq = reinterpret_cast<bf16*>(dq.data_ptr());
+  bf16* pdk = reinterpret_cast<bf16*>(dk.data_ptr());
+  bf16* pdv = reinterpret_cast<bf16*>(dv.data_ptr());
+  for (int g0 = 0; g0 < Hk; g0 += kvh) {
+    const int n = std::min(kvh, Hk - g0);
+    ks<<<dim3(nb, n * G), LS::THREADS, LS::BYTES, stream>>>(q128, o128, k128, v128, lse, delta, ds, jlo, off, T, Tp,
+                                                             nb, G, g0 * G, ntmax, window, scale, pbuf, dsbuf, status);
+    const int64_t jobs = (int64_t)nb * n * 2 * LA::NH + (int64_t)nb * n * G * LA::NH;
+    ka<<<(unsigned)jobs, LA::THREADS, LA::BYTES, stream>>>(q64, o64, k64, jlo, off, ihi, T, nb, Hq, Hk, G, g0, n,
+                                                           ntmax, scale, pbuf, dsbuf, pdq, pdk, pdv, status);
+  }
+}
+
+}  // namespace
+
+// dq, dk, dv of the packed-varlen attention (head_dim 256 / 512) through P / dS tiles in HBM;
+// `tile_budget_bytes` bounds the tile buffers (whole GQA groups per pass, at least one).
+std::vector<torch::Tensor> attn_bwd_mat(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                        torch::Tensor o, torch::Tensor lse, torch::Tensor doc_start, int64_t window,
+                                        double scale, int64_t tile_budget_bytes) {
+  TORCH_CHECK(q.is_cuda() && q.is_contiguous() && k.is_contiguous() && v.is_contiguous() && o.is_contiguous(),
+              "attn_bwd_mat: contiguous CUDA tensors");
+  TORCH_CHECK(q.scalar_type() == torch::kBFloat16 && k.scalar_type() == torch::kBFloat16 &&
+                  v.scalar_type() == torch::kBFloat16, "attn_bwd_mat: bf16");
+  const at::cuda::CUDAGuard guard(q.device());
+  const int T = (int)q.size(0), Hq = (int)q.size(1), Hk = (int)k.size(1), D = (int)q.size(2);
+  TORCH_CHECK(Hq % Hk == 0 && v.size(1) == Hk && v.size(2) == D, "attn_bwd_mat: GQA shapes");
+  auto dq = torch::empty_like(q), dk = torch::empty_like(k), dv = torch::empty_like(v);
+  if (T == 0) return {dq, dk, dv};
+  auto doc = dout.contiguous();
+  BwdPrep prep = bwd_prep(o, doc, lse, doc_start, T, Hq, D);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  int* st = attn_status(q.get_device()).data_ptr<int>();
+  switch (D) {
+    case 256: bwd_mat_all<256>(q, k, v, doc, prep.lse.data_ptr<float>(), prep.delta.data_ptr<float>(), prep.ds.data_ptr<int>(), T, prep.Tp, (int)window, (float)scale, tile_budget_bytes, dq, dk, dv, st, stream); break;
+    case 512: bwd_mat_all<512>(q, k, v, doc, prep.lse.data_ptr<float>(), prep.delta.data_ptr<float>(), prep.ds.data_ptr<int>(), T, prep.Tp, (int)window, (float)scale, tile_budget_bytes, dq, dk, dv, st, stream); break;
+    default: TORCH_CHECK(false, "attn_bwd_mat: head_dim must be 256 or 512");
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {dq, dk, dv};

@@ -67,6 +67,9 @@ torch::Tensor attn_tc_status(int64_t device);
 std::vector<torch::Tensor> attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                        torch::Tensor o, torch::Tensor lse, torch::Tensor doc_start, int64_t window,
                                        double scale);
+std::vector<torch::Tensor> attn_bwd_mat(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                        torch::Tensor o, torch::Tensor lse, torch::Tensor doc_start, int64_t window,
+                                        double scale, int64_t tile_budget_bytes);
 // gemm.cu
 torch::Tensor gemm_tc(torch::Tensor A, torch::Tensor B, int64_t block_n);
 torch::Tensor gemm_status(int64_t device);
@@ -110,6 +113,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd_tc", &attn_fwd_tc);
   m.def("attn_tc_status", &attn_tc_status);
   m.def("attn_bwd_tc", &attn_bwd_tc);
+  m.def("attn_bwd_mat", &attn_bwd_mat);
   m.def("gemm_tc", &gemm_tc, py::arg("A"), py::arg("B"), py::arg("block_n") = 256);
   m.def("gemm_status", &gemm_status);
   m.def("nf4_quantize", &nf4_quantize);

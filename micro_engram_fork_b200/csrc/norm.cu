@@ -283,90 +283,149 @@ __global__ void post_norm_add_bwd_kernel(const bf16* __restrict__ dxo, const bf1
 
 // ---------------------------------------------------------------------------- q/k/v norm + RoPE
 // qkv [N, (Hq + 2*Hk) * D] (the fused projection's output: q heads, then k heads, then v
-// heads). One warp per (token, head). Each lane owns VH elements of each half of the head
-// (RoPE pairs element j with j + D/2). q/k: bf16(rms(x)*w) then the HF bf16 rotary formula
-// bf16(bf16(x*cos) + bf16(rot(x)*sin)) with cos/sin = bf16(cos/sin(pos * inv_freq)); v:
-// bf16(rms(x)) with no weight.
+// heads). A block takes QKV_TOK tokens at a time: it first fills a shared table of the
+// tokens' rotary cos/sin (one sincos per (token, frequency), shared by every q/k head of the
+// token), then one warp per (token, head) row. Each lane owns VH consecutive elements of each
+// half of the head (RoPE pairs element j with j + D/2), loaded and stored as one vector.
+// q/k: bf16(rms(x)*w) then the HF bf16 rotary formula bf16(bf16(x*cos) + bf16(rot(x)*sin))
+// with cos/sin = bf16(cos/sin(pos * inv_freq)); v: bf16(rms(x)) with no weight.
+constexpr int QKV_TOK = 4;
+
 template <int VH>
-__global__ void qkv_norm_rope_kernel(const bf16* __restrict__ qkv, const float* __restrict__ qw,
-                                     const float* __restrict__ kw, const float* __restrict__ inv_freq,
-                                     const int64_t* __restrict__ pos, int64_t N, int Hq, int Hk, int kv_shared,
-                                     float eps, bf16* __restrict__ q, bf16* __restrict__ k, bf16* __restrict__ v,
-                                     float* __restrict__ rstd) {
+ME_DEVICE void ld_bf(const bf16* __restrict__ p, float (&o)[VH]) {
+  if constexpr (VH == 8) {
+    BF16x8 t;
+    t.u = *reinterpret_cast<const uint4*>(p);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = bf2f(t.h[e]);
+  } else if constexpr (VH == 4) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&u.x);
+    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&u.y);
+    o[0] = __low2float(a), o[1] = __high2float(a), o[2] = __low2float(b), o[3] = __high2float(b);
+  } else if constexpr (VH == 2) {
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(p);
+    o[0] = __low2float(a), o[1] = __high2float(a);
+  } else {
+    o[0] = bf2f(p[0]);
+  }
+}
+
+template <int VH>
+ME_DEVICE void st_bf(bf16* __restrict__ p, const float (&o)[VH]) {
+  if constexpr (VH == 8) {
+    BF16x8 t;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) t.h[e] = f2bf(o[e]);
+    *reinterpret_cast<uint4*>(p) = t.u;
+  } else if constexpr (VH == 4) {
+    const __nv_bfloat162 a = __floats2bfloat162_rn(o[0], o[1]), b = __floats2bfloat162_rn(o[2], o[3]);
+    uint2 u;
+    u.x = *reinterpret_cast<const uint32_t*>(&a);
+    u.y = *reinterpret_cast<const uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(p) = u;
+  } else if constexpr (VH == 2) {
+    *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(o[0], o[1]);
+  } else {
+    p[0] = f2bf(o[0]);
+  }
+}
+
+// tab[t * HALF + e * 32 + lane] = (bf16(cos), bf16(sin)) of pos[n0 + t] * inv_freq[lane * VH + e]:
+// the order in which a warp reads it, so each read of the table is 32 consecutive float2.
+template <int VH>
+ME_DEVICE void rope_table(float2* __restrict__ tab, const float* __restrict__ inv_freq,
+                          const int64_t* __restrict__ pos, int64_t n0, int64_t N) {
+  constexpr int HALF = VH * 32;
+  for (int i = threadIdx.x; i < QKV_TOK * HALF; i += blockDim.x) {
+    const int t = i / HALF, j = i % HALF;
+    float sn = 0.f, cs = 1.f;
+    if (n0 + t < N) sincosf((float)pos[n0 + t] * inv_freq[j], &sn, &cs);
+    tab[t * HALF + (j % VH) * 32 + j / VH] = make_float2(bf2f(f2bf(cs)), bf2f(f2bf(sn)));
+  }
+}
+
+template <int VH>
+__global__ void __launch_bounds__(256) qkv_norm_rope_kernel(
+    const bf16* __restrict__ qkv, const float* __restrict__ qw, const float* __restrict__ kw,
+    const float* __restrict__ inv_freq, const int64_t* __restrict__ pos, int64_t N, int Hq, int Hk, int kv_shared,
+    float eps, bf16* __restrict__ q, bf16* __restrict__ k, bf16* __restrict__ v, float* __restrict__ rstd) {
   constexpr int D = VH * 64, HALF = D / 2;
-  const int lane = threadIdx.x & 31;
-  const int H = Hq + 2 * Hk;                     // output heads (q, k, v)
-  const int HI = kv_shared ? Hq + Hk : H;        // input heads per row (v = raw k when shared)
-  const int64_t total = N * H;
-  for (int64_t wrow = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); wrow < total;
-       wrow += (int64_t)gridDim.x * (blockDim.x >> 5)) {
-    const int64_t n = wrow / H;
-    const int hd = (int)(wrow % H);
-    const int src_hd = (kv_shared && hd >= Hq + Hk) ? hd - Hk : hd;
-    const bf16* src = qkv + n * (int64_t)HI * D + (int64_t)src_hd * D;
-    float lo[VH], hi[VH];
-    const int base = lane * VH;
+  __shared__ float2 tab[QKV_TOK * HALF];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int H = Hq + 2 * Hk;               // output heads (q, k, v)
+  const int HI = kv_shared ? Hq + Hk : H;  // input heads per row (v = raw k when shared)
+  const int base = lane * VH;
+  const int64_t nblk = (N + QKV_TOK - 1) / QKV_TOK;
+  for (int64_t blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+    const int64_t n0 = blk * QKV_TOK;
+    __syncthreads();  // every warp is done with the previous tokens' table
+    rope_table<VH>(tab, inv_freq, pos, n0, N);
+    __syncthreads();
+    const int rows = (int)(N - n0 < QKV_TOK ? N - n0 : QKV_TOK) * H;
+    for (int r = warp; r < rows; r += nwarps) {
+      const int t = r / H, hd = r % H;
+      const int64_t n = n0 + t;
+      const int src_hd = (kv_shared && hd >= Hq + Hk) ? hd - Hk : hd;
+      const bf16* src = qkv + n * (int64_t)HI * D + (int64_t)src_hd * D;
+      float lo[VH], hi[VH];
+      ld_bf<VH>(src + base, lo);
+      ld_bf<VH>(src + HALF + base, hi);
+      float ss = 0.f;
 #pragma unroll
-    for (int e = 0; e < VH; ++e) {
-      lo[e] = bf2f(src[base + e]);
-      hi[e] = bf2f(src[HALF + base + e]);
-    }
-    float ss = 0.f;
+      for (int e = 0; e < VH; ++e) ss += lo[e] * lo[e] + hi[e] * hi[e];
+      const float rs = rsqrtf(warp_sum(ss) / D + eps);
+      if (lane == 0) rstd[n * H + hd] = rs;
+      float ol[VH], oh[VH];
+      bf16* dst;
+      if (hd >= Hq + Hk) {  // v: plain rms norm
+        dst = v + (n * Hk + (hd - Hq - Hk)) * (int64_t)D;
 #pragma unroll
-    for (int e = 0; e < VH; ++e) ss += lo[e] * lo[e] + hi[e] * hi[e];
-    const float rs = rsqrtf(warp_sum(ss) / D + eps);
-    if (lane == 0) rstd[wrow] = rs;
-    bf16* dst;
-    if (hd >= Hq + Hk) {  // v: plain rms norm
-      dst = v + (n * Hk + (hd - Hq - Hk)) * (int64_t)D;
+        for (int e = 0; e < VH; ++e) ol[e] = lo[e] * rs, oh[e] = hi[e] * rs;
+      } else {
+        const float* w = hd < Hq ? qw : kw;
+        dst = hd < Hq ? q + (n * Hq + hd) * (int64_t)D : k + (n * Hk + (hd - Hq)) * (int64_t)D;
+        const float2* cs = tab + t * HALF + lane;
 #pragma unroll
-      for (int e = 0; e < VH; ++e) {
-        dst[base + e] = f2bf(lo[e] * rs);
-        dst[HALF + base + e] = f2bf(hi[e] * rs);
+        for (int e = 0; e < VH; ++e) {
+          const int j = base + e;
+          const float a = bf2f(f2bf(lo[e] * rs * w[j]));
+          const float b = bf2f(f2bf(hi[e] * rs * w[HALF + j]));
+          const float2 c = cs[e * 32];
+          // rotate_half: (-b, a)
+          ol[e] = bf2f(f2bf(a * c.x)) + bf2f(f2bf(-b * c.y));
+          oh[e] = bf2f(f2bf(b * c.x)) + bf2f(f2bf(a * c.y));
+        }
       }
-      continue;
-    }
-    const float* w = hd < Hq ? qw : kw;
-    dst = hd < Hq ? q + (n * Hq + hd) * (int64_t)D : k + (n * Hk + (hd - Hq)) * (int64_t)D;
-    const float p = (float)pos[n];
-#pragma unroll
-    for (int e = 0; e < VH; ++e) {
-      const int j = base + e;
-      const float a = bf2f(f2bf(lo[e] * rs * w[j]));
-      const float b = bf2f(f2bf(hi[e] * rs * w[HALF + j]));
-      float sn, cs;
-      sincosf(p * inv_freq[j], &sn, &cs);
-      const float c = bf2f(f2bf(cs)), s = bf2f(f2bf(sn));
-      // rotate_half: (-b, a)
-      dst[j] = f2bf(bf2f(f2bf(a * c)) + bf2f(f2bf(-b * s)));
-      dst[HALF + j] = f2bf(bf2f(f2bf(b * c)) + bf2f(f2bf(a * s)));
+      st_bf<VH>(dst + base, ol);
+      st_bf<VH>(dst + HALF + base, oh);
     }
   }
 }
 
-// Backward: dq/dk/dv (attention layout) -> d_qkv (projection layout). One warp per input
-// head; with kv_shared (v = raw k) the k head's warp adds the v path's gradient as well.
+// Backward: dq/dk/dv (attention layout) -> d_qkv (projection layout). Same token blocks and
+// shared cos/sin table as the forward; one warp per input head; with kv_shared (v = raw k)
+// the k head's warp adds the v path's gradient as well. cs == nullptr: the v path (no weight,
+// no rotation).
 template <int VH>
 ME_DEVICE void norm_bwd_head(const float (&xl)[VH], const float (&xh)[VH], const bf16* __restrict__ gsrc,
-                             const float* __restrict__ w, const float* __restrict__ inv_freq, float p, float rs,
-                             int base, float (&ol)[VH], float (&oh)[VH]) {
+                             const float* __restrict__ w, const float2* __restrict__ cs, float rs, int base,
+                             float (&ol)[VH], float (&oh)[VH]) {
   constexpr int D = VH * 64, HALF = D / 2;
-  float gl[VH], gh[VH], wl[VH], wh[VH];
+  float yl[VH], yh[VH], gl[VH], gh[VH], wl[VH], wh[VH];
+  ld_bf<VH>(gsrc + base, yl);
+  ld_bf<VH>(gsrc + HALF + base, yh);
 #pragma unroll
   for (int e = 0; e < VH; ++e) {
-    const int j = base + e;
-    const float yl = bf2f(gsrc[j]), yh = bf2f(gsrc[HALF + j]);
-    if (w) {
-      float sn, cs;
-      sincosf(p * inv_freq[j], &sn, &cs);
-      const float c = bf2f(f2bf(cs)), s = bf2f(f2bf(sn));
-      gl[e] = yl * c + yh * s;  // adjoint of (a, b) -> (a c - b s, b c + a s)
-      gh[e] = yh * c - yl * s;
-      wl[e] = w[j];
-      wh[e] = w[HALF + j];
+    if (cs) {
+      const float2 c = cs[e * 32];
+      gl[e] = yl[e] * c.x + yh[e] * c.y;  // adjoint of (a, b) -> (a c - b s, b c + a s)
+      gh[e] = yh[e] * c.x - yl[e] * c.y;
+      wl[e] = w[base + e];
+      wh[e] = w[HALF + base + e];
     } else {
-      gl[e] = yl;
-      gh[e] = yh;
+      gl[e] = yl[e];
+      gh[e] = yh[e];
       wl[e] = wh[e] = 1.f;
     }
   }
@@ -382,49 +441,49 @@ ME_DEVICE void norm_bwd_head(const float (&xl)[VH], const float (&xh)[VH], const
 }
 
 template <int VH>
-__global__ void qkv_norm_rope_bwd_kernel(const bf16* __restrict__ dq, const bf16* __restrict__ dk,
-                                         const bf16* __restrict__ dv, const bf16* __restrict__ qkv,
-                                         const float* __restrict__ qw, const float* __restrict__ kw,
-                                         const float* __restrict__ inv_freq, const int64_t* __restrict__ pos,
-                                         const float* __restrict__ rstd, int64_t N, int Hq, int Hk, int kv_shared,
-                                         bf16* __restrict__ dqkv) {
+__global__ void __launch_bounds__(256) qkv_norm_rope_bwd_kernel(
+    const bf16* __restrict__ dq, const bf16* __restrict__ dk, const bf16* __restrict__ dv,
+    const bf16* __restrict__ qkv, const float* __restrict__ qw, const float* __restrict__ kw,
+    const float* __restrict__ inv_freq, const int64_t* __restrict__ pos, const float* __restrict__ rstd, int64_t N,
+    int Hq, int Hk, int kv_shared, bf16* __restrict__ dqkv) {
   constexpr int D = VH * 64, HALF = D / 2;
-  const int lane = threadIdx.x & 31;
+  __shared__ float2 tab[QKV_TOK * HALF];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int H = Hq + 2 * Hk;
   const int HI = kv_shared ? Hq + Hk : H;
-  const int64_t total = N * HI;
-  for (int64_t wrow = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); wrow < total;
-       wrow += (int64_t)gridDim.x * (blockDim.x >> 5)) {
-    const int64_t n = wrow / HI;
-    const int hd = (int)(wrow % HI);
-    const bf16* src = qkv + n * (int64_t)HI * D + (int64_t)hd * D;
-    const int base = lane * VH;
-    float xl[VH], xh[VH], ol[VH], oh[VH];
+  const int base = lane * VH;
+  const int64_t nblk = (N + QKV_TOK - 1) / QKV_TOK;
+  for (int64_t blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+    const int64_t n0 = blk * QKV_TOK;
+    __syncthreads();
+    rope_table<VH>(tab, inv_freq, pos, n0, N);
+    __syncthreads();
+    const int rows = (int)(N - n0 < QKV_TOK ? N - n0 : QKV_TOK) * HI;
+    for (int r = warp; r < rows; r += nwarps) {
+      const int t = r / HI, hd = r % HI;
+      const int64_t n = n0 + t;
+      const int64_t off = n * (int64_t)HI * D + (int64_t)hd * D;
+      float xl[VH], xh[VH], ol[VH], oh[VH];
+      ld_bf<VH>(qkv + off + base, xl);
+      ld_bf<VH>(qkv + off + HALF + base, xh);
 #pragma unroll
-    for (int e = 0; e < VH; ++e) {
-      xl[e] = bf2f(src[base + e]);
-      xh[e] = bf2f(src[HALF + base + e]);
-      ol[e] = oh[e] = 0.f;
-    }
-    const float p = (float)pos[n];
-    if (hd < Hq) {
-      norm_bwd_head<VH>(xl, xh, dq + (n * Hq + hd) * (int64_t)D, qw, inv_freq, p, rstd[n * H + hd], base, ol, oh);
-    } else if (hd < Hq + Hk) {
-      const int kh = hd - Hq;
-      norm_bwd_head<VH>(xl, xh, dk + (n * Hk + kh) * (int64_t)D, kw, inv_freq, p, rstd[n * H + hd], base, ol, oh);
-      if (kv_shared)
-        norm_bwd_head<VH>(xl, xh, dv + (n * Hk + kh) * (int64_t)D, nullptr, inv_freq, p, rstd[n * H + Hq + Hk + kh],
-                          base, ol, oh);
-    } else {
-      const int vh = hd - Hq - Hk;
-      norm_bwd_head<VH>(xl, xh, dv + (n * Hk + vh) * (int64_t)D, nullptr, inv_freq, p, rstd[n * H + hd], base, ol,
-                        oh);
-    }
-    bf16* dst = dqkv + n * (int64_t)HI * D + (int64_t)hd * D;
-#pragma unroll
-    for (int e = 0; e < VH; ++e) {
-      dst[base + e] = f2bf(ol[e]);
-      dst[HALF + base + e] = f2bf(oh[e]);
+      for (int e = 0; e < VH; ++e) ol[e] = oh[e] = 0.f;
+      const float2* cs = tab + t * HALF + lane;
+      if (hd < Hq) {
+        norm_bwd_head<VH>(xl, xh, dq + (n * Hq + hd) * (int64_t)D, qw, cs, rstd[n * H + hd], base, ol, oh);
+      } else if (hd < Hq + Hk) {
+        const int kh = hd - Hq;
+        norm_bwd_head<VH>(xl, xh, dk + (n * Hk + kh) * (int64_t)D, kw, cs, rstd[n * H + hd], base, ol, oh);
+        if (kv_shared)
+          norm_bwd_head<VH>(xl, xh, dv + (n * Hk + kh) * (int64_t)D, nullptr, nullptr, rstd[n * H + Hq + Hk + kh],
+                            base, ol, oh);
+      } else {
+        const int vh = hd - Hq - Hk;
+        norm_bwd_head<VH>(xl, xh, dv + (n * Hk + vh) * (int64_t)D, nullptr, nullptr, rstd[n * H + hd], base, ol,
+                          oh);
+      }
+      st_bf<VH>(dqkv + off + base, ol);
+      st_bf<VH>(dqkv + off + HALF + base, oh);
     }
   }
 }
@@ -606,9 +665,9 @@ std::vector<torch::Tensor> qkv_norm_rope(torch::Tensor qkv, torch::Tensor qw, to
   auto rstd = torch::empty({N, Hq + 2 * Hk}, opts.dtype(torch::kFloat32));
   if (N == 0) return {q, k, v, rstd};
   auto pos64 = pos.to(torch::kLong).contiguous();
+  if (reinterpret_cast<uintptr_t>(qkv.data_ptr()) % 16) qkv = qkv.clone();  // the kernel's vector loads
   const int threads = 256;
-  const int64_t rows = N * (Hq + 2 * Hk);
-  const int grid = (int)std::min<int64_t>((rows + 7) / 8, (int64_t)sm_count() * 16);
+  const int grid = (int)std::min<int64_t>((N + QKV_TOK - 1) / QKV_TOK, (int64_t)sm_count() * 8);
   auto stream = at::cuda::getCurrentCUDAStream();
 #define ME_QKV(VH)                                                                                            \
   qkv_norm_rope_kernel<VH><<<grid, threads, 0, stream>>>(CBFP(qkv), qw.data_ptr<float>(), kw.data_ptr<float>(), \
@@ -629,13 +688,17 @@ torch::Tensor qkv_norm_rope_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tenso
                                 torch::Tensor rstd, int64_t Hq, int64_t Hk, int64_t D, bool kv_shared) {
   const at::cuda::CUDAGuard guard(qkv.device());
   const int64_t N = qkv.size(0);
-  auto dqkv = torch::empty_like(qkv);
+  auto dqkv = torch::empty(qkv.sizes(), qkv.options());
   if (N == 0) return dqkv;
-  auto dqc = dq.contiguous(), dkc = dk.contiguous(), dvc = dv.contiguous();
+  auto aligned = [](torch::Tensor t) {  // the kernel's vector loads want 16-byte aligned rows
+    t = t.contiguous();
+    return reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 ? t.clone() : t;
+  };
+  auto dqc = aligned(dq), dkc = aligned(dk), dvc = aligned(dv);
+  qkv = aligned(qkv);
   auto pos64 = pos.to(torch::kLong).contiguous();
   const int threads = 256;
-  const int64_t rows = N * (Hq + (kv_shared ? 1 : 2) * Hk);
-  const int grid = (int)std::min<int64_t>((rows + 7) / 8, (int64_t)sm_count() * 16);
+  const int grid = (int)std::min<int64_t>((N + QKV_TOK - 1) / QKV_TOK, (int64_t)sm_count() * 8);
   auto stream = at::cuda::getCurrentCUDAStream();
 #define ME_QKVB(VH)                                                                                           \
   qkv_norm_rope_bwd_kernel<VH><<<grid, threads, 0, stream>>>(                                                  \

@@ -128,12 +128,13 @@ ME_DEVICE uint64_t desc_mn_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sb
   return d;
 }
 
-// kind::f16 instruction descriptor: bf16 A/B, fp32 D, M=m, N=n; A K-major, B K-major unless
-// b_mn_major (B stored N-contiguous).
-ME_HOST_DEVICE uint32_t idesc_bf16(int m, int n, bool b_mn_major = false) {
+// kind::f16 instruction descriptor: bf16 A/B, fp32 D, M=m, N=n; A and B K-major unless
+// b_mn_major (B stored N-contiguous) / a_mn_major (A stored M-contiguous).
+ME_HOST_DEVICE uint32_t idesc_bf16(int m, int n, bool b_mn_major = false, bool a_mn_major = false) {
   return (1u << 4)                      // D format F32
          | (1u << 7)                    // A format BF16
          | (1u << 10)                   // B format BF16
+         | ((a_mn_major ? 1u : 0u) << 15)
          | ((b_mn_major ? 1u : 0u) << 16)
          | ((uint32_t)(n >> 3) << 17)   // N >> 3
          | ((uint32_t)(m >> 4) << 24);  // M >> 4

@@ -11,6 +11,8 @@ The sm_100a kernels (csrc/attention.cu) do forward and backward on this layout w
 document bounds computed per tile from `doc_start`; the reference below builds the dense
 mask and is used on CPU and as the oracle.
 """
+import os
+
 import torch
 
 from .. import native
@@ -79,9 +81,22 @@ def attention_fwd_mma(q, k, v, doc_start, window=None, scale=1.0):
     return native().attn_fwd(q, k, v, doc_start, int(window or 0), float(scale))
 
 
+# Byte budget of the P / dS tile buffers of the head_dim-512 backward (heads are processed in
+# passes of whole GQA groups that fit; at least one group per pass).
+TILE_BUDGET = int(float(os.environ.get("ME_ATTN_TILE_BUDGET_GIB", "2.5")) * 2**30)
+
+
 def attention_bwd(do, q, k, v, o, lse, doc_start, window=None, scale=1.0):
-    """(dq, dk, dv) on the sm_100a kernels: the tcgen05/TMEM backward for head_dim <= 256, the
-    warp-level mma.sync backward for head_dim 512 (whose resident tiles exceed shared memory)."""
+    """(dq, dk, dv) on the sm_100a tcgen05/TMEM kernels: for head_dim <= 256 the fused backward
+    (S and dP recomputed per output, nothing written but the gradients); for head_dim 512, whose
+    128 x 512 accumulator fills TMEM and whose resident Q + dO no longer fit shared memory, the
+    backward that writes the P and dS tiles to HBM once and sums them into dQ, dK and dV as
+    block-sparse GEMMs."""
     if q.shape[-1] <= 256:
         return native().attn_bwd_tc(do, q, k, v, o, lse, doc_start, int(window or 0), float(scale))
+    return native().attn_bwd_mat(do, q, k, v, o, lse, doc_start, int(window or 0), float(scale), TILE_BUDGET)
+
+
+def attention_bwd_mma(do, q, k, v, o, lse, doc_start, window=None, scale=1.0):
+    """The first-generation warp-level mma.sync backward (kept for comparison and tests)."""
     return native().attn_bwd(do, q, k, v, o, lse, doc_start, int(window or 0), float(scale))

@@ -3,7 +3,7 @@ events (warm-up, synchronize on both sides) and reported against the measured ro
 (MEASURED_PEAKS.json: cuBLAS bf16 burst TFLOP/s and copy bandwidth; the recipe's fallback
 figures otherwise). Also the workload that the committed ncu summaries in profiles/ capture.
 
-  python -m micro_engram_fork_b200.utils.kernel_bench [--case all|gemm|attn_fwd|attn_bwd|gate|ce] [--iters N]
+  python -m micro_engram_fork_b200.utils.kernel_bench [--case all|gemm|attn_fwd|attn_bwd|gate|ce|qkv] [--iters N]
 """
 import argparse
 import json
@@ -89,6 +89,8 @@ def case_attn_fwd(C, dev, it, pk):
 
 
 def case_attn_bwd(C, dev, it, pk):
+    from ..ops.attention import TILE_BUDGET
+
     out = {}
     ds = _docs(8192, dev)
     for (D, Hk, W) in ((256, 16, 1024), (512, 4, 0)):
@@ -96,9 +98,10 @@ def case_attn_bwd(C, dev, it, pk):
         o, lse = C.attn_fwd_tc(q, k, v, ds, W, 1.0)
         do = torch.randn_like(o)
         fl = 2.5 * _attn_flops(ds, W, D, 32)
-        runs = [("mma.sync", lambda: C.attn_bwd(do, q, k, v, o, lse, ds, W, 1.0))]
+        runs = [("mma.sync", lambda: C.attn_bwd(do, q, k, v, o, lse, ds, W, 1.0)),
+                ("tcgen05 P/dS tiles", lambda: C.attn_bwd_mat(do, q, k, v, o, lse, ds, W, 1.0, TILE_BUDGET))]
         if D <= 256:
-            runs.append(("tcgen05", lambda: C.attn_bwd_tc(do, q, k, v, o, lse, ds, W, 1.0)))
+            runs.append(("tcgen05 fused", lambda: C.attn_bwd_tc(do, q, k, v, o, lse, ds, W, 1.0)))
         for name, fn in runs:
             ms = _time(fn, it)
             out[f"hd{D} bwd {name}"] = {"ms": round(ms, 4), "useful_tflops": round(fl / ms / 1e9, 1),
@@ -136,7 +139,34 @@ def case_ce(C, dev, it, pk):
                                    "frac_of_hbm": round(nbytes / ms / 1e6 / pk["hbm_gbs"], 3)}}
 
 
-CASES = {"gemm": case_gemm, "attn_fwd": case_attn_fwd, "attn_bwd": case_attn_bwd, "gate": case_gate, "ce": case_ce}
+def case_qkv(C, dev, it, pk):
+    """q/k/v RMSNorm + RoPE, forward and backward, on one packed 8192-token step: a sliding layer
+    (32 q heads, 16 k + 16 v heads of 256) and a global one (32 q heads of 512, 4 k heads, v = k)."""
+    from ..models.gemma import GemmaConfig
+
+    cfg, T = GemmaConfig(), 8192
+    pos = torch.cat([torch.arange(n) for n in (2000, 3000, 1192, 2000)]).to(dev)
+    r = {}
+    for kind, D, Hk, shared in (("sliding", 256, 16, False), ("global", 512, 4, True)):
+        Hq = 32
+        HI, H = Hq + (1 if shared else 2) * Hk, Hq + 2 * Hk
+        inv = cfg.inv_freq(f"{kind}_attention" if kind == "sliding" else "full_attention", D).to(dev)
+        qkv = torch.randn(T, HI * D, device=dev).to(torch.bfloat16)
+        w = torch.rand(D, device=dev) + 0.5
+        q, k, v, rs = C.qkv_norm_rope(qkv, w, w, inv, pos, Hq, Hk, D, shared, 1e-6)
+        fwd_bytes = T * HI * D * 2 + T * H * D * 2 + T * H * 4
+        bwd_bytes = T * H * D * 2 + 2 * T * HI * D * 2 + T * H * 4
+        ms = _time(lambda: C.qkv_norm_rope(qkv, w, w, inv, pos, Hq, Hk, D, shared, 1e-6), it)
+        r[f"{kind} D{D} fwd"] = {"ms": round(ms, 4), "gbs": round(fwd_bytes / ms / 1e6, 1),
+                                 "frac_of_hbm": round(fwd_bytes / ms / 1e6 / pk["hbm_gbs"], 3)}
+        ms = _time(lambda: C.qkv_norm_rope_bwd(q, k, v, qkv, w, w, inv, pos, rs, Hq, Hk, D, shared), it)
+        r[f"{kind} D{D} bwd"] = {"ms": round(ms, 4), "gbs": round(bwd_bytes / ms / 1e6, 1),
+                                 "frac_of_hbm": round(bwd_bytes / ms / 1e6 / pk["hbm_gbs"], 3)}
+    return r
+
+
+CASES = {"gemm": case_gemm, "attn_fwd": case_attn_fwd, "attn_bwd": case_attn_bwd, "gate": case_gate, "ce": case_ce,
+         "qkv": case_qkv}
 
 
 def main(argv=None):
