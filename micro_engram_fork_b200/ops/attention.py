@@ -81,20 +81,20 @@ def attention_fwd_mma(q, k, v, doc_start, window=None, scale=1.0):
     return native().attn_fwd(q, k, v, doc_start, int(window or 0), float(scale))
 
 
-# Byte budget of the P / dS tile buffers of the head_dim-512 backward (heads are processed in
-# passes of whole GQA groups that fit; at least one group per pass).
+# Byte budget of the P / dS tile buffers of the tiled backward (heads are processed in passes
+# of whole GQA groups that fit; at least one group per pass).
 TILE_BUDGET = int(float(os.environ.get("ME_ATTN_TILE_BUDGET_GIB", "2.5")) * 2**30)
 
 
 def attention_bwd(do, q, k, v, o, lse, doc_start, window=None, scale=1.0):
-    """(dq, dk, dv) on the sm_100a tcgen05/TMEM kernels: for head_dim <= 256 the fused backward
-    (S and dP recomputed per output, nothing written but the gradients); for head_dim 512, whose
-    128 x 512 accumulator fills TMEM and whose resident Q + dO no longer fit shared memory, the
-    backward that writes the P and dS tiles to HBM once and sums them into dQ, dK and dV as
-    block-sparse GEMMs."""
-    if q.shape[-1] <= 256:
-        return native().attn_bwd_tc(do, q, k, v, o, lse, doc_start, int(window or 0), float(scale))
-    return native().attn_bwd_mat(do, q, k, v, o, lse, doc_start, int(window or 0), float(scale), TILE_BUDGET)
+    """(dq, dk, dv) on the sm_100a tcgen05/TMEM kernels. head_dim 256 and 512: the backward that
+    writes the P and dS tiles to HBM once (bf16) and sums them into dQ, dK and dV as block-sparse
+    GEMMs (5 tile products, no recomputation; 2.2x faster than the fused kernels at hd256 and the
+    only tcgen05 form at hd512, whose 128 x 512 accumulator fills TMEM). Narrower heads: the fused
+    backward (S and dP recomputed per output, nothing written but the gradients)."""
+    if q.shape[-1] >= 256:
+        return native().attn_bwd_mat(do, q, k, v, o, lse, doc_start, int(window or 0), float(scale), TILE_BUDGET)
+    return native().attn_bwd_tc(do, q, k, v, o, lse, doc_start, int(window or 0), float(scale))
 
 
 def attention_bwd_mma(do, q, k, v, o, lse, doc_start, window=None, scale=1.0):
