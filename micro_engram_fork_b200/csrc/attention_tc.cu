@@ -1,19 +1,23 @@
 // tcgen05 (5th-gen tensor core) packed-varlen attention forward for sm_100a.
 //
 // One CTA = 128 queries of one head (M = 128 TMEM lanes) x DV output columns, looping over
-// key blocks of 64. Warp roles (192 threads):
+// key blocks of 64. Warp roles (320 threads):
 //   warp 0     TMA producer: Q once (D/64 chunks of 128x64, 128B swizzle), K in 64x64 chunks
 //              through a KS-deep ring, V in 64-key x DV blocks through a VS-deep ring (3-D
 //              tensor maps over [T, H, D]; no multicast)
 //   warp 1     TMEM owner + single-thread MMA issuer:
 //                S_j = Q K_j^T  into one of two 64-column S buffers  (A, B K-major)
-//                O  += P_j V_j  into a DV-column O accumulator       (B = V, N-contiguous)
-//              tcgen05.commit releases K/V stages and signals S-ready / PV-done
-//   warps 2-5  softmax: each thread owns one query row = one TMEM lane; reads its 64 scores
-//              (tcgen05.ld), applies the document / causal / sliding-window mask, keeps a
-//              running max with lazy rescaling (O in TMEM is rescaled only when the max grows
-//              by more than 2^8, warp-uniformly), writes P (bf16) into shared memory for the PV
-//              MMA, and finally normalises O out of TMEM and writes O and the LSE.
+//                O  += P_j V_j  into a DV-column O accumulator       (A = P_j from one of two
+//                               shared-memory buffers, B = V, N-contiguous)
+//              tcgen05.commit releases K/V stages and signals S-ready / P-free / PV-done
+//   warps 2-9  softmax, two warps per TMEM lane quarter: each thread owns one query row and 32
+//              of the block's 64 keys (tcgen05.ld), applies the document / causal / sliding-window
+//              mask, agrees with its partner thread on the row max through shared memory and a
+//              per-quarter mbarrier, keeps a running max with lazy rescaling (O in TMEM is
+//              rescaled only when the max grows by more than 2^8, warp-uniformly, each warp its
+//              half of the columns), writes its half of P (bf16) into the P buffer of the block's
+//              parity (free once PV_{j-2} is done, so softmax j overlaps PV_{j-1}), and finally
+//              normalises its half of O out of TMEM and writes O and the LSE.
 // Every wait is bounded (2 s); a timeout records ME_ERR_TIMEOUT in the status word and the
 // kernel frees TMEM and returns.
 #include <torch/extension.h>
@@ -42,30 +46,31 @@ struct AttnLayout {
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_OFF + Q_BYTES;
   static constexpr int V_OFF = K_OFF + KS * KCH_BYTES;
-  static constexpr int P_OFF = V_OFF + VS * V_BYTES;
-  static constexpr int BAR_OFF = P_OFF + P_BYTES;
-  static constexpr int N_BARS = 1 + 2 * KS + 2 * VS + 2 + 2 + 1 + 1 + 1;
+  static constexpr int P_OFF = V_OFF + VS * V_BYTES;           // two P buffers
+  static constexpr int RED_OFF = P_OFF + 2 * P_BYTES;          // [2 parity][2 half][128 rows] fp32
+  static constexpr int BAR_OFF = RED_OFF + 2 * 2 * BM * 4;
+  static constexpr int N_BARS = 1 + 2 * KS + 2 * VS + 2 + 2 + 2 + 2 + 1 + 4;
   static constexpr int BYTES = BAR_OFF + N_BARS * 8 + 16 + 1024;
   static constexpr uint32_t TMEM_COLS = (128 + DV) <= 256 ? 256 : 512;
   static constexpr int O_COL = 128;
+  static constexpr int THREADS = 320, NSOFT = 256;  // warp 0 TMA, warp 1 MMA, warps 2-9 softmax
   static_assert(BYTES <= 232448, "shared memory");
 };
 
-ME_DEVICE float warp_any_f(bool p) { return __any_sync(0xffffffffu, p) ? 1.f : 0.f; }
-
 template <int D, int DV, int KS, int VS>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                        const __grid_constant__ CUtensorMap tv, const int* __restrict__ doc_start, int T, int Hq,
                        int Hk, int window, float scale, bf16* __restrict__ o, float* __restrict__ lse, int* status) {
   using L = AttnLayout<D, DV, KS, VS>;
-  constexpr int BM = L::BM, BN = L::BN, NC = L::NC;
+  constexpr int BM = L::BM, BN = L::BN, NC = L::NC, HB = BN / 2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + L::Q_OFF;
   uint8_t* sK = smem + L::K_OFF;
   uint8_t* sV = smem + L::V_OFF;
   uint8_t* sP = smem + L::P_OFF;
+  float* red = reinterpret_cast<float*>(smem + L::RED_OFF);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
   uint64_t* q_full = bars;
   uint64_t* k_full = q_full + 1;
@@ -75,9 +80,10 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* s_full = v_empty + VS;
   uint64_t* s_free = s_full + 2;
   uint64_t* p_full = s_free + 2;
-  uint64_t* pv_done = p_full + 1;
-  uint64_t* o_final = pv_done + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + 1);
+  uint64_t* pv_done = p_full + 2;
+  uint64_t* o_final = pv_done + 2;
+  uint64_t* pair = o_final + 1;  // per TMEM lane quarter: the two warps sharing its rows
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pair + 4);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -100,11 +106,12 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 128);
+      mbar_init(&s_free[i], L::NSOFT);
+      mbar_init(&p_full[i], L::NSOFT);
+      mbar_init(&pv_done[i], 1);
     }
-    mbar_init(p_full, 128);
-    mbar_init(pv_done, 1);
     mbar_init(o_final, 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&pair[i], 64);
     *abort = 0;
     fence_barrier_init();
     prefetch_tmap(&tq);
@@ -166,18 +173,19 @@ __global__ void __launch_bounds__(192, 1)
       bool ok = mbar_wait(q_full, 0, status, 20, abort);
       auto issue_pv = [&](int i) {
         if (!ok) return;
-        const int vb = i % VS;
-        if (!mbar_wait(p_full, i & 1, status, 21, abort) || !mbar_wait(&v_full[vb], (i / VS) & 1, status, 22, abort)) {
+        const int vb = i % VS, pb = i & 1;
+        if (!mbar_wait(&p_full[pb], (i >> 1) & 1, status, 21, abort) ||
+            !mbar_wait(&v_full[vb], (i / VS) & 1, status, 22, abort)) {
           ok = false;
           return;
         }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
-          umma_bf16(tmem + L::O_COL, desc_sw128(aP + kk * 32),
+          umma_bf16(tmem + L::O_COL, desc_sw128(aP + pb * L::P_BYTES + kk * 32),
                     desc_mn_sw128(aV + vb * L::V_BYTES + kk * 16 * 128, BN * 128, 1024), id_o, (i > 0 || kk > 0));
         umma_commit(&v_empty[vb]);
-        umma_commit(pv_done);
+        umma_commit(&pv_done[pb]);
       };
       for (int j = 0; j < nkb && ok; ++j) {
         const int b = j & 1;
@@ -207,35 +215,44 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
-    const int q = warp & 3;
+    // warps 2-9: TMEM lane quarter (warp & 3) and column half (warp - 2) / 4: the two warps of a
+    // quarter share its 32 rows, each scoring 32 of the 64 keys of a block and owning half of O's
+    // columns; they agree on the running max through `red` and their pair barrier every block.
+    const int q = warp & 3, half = (warp - 2) >> 2;
     const int r = q * 32 + lane;
     const int t = q0 + r;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     const int ds_t = t < T ? doc_start[t] : 0;
     const int lo = window > 0 ? max(ds_t, t - window + 1) : ds_t;
-    float m_used = -INFINITY, l = 0.f;
+    float m_used = -INFINITY, l = 0.f;  // l: this half's share of the row sum
     bool ok = true;
     for (int j = 0; j < nkb && ok; ++j) {
-      const int b = j & 1, kb = kb_first + j * BN;
+      const int b = j & 1, kb = kb_first + j * BN + half * HB;
       if (!mbar_wait(&s_full[b], (j >> 1) & 1, status, 30, abort)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float s[BN];
-      tmem_ld32(tmem + lane_base + b * BN, *reinterpret_cast<float(*)[32]>(&s[0]));
-      tmem_ld32(tmem + lane_base + b * BN + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
+      float s[HB];
+      tmem_ld32(tmem + lane_base + b * BN + half * HB, s);
       tc_fence_before();
       mbar_arrive(&s_free[b]);
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
+      for (int c = 0; c < HB; ++c) {
         const int sc = kb + c;
         float x = s[c] * scale;
         if (t >= T || sc > t || sc < lo || sc >= T) x = -INFINITY;
         s[c] = x;
         mx = fmaxf(mx, x);
       }
+      red[((j & 1) * 2 + half) * BM + r] = mx;
+      mbar_arrive(&pair[q]);
+      if (!mbar_wait(&pair[q], j & 1, status, 33, abort)) {
+        ok = false;
+        break;
+      }
+      mx = fmaxf(mx, red[((j & 1) * 2 + (half ^ 1)) * BM + r]);
       float m_new = m_used, alpha = 1.f;
       bool resc = false;
       if (mx > -INFINITY) {
@@ -250,56 +267,73 @@ __global__ void __launch_bounds__(192, 1)
       }
       float sum = 0.f;
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
+      for (int c = 0; c < HB; ++c) {
         const float p = (s[c] == -INFINITY) ? 0.f : __expf(s[c] - m_new);
         s[c] = p;
         sum += p;
       }
       l = l * alpha + sum;
       m_used = m_new;
-      // PV_{j-1} must be done: the P buffer is reused and O may be rescaled
-      if (j >= 1 && !mbar_wait(pv_done, (j - 1) & 1, status, 31, abort)) {
-        ok = false;
-        break;
-      }
-      if (j >= 1 && __any_sync(0xffffffffu, resc)) {
+      const int pb = j & 1;
+      // O may be rescaled only once PV_{j-1} is done; P buffer pb is free once PV_{j-2} is
+      const bool any_resc = j >= 1 && __any_sync(0xffffffffu, resc);
+      if (any_resc) {
+        if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, status, 31, abort)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const float f = resc ? alpha : 1.f;
 #pragma unroll 1
-        for (int cc = 0; cc < DV / 32; ++cc) {
+        for (int cc = 0; cc < DV / 64; ++cc) {
           float v[32];
-          tmem_ld32(tmem + lane_base + L::O_COL + cc * 32, v);
+          const uint32_t col = L::O_COL + half * (DV / 2) + cc * 32;
+          tmem_ld32(tmem + lane_base + col, v);
 #pragma unroll
           for (int e = 0; e < 32; ++e) v[e] *= f;
-          tmem_st32(tmem + lane_base + L::O_COL + cc * 32, v);
+          tmem_st32(tmem + lane_base + col, v);
         }
         tmem_st_wait();
       }
-      // P row r: 64 bf16 = 8 swizzled 16-byte chunks
+      if (j >= 2 && !mbar_wait(&pv_done[pb], ((j - 2) >> 1) & 1, status, 34, abort)) {
+        ok = false;
+        break;
+      }
+      // P row r, this half's 32 keys: 4 swizzled 16-byte chunks of the 128-byte row
+      const uint32_t prow = smem_addr(sP) + pb * L::P_BYTES + r * 128;
 #pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
+      for (int c8 = 0; c8 < HB / 8; ++c8) {
         BF16x8 pk;
 #pragma unroll
         for (int e = 0; e < 8; ++e) pk.h[e] = f2bf(s[c8 * 8 + e]);
-        const uint32_t addr = smem_addr(sP) + r * 128 + ((c8 ^ (r & 7)) << 4);
+        const int chunk = half * (HB / 8) + c8;
+        const uint32_t addr = prow + ((chunk ^ (r & 7)) << 4);
         asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk.u.x), "r"(pk.u.y), "r"(pk.u.z),
                      "r"(pk.u.w)
                      : "memory");
       }
       fence_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[pb]);
+    }
+    // row sum = both halves' shares (one more pair phase)
+    if (ok) {
+      red[((nkb & 1) * 2 + half) * BM + r] = l;
+      mbar_arrive(&pair[q]);
+      ok = mbar_wait(&pair[q], nkb & 1, status, 35, abort);
+      if (ok) l += red[((nkb & 1) * 2 + (half ^ 1)) * BM + r];
     }
     if (ok && mbar_wait(o_final, 0, status, 32, abort)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const int64_t ldo = (int64_t)Hq * D;
 #pragma unroll 1
-      for (int cc = 0; cc < DV / 32; ++cc) {
+      for (int cc = 0; cc < DV / 64; ++cc) {
         float v[32];
-        tmem_ld32(tmem + lane_base + L::O_COL + cc * 32, v);
+        const int c0 = half * (DV / 2) + cc * 32;
+        tmem_ld32(tmem + lane_base + L::O_COL + c0, v);
         if (t < T) {
-          bf16* dst = o + (int64_t)t * ldo + (int64_t)h * D + dv0 + cc * 32;
+          bf16* dst = o + (int64_t)t * ldo + (int64_t)h * D + dv0 + c0;
 #pragma unroll
           for (int j8 = 0; j8 < 4; ++j8) {
             BF16x8 ov;
@@ -309,7 +343,7 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
-      if (blockIdx.z == 0 && t < T) lse[(int64_t)h * T + t] = m_used + logf(l);
+      if (blockIdx.z == 0 && half == 0 && t < T) lse[(int64_t)h * T + t] = m_used + logf(l);
     }
   }
   tc_fence_before();
@@ -359,7 +393,7 @@ void launch_fwd_tc(const torch::Tensor& q, const torch::Tensor& k, const torch::
   auto kern = attn_fwd_tc_kernel<D, DV, KS, VS>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
   dim3 grid((T + 127) / 128, Hq, D / DV);
-  kern<<<grid, 192, L::BYTES, stream>>>(tq, tk, tv, ds, T, Hq, Hk, window, scale,
+  kern<<<grid, L::THREADS, L::BYTES, stream>>>(tq, tk, tv, ds, T, Hq, Hk, window, scale,
                                         reinterpret_cast<bf16*>(o.data_ptr()), lse.data_ptr<float>(), status);
 }
 
@@ -389,8 +423,8 @@ std::vector<torch::Tensor> attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::
   switch (D) {
     case 64: launch_fwd_tc<64, 64, 8, 4>(q, k, v, ds.data_ptr<int>(), (int)window, (float)scale, o, lse, st, stream); break;
     case 128: launch_fwd_tc<128, 128, 8, 4>(q, k, v, ds.data_ptr<int>(), (int)window, (float)scale, o, lse, st, stream); break;
-    case 256: launch_fwd_tc<256, 256, 6, 3>(q, k, v, ds.data_ptr<int>(), (int)window, (float)scale, o, lse, st, stream); break;
-    case 512: launch_fwd_tc<512, 256, 4, 1>(q, k, v, ds.data_ptr<int>(), (int)window, (float)scale, o, lse, st, stream); break;
+    case 256: launch_fwd_tc<256, 256, 4, 2>(q, k, v, ds.data_ptr<int>(), (int)window, (float)scale, o, lse, st, stream); break;
+    case 512: launch_fwd_tc<512, 256, 3, 1>(q, k, v, ds.data_ptr<int>(), (int)window, (float)scale, o, lse, st, stream); break;
     default: TORCH_CHECK(false, "attn_fwd_tc: head_dim must be 64, 128, 256 or 512");
   }
   return {o, lse};
@@ -934,11 +968,16 @@ __global__ void attn_tiles_kernel(const int* __restrict__ ds, int nb, int window
 
 template <int D>
 struct SdpLayout {
+  // head_dim <= 256: Q_i and dO_i stay resident (loaded once per CTA) and the ring streams only
+  // K_j / V_j chunks; wider heads stream all four operands chunk by chunk.
+  static constexpr bool RES = D <= 256;
   static constexpr int NC = D / 64, NS = 3;
   static constexpr int CH = MT * 128;  // one 128-row x 64-column chunk (16 KB)
-  static constexpr int STAGE = 4 * CH;  // Q_i, dO_i, K_j, V_j chunks
-  static constexpr int BAR_OFF = NS * STAGE;
-  static constexpr int N_BARS = 2 * NS + 2 + 2;
+  static constexpr int RES_BYTES = RES ? 2 * NC * CH : 0;  // resident Q_i, dO_i
+  static constexpr int STAGE = (RES ? 2 : 4) * CH;         // [Q_i, dO_i,] K_j, V_j chunks
+  static constexpr int RING_OFF = RES_BYTES;
+  static constexpr int BAR_OFF = RING_OFF + NS * STAGE;
+  static constexpr int N_BARS = 2 * NS + 2 + 2 + 1;
   static constexpr int BYTES = BAR_OFF + N_BARS * 8 + 16 + 1024;
   static constexpr int THREADS = 320, NEPI = 256;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
   static_assert(BYTES <= 232448, "shared memory");
@@ -961,8 +1000,10 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* empty = full + NS;
   uint64_t* s_full = empty + NS;
   uint64_t* s_free = s_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_free + 2);
+  uint64_t* r_full = s_free + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(r_full + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* ring = smem + L::RING_OFF;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int i = blockIdx.x, hl = blockIdx.y, h = h0 + hl, g = h / G;
@@ -984,6 +1025,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&s_full[b], 1);
       mbar_init(&s_free[b], L::NEPI);
     }
+    mbar_init(r_full, 1);
     *abort = 0;
     fence_barrier_init();
     prefetch_tmap(&tq);
@@ -1000,26 +1042,37 @@ __global__ void __launch_bounds__(320, 1)
   if (warp == 0) {
     if (lane == 0 && nit > 0) {
       // ------------------------------------------------------------------ producer
+      if (L::RES) {
+        mbar_expect_tx(r_full, L::RES_BYTES);
+        for (int c = 0; c < NC; ++c) {
+          tma_load_3d(smem + c * L::CH, &tq, r_full, c * 64, h, i * MT);
+          tma_load_3d(smem + (NC + c) * L::CH, &to, r_full, c * 64, h, i * MT);
+        }
+      }
       int issued = 0;
       for (int it = 0; it < nit; ++it) {
         const int s = it % NS, c = it % NC, j = jlo + it / NC;
         if (it >= NS && !mbar_wait(&empty[s], ((it / NS) - 1) & 1, status, 71, abort)) break;
-        uint8_t* st = smem + s * L::STAGE;
+        uint8_t* st = ring + s * L::STAGE;
         mbar_expect_tx(&full[s], L::STAGE);
-        tma_load_3d(st, &tq, &full[s], c * 64, h, i * MT);
-        tma_load_3d(st + L::CH, &to, &full[s], c * 64, h, i * MT);
-        tma_load_3d(st + 2 * L::CH, &tk, &full[s], c * 64, g, j * MT);
-        tma_load_3d(st + 3 * L::CH, &tv, &full[s], c * 64, g, j * MT);
+        if (!L::RES) {
+          tma_load_3d(st, &tq, &full[s], c * 64, h, i * MT);
+          tma_load_3d(st + L::CH, &to, &full[s], c * 64, h, i * MT);
+          st += 2 * L::CH;
+        }
+        tma_load_3d(st, &tk, &full[s], c * 64, g, j * MT);
+        tma_load_3d(st + L::CH, &tv, &full[s], c * 64, g, j * MT);
         issued = it + 1;
       }
-      for (int it = max(0, issued - NS); it < issued; ++it)  // drain copies in flight
+      if (L::RES) mbar_wait(r_full, 0, status, 79, nullptr);  // drain copies in flight
+      for (int it = max(0, issued - NS); it < issued; ++it)
         mbar_wait(&full[it % NS], (it / NS) & 1, status, 79, nullptr);
     }
   } else if (warp == 1) {
     if (lane == 0 && nit > 0) {
       // ------------------------------------------------------------------ MMA issuer
       const uint32_t id = idesc_bf16(128, 128);
-      bool ok = true;
+      bool ok = !L::RES || mbar_wait(r_full, 0, status, 75, abort);
       for (int it = 0; it < nit && ok; ++it) {
         const int s = it % NS, c = it % NC, tt = it / NC, b = tt & 1;
         if (c == 0 && tt >= 2 && !mbar_wait(&s_free[b], ((tt - 2) >> 1) & 1, status, 72, abort)) {
@@ -1031,11 +1084,15 @@ __global__ void __launch_bounds__(320, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t a = smem_addr(smem + s * L::STAGE);
+        // A operands: Q_i / dO_i chunk c (resident or in the stage); B operands: K_j / V_j chunk
+        const uint32_t st = smem_addr(ring + s * L::STAGE);
+        const uint32_t aq = L::RES ? smem_addr(smem + c * L::CH) : st;
+        const uint32_t ao = L::RES ? smem_addr(smem + (NC + c) * L::CH) : st + L::CH;
+        const uint32_t bk = L::RES ? st : st + 2 * L::CH;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          umma_bf16(tmem + b * 256, desc_sw128(a + kk * 32), desc_sw128(a + 2 * L::CH + kk * 32), id, (c | kk) != 0);
-          umma_bf16(tmem + b * 256 + 128, desc_sw128(a + L::CH + kk * 32), desc_sw128(a + 3 * L::CH + kk * 32), id,
+          umma_bf16(tmem + b * 256, desc_sw128(aq + kk * 32), desc_sw128(bk + kk * 32), id, (c | kk) != 0);
+          umma_bf16(tmem + b * 256 + 128, desc_sw128(ao + kk * 32), desc_sw128(bk + L::CH + kk * 32), id,
                     (c | kk) != 0);
         }
         umma_commit(&empty[s]);

@@ -421,3 +421,30 @@ def test_attention_fwd_tcgen05(D, Hq, Hk, window, lens):
     ob, _ = attention_ref(q, k, v, ds, window, scale)
     noise_floor_check(o, o32, ob.to(torch.bfloat16), rel=2.0, eps=2e-3, name="attn tc out")
     torch.testing.assert_close(lse, lse32, rtol=1e-3, atol=1e-3)
+
+
+@cuda
+@pytest.mark.parametrize("D,Hq,Hk,window", [(128, 4, 2, None), (256, 4, 2, 300), (512, 4, 1, None)])
+def test_attention_fwd_tcgen05_rescale(D, Hq, Hk, window):
+    """Logits with a large spread (scale 1, keys growing along the sequence): the running max
+    climbs block after block, so the lazy O rescale and the two softmax warps' max exchange run
+    on most blocks."""
+    import micro_engram_fork_b200 as me
+    from micro_engram_fork_b200.ops.attention import attention_ref, doc_starts
+
+    torch.manual_seed(1)
+    lens = [600, 3, 420]
+    T = sum(lens)
+    pos = torch.cat([torch.arange(n) for n in lens]).to(_dev())
+    ds = doc_starts(pos)
+    q = (torch.randn(T, Hq, D, device=_dev()) * 0.5 + 0.3).to(torch.bfloat16)
+    ramp = torch.linspace(0.0, 1.0, T, device=_dev())[:, None, None]
+    k = (torch.randn(T, Hk, D, device=_dev()) * 0.5 + ramp).to(torch.bfloat16)
+    v = torch.randn(T, Hk, D, device=_dev()).to(torch.bfloat16)
+    o, lse = me.native().attn_fwd_tc(q, k, v, ds, window or 0, 1.0)
+    torch.cuda.synchronize()
+    assert int(me.native().attn_tc_status(0)[0]) == 0, "tcgen05 attention reported a timeout"
+    o32, lse32 = attention_ref(q.float(), k.float(), v.float(), ds, window, 1.0)
+    ob, _ = attention_ref(q, k, v, ds, window, 1.0)
+    noise_floor_check(o, o32, ob.to(torch.bfloat16), rel=2.0, eps=2e-3, name="attn tc out (rescale)")
+    torch.testing.assert_close(lse, lse32, rtol=1e-3, atol=1e-2)
