@@ -109,13 +109,15 @@ class MicroEngram(nn.Module):
 
     # ------------------------------------------------------------------ row sharding
     def shard_rows(self, rank, world, device=None, dtype=None, requires_grad=True, empty=False, pin_memory=False,
-                   group=None):
+                   group=None, row_capacity=None):
         """Keep only this rank's rows of every table (ceil(rows/world) per rank).
 
         Rows come from the loaded tables when they exist, else a fresh N(0, 0.02) init with
         the per-rank seed `seed*1_000_003 + rank`, or stay uninitialised with `empty=True`
         (a server that loads the real rows next). On a CUDA device the rows live in a
-        RowStore (peer-mapped when world > 1) that the fused lookup reads directly.
+        RowStore (peer-mapped when world > 1) that the fused lookup reads directly;
+        `row_capacity` bounds the rows one optimizer step can touch on a rank (its compact
+        gradient accumulator; a frozen or serving copy gets none).
         """
         from .rows import row_range
 
@@ -132,7 +134,8 @@ class MicroEngram(nn.Module):
         if on_cuda:
             from micro_engram_fork_b200.parallel.row_store import RowStore
 
-            store = RowStore(self.table_rows, self.engram_dim, dtype, rank, world, device, group=group)
+            cap = row_capacity if requires_grad else 1
+            store = RowStore(self.table_rows, self.engram_dim, dtype, rank, world, device, group=group, capacity=cap)
             shards = []
             gen = None
             for k, (_a, c) in enumerate(spans):

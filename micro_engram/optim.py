@@ -104,18 +104,21 @@ class LazyAdamW(torch.optim.Optimizer):
 
         coef = getattr(store, "coef", None)
         if group["lazy"]:
-            adam_touched(p.data, state["exp_avg"], state["exp_avg_sq"], store.acc[k], store.bits[k],
+            adam_touched(p.data, state["exp_avg"], state["exp_avg_sq"], store.acc[k], store.pos[k],
                          store.list[k], store.count[k], coef, lr, beta1, beta2, eps, wd, bc1, bc2, sr, seed,
                          int(step), k)
-        else:
+        else:  # every row steps: densify the compact accumulator for this table
             n = p.shape[0]
-            g = store.acc[k][:n]
+            g = store.dense_grad(k)[:n]
             if coef is not None:
                 g.mul_(coef)
             adam_dense(p.data, g, state["exp_avg"], state["exp_avg_sq"], lr, beta1, beta2, eps, wd, bc1, bc2,
                        1.0, sr, seed, int(step))
-            store.acc[k].zero_()
-            store.bits[k].zero_()
+            del g
+            used = min(int(store.count[k][0]), store.cap[k])
+            rows = store.list[k][:used].long()
+            store.pos[k].index_fill_(0, rows[rows >= 0], 0)
+            store.acc[k][:used].zero_()
         store.count[k].zero_()
 
     # ------------------------------------------------------------------ everything else

@@ -173,7 +173,7 @@ def _norm(v):
 
 
 def build_slot(spec, init_from, frozen, model, text_cfg, canon, dtype=None, sharding=None, get_ids=None,
-               device=None, group=None):
+               device=None, group=None, row_capacity=None):
     """Build one engram (fresh, or from init_from), row-shard it when asked, attach it."""
     pad = text_cfg.pad_token_id or 0
     source, sd, src_spec = None, None, None
@@ -240,7 +240,7 @@ def build_slot(spec, init_from, frozen, model, text_cfg, canon, dtype=None, shar
                       else torch.device("cpu"))
         _, layer_dtype = layer_device_dtype(find_text_layers(model)[1][spec["layer"]])
         engram.shard_rows(rank, world, device=device, dtype=dt or layer_dtype, requires_grad=not frozen,
-                          group=group)
+                          group=group, row_capacity=row_capacity)
     where, _ = attach_engram(model, engram, spec["layer"], dtype=dt, get_ids=get_ids)
     n = sum(p.numel() for p in _params(engram))
     LOG.warning(f"[micro_engram] attached at {where}: {n / 1e6:.1f}M params, {spec['gate']} gate, "

@@ -127,11 +127,14 @@ class Trainer:
         from ..rows import _group
 
         self.slots = []
+        # one optimizer step looks up at most (bins per step over all ranks) x sequence_len rows
+        # per table on any rank: the bound of the row stores' compact gradient accumulators
+        row_capacity = self.plan.per_step * cfg.sequence_len
         for spec, init_from, frozen in engram_requests(cfg):
             spec["canon_path"] = cfg.micro_engram_canon_path
             self.slots.append(build_slot(spec, init_from, frozen, model, text_cfg, canon, dtype=cfg.micro_engram_dtype,
                                          sharding="rows", get_ids=lambda: (self.ctx["ids"], self.ctx["pos"]),
-                                         device=self.device, group=_group(self.world)))
+                                         device=self.device, group=_group(self.world), row_capacity=row_capacity))
         for s in self.slots:
             if s.frozen:
                 for p in _params(s.engram):
@@ -378,6 +381,10 @@ class Trainer:
                 self.pbar.refresh()
             if self.global_step % cfg.logging_steps == 0 or self.global_step == self.total_steps:
                 dt = time.time() - t_last
+                for slot in self.slots:  # a row-store kernel error (bounds, capacity, timeout) stops the run
+                    store = slot.engram.__dict__.get("row_store")
+                    if store is not None:
+                        store.check_status()
                 logs.update(self._memory())
                 logs.update(self._engram_logs())
                 logs.update({"epoch": round(self.epoch + self.step_in_epoch / max(1, n_ep), 4),

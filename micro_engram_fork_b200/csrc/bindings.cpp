@@ -8,13 +8,13 @@ torch::Tensor engram_hash_prev(torch::Tensor ids, torch::Tensor canon, torch::Te
                                torch::Tensor rows, int64_t pad_id);
 torch::Tensor engram_gather(torch::Tensor idx, torch::Tensor ptrs, torch::Tensor per, int64_t world, int64_t dim,
                             int64_t src_dtype, torch::ScalarType out_dtype, c10::optional<torch::Tensor> status);
-void engram_scatter_grad(torch::Tensor g, torch::Tensor idx, torch::Tensor acc_ptrs, torch::Tensor bit_ptrs,
-                         torch::Tensor list_ptrs, torch::Tensor cnt_ptrs, torch::Tensor per, int64_t world,
-                         double scale, c10::optional<torch::Tensor> status, int64_t my_rank);
-void engram_touched_sqnorm(torch::Tensor acc_ptrs, torch::Tensor list_ptrs, torch::Tensor cnt_ptrs, int64_t dim,
+void engram_scatter_grad(torch::Tensor g, torch::Tensor idx, torch::Tensor acc_ptrs, torch::Tensor pos_ptrs,
+                         torch::Tensor list_ptrs, torch::Tensor cnt_ptrs, torch::Tensor per, torch::Tensor caps,
+                         int64_t world, double scale, c10::optional<torch::Tensor> status, int64_t my_rank);
+void engram_touched_sqnorm(torch::Tensor acc_ptrs, torch::Tensor cnt_ptrs, torch::Tensor caps, int64_t dim,
                            torch::Tensor sq);
 void engram_clip_coef(torch::Tensor sq, double max_norm, torch::Tensor coef, torch::Tensor norm);
-void engram_adam_touched(torch::Tensor p, torch::Tensor m, torch::Tensor v, torch::Tensor acc, torch::Tensor bits,
+void engram_adam_touched(torch::Tensor p, torch::Tensor m, torch::Tensor v, torch::Tensor acc, torch::Tensor pos,
                          torch::Tensor list, torch::Tensor cnt, c10::optional<torch::Tensor> coef, double lr,
                          double beta1, double beta2, double eps, double wd, double bc1, double bc2, bool sr,
                          int64_t seed, int64_t step, int64_t table_id);

@@ -149,91 +149,101 @@ __global__ void gather_kernel(const int64_t* __restrict__ idx, int64_t N, int n_
 // ------------------------------------------------------------------------------ row grads
 // Backward of the gather: every looked-up row's gradient (scaled by `scale`, 1/world as the
 // reference's owner-side average) is added into the owner's fp32 accumulator with float4
-// atomics (peer memory over NVLink when the owner is another GPU), and the row is marked
-// touched in the owner's bitmap; the first toucher appends it to the owner's touched list.
-// State pointer table layout, per (rank, table): acc [per, dim] fp32, bits [ceil(per/32)]
-// u32, list [per] i32, count [1] i32.
+// atomics (peer memory over NVLink when the owner is another GPU). The accumulator is
+// compact: a row's gradient lives in a slot of [cap, dim], cap = the rows one optimizer step
+// can touch (tokens per step x ranks, at most the shard's rows). pos[row] = slot + 1 (0 =
+// untouched); the first event on a row reserves a slot with one atomicAdd on the count and
+// installs it with one atomicCAS on pos (a loser of that race leaves its reserved slot as a
+// hole: list[slot] = -1, accumulator row zero). Each event reserves at most one slot, so
+// cap = events per step can never be exceeded. One warp per (token, table) event; lane 0
+// resolves the slot, all lanes add dim/32 floats. State pointer table layout, per
+// (rank, table): acc [cap, dim] fp32, pos [per] i32, list [cap] i32, count [1] i32.
 template <typename Tg>
 __global__ void scatter_grad_kernel(const Tg* __restrict__ g, const int64_t* __restrict__ idx,
                                     int64_t N, int n_tables, int dim,
                                     const int64_t* __restrict__ acc_ptrs,
-                                    const int64_t* __restrict__ bit_ptrs,
+                                    const int64_t* __restrict__ pos_ptrs,
                                     const int64_t* __restrict__ list_ptrs,
                                     const int64_t* __restrict__ cnt_ptrs,
-                                    const int64_t* __restrict__ per, int world, float scale,
-                                    int* status, int my_rank) {
+                                    const int64_t* __restrict__ per, const int64_t* __restrict__ caps, int world,
+                                    float scale, int* status, int my_rank) {
+  const int lane = threadIdx.x & 31;
   const int chunks = dim / 4;
-  const int64_t total = N * n_tables * chunks;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int c = (int)(i % chunks);
-    const int64_t nk = i / chunks;
-    const int k = (int)(nk % n_tables);
-    const int64_t n = nk / n_tables;
+  const int64_t total = N * n_tables;
+  for (int64_t e = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; e < total;
+       e += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int k = (int)(e % n_tables);
+    const int64_t n = e / n_tables;
     const int64_t row = idx[(int64_t)k * N + n];
     const int64_t pk = per[k];
     const int owner = (int)(row / pk);
     const int64_t local = row - (int64_t)owner * pk;
 #ifdef ME_BOUNDS_CHECK
     if (row < 0 || owner >= world) {
-      report(status, ME_ERR_BOUNDS, (int)k);
+      if (lane == 0) report(status, ME_ERR_BOUNDS, (int)k);
       continue;
     }
 #endif
-    const Tg* src = g + n * (int64_t)n_tables * dim + (int64_t)k * dim + c * 4;
-    float4 v;
-    if constexpr (sizeof(Tg) == 2) {
-      const __nv_bfloat162* s2 = reinterpret_cast<const __nv_bfloat162*>(src);
-      const float2 a = __bfloat1622float2(s2[0]), b = __bfloat1622float2(s2[1]);
-      v = make_float4(a.x * scale, a.y * scale, b.x * scale, b.y * scale);
-    } else {
-      const float4 a = *reinterpret_cast<const float4*>(src);
-      v = make_float4(a.x * scale, a.y * scale, a.z * scale, a.w * scale);
-    }
     const int slot = owner * n_tables + k;
-    float* acc = reinterpret_cast<float*>(acc_ptrs[slot]) + local * dim + c * 4;
-    if (owner == my_rank) {
-      atomicAdd(reinterpret_cast<float4*>(acc), v);  // local memory: one 16-byte vector atomic
-    } else {  // a peer's memory over NVLink: plain fp32 atomics
-      atomicAdd(acc + 0, v.x);
-      atomicAdd(acc + 1, v.y);
-      atomicAdd(acc + 2, v.z);
-      atomicAdd(acc + 3, v.w);
-    }
-    if (c == 0) {
-      uint32_t* bits = reinterpret_cast<uint32_t*>(bit_ptrs[slot]);
-      const uint32_t bit = 1u << (local & 31);
-      const uint32_t old = atomicOr(bits + (local >> 5), bit);
-      if (!(old & bit)) {
-        int* cnt = reinterpret_cast<int*>(cnt_ptrs[slot]);
-        const int pos = atomicAdd(cnt, 1);
-        if (pos < pk) {
-          reinterpret_cast<int*>(list_ptrs[slot])[pos] = (int)local;
+    int s = 0;
+    if (lane == 0) {
+      int* pos = reinterpret_cast<int*>(pos_ptrs[slot]) + local;
+      s = *reinterpret_cast<volatile int*>(pos);
+      if (s == 0) {
+        const int t = atomicAdd(reinterpret_cast<int*>(cnt_ptrs[slot]), 1);
+        if (t < caps[k]) {
+          const int old = atomicCAS(pos, 0, t + 1);
+          reinterpret_cast<int*>(list_ptrs[slot])[t] = old == 0 ? (int)local : -1;
+          s = old == 0 ? t + 1 : old;
         } else {
-          report(status, ME_ERR_CAPACITY, k);
+          s = atomicAdd(pos, 0);  // another event may have installed a slot meanwhile
+          if (s == 0) report(status, ME_ERR_CAPACITY, k);
         }
+      }
+    }
+    s = __shfl_sync(0xffffffffu, s, 0);
+    if (s <= 0) continue;
+    float* acc = reinterpret_cast<float*>(acc_ptrs[slot]) + (int64_t)(s - 1) * dim;
+    const Tg* src = g + n * (int64_t)n_tables * dim + (int64_t)k * dim;
+    for (int c = lane; c < chunks; c += 32) {
+      float4 v;
+      if constexpr (sizeof(Tg) == 2) {
+        const __nv_bfloat162* s2 = reinterpret_cast<const __nv_bfloat162*>(src + c * 4);
+        const float2 a = __bfloat1622float2(s2[0]), b = __bfloat1622float2(s2[1]);
+        v = make_float4(a.x * scale, a.y * scale, b.x * scale, b.y * scale);
+      } else {
+        const float4 a = *reinterpret_cast<const float4*>(src + c * 4);
+        v = make_float4(a.x * scale, a.y * scale, a.z * scale, a.w * scale);
+      }
+      float* dst = acc + c * 4;
+      if (owner == my_rank) {
+        atomicAdd(reinterpret_cast<float4*>(dst), v);  // local memory: one 16-byte vector atomic
+      } else {  // a peer's memory over NVLink: plain fp32 atomics
+        atomicAdd(dst + 0, v.x);
+        atomicAdd(dst + 1, v.y);
+        atomicAdd(dst + 2, v.z);
+        atomicAdd(dst + 3, v.w);
       }
     }
   }
 }
 
 // Sum of squares of the touched rows' accumulated gradients (every row lives on exactly one
-// rank, so the sum over ranks is the global table norm^2). counts are read on the device.
+// rank, so the sum over ranks is the global table norm^2): the first min(count, cap) slots of
+// each compact accumulator (holes are zero). counts are read on the device.
 __global__ void touched_sqnorm_kernel(const int64_t* __restrict__ acc_ptrs,
-                                      const int64_t* __restrict__ list_ptrs,
-                                      const int64_t* __restrict__ cnt_ptrs, int n_tables, int dim,
-                                      float* __restrict__ out) {
+                                      const int64_t* __restrict__ cnt_ptrs, const int64_t* __restrict__ caps,
+                                      int n_tables, int dim, float* __restrict__ out) {
   __shared__ float scratch[64];
   float local_sum = 0.f;
   const int lane = threadIdx.x & 31;
   const int warps_total = gridDim.x * (blockDim.x >> 5);
   const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   for (int k = 0; k < n_tables; ++k) {
-    const int cnt = *reinterpret_cast<const int*>(cnt_ptrs[k]);
-    const int* list = reinterpret_cast<const int*>(list_ptrs[k]);
+    const int cnt = (int)min((int64_t)*reinterpret_cast<const int*>(cnt_ptrs[k]), caps[k]);
     const float* acc = reinterpret_cast<const float*>(acc_ptrs[k]);
     for (int r = wid; r < cnt; r += warps_total) {
-      const float* a = acc + (int64_t)list[r] * dim;
+      const float* a = acc + (int64_t)r * dim;
       for (int j = lane; j < dim; j += 32) local_sum += a[j] * a[j];
     }
   }
@@ -252,22 +262,27 @@ __global__ void clip_coef_kernel(const float* sq, float max_norm, float* coef, f
 // rows whose gradient is all zero are left alone; rowwise keeps ONE fp32 second moment per
 // row (mean of g^2 over the row); bf16 weights/moments are written back with stochastic
 // rounding (Philox4x32-10 keyed by seed/step, counter = row, column block). The
-// accumulator row and its touched bit are cleared for the next step. One warp per row.
+// accumulator slot and the row's pos entry are cleared for the next step. One warp per slot
+// of the compact accumulator (holes, list = -1, are only cleared).
 template <typename Tp, typename Tm>
 __global__ void adam_touched_kernel(Tp* __restrict__ p, Tm* __restrict__ m, float* __restrict__ v_row,
                                     Tm* __restrict__ v_val, float* __restrict__ acc,
-                                    uint32_t* __restrict__ bits, const int* __restrict__ list,
-                                    const int* __restrict__ cnt_ptr, int dim, const float* coef_ptr,
+                                    int* __restrict__ pos, const int* __restrict__ list,
+                                    const int* __restrict__ cnt_ptr, int cap, int dim, const float* coef_ptr,
                                     float lr, float beta1, float beta2, float eps, float wd, float bc1,
                                     float bc2_sqrt, int sr, uint32_t seed, uint32_t step,
                                     uint32_t table_id) {
   const int lane = threadIdx.x & 31;
   const int warps_total = gridDim.x * (blockDim.x >> 5);
-  const int cnt = *cnt_ptr;
+  const int cnt = min(*cnt_ptr, cap);
   const float coef = coef_ptr ? *coef_ptr : 1.f;
   for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < cnt; r += warps_total) {
     const int64_t row = list[r];
-    float* a = acc + row * dim;
+    float* a = acc + (int64_t)r * dim;
+    if (row < 0) {
+      for (int j = lane; j < dim; j += 32) a[j] = 0.f;
+      continue;
+    }
     // gradient of this row (dim <= 256: at most 8 per lane)
     float g[8];
     bool nz = false;
@@ -283,7 +298,7 @@ __global__ void adam_touched_kernel(Tp* __restrict__ p, Tm* __restrict__ m, floa
         a[j] = 0.f;
       }
     }
-    if (lane == 0) atomicAnd(bits + (row >> 5), ~(1u << (row & 31)));
+    if (lane == 0) pos[row] = 0;
     if (!__any_sync(0xffffffffu, nz)) continue;
     float vr = 0.f;
     if (v_row) {
@@ -821,9 +836,9 @@ torch::Tensor engram_gather(torch::Tensor idx, torch::Tensor ptrs, torch::Tensor
   return mem;
 }
 
-void engram_scatter_grad(torch::Tensor g, torch::Tensor idx, torch::Tensor acc_ptrs, torch::Tensor bit_ptrs,
-                         torch::Tensor list_ptrs, torch::Tensor cnt_ptrs, torch::Tensor per, int64_t world,
-                         double scale, c10::optional<torch::Tensor> status, int64_t my_rank) {
+void engram_scatter_grad(torch::Tensor g, torch::Tensor idx, torch::Tensor acc_ptrs, torch::Tensor pos_ptrs,
+                         torch::Tensor list_ptrs, torch::Tensor cnt_ptrs, torch::Tensor per, torch::Tensor caps,
+                         int64_t world, double scale, c10::optional<torch::Tensor> status, int64_t my_rank) {
   check_cuda(g, "g");
   check_cuda(idx, "idx");
   const at::cuda::CUDAGuard guard(g.device());
@@ -833,31 +848,32 @@ void engram_scatter_grad(torch::Tensor g, torch::Tensor idx, torch::Tensor acc_p
   const int dim = (int)(g.size(1) / nt);
   TORCH_CHECK(dim % 4 == 0, "engram dim must be a multiple of 4");
   const int threads = 256;
-  const int grid = grid_for(N * nt * (dim / 4), threads);
+  const int grid = grid_for(N * nt * 32, threads);  // one warp per (token, table) event
   auto stream = at::cuda::getCurrentCUDAStream();
   int* st = status.has_value() ? status->data_ptr<int>() : nullptr;
   if (g.scalar_type() == torch::kBFloat16) {
     scatter_grad_kernel<__nv_bfloat16><<<grid, threads, 0, stream>>>(
         reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), idx.data_ptr<int64_t>(), N, nt, dim,
-        acc_ptrs.data_ptr<int64_t>(), bit_ptrs.data_ptr<int64_t>(), list_ptrs.data_ptr<int64_t>(),
-        cnt_ptrs.data_ptr<int64_t>(), per.data_ptr<int64_t>(), world, (float)scale, st, (int)my_rank);
+        acc_ptrs.data_ptr<int64_t>(), pos_ptrs.data_ptr<int64_t>(), list_ptrs.data_ptr<int64_t>(),
+        cnt_ptrs.data_ptr<int64_t>(), per.data_ptr<int64_t>(), caps.data_ptr<int64_t>(), world, (float)scale, st,
+        (int)my_rank);
   } else {
     TORCH_CHECK(g.scalar_type() == torch::kFloat32, "row grads must be bf16 or fp32");
     scatter_grad_kernel<float><<<grid, threads, 0, stream>>>(
         g.data_ptr<float>(), idx.data_ptr<int64_t>(), N, nt, dim, acc_ptrs.data_ptr<int64_t>(),
-        bit_ptrs.data_ptr<int64_t>(), list_ptrs.data_ptr<int64_t>(), cnt_ptrs.data_ptr<int64_t>(),
-        per.data_ptr<int64_t>(), world, (float)scale, st, (int)my_rank);
+        pos_ptrs.data_ptr<int64_t>(), list_ptrs.data_ptr<int64_t>(), cnt_ptrs.data_ptr<int64_t>(),
+        per.data_ptr<int64_t>(), caps.data_ptr<int64_t>(), world, (float)scale, st, (int)my_rank);
   }
 }
 
 // sq (fp32 [1], accumulated into) += sum over the local touched rows of acc^2.
-void engram_touched_sqnorm(torch::Tensor acc_ptrs, torch::Tensor list_ptrs, torch::Tensor cnt_ptrs,
-                           int64_t dim, torch::Tensor sq) {
+void engram_touched_sqnorm(torch::Tensor acc_ptrs, torch::Tensor cnt_ptrs, torch::Tensor caps, int64_t dim,
+                           torch::Tensor sq) {
   const at::cuda::CUDAGuard guard(sq.device());
   const int nt = (int)acc_ptrs.numel();
   touched_sqnorm_kernel<<<sm_count() * 2, 512, 0, at::cuda::getCurrentCUDAStream()>>>(
-      acc_ptrs.data_ptr<int64_t>(), list_ptrs.data_ptr<int64_t>(), cnt_ptrs.data_ptr<int64_t>(), nt,
-      (int)dim, sq.data_ptr<float>());
+      acc_ptrs.data_ptr<int64_t>(), cnt_ptrs.data_ptr<int64_t>(), caps.data_ptr<int64_t>(), nt, (int)dim,
+      sq.data_ptr<float>());
 }
 
 void engram_clip_coef(torch::Tensor sq, double max_norm, torch::Tensor coef, torch::Tensor norm) {
@@ -867,7 +883,7 @@ void engram_clip_coef(torch::Tensor sq, double max_norm, torch::Tensor coef, tor
 }
 
 void engram_adam_touched(torch::Tensor p, torch::Tensor m, torch::Tensor v, torch::Tensor acc,
-                         torch::Tensor bits, torch::Tensor list, torch::Tensor cnt,
+                         torch::Tensor pos, torch::Tensor list, torch::Tensor cnt,
                          c10::optional<torch::Tensor> coef, double lr, double beta1, double beta2,
                          double eps, double wd, double bc1, double bc2, bool sr, int64_t seed,
                          int64_t step, int64_t table_id) {
@@ -879,6 +895,9 @@ void engram_adam_touched(torch::Tensor p, torch::Tensor m, torch::Tensor v, torc
   const bool rowwise = v.dim() == 1;
   TORCH_CHECK(rowwise ? v.scalar_type() == torch::kFloat32 : v.scalar_type() == p.scalar_type(),
               "exp_avg_sq dtype");
+  TORCH_CHECK(acc.dim() == 2 && acc.size(1) == dim && pos.numel() >= p.size(0) && list.numel() >= acc.size(0),
+              "compact accumulator shapes");
+  const int cap = (int)acc.size(0);
   const int threads = 256;
   const int grid = sm_count() * 4;
   auto stream = at::cuda::getCurrentCUDAStream();
@@ -889,15 +908,13 @@ void engram_adam_touched(torch::Tensor p, torch::Tensor m, torch::Tensor v, torc
     adam_touched_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, threads, 0, stream>>>(
         reinterpret_cast<__nv_bfloat16*>(p.data_ptr()), reinterpret_cast<__nv_bfloat16*>(m.data_ptr()), vrow,
         rowwise ? nullptr : reinterpret_cast<__nv_bfloat16*>(v.data_ptr()), acc.data_ptr<float>(),
-        reinterpret_cast<uint32_t*>(bits.data_ptr<int32_t>()), list.data_ptr<int>(), cnt.data_ptr<int>(), dim,
-        cp, (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd, (float)bc1, bc2s, sr ? 1 : 0,
+        pos.data_ptr<int>(), list.data_ptr<int>(), cnt.data_ptr<int>(), cap, dim, cp, (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd, (float)bc1, bc2s, sr ? 1 : 0,
         (uint32_t)seed, (uint32_t)step, (uint32_t)table_id);
   } else {
     TORCH_CHECK(p.scalar_type() == torch::kFloat32, "tables must be bf16 or fp32");
     adam_touched_kernel<float, float><<<grid, threads, 0, stream>>>(
         p.data_ptr<float>(), m.data_ptr<float>(), vrow, rowwise ? nullptr : v.data_ptr<float>(),
-        acc.data_ptr<float>(), reinterpret_cast<uint32_t*>(bits.data_ptr<int32_t>()), list.data_ptr<int>(),
-        cnt.data_ptr<int>(), dim, cp, (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd,
+        acc.data_ptr<float>(), pos.data_ptr<int>(), list.data_ptr<int>(), cnt.data_ptr<int>(), cap, dim, cp, (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd,
         (float)bc1, bc2s, 0, (uint32_t)seed, (uint32_t)step, (uint32_t)table_id);
   }
 }

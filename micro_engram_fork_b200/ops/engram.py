@@ -82,9 +82,11 @@ def gate(h, k, v, q_delta=None, k_delta=None, keep=None, sqrt_gate=False, gate_a
 
 
 # ------------------------------------------------------------------------- optimizer kernels
-def adam_touched(p, m, v, acc, bits, lst, cnt, coef, lr, beta1, beta2, eps, wd, bc1, bc2, sr, seed, step,
+def adam_touched(p, m, v, acc, pos, lst, cnt, coef, lr, beta1, beta2, eps, wd, bc1, bc2, sr, seed, step,
                  table_id):
-    native().engram_adam_touched(p, m, v, acc, bits, lst, cnt, coef, lr, beta1, beta2, eps, wd, bc1, bc2, sr,
+    """AdamW on the rows of one table shard that hold a slot of the compact accumulator `acc`
+    [cap, dim] (slot -> row in `lst`, row -> slot + 1 in `pos`); clears slots and pos."""
+    native().engram_adam_touched(p, m, v, acc, pos, lst, cnt, coef, lr, beta1, beta2, eps, wd, bc1, bc2, sr,
                                  seed, step, table_id)
 
 

@@ -6,10 +6,16 @@ layout), in ONE buffer laid out identically on every rank so a peer's row is at
 `ptr[owner] + offset(table) + local_row * row_bytes`:
 
     per table k:  weight [per_k, dim]  (table dtype)   read by peers' gathers
-                  acc    [per_k, dim]  fp32            peers' row gradients land here
-                  bits   [ceil(per_k/32)] u32          touched bitmap
-                  list   [per_k] i32                   touched rows, in arrival order
-                  count  [4] i32                       number of touched rows
+                  acc    [cap_k, dim]  fp32            compact: peers' row gradients land in slots
+                  pos    [per_k] i32                   row -> slot + 1 (0: untouched this step)
+                  list   [cap_k] i32                   slot -> row (-1: a slot lost to a race)
+                  count  [4] i32                       slots handed out this step
+
+cap_k = min(per_k, capacity): `capacity` is the number of (token, table) lookups one
+optimizer step can push to a rank (tokens per step per rank x ranks); every lookup takes at
+most one slot, so the compact accumulator cannot overflow, and it replaces a dense fp32
+accumulator as large as the table (2x the bf16 table) with a few hundred MB. Without a
+capacity (inference, tests) cap_k = per_k.
 
 With world > 1 the buffer is a SymmBuffer (CUDA IPC over NVLink); kernels index it
 through device tables of per-rank addresses. The optimizer moments live in ordinary local
@@ -29,7 +35,7 @@ def _align(n):
 class RowStore:
     _created = 0
 
-    def __init__(self, table_rows, dim, dtype, rank, world, device, group=None):
+    def __init__(self, table_rows, dim, dtype, rank, world, device, group=None, capacity=None):
         RowStore._created += 1
         self.salt = RowStore._created  # decorrelates the rounding bits of different engrams
         self.coef = None  # device clip coefficient for the next optimizer step
@@ -40,6 +46,7 @@ class RowStore:
         self.device = torch.device(device)
         self.nt = len(self.table_rows)
         self.per = [-(-r // self.world) for r in self.table_rows]
+        self.cap = [p if capacity is None else max(1, min(p, int(capacity))) for p in self.per]
         self.counts = []
         for r, p in zip(self.table_rows, self.per):
             start = min(self.rank * p, r)
@@ -47,16 +54,16 @@ class RowStore:
         esz = torch.empty((), dtype=dtype).element_size()
         self.layout = []  # per table: dict of byte offsets
         off = 0
-        for p in self.per:
+        for p, c in zip(self.per, self.cap):
             ent = {}
             ent["weight"] = off
             off = _align(off + p * self.dim * esz)
             ent["acc"] = off
-            off = _align(off + p * self.dim * 4)
-            ent["bits"] = off
-            off = _align(off + (-(-p // 32)) * 4)
-            ent["list"] = off
+            off = _align(off + c * self.dim * 4)
+            ent["pos"] = off
             off = _align(off + p * 4)
+            ent["list"] = off
+            off = _align(off + c * 4)
             ent["count"] = off
             off = _align(off + 16)
             self.layout.append(ent)
@@ -80,12 +87,12 @@ class RowStore:
                     n *= s
                 nb = n * torch.empty((), dtype=dt).element_size()
                 return self._raw[o:o + nb].view(dt).view(*shape)
-        self.weights, self.acc, self.bits, self.list, self.count = [], [], [], [], []
-        for k, (p, ent) in enumerate(zip(self.per, self.layout)):
+        self.weights, self.acc, self.pos, self.list, self.count = [], [], [], [], []
+        for k, (p, c, ent) in enumerate(zip(self.per, self.cap, self.layout)):
             self.weights.append(view(ent["weight"], (p, self.dim), dtype))
-            self.acc.append(view(ent["acc"], (p, self.dim), torch.float32))
-            self.bits.append(view(ent["bits"], (-(-p // 32),), torch.int32))
-            self.list.append(view(ent["list"], (p,), torch.int32))
+            self.acc.append(view(ent["acc"], (c, self.dim), torch.float32))
+            self.pos.append(view(ent["pos"], (p,), torch.int32))
+            self.list.append(view(ent["list"], (c,), torch.int32))
             self.count.append(view(ent["count"], (4,), torch.int32))
 
         def table(kind):
@@ -94,7 +101,7 @@ class RowStore:
 
         self.w_ptrs = table("weight")
         self.acc_ptrs = table("acc")
-        self.bit_ptrs = table("bits")
+        self.pos_ptrs = table("pos")
         self.list_ptrs = table("list")
         self.cnt_ptrs = table("count")
         # this rank's own entries (for the optimizer and the norm)
@@ -103,6 +110,7 @@ class RowStore:
         self.own_list_ptrs = self.list_ptrs[own].contiguous()
         self.own_cnt_ptrs = self.cnt_ptrs[own].contiguous()
         self.per_t = torch.tensor(self.per, dtype=torch.int64, device=self.device)
+        self.cap_t = torch.tensor(self.cap, dtype=torch.int64, device=self.device)
         self.status = torch.zeros(2, dtype=torch.int32, device=self.device)
         self.pending = False  # row gradients were pushed since the last optimizer step
 
@@ -112,10 +120,20 @@ class RowStore:
         return self.weights[k][:self.counts[k]]
 
     def touched(self, k):
-        """(local rows, fp32 grads) of table k's touched rows: one host sync (tests/logging)."""
-        n = int(self.count[k][0])
+        """(local rows, fp32 grads) of table k's touched rows, in slot order: one host sync
+        (tests/logging)."""
+        n = min(int(self.count[k][0]), self.cap[k])
         rows = self.list[k][:n].long()
-        return rows, self.acc[k].index_select(0, rows)
+        keep = rows >= 0
+        return rows[keep], self.acc[k][:n][keep]
+
+    def dense_grad(self, k):
+        """Table k's accumulated gradient as a dense fp32 [per_k, dim] tensor (the non-lazy
+        optimizer's input; zeros on untouched rows)."""
+        rows, g = self.touched(k)
+        out = torch.zeros(self.per[k], self.dim, dtype=torch.float32, device=self.device)
+        out.index_copy_(0, rows, g)
+        return out
 
     # ---------------------------------------------------------------- kernels
     def gather(self, idx, out_dtype):
@@ -126,12 +144,13 @@ class RowStore:
 
     def push_grads(self, g, idx, scale):
         """Row gradients g [N, n_tables*dim] of the looked-up rows -> the owners' accumulators."""
-        native().engram_scatter_grad(g.contiguous(), idx, self.acc_ptrs, self.bit_ptrs, self.list_ptrs,
-                                     self.cnt_ptrs, self.per_t, self.world, float(scale), self.status, self.rank)
+        native().engram_scatter_grad(g.contiguous(), idx, self.acc_ptrs, self.pos_ptrs, self.list_ptrs,
+                                     self.cnt_ptrs, self.per_t, self.cap_t, self.world, float(scale), self.status,
+                                     self.rank)
         self.pending = True
 
     def sqnorm_into(self, sq):
-        native().engram_touched_sqnorm(self.own_acc_ptrs, self.own_list_ptrs, self.own_cnt_ptrs, self.dim, sq)
+        native().engram_touched_sqnorm(self.own_acc_ptrs, self.own_cnt_ptrs, self.cap_t, self.dim, sq)
 
     def clear_counts(self):
         for c in self.count:
@@ -139,13 +158,14 @@ class RowStore:
         self.pending = False
 
     def zero_grads(self):
-        """Drop pending gradients (zero_grad without a step): clears only the touched rows."""
+        """Drop pending gradients (zero_grad without a step): clears only the used slots and
+        their rows' pos entries."""
         for k in range(self.nt):
-            n = int(self.count[k][0])
+            n = min(int(self.count[k][0]), self.cap[k])
             if n:
                 rows = self.list[k][:n].long()
-                self.acc[k].index_fill_(0, rows, 0.0)
-                self.bits[k].zero_()
+                self.pos[k].index_fill_(0, rows[rows >= 0], 0)
+                self.acc[k][:n].zero_()
         self.clear_counts()
 
     def check_status(self):

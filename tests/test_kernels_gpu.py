@@ -52,17 +52,21 @@ def test_hash_exact():
 
 
 @cuda
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-def test_gather_and_row_grads(dtype):
+@pytest.mark.parametrize("dtype,capacity,hot", [(torch.bfloat16, None, False), (torch.float32, None, False),
+                                                (torch.bfloat16, 517, False), (torch.float32, 517, True)])
+def test_gather_and_row_grads(dtype, capacity, hot):
+    """Row gradients land in the compact accumulator: with a capacity of exactly the lookups
+    per table (the trainer's bound), and with every lookup on 7 hot rows so that many warps
+    race for the same fresh row (slots lost to the race stay empty holes)."""
     from micro_engram_fork_b200.parallel.row_store import RowStore
 
     torch.manual_seed(0)
     rows = [1000, 1000, 3001]
-    st = RowStore(rows, 64, dtype, 0, 1, _dev())
+    st = RowStore(rows, 64, dtype, 0, 1, _dev(), capacity=capacity)
     full = [torch.randn(r, 64) * 0.02 for r in rows]
     for k in range(3):
         st.shard(k).copy_(full[k].to(dtype))
-    idx = torch.stack([torch.randint(0, r, (517,)) for r in rows]).to(_dev())
+    idx = torch.stack([torch.randint(0, 7 if hot else r, (517,)) for r in rows]).to(_dev())
     mem = st.gather(idx, torch.bfloat16)
     ref = torch.cat([full[k].to(dtype)[idx[k].cpu()] for k in range(3)], dim=1)
     assert torch.equal(mem.cpu(), ref.to(torch.bfloat16))
@@ -77,6 +81,9 @@ def test_gather_and_row_grads(dtype):
         assert r.numel() == torch.unique(idx[k]).numel()
         torch.testing.assert_close(gr.cpu(), want[r.cpu()], rtol=1e-5, atol=1e-6)
         assert torch.equal(torch.sort(r.cpu()).values, torch.unique(idx[k].cpu()))
+        assert int((st.pos[k] > 0).sum()) == r.numel()
+    st.zero_grads()
+    assert all(int(st.pos[k].abs().sum()) == 0 and float(st.acc[k].abs().sum()) == 0.0 for k in range(3))
 
 
 def _gate_ref(h, k, v, qs, ks, sqrt_gate, keep=None):
@@ -136,7 +143,7 @@ def test_adam_touched_matches_reference():
 
     torch.manual_seed(0)
     rows, dim = 2000, 64
-    st = RowStore([rows], dim, torch.float32, 0, 1, _dev())
+    st = RowStore([rows], dim, torch.float32, 0, 1, _dev(), capacity=700)
     w0 = torch.randn(rows, dim) * 0.02
     st.shard(0).copy_(w0)
     idx = torch.randint(0, rows, (1, 700), device=_dev())
@@ -144,7 +151,7 @@ def test_adam_touched_matches_reference():
     st.push_grads(g, idx, 1.0)
     m = torch.zeros(rows, dim, device=_dev())
     v = torch.zeros(rows, device=_dev())
-    adam_touched(st.shard(0), m, v, st.acc[0], st.bits[0], st.list[0], st.count[0], None, 1e-2, 0.9, 0.999, 1e-8,
+    adam_touched(st.shard(0), m, v, st.acc[0], st.pos[0], st.list[0], st.count[0], None, 1e-2, 0.9, 0.999, 1e-8,
                  0.0, 1 - 0.9, 1 - 0.999, False, 1, 1, 0)
     # reference: sparse rowwise LazyAdamW on CPU
     p = torch.nn.Parameter(w0.clone())
@@ -156,7 +163,7 @@ def test_adam_touched_matches_reference():
     opt.step()
     torch.testing.assert_close(st.shard(0).cpu(), p.detach(), rtol=1e-5, atol=1e-6)
     torch.testing.assert_close(v.cpu(), opt.state[p]["exp_avg_sq"], rtol=1e-4, atol=1e-9)
-    assert float(st.acc[0].abs().sum()) == 0.0 and int(st.bits[0].abs().sum()) == 0
+    assert float(st.acc[0].abs().sum()) == 0.0 and int(st.pos[0].abs().sum()) == 0
 
 
 @cuda
