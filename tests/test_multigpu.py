@@ -1,6 +1,7 @@
 """Row-sharded engram on 2+ GPUs (NCCL + peer-mapped row stores): the fused gather reads
 rows straight from their owners over NVLink, the backward pushes row gradients into the
-owners' accumulators, and the touched-row Adam updates them. The oracle is the full-table
+owners' compact accumulators (peer atomics claim the slots), and the touched-row Adam
+updates them. The oracle is the full-table
 engram with FSDP-style averaged gradients, run on the same GPUs. Skipped with fewer than 2
 GPUs; every rank runs the same collectives in the same order."""
 import copy
@@ -37,7 +38,8 @@ def _worker(rank, world, port, q):
             full.value.weight.normal_(std=0.05)
         full = full.to(dev).to(torch.bfloat16)
         sh = copy.deepcopy(full)
-        sh.shard_rows(rank, world, device=dev, dtype=torch.bfloat16)
+        # 600 lookups per table per rank and step: the compact accumulators hold 600 x world slots
+        sh.shard_rows(rank, world, device=dev, dtype=torch.bfloat16, row_capacity=600 * world)
         assert sh.row_store is not None and sh.row_store.world == world
         g = torch.Generator().manual_seed(10 + rank)
         ids = torch.randint(3, 500, (2, 300), generator=g).to(dev)
