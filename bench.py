@@ -262,6 +262,7 @@ def run_ours(args):
                                                    " and o-proj kept on the GPU, norms/RoPE/MLP recomputed; none ="
                                                    " nothing recomputed)",
                        "activation_checkpointing_plan": getattr(trainer, "ckpt_plan", None),
+                       "table_moments_on_host": getattr(trainer, "table_moments_on_host", None),
                        "peak_hbm_reserved_gib": round(torch.cuda.max_memory_reserved() / 2 ** 30, 1),
                        "activation_offloading": "layer inputs to pinned host memory, prefetched in the backward",
                        "l2": "inputs larger than L2 (61 GB base streamed per step), no flush"},

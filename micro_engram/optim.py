@@ -44,16 +44,33 @@ class LazyAdamW(torch.optim.Optimizer):
                  stochastic_rounding=True):
         super().__init__(params, dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay, lazy=lazy,
                                       rowwise=rowwise, stochastic_rounding=stochastic_rounding))
+        self.row_moments_on_host = False
 
     @staticmethod
-    def init_state(state, p, group):
-        """Fresh state: exp_avg like p; exp_avg_sq like p, or [rows] fp32 when row-wise."""
+    def _host_moment(p):
+        """Lazy row-store tables can keep their table-sized moments in pinned host memory: the
+        touched-row kernel reads and writes them in place over PCIe (mapped memory), a few
+        rows per step."""
+        return getattr(p, "_row_store", None) is not None and p.is_cuda
+
+    @staticmethod
+    def init_state(state, p, group, on_host=False):
+        """Fresh state: exp_avg like p (pinned host memory with `on_host`); exp_avg_sq like p,
+        or [rows] fp32 when row-wise."""
         state["step"] = torch.zeros((), dtype=torch.float32)
-        state["exp_avg"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+        if on_host:
+            state["exp_avg"] = torch.zeros(p.shape, dtype=p.dtype, pin_memory=True)
+        else:
+            state["exp_avg"] = torch.zeros_like(p, memory_format=torch.preserve_format)
         if group.get("rowwise") and p.dim() >= 2:
             state["exp_avg_sq"] = torch.zeros(p.shape[0], dtype=torch.float32, device=p.device)
+        elif on_host:
+            state["exp_avg_sq"] = torch.zeros(p.shape, dtype=p.dtype, pin_memory=True)
         else:
             state["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+
+    def _on_host(self, p, group):
+        return self.row_moments_on_host and group["lazy"] and self._host_moment(p)
 
     @torch.no_grad()
     def materialize_state(self):
@@ -62,7 +79,28 @@ class LazyAdamW(torch.optim.Optimizer):
         for group in self.param_groups:
             for p in group["params"]:
                 if not self.state[p]:
-                    self.init_state(self.state[p], p, group)
+                    self.init_state(self.state[p], p, group, self._on_host(p, group))
+
+    @torch.no_grad()
+    def move_row_moments_to_host(self):
+        """Move the lazy row-store tables' exp_avg (and a per-value exp_avg_sq), each as large
+        as the tables, to pinned host memory, now and for state created later. Returns the
+        device bytes freed."""
+        self.row_moments_on_host = True
+        freed = 0
+        for group in self.param_groups:
+            for p in group["params"]:
+                st = self.state[p]
+                if not (st and self._on_host(p, group)):
+                    continue
+                for key in ("exp_avg", "exp_avg_sq"):  # exp_avg_sq only when it is per value
+                    t = st[key]
+                    if t.is_cuda and t.shape == p.shape:
+                        host = torch.empty(p.shape, dtype=t.dtype, pin_memory=True)
+                        host.copy_(t)
+                        freed += t.numel() * t.element_size()
+                        st[key] = host
+        return freed
 
     @torch.no_grad()
     def step(self, closure=None):
@@ -92,7 +130,7 @@ class LazyAdamW(torch.optim.Optimizer):
             return
         state = self.state[p]
         if not state:
-            self.init_state(state, p, group)
+            self.init_state(state, p, group, self._on_host(p, group))
         state["step"] += 1
         step = float(state["step"])
         beta1, beta2 = group["betas"]

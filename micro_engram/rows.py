@@ -348,7 +348,7 @@ class RowTables:
                     continue
                 st = self.optimizer.state[p]
                 if not st:
-                    LazyAdamW.init_state(st, p, group)
+                    LazyAdamW.init_state(st, p, group, self.optimizer._on_host(p, group))
                 otempl[f"{key}.exp_avg"] = _dtensor(st["exp_avg"], rows, self.world)
                 saved_dims = len(ometa[f"{key}.exp_avg_sq"].size)
                 sq = st["exp_avg_sq"]

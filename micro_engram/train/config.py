@@ -21,10 +21,15 @@ Keys this framework adds (all optional, defaults keep the reference's behaviour)
   gradient_checkpointing_reserve_gib
                        HBM the auto plan leaves free for the backward's working set, the loss
                        chunks and the allocator (plus 4% of the GPU's memory)
+  table_moments_on_host
+                       true | false | "auto": keep the lazy optimizer's table-sized moments of
+                       the engram tables in pinned host memory (the touched-row update reads
+                       and writes them over PCIe, a few MB per step); auto does so when the
+                       HBM it frees lets the auto checkpointing plan drop recomputation
 """
 import logging
 import os
-from typing import Any, Dict, List, Literal, Optional
+from typing import Any, Dict, List, Literal, Optional, Union
 
 import yaml
 from pydantic import BaseModel, ConfigDict, model_validator
@@ -139,6 +144,7 @@ class TrainConfig(MicroEngramArgs):
     # auto: selective where it fits in HBM, plus no recompute at all for as many layers as still fit
     gradient_checkpointing_policy: Literal["full", "selective", "auto"] = "full"
     gradient_checkpointing_reserve_gib: float = 23.0
+    table_moments_on_host: Union[bool, Literal["auto"]] = "auto"
     activation_offloading: bool = False
     no_grad_prefix: bool = True
     sharded_vocab: bool = True

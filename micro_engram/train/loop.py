@@ -180,10 +180,24 @@ class Trainer:
                               sparse_grads=bool(cfg.sparse_row_grads and opt in ("lazy_adam", "rowwise_adam")))
         if cfg.optimizer and not str(cfg.optimizer).startswith("adamw"):
             _log0(f"[micro_engram] optimizer: {cfg.optimizer} is not used; key/value/scales use AdamW")
-        if self.device.type == "cuda" and self.rows.optimizer is not None:
-            self.rows.optimizer.materialize_state()  # the tables' Adam state counts in memory planning
+        ropt = self.rows.optimizer if self.device.type == "cuda" else None
+        host_moments = cfg.table_moments_on_host
+        if ropt is not None:
+            if host_moments is True:
+                ropt.row_moments_on_host = True
+            ropt.materialize_state()  # the tables' Adam state counts in memory planning
         if cfg.gradient_checkpointing and cfg.gradient_checkpointing_policy == "auto" and self.device.type == "cuda":
             self._plan_checkpointing(no_grad_upto)
+            trained = sum(self.ckpt_plan.values())
+            if ropt is not None and host_moments == "auto" and self.ckpt_plan["none"] < trained:
+                # HBM is short of keeping every layer's activations: the table moments go to
+                # pinned host memory (same decision on every rank: the plan is min over ranks)
+                freed = ropt.move_row_moments_to_host()
+                torch.cuda.empty_cache()
+                _log0(f"[micro_engram] table optimizer moments -> pinned host memory ({freed / 2**30:.1f} GiB "
+                      f"of HBM freed); re-planning")
+                self._plan_checkpointing(no_grad_upto)
+        self.table_moments_on_host = bool(ropt is not None and ropt.row_moments_on_host)
         self.total_steps = self._count_steps()
         self.scheduler = self._scheduler()
         self.offload = ActivationOffload(self.device) if (cfg.activation_offloading and self.device.type == "cuda") \

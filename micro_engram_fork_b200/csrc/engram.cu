@@ -892,6 +892,19 @@ void engram_adam_touched(torch::Tensor p, torch::Tensor m, torch::Tensor v, torc
   const int dim = (int)p.size(1);
   TORCH_CHECK(dim <= 256, "engram dim above 256 is not supported by the touched-row Adam");
   TORCH_CHECK(m.scalar_type() == p.scalar_type(), "exp_avg must have the weight dtype");
+  TORCH_CHECK(m.is_contiguous() && m.numel() == p.numel(), "exp_avg must be contiguous and shaped like the table");
+  // moments on this GPU, or in pinned host memory that the kernel reads and writes in place
+  // through its device mapping (only the touched rows cross PCIe)
+  auto device_view = [](const torch::Tensor& t, const char* name) -> void* {
+    if (t.is_cuda()) return t.data_ptr();
+    TORCH_CHECK(t.is_pinned(), name, " must live on the GPU or in pinned host memory");
+    cudaPointerAttributes attr;
+    C10_CUDA_CHECK(cudaPointerGetAttributes(&attr, t.data_ptr()));
+    TORCH_CHECK(attr.type == cudaMemoryTypeHost && attr.devicePointer != nullptr, name,
+                ": pinned host memory without a device mapping");
+    return attr.devicePointer;
+  };
+  void* m_dev = device_view(m, "exp_avg");
   const bool rowwise = v.dim() == 1;
   TORCH_CHECK(rowwise ? v.scalar_type() == torch::kFloat32 : v.scalar_type() == p.scalar_type(),
               "exp_avg_sq dtype");
@@ -903,17 +916,19 @@ void engram_adam_touched(torch::Tensor p, torch::Tensor m, torch::Tensor v, torc
   auto stream = at::cuda::getCurrentCUDAStream();
   const float* cp = coef.has_value() ? coef->data_ptr<float>() : nullptr;
   const float bc2s = (float)std::sqrt(bc2);
-  float* vrow = rowwise ? v.data_ptr<float>() : nullptr;
+  TORCH_CHECK(!rowwise || v.is_cuda(), "a row-wise exp_avg_sq stays on the GPU");
+  void* v_dev = device_view(v, "exp_avg_sq");
+  float* vrow = rowwise ? reinterpret_cast<float*>(v_dev) : nullptr;
   if (p.scalar_type() == torch::kBFloat16) {
     adam_touched_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, threads, 0, stream>>>(
-        reinterpret_cast<__nv_bfloat16*>(p.data_ptr()), reinterpret_cast<__nv_bfloat16*>(m.data_ptr()), vrow,
-        rowwise ? nullptr : reinterpret_cast<__nv_bfloat16*>(v.data_ptr()), acc.data_ptr<float>(),
+        reinterpret_cast<__nv_bfloat16*>(p.data_ptr()), reinterpret_cast<__nv_bfloat16*>(m_dev), vrow,
+        rowwise ? nullptr : reinterpret_cast<__nv_bfloat16*>(v_dev), acc.data_ptr<float>(),
         pos.data_ptr<int>(), list.data_ptr<int>(), cnt.data_ptr<int>(), cap, dim, cp, (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd, (float)bc1, bc2s, sr ? 1 : 0,
         (uint32_t)seed, (uint32_t)step, (uint32_t)table_id);
   } else {
     TORCH_CHECK(p.scalar_type() == torch::kFloat32, "tables must be bf16 or fp32");
     adam_touched_kernel<float, float><<<grid, threads, 0, stream>>>(
-        p.data_ptr<float>(), m.data_ptr<float>(), vrow, rowwise ? nullptr : v.data_ptr<float>(),
+        p.data_ptr<float>(), reinterpret_cast<float*>(m_dev), vrow, rowwise ? nullptr : reinterpret_cast<float*>(v_dev),
         acc.data_ptr<float>(), pos.data_ptr<int>(), list.data_ptr<int>(), cnt.data_ptr<int>(), cap, dim, cp, (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd,
         (float)bc1, bc2s, 0, (uint32_t)seed, (uint32_t)step, (uint32_t)table_id);
   }

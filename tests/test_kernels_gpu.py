@@ -167,6 +167,39 @@ def test_adam_touched_matches_reference():
 
 
 @cuda
+@pytest.mark.parametrize("rowwise", [True, False])
+def test_adam_touched_host_moments_match_device(rowwise):
+    """The touched-row AdamW with its table-sized moments in pinned host memory (read and
+    written in place through the device mapping) gives bit-identical weights and moments."""
+    from micro_engram_fork_b200.ops.engram import adam_touched
+    from micro_engram_fork_b200.parallel.row_store import RowStore
+
+    torch.manual_seed(0)
+    rows, dim = 3000, 64
+    idx = torch.randint(0, rows, (1, 900), device=_dev())
+    g = torch.randn(900, dim, device=_dev()).to(torch.bfloat16)
+    w0 = (torch.randn(rows, dim) * 0.02).to(torch.bfloat16)
+    m0 = (torch.randn(rows, dim) * 0.01).to(torch.bfloat16)
+    v0 = torch.rand(rows) * 1e-4 if rowwise else (torch.rand(rows, dim) * 1e-4).to(torch.bfloat16)
+    out = []
+    for host in (False, True):
+        st = RowStore([rows], dim, torch.bfloat16, 0, 1, _dev(), capacity=900)
+        st.shard(0).copy_(w0)
+        m, v = m0.clone(), v0.clone()
+        m = m.pin_memory() if host else m.to(_dev())
+        v = v.to(_dev()) if (rowwise or not host) else v.pin_memory()
+        for step in (1, 2):
+            st.push_grads(g, idx, 1.0)
+            adam_touched(st.shard(0), m, v, st.acc[0], st.pos[0], st.list[0], st.count[0], None, 1e-2, 0.9, 0.999,
+                         1e-8, 0.01, 1 - 0.9 ** step, 1 - 0.999 ** step, True, 5, step, 0)
+            st.count[0].zero_()
+        torch.cuda.synchronize()
+        out.append((st.shard(0).cpu().clone(), m.cpu().clone(), v.cpu().clone()))
+    for a, b in zip(out[0], out[1]):
+        assert torch.equal(a, b)
+
+
+@cuda
 def test_stochastic_rounding_unbiased():
     from micro_engram_fork_b200.ops.engram import adam_dense
 
