@@ -489,51 +489,64 @@ __global__ void __launch_bounds__(256) qkv_norm_rope_bwd_kernel(
 }
 
 // ---------------------------------------------------------------------------- GeGLU
-// gu [N, 2F] = [gate | up]; m = bf16(bf16(gelu_tanh(gate)) * up)
-ME_DEVICE float gelu_tanh(float x) {
+// gu [N, 2F] = [gate | up]; m = bf16(bf16(gelu_tanh(gate)) * up).
+// gelu_tanh(x) = 0.5 x (1 + tanh(y)), y = k0 (x + k1 x^3), evaluated as x * s with
+// s = 0.5 (1 + tanh(y)) = 1 / (1 + e^{-2y}): one exponential and one division per element
+// (and s -> 0 without cancellation for very negative x). Its derivative:
+// s + x * 0.5 (1 - tanh^2 y) y' = s + 2 x s (1 - s) k0 (1 + 3 k1 x^2).
+ME_DEVICE float gelu_gate(float x) {
   const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-  return 0.5f * x * (1.f + tanhf(k0 * (x + k1 * x * x * x)));
+  const float y = k0 * (x + k1 * x * x * x);
+  return __fdividef(1.f, 1.f + __expf(-2.f * y));
 }
+ME_DEVICE float gelu_tanh(float x) { return x * gelu_gate(x); }
 ME_DEVICE float gelu_tanh_grad(float x) {
   const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-  const float t = tanhf(k0 * (x + k1 * x * x * x));
-  return 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * k0 * (1.f + 3.f * k1 * x * x);
+  const float s = gelu_gate(x);
+  return s + 2.f * x * s * (1.f - s) * k0 * (1.f + 3.f * k1 * x * x);
 }
 
+// One block per row (grid-stride over rows), 16-byte vectors along the row: no index division.
 __global__ void geglu_fwd_kernel(const bf16* __restrict__ gu, int64_t N, int F, bf16* __restrict__ m) {
   const int fv = F / 8;
-  const int64_t total = N * fv;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t n = i / fv;
-    const int c = (int)(i % fv);
-    BF16x8 g, u, o;
-    g.u = reinterpret_cast<const uint4*>(gu + n * 2 * F)[c];
-    u.u = reinterpret_cast<const uint4*>(gu + n * 2 * F + F)[c];
+  for (int64_t n = blockIdx.x; n < N; n += gridDim.x) {
+    const uint4* gp = reinterpret_cast<const uint4*>(gu + n * 2 * F);
+    const uint4* up = gp + fv;
+    uint4* op = reinterpret_cast<uint4*>(m + n * F);
+    for (int c = threadIdx.x; c < fv; c += blockDim.x) {
+      BF16x8 g, u, o;
+      g.u = gp[c];
+      u.u = up[c];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) o.h[e] = f2bf(bf2f(f2bf(gelu_tanh(bf2f(g.h[e])))) * bf2f(u.h[e]));
-    reinterpret_cast<uint4*>(m + n * F)[c] = o.u;
+      for (int e = 0; e < 8; ++e) o.h[e] = f2bf(bf2f(f2bf(gelu_tanh(bf2f(g.h[e])))) * bf2f(u.h[e]));
+      op[c] = o.u;
+    }
   }
 }
 
 __global__ void geglu_bwd_kernel(const bf16* __restrict__ dm, const bf16* __restrict__ gu, int64_t N, int F,
                                  bf16* __restrict__ dgu) {
   const int fv = F / 8;
-  const int64_t total = N * fv;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t n = i / fv;
-    const int c = (int)(i % fv);
-    BF16x8 g, u, d, og, ou;
-    g.u = reinterpret_cast<const uint4*>(gu + n * 2 * F)[c];
-    u.u = reinterpret_cast<const uint4*>(gu + n * 2 * F + F)[c];
-    d.u = reinterpret_cast<const uint4*>(dm + n * F)[c];
+  for (int64_t n = blockIdx.x; n < N; n += gridDim.x) {
+    const uint4* gp = reinterpret_cast<const uint4*>(gu + n * 2 * F);
+    const uint4* up = gp + fv;
+    const uint4* dp = reinterpret_cast<const uint4*>(dm + n * F);
+    uint4* ogp = reinterpret_cast<uint4*>(dgu + n * 2 * F);
+    uint4* oup = ogp + fv;
+    for (int c = threadIdx.x; c < fv; c += blockDim.x) {
+      BF16x8 g, u, d, og, ou;
+      g.u = gp[c];
+      u.u = up[c];
+      d.u = dp[c];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float x = bf2f(g.h[e]), up = bf2f(u.h[e]), dd = bf2f(d.h[e]);
-      og.h[e] = f2bf(dd * up * gelu_tanh_grad(x));
-      ou.h[e] = f2bf(dd * bf2f(f2bf(gelu_tanh(x))));
+      for (int e = 0; e < 8; ++e) {
+        const float x = bf2f(g.h[e]), upv = bf2f(u.h[e]), dd = bf2f(d.h[e]);
+        og.h[e] = f2bf(dd * upv * gelu_tanh_grad(x));
+        ou.h[e] = f2bf(dd * bf2f(f2bf(gelu_tanh(x))));
+      }
+      ogp[c] = og.u;
+      oup[c] = ou.u;
     }
-    reinterpret_cast<uint4*>(dgu + n * 2 * F)[c] = og.u;
-    reinterpret_cast<uint4*>(dgu + n * 2 * F + F)[c] = ou.u;
   }
 }
 
@@ -725,8 +738,7 @@ torch::Tensor geglu_fwd(torch::Tensor gu) {
   auto m = torch::empty(sizes, gu.options());
   if (N == 0) return m;
   const int threads = 256;
-  const int64_t work = N * (F / 8);
-  const int grid = (int)std::min<int64_t>((work + threads - 1) / threads, (int64_t)sm_count() * 8);
+  const int grid = (int)std::min<int64_t>(N, (int64_t)sm_count() * 8);
   geglu_fwd_kernel<<<grid, threads, 0, at::cuda::getCurrentCUDAStream()>>>(CBFP(gu), N, F, BFP(m));
   return m;
 }
@@ -740,8 +752,7 @@ torch::Tensor geglu_bwd(torch::Tensor dm, torch::Tensor gu) {
   auto dgu = torch::empty_like(gu);
   if (N == 0) return dgu;
   const int threads = 256;
-  const int64_t work = N * (F / 8);
-  const int grid = (int)std::min<int64_t>((work + threads - 1) / threads, (int64_t)sm_count() * 8);
+  const int grid = (int)std::min<int64_t>(N, (int64_t)sm_count() * 8);
   geglu_bwd_kernel<<<grid, threads, 0, at::cuda::getCurrentCUDAStream()>>>(CBFP(dmc), CBFP(gu), N, F, BFP(dgu));
   return dgu;
 }

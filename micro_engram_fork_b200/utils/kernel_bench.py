@@ -3,7 +3,7 @@ events (warm-up, synchronize on both sides) and reported against the measured ro
 (MEASURED_PEAKS.json: cuBLAS bf16 burst TFLOP/s and copy bandwidth; the recipe's fallback
 figures otherwise). Also the workload that the committed ncu summaries in profiles/ capture.
 
-  python -m micro_engram_fork_b200.utils.kernel_bench [--case all|gemm|attn_fwd|attn_bwd|gate|ce|qkv] [--iters N]
+  python -m micro_engram_fork_b200.utils.kernel_bench [--case all|gemm|attn_fwd|attn_bwd|gate|ce|qkv|geglu] [--iters N]
 """
 import argparse
 import json
@@ -165,8 +165,25 @@ def case_qkv(C, dev, it, pk):
     return r
 
 
+def case_geglu(C, dev, it, pk):
+    """GeGLU forward and backward on one 8192-token step of the 31B-class MLP (F = 21504)."""
+    N, F = 8192, 21504
+    gu = torch.randn(N, 2 * F, device=dev).to(torch.bfloat16)
+    dm = torch.randn(N, F, device=dev).to(torch.bfloat16)
+    fwd_bytes = N * 2 * F * 2 + N * F * 2
+    bwd_bytes = N * 2 * F * 2 + N * F * 2 + N * 2 * F * 2
+    r = {}
+    ms = _time(lambda: C.geglu_fwd(gu), it)
+    r["geglu fwd"] = {"ms": round(ms, 4), "gbs": round(fwd_bytes / ms / 1e6, 1),
+                      "frac_of_hbm": round(fwd_bytes / ms / 1e6 / pk["hbm_gbs"], 3)}
+    ms = _time(lambda: C.geglu_bwd(dm, gu), it)
+    r["geglu bwd"] = {"ms": round(ms, 4), "gbs": round(bwd_bytes / ms / 1e6, 1),
+                      "frac_of_hbm": round(bwd_bytes / ms / 1e6 / pk["hbm_gbs"], 3)}
+    return r
+
+
 CASES = {"gemm": case_gemm, "attn_fwd": case_attn_fwd, "attn_bwd": case_attn_bwd, "gate": case_gate, "ce": case_ce,
-         "qkv": case_qkv}
+         "qkv": case_qkv, "geglu": case_geglu}
 
 
 def main(argv=None):
