@@ -55,6 +55,10 @@ class VocabShard:
         self.softcap = softcap
         fit = max(64, chunk_bytes // max(1, world * self.per * 4))
         self.chunk = max(1, min(chunk_tokens, fit))
+        # the CUDA path keeps each chunk's logits in bf16 (and overwrites them with their
+        # gradient): 1 GiB of logits per chunk, i.e. 2048-token chunks at the benchmark vocab
+        fit16 = max(64, (1 << 30) // max(1, world * self.per * 2))
+        self.chunk_bf16 = max(1, min(chunk_tokens, fit16))
 
     @property
     def group(self):
@@ -88,7 +92,7 @@ class VocabShard:
         count = (labels != IGNORE).sum()
         labels = labels.to(hidden.device)
         if use_native(hidden) and self.weight.dtype == torch.bfloat16:
-            total = _FusedVocabCE.apply(hidden, labels, self)
+            total = _FusedVocabCE.apply(hidden, labels, self, torch.is_grad_enabled() and hidden.requires_grad)
         else:
             total = _VocabParallelCE.apply(hidden, labels, self)
         return total, count
@@ -186,25 +190,30 @@ class _VocabParallelCE(torch.autograd.Function):
 
 
 class _FusedVocabCE(torch.autograd.Function):
-    """CUDA path: bf16 logits GEMM + one-pass softcap/LSE row kernel; in-place gradient."""
+    """CUDA path: bf16 logits GEMM + one-pass softcap/LSE row kernel, and, in the same pass over
+    each chunk, the gradient: the logits are overwritten in place with (softmax - onehot) *
+    softcap' (unscaled), multiplied into dH with fp32 output and reduce-scattered to the
+    token's rank. The backward only scales this rank's dH rows by the incoming gradient (the
+    loss is linear in it, and reduce-scatter keeps each token's row on its own rank), so the
+    logits GEMM runs once per chunk instead of twice."""
 
     @staticmethod
-    def forward(ctx, hidden, labels, shard):
+    def forward(ctx, hidden, labels, shard, need_grad):
         from micro_engram_fork_b200 import native
 
         C = native()
         world, group, w = shard.world, shard.group, shard.weight
-        N, c = hidden.shape[0], shard.chunk
+        N, c = hidden.shape[0], shard.chunk_bf16
         cap = float(shard.softcap or 0.0)
         h = hidden.detach().to(w.dtype)
-        lses, total = [], torch.zeros((), dtype=torch.float32, device=hidden.device)
+        total = torch.zeros((), dtype=torch.float32, device=hidden.device)
+        dh = torch.empty(N, shard.d, dtype=torch.float32, device=hidden.device) if need_grad else None
         for a in range(0, N, c):
             b = min(N, a + c)
             H = _gather(h[a:b], group, world)
             L = _gather(labels[a:b].contiguous(), group, world)
             z = H @ w.t()
             m, s, tgt = C.ce_fwd(z, L, shard.start, cap)
-            del z
             if world > 1:
                 M = m.clone()
                 dist.all_reduce(M, op=dist.ReduceOp.MAX, group=group)
@@ -216,38 +225,18 @@ class _FusedVocabCE(torch.autograd.Function):
             own = slice(shard.rank * n, (shard.rank + 1) * n)
             valid = L[own] != IGNORE
             total = total + torch.where(valid, lse[own] - tgt[own], torch.zeros_like(lse[own])).sum()
-            lses.append(lse)
-        ctx.shard = shard
-        ctx.save_for_backward(hidden.detach(), labels, *lses)
+            if need_grad:
+                C.ce_bwd_inplace(z, L, shard.start, cap, lse, (L != IGNORE).float())
+                dH = torch.mm(z, w, out_dtype=torch.float32)
+                dh[a:b] = _reduce_scatter(dH, n, shard.d, group, world)
+            del z
+        ctx.dh, ctx.hdtype = dh, hidden.dtype
         return total
 
     @staticmethod
     def backward(ctx, g):
-        from micro_engram_fork_b200 import native
-
-        C = native()
-        shard = ctx.shard
-        hidden, labels, *lses = ctx.saved_tensors
-        world, group, w = shard.world, shard.group, shard.weight
-        N, c = hidden.shape[0], shard.chunk
-        cap = float(shard.softcap or 0.0)
-        gs = _gather(g.detach().float().reshape(1), group, world)
-        h = hidden.to(w.dtype)
-        grad = torch.empty(N, shard.d, dtype=hidden.dtype, device=hidden.device)
-        for k, a in enumerate(range(0, N, c)):
-            b = min(N, a + c)
-            n = b - a
-            H = _gather(h[a:b], group, world)
-            L = _gather(labels[a:b].contiguous(), group, world)
-            z = H @ w.t()
-            w_row = gs.repeat_interleave(n) * (L != IGNORE).float()
-            C.ce_bwd_inplace(z, L, shard.start, cap, lses[k], w_row)
-            if world > 1:
-                dH = torch.matmul(z, w).float()
-                grad[a:b] = _reduce_scatter(dH, n, shard.d, group, world).to(grad.dtype)
-            else:
-                grad[a:b] = torch.matmul(z, w).to(grad.dtype)
-        return grad, None, None
+        dh, ctx.dh = ctx.dh, None
+        return (dh * g.float()).to(ctx.hdtype), None, None, None
 
 
 def reference_loss_sum(hidden, labels, weight, softcap=None):
