@@ -224,7 +224,9 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     const int ds_t = t < T ? doc_start[t] : 0;
     const int lo = window > 0 ? max(ds_t, t - window + 1) : ds_t;
-    float m_used = -INFINITY, l = 0.f;  // l: this half's share of the row sum
+    // scores are kept in log2 units: p = 2^(s * scale * log2(e) - m), one FFMA + one ex2 per key
+    const float sl2 = scale * 1.4426950408889634f;
+    float m_used = -INFINITY, l = 0.f;  // m_used in log2 units; l: this half's share of the row sum
     bool ok = true;
     for (int j = 0; j < nkb && ok; ++j) {
       const int b = j & 1, kb = kb_first + j * BN + half * HB;
@@ -238,13 +240,16 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_before();
       mbar_arrive(&s_free[b]);
       float mx = -INFINITY;
+      if (t < T && kb >= lo && kb + HB - 1 <= t) {  // every key of this half-block is visible
 #pragma unroll
-      for (int c = 0; c < HB; ++c) {
-        const int sc = kb + c;
-        float x = s[c] * scale;
-        if (t >= T || sc > t || sc < lo || sc >= T) x = -INFINITY;
-        s[c] = x;
-        mx = fmaxf(mx, x);
+        for (int c = 0; c < HB; ++c) mx = fmaxf(mx, s[c]);
+      } else {
+#pragma unroll
+        for (int c = 0; c < HB; ++c) {
+          const int sc = kb + c;
+          if (t >= T || sc > t || sc < lo) s[c] = -INFINITY;  // sc <= t < T: the key exists
+          mx = fmaxf(mx, s[c]);
+        }
       }
       red[((j & 1) * 2 + half) * BM + r] = mx;
       mbar_arrive(&pair[q]);
@@ -252,25 +257,30 @@ __global__ void __launch_bounds__(320, 1)
         ok = false;
         break;
       }
-      mx = fmaxf(mx, red[((j & 1) * 2 + (half ^ 1)) * BM + r]);
+      mx = fmaxf(mx, red[((j & 1) * 2 + (half ^ 1)) * BM + r]) * sl2;  // raw max -> log2 units
       float m_new = m_used, alpha = 1.f;
       bool resc = false;
       if (mx > -INFINITY) {
         if (m_used == -INFINITY) {
           m_new = mx;
           alpha = 0.f;  // nothing accumulated yet (l = 0, O rows are zero)
-        } else if (mx > m_used + 8.f) {
+        } else if (mx > m_used + 11.5415602f) {  // grew by more than e^8
           m_new = mx;
-          alpha = __expf(m_used - m_new);
+          alpha = ex2_approx(m_used - m_new);
           resc = true;
         }
       }
       float sum = 0.f;
+      if (m_new == -INFINITY) {  // nothing visible yet on this row
 #pragma unroll
-      for (int c = 0; c < HB; ++c) {
-        const float p = (s[c] == -INFINITY) ? 0.f : __expf(s[c] - m_new);
-        s[c] = p;
-        sum += p;
+        for (int c = 0; c < HB; ++c) s[c] = 0.f;
+      } else {
+#pragma unroll
+        for (int c = 0; c < HB; ++c) {
+          const float p = ex2_approx(fmaf(s[c], sl2, -m_new));  // masked keys: 2^-inf = 0
+          s[c] = p;
+          sum += p;
+        }
       }
       l = l * alpha + sum;
       m_used = m_new;
@@ -305,7 +315,7 @@ __global__ void __launch_bounds__(320, 1)
       for (int c8 = 0; c8 < HB / 8; ++c8) {
         BF16x8 pk;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) pk.h[e] = f2bf(s[c8 * 8 + e]);
+        for (int e = 0; e < 4; ++e) pk.h2[e] = __floats2bfloat162_rn(s[c8 * 8 + 2 * e], s[c8 * 8 + 2 * e + 1]);
         const int chunk = half * (HB / 8) + c8;
         const uint32_t addr = prow + ((chunk ^ (r & 7)) << 4);
         asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk.u.x), "r"(pk.u.y), "r"(pk.u.z),
@@ -343,7 +353,7 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
       }
-      if (blockIdx.z == 0 && half == 0 && t < T) lse[(int64_t)h * T + t] = m_used + logf(l);
+      if (blockIdx.z == 0 && half == 0 && t < T) lse[(int64_t)h * T + t] = (m_used + log2f(l)) * 0.6931471805599453f;
     }
   }
   tc_fence_before();
@@ -1105,10 +1115,12 @@ __global__ void __launch_bounds__(320, 1)
     const int qq = warp & 3, half = (warp - 2) >> 2;
     const int r = qq * 32 + lane, row = i * MT + r;
     const uint32_t lane_base = (uint32_t)(qq * 32) << 16;
-    float lse_r = 0.f, delta_r = 0.f;
+    // p = 2^(s * scale * log2(e) - lse * log2(e)): one FFMA + one ex2 per element
+    const float sl2 = scale * 1.4426950408889634f;
+    float lse2 = INFINITY, delta_r = 0.f;  // rows past T: p = 2^-inf = 0
     int lo_r = 0;
     if (row < T) {
-      lse_r = lse[(int64_t)h * Tp + row];
+      lse2 = lse[(int64_t)h * Tp + row] * 1.4426950408889634f;
       delta_r = delta[(int64_t)h * Tp + row];
       lo_r = ds[row];
       if (window > 0) lo_r = max(lo_r, row - window + 1);
@@ -1125,17 +1137,22 @@ __global__ void __launch_bounds__(320, 1)
         float sv[32], dp[32];
         tmem_ld32(tmem + lane_base + b * 256 + half * 64 + sub * 32, sv);
         tmem_ld32(tmem + lane_base + b * 256 + 128 + half * 64 + sub * 32, dp);
+        const int k0 = j * MT + half * 64 + sub * 32;
+        if (!(k0 >= lo_r && k0 + 31 <= row)) {  // not every key visible: mask (rows past T have lse2 = inf)
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            if (k0 + c > row || k0 + c < lo_r) sv[c] = -INFINITY;
+        }
 #pragma unroll
         for (int u4 = 0; u4 < 4; ++u4) {
           BF16x8 pk, dk;
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int cidx = u4 * 8 + e;
-            const int key = j * MT + half * 64 + sub * 32 + cidx;
-            const bool valid = row < T && key <= row && key >= lo_r;
-            const float p = valid ? __expf(sv[cidx] * scale - lse_r) : 0.f;
-            pk.h[e] = f2bf(p);
-            dk.h[e] = f2bf(p * (dp[cidx] - delta_r));
+          for (int e = 0; e < 4; ++e) {
+            const int c0 = u4 * 8 + 2 * e;
+            const float p0 = ex2_approx(fmaf(sv[c0], sl2, -lse2));
+            const float p1 = ex2_approx(fmaf(sv[c0 + 1], sl2, -lse2));
+            pk.h2[e] = __floats2bfloat162_rn(p0, p1);
+            dk.h2[e] = __floats2bfloat162_rn(p0 * (dp[c0] - delta_r), p1 * (dp[c0 + 1] - delta_r));
           }
           const int u = sub * 4 + u4;
           const int pos = (u ^ (r & 7)) << 4;
