@@ -155,6 +155,7 @@ def count_launches(trainer, micro):
             "qkv_norm_rope_bwd_kernel", "geglu_fwd_kernel", "geglu_bwd_kernel", "ce_fwd_kernel", "ce_bwd_kernel",
             "attn_fwd_kernel", "attn_fwd_tc_kernel", "attn_bwd_pre_kernel", "attn_bwd_dkdv_kernel",
             "attn_bwd_dq_kernel", "attn_bwd_tc_kernel", "attn_delta_kernel", "doc_end_from_start_kernel",
+            "attn_tiles_kernel", "attn_bwd_sdp_kernel", "attn_bwd_acc_kernel",
             "gemm_tc_kernel", "nf4_dequant_kernel", "nf4_quantize_kernel")
     pat = re.compile(r"\b(" + "|".join(ours) + r")\b")
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
