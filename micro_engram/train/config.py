@@ -21,6 +21,8 @@ Keys this framework adds (all optional, defaults keep the reference's behaviour)
   gradient_checkpointing_reserve_gib
                        HBM the auto plan leaves free for the backward's working set, the loss
                        chunks and the allocator (plus 4% of the GPU's memory)
+  dense_allreduce      "p2p" (default on CUDA with 2+ GPUs: one kernel signals, waits and sums
+                       every rank's gradients straight out of its memory over NVLink) or "nccl"
   table_moments_on_host
                        true | false | "auto": keep the lazy optimizer's table-sized moments of
                        the engram tables in pinned host memory (the touched-row update reads
@@ -145,6 +147,7 @@ class TrainConfig(MicroEngramArgs):
     gradient_checkpointing_policy: Literal["full", "selective", "auto"] = "full"
     gradient_checkpointing_reserve_gib: float = 23.0
     table_moments_on_host: Union[bool, Literal["auto"]] = "auto"
+    dense_allreduce: Literal["p2p", "nccl"] = "nccl"
     activation_offloading: bool = False
     no_grad_prefix: bool = True
     sharded_vocab: bool = True

@@ -336,6 +336,23 @@ class Trainer:
         return self.scheduler.lr_lambdas[0](self.scheduler.last_epoch)
 
     def _reduce_dense(self):
+        """Mean of the replicated dense parameters' gradients over ranks (fp32). CUDA with
+        dense_allreduce: p2p: the fused peer-memory kernel over every dense parameter (a rank
+        without a gradient contributes zeros; only existing gradients are overwritten);
+        otherwise one flat NCCL all_reduce."""
+        if self.world > 1 and self.device.type == "cuda" and self.cfg.dense_allreduce == "p2p" and self.dense:
+            if getattr(self, "_p2p_ar", None) is None:
+                from micro_engram_fork_b200.parallel.allreduce import P2PAllReduce
+
+                self._p2p_ar = P2PAllReduce(sum(p.numel() for p in self.dense), self.device)
+            flat = self._p2p_ar([p.grad if p.grad is not None else torch.zeros_like(p) for p in self.dense])
+            k = 0
+            for p in self.dense:
+                n = p.numel()
+                if p.grad is not None:
+                    p.grad.copy_(flat[k:k + n].view_as(p.grad))
+                k += n
+            return
         grads = [p.grad for p in self.dense if p.grad is not None]
         if not grads:
             return
@@ -399,6 +416,8 @@ class Trainer:
                     store = slot.engram.__dict__.get("row_store")
                     if store is not None:
                         store.check_status()
+                if getattr(self, "_p2p_ar", None) is not None:
+                    self._p2p_ar.check_status()
                 logs.update(self._memory())
                 logs.update(self._engram_logs())
                 logs.update({"epoch": round(self.epoch + self.step_in_epoch / max(1, n_ep), 4),

@@ -67,6 +67,8 @@ torch::Tensor attn_tc_status(int64_t device);
 std::vector<torch::Tensor> attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                        torch::Tensor o, torch::Tensor lse, torch::Tensor doc_start, int64_t window,
                                        double scale);
+void p2p_allreduce_mean(torch::Tensor bases, int64_t rank, int64_t stage_off, int64_t n, int64_t call, double scale,
+                        double timeout_s, torch::Tensor out, torch::Tensor status);
 std::vector<torch::Tensor> attn_bwd_mat(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                         torch::Tensor o, torch::Tensor lse, torch::Tensor doc_start, int64_t window,
                                         double scale, int64_t tile_budget_bytes);
@@ -114,6 +116,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_tc_status", &attn_tc_status);
   m.def("attn_bwd_tc", &attn_bwd_tc);
   m.def("attn_bwd_mat", &attn_bwd_mat);
+  m.def("p2p_allreduce_mean", &p2p_allreduce_mean);
   m.def("gemm_tc", &gemm_tc, py::arg("A"), py::arg("B"), py::arg("block_n") = 256);
   m.def("gemm_status", &gemm_status);
   m.def("nf4_quantize", &nf4_quantize);

@@ -1,0 +1,108 @@
+// One-shot all-reduce (mean) of the replicated dense engram gradients over peer memory
+// (CUDA IPC mappings of every rank's symmetric buffer, NVLink 5 / NVSwitch), in ONE kernel:
+// signal, wait, reduce. It replaces the flat fp32 NCCL all_reduce / world of the reference
+// (micro_engram/train/loop.py:316-327); the semantics (sum over ranks, then / world, in fp32)
+// are the same.
+//
+// Buffer layout on every rank (same offsets everywhere):
+//   flags  [world] u32 at offset 0: flags[r] = last call number rank r has staged
+//   stage  [2][np] fp32 at offset `stage_off`, np = n rounded up to a multiple of 4 so both
+//          halves start 16-byte aligned for the float4 loads: the caller packs its gradients into
+//          stage[call & 1] before the kernel (double buffering: a rank can be at most one call
+//          ahead of a peer that is still reading, since call c+1 cannot finish before every
+//          peer has signalled c+1, which each does only after finishing call c)
+// Every block of the kernel: (1) release-stores `call` into flags[rank] of every peer (idempotent,
+// so no block depends on another block being scheduled), (2) waits with acquire loads until
+// every flags[r] >= call, at most `timeout_ns` (then records ME_ERR_TIMEOUT and returns without
+// writing), (3) sums its slice of stage[call & 1] over all ranks (L2-only loads: no stale L1
+// lines from the call two steps back) and writes out = sum * scale.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+using namespace me;
+
+namespace {
+
+ME_DEVICE void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+ME_DEVICE uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+constexpr int MAX_RANKS = 16;
+
+__global__ void __launch_bounds__(256) p2p_allreduce_mean_kernel(const int64_t* __restrict__ bases, int world,
+                                                                  int rank, int64_t stage_off, int64_t n,
+                                                                  uint32_t call, float scale, uint64_t timeout_ns,
+                                                                  float* __restrict__ out, int* status) {
+  __shared__ int failed;
+  if (threadIdx.x == 0) failed = 0;
+  __syncthreads();
+  if (threadIdx.x < world) {
+    uint32_t* peer_flags = reinterpret_cast<uint32_t*>(bases[threadIdx.x]);
+    st_release_sys(peer_flags + rank, call);
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(bases[rank]) + threadIdx.x;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 0;; ++it) {
+      if ((int32_t)(ld_acquire_sys(mine) - call) >= 0) break;
+      if ((it & 63u) == 63u && globaltimer_ns() - t0 > timeout_ns) {
+        report(status, ME_ERR_TIMEOUT, threadIdx.x);
+        failed = 1;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (failed) return;
+  const int64_t par = (int64_t)(call & 1u) * ((n + 3) / 4 * 4);  // half stride np: 16-byte aligned
+  const float* src[MAX_RANKS];
+#pragma unroll
+  for (int r = 0; r < MAX_RANKS; ++r)
+    src[r] = r < world ? reinterpret_cast<const float*>(bases[r] + stage_off) + par : nullptr;
+  const int64_t n4 = n / 4;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 0; r < world; ++r) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(src[r]) + i);
+      acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
+    }
+    reinterpret_cast<float4*>(out)[i] = make_float4(acc.x * scale, acc.y * scale, acc.z * scale, acc.w * scale);
+  }
+  for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float acc = 0.f;
+    for (int r = 0; r < world; ++r) acc += __ldcg(src[r] + i);
+    out[i] = acc * scale;
+  }
+}
+
+}  // namespace
+
+// out[n] fp32 = (sum over ranks of their stage[call & 1][:n]) * scale. `bases` [world] int64:
+// every rank's symmetric-buffer base address (this rank's own at index `rank`).
+void p2p_allreduce_mean(torch::Tensor bases, int64_t rank, int64_t stage_off, int64_t n, int64_t call, double scale,
+                        double timeout_s, torch::Tensor out, torch::Tensor status) {
+  TORCH_CHECK(bases.is_cuda() && bases.scalar_type() == torch::kInt64, "bases: int64 CUDA tensor");
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == torch::kFloat32 && out.is_contiguous() && out.numel() >= n,
+              "out: contiguous fp32 CUDA tensor of n elements");
+  TORCH_CHECK(status.is_cuda() && status.scalar_type() == torch::kInt32, "status: int32 CUDA tensor");
+  const int world = (int)bases.numel();
+  TORCH_CHECK(world >= 1 && world <= MAX_RANKS && rank >= 0 && rank < world, "p2p_allreduce: 1..16 ranks");
+  TORCH_CHECK(stage_off % 16 == 0 && reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
+              "p2p_allreduce: 16-byte aligned stage and output");
+  const at::cuda::CUDAGuard guard(out.device());
+  if (n == 0) return;
+  int dev = out.get_device(), sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = (int)std::min<int64_t>((n / 4 + 255) / 256 + 1, (int64_t)sms * 2);
+  p2p_allreduce_mean_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      bases.data_ptr<int64_t>(), world, (int)rank, stage_off, n, (uint32_t)call, (float)scale,
+      (uint64_t)(timeout_s * 1e9), out.data_ptr<float>(), status.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}

@@ -23,7 +23,7 @@ CXX = ["-O3", "-std=c++17"]
 
 SOURCES = [os.path.join(CSRC, f) for f in (
     "bindings.cpp", "symm.cpp", "engram.cu", "norm.cu", "ce.cu", "attention.cu", "attention_tc.cu", "gemm.cu",
-    "nf4.cu",
+    "p2p.cu", "nf4.cu",
 )]
 
 setup(
