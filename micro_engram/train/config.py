@@ -147,7 +147,7 @@ class TrainConfig(MicroEngramArgs):
     gradient_checkpointing_policy: Literal["full", "selective", "auto"] = "full"
     gradient_checkpointing_reserve_gib: float = 23.0
     table_moments_on_host: Union[bool, Literal["auto"]] = "auto"
-    dense_allreduce: Literal["p2p", "nccl"] = "nccl"
+    dense_allreduce: Literal["p2p", "nccl"] = "p2p"
     activation_offloading: bool = False
     no_grad_prefix: bool = True
     sharded_vocab: bool = True
