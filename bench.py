@@ -239,6 +239,13 @@ def run_ours(args):
     e1.record()
     sync()
     e2e_ms = e0.elapsed_time(e1)
+    # a kernel-side error (row-store bounds/capacity, a bounded peer wait that ran out) fails the run
+    for slot in trainer.slots:
+        store = slot.engram.__dict__.get("row_store")
+        if store is not None:
+            store.check_status()
+    if getattr(trainer, "_p2p_ar", None) is not None:
+        trainer._p2p_ar.check_status()
 
     vals = torch.tensor([dev_ms, e2e_ms], dtype=torch.float64, device=device)
     if world > 1:
