@@ -340,7 +340,8 @@ class Trainer:
         dense_allreduce: p2p: the fused peer-memory kernel over every dense parameter (a rank
         without a gradient contributes zeros; only existing gradients are overwritten);
         otherwise one flat NCCL all_reduce."""
-        if self.world > 1 and self.device.type == "cuda" and self.cfg.dense_allreduce == "p2p" and self.dense:
+        if (1 < self.world <= 16 and self.device.type == "cuda" and self.cfg.dense_allreduce == "p2p"
+                and self.dense):  # one node: the kernel's peer table holds up to 16 ranks
             if getattr(self, "_p2p_ar", None) is None:
                 from micro_engram_fork_b200.parallel.allreduce import P2PAllReduce
 

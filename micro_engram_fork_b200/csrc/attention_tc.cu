@@ -1174,7 +1174,9 @@ __global__ void __launch_bounds__(320, 1)
 
 template <int D>
 struct AccLayout {
-  static constexpr int DN = D < 256 ? D : 256, NH = D / DN, NS = 4;
+  // two stages and two CTAs per SM (2 x 97 KB of shared memory, 2 x 256 TMEM columns): while one
+  // CTA drains its accumulator the other keeps the tensor pipe fed
+  static constexpr int DN = D < 256 ? D : 256, NH = D / DN, NS = 2;
   static constexpr int A_BYTES = 128 * 128;  // 128 M x 64 K (K-major) or 64 K x 128 M (two 8 KB pieces)
   static constexpr int B_BYTES = 64 * DN * 2;  // 64 K rows x DN columns: DN / 64 boxes of 8 KB
   static constexpr int STAGE = A_BYTES + B_BYTES;
@@ -1190,7 +1192,7 @@ struct AccLayout {
 // Job list of one pass: first the dV / dK blocks (kvh kv heads x key blocks x {dV, dK} x NH
 // column halves; the longest jobs), then the dQ blocks (kvh * G query heads x query blocks x NH).
 template <int D>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192, 2)
     attn_bwd_acc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap to,
                         const __grid_constant__ CUtensorMap tk, const int* __restrict__ jlo_a,
                         const int* __restrict__ off_a, const int* __restrict__ ihi_a, int T, int nb, int Hq, int Hk,

@@ -65,14 +65,32 @@ __global__ void __launch_bounds__(256) p2p_allreduce_mean_kernel(const int64_t* 
 #pragma unroll
   for (int r = 0; r < MAX_RANKS; ++r)
     src[r] = r < world ? reinterpret_cast<const float*>(bases[r] + stage_off) + par : nullptr;
+  // UNR float4 per thread and iteration, all ranks' loads issued before any add: enough bytes in
+  // flight to cover the NVLink round trip
+  constexpr int UNR = 4;
   const int64_t n4 = n / 4;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < n4; i0 += stride * UNR) {
+    float4 acc[UNR];
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int r = 0; r < world; ++r) {
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(src[r]) + i);
-      acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
+      float4 v[UNR];
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        const int64_t i = i0 + u * stride;
+        v[u] = i < n4 ? __ldcg(reinterpret_cast<const float4*>(src[r]) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) acc[u].x += v[u].x, acc[u].y += v[u].y, acc[u].z += v[u].z, acc[u].w += v[u].w;
     }
-    reinterpret_cast<float4*>(out)[i] = make_float4(acc.x * scale, acc.y * scale, acc.z * scale, acc.w * scale);
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i < n4)
+        reinterpret_cast<float4*>(out)[i] =
+            make_float4(acc[u].x * scale, acc[u].y * scale, acc[u].z * scale, acc[u].w * scale);
+    }
   }
   for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
