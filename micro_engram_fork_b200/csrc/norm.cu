@@ -200,7 +200,7 @@ __global__ void post_norm_add_kernel(const bf16* __restrict__ r, const bf16* __r
 //   gy = g * ls                                  (grad of r + n(a))
 //   dr = gy ; da = rmsnorm_bwd(gy; a, w_post)
 template <int VPT>
-__global__ void post_norm_add_bwd_kernel(const bf16* __restrict__ dxo, const bf16* __restrict__ dh,
+__global__ void __launch_bounds__(256, 3) post_norm_add_bwd_kernel(const bf16* __restrict__ dxo, const bf16* __restrict__ dh,
                                          const bf16* __restrict__ a, const bf16* __restrict__ x,
                                          const float* __restrict__ w_post, const float* __restrict__ ls_ptr,
                                          const float* __restrict__ w_next, const float* __restrict__ rstd_a,
@@ -441,7 +441,7 @@ ME_DEVICE void norm_bwd_head(const float (&xl)[VH], const float (&xh)[VH], const
 }
 
 template <int VH>
-__global__ void __launch_bounds__(256) qkv_norm_rope_bwd_kernel(
+__global__ void __launch_bounds__(256, 4) qkv_norm_rope_bwd_kernel(
     const bf16* __restrict__ dq, const bf16* __restrict__ dk, const bf16* __restrict__ dv,
     const bf16* __restrict__ qkv, const float* __restrict__ qw, const float* __restrict__ kw,
     const float* __restrict__ inv_freq, const int64_t* __restrict__ pos, const float* __restrict__ rstd, int64_t N,
