@@ -145,7 +145,7 @@ __global__ void rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const bf16* __re
 //   x = bf16(bf16(r + bf16(rms(a) * w_post)) * ls)      (ls: the layer scalar, or 1)
 //   h = bf16(rms(x) * w_next)                           (if w_next: the next pre-norm)
 template <int VPT>
-__global__ void post_norm_add_kernel(const bf16* __restrict__ r, const bf16* __restrict__ a,
+__global__ void __launch_bounds__(256, 4) post_norm_add_kernel(const bf16* __restrict__ r, const bf16* __restrict__ a,
                                      const float* __restrict__ w_post, const float* __restrict__ ls_ptr,
                                      const float* __restrict__ w_next, int64_t N, int d, float eps,
                                      bf16* __restrict__ x_out, bf16* __restrict__ h_out,
