@@ -389,12 +389,15 @@ __global__ void __launch_bounds__(256) qkv_norm_rope_kernel(
 #pragma unroll
         for (int e = 0; e < VH; ++e) {
           const int j = base + e;
-          const float a = bf2f(f2bf(lo[e] * rs * w[j]));
-          const float b = bf2f(f2bf(hi[e] * rs * w[HALF + j]));
+          // the same bf16 roundings as below, two values per cvt.rn.bf16x2
+          const float2 ab = __bfloat1622float2(__floats2bfloat162_rn(lo[e] * rs * w[j], hi[e] * rs * w[HALF + j]));
+          const float a = ab.x, b = ab.y;
           const float2 c = cs[e * 32];
-          // rotate_half: (-b, a)
-          ol[e] = bf2f(f2bf(a * c.x)) + bf2f(f2bf(-b * c.y));
-          oh[e] = bf2f(f2bf(b * c.x)) + bf2f(f2bf(a * c.y));
+          // rotate_half: (-b, a); ol = bf16(a c) + bf16(-b s), oh = bf16(b c) + bf16(a s)
+          const float2 t1 = __bfloat1622float2(__floats2bfloat162_rn(a * c.x, -b * c.y));
+          const float2 t2 = __bfloat1622float2(__floats2bfloat162_rn(b * c.x, a * c.y));
+          ol[e] = t1.x + t1.y;
+          oh[e] = t2.x + t2.y;
         }
       }
       st_bf<VH>(dst + base, ol);
