@@ -452,10 +452,11 @@ torch::Tensor attn_tc_status(int64_t device) { return attn_status((int)device); 
 //   MODE_DV  resident K; S^T = K Q^T, P^T -> smem, dV += P^T dO
 // with P = exp(scale * S - LSE) from the forward's LSE. dK and dV sum over the GQA group inside
 // the CTA (no atomics); dQ and dK carry the softmax scale. TMEM: two S buffers, two dP
-// buffers, one D-column accumulator. Warp roles as in the forward: warp 0 TMA producer (Q/K/V/dO
-// tiles by 3-D tensor maps; per-query LSE, delta and document starts by untiled bulk copies),
-// warp 1 TMEM owner + MMA issuer, warps 2-5 one row (TMEM lane) per thread. Every wait is
-// bounded; a timeout records ME_ERR_TIMEOUT and the kernel frees TMEM and returns.
+// buffers, one D-column accumulator. Warp roles: warp 0 TMA producer (Q/K/V/dO tiles by 3-D
+// tensor maps; per-query LSE, delta and document starts by untiled bulk copies), warp 1 TMEM
+// owner + MMA issuer, warps 2-9 elementwise, two per TMEM lane quarter: one row (TMEM lane) per
+// thread and half of each block's BC columns per warp. Every wait is bounded; a timeout records
+// ME_ERR_TIMEOUT and the kernel frees TMEM and returns.
 namespace {
 
 enum { MODE_DQ = 0, MODE_DK = 1, MODE_DV = 2 };
