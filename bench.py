@@ -156,7 +156,8 @@ def count_launches(trainer, micro):
             "attn_fwd_kernel", "attn_fwd_tc_kernel", "attn_bwd_pre_kernel", "attn_bwd_dkdv_kernel",
             "attn_bwd_dq_kernel", "attn_bwd_tc_kernel", "attn_delta_kernel", "doc_end_from_start_kernel",
             "attn_tiles_kernel", "attn_bwd_sdp_kernel", "attn_bwd_acc_kernel",
-            "gemm_tc_kernel", "nf4_dequant_kernel", "nf4_quantize_kernel")
+            "gemm_pair_kernel", "nf4_dequant_kernel", "nf4_quantize_kernel", "p2p_allreduce_mean_kernel",
+            "layer_gather_kernel")
     pat = re.compile(r"\b(" + "|".join(ours) + r")\b")
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         trainer.train_step(micro)
@@ -172,6 +173,32 @@ def count_launches(trainer, micro):
             if pat.search(ev.name):
                 n_ours += 1
     return n_ours, n_all
+
+
+def phase_breakdown(trainer, micro, world):
+    """Device time per phase of one untimed step (CUDA events around embed / forward / loss /
+    backward / reduce / optimizer), max over ranks, plus the spread of the whole step over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from micro_engram_fork_b200.utils.timers import PhaseTimers
+
+    timers, trainer.timers = trainer.timers, PhaseTimers(enabled=True, device=trainer.device)
+    try:
+        trainer.train_step(micro)
+        ms = trainer.timers.report()
+    finally:
+        trainer.timers = timers
+    names = sorted(ms)
+    vals = torch.tensor([ms[n] for n in names] + [sum(ms.values())], dtype=torch.float64, device=trainer.device)
+    lo = vals.clone()
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+    out = {n: round(v, 2) for n, v in zip(names, vals.tolist())}
+    out["step_max_over_ranks"] = round(vals[-1].item(), 2)
+    out["step_min_over_ranks"] = round(lo[-1].item(), 2)
+    return out
 
 
 def run_ours(args):
@@ -209,6 +236,7 @@ def run_ours(args):
     for _ in range(args.warmup):
         trainer.train_step(next_micro())
     n_ours, n_all = count_launches(trainer, next_micro())
+    phases = phase_breakdown(trainer, next_micro(), world)
 
     # device-timed: inputs staged on the GPU before the timed region
     staged = []
@@ -223,7 +251,7 @@ def run_ours(args):
     tokens = 0
     t0.record()
     for micro, batches in staged:
-        trainer.train_step(micro, batches=batches)
+        trainer.train_step(micro, batches=batches, sync=False)  # no host read: the device-timed loop
         tokens += SEQ * MBS * GA
     t1.record()
     sync()
@@ -279,6 +307,7 @@ def run_ours(args):
                     "h2d_bytes_per_step": GA * 3 * SEQ * MBS * 8, "d2h_bytes_per_step": 16},
             "gpu_launches": n_ours * args.steps,
             "gpu_launches_all_per_step": n_all,
+            "phase_ms_one_step": phases,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -400,6 +429,10 @@ def run_reference(args):
     ms = float(ms)
     value = SEQ * MBS * GA * args.steps * world / (ms / 1e3)
     if rank == 0:
+        # the stock train_step collates each step on the host, copies it to the GPU and reads the
+        # loss back, so this timed loop is already end to end through the reference's public API
+        e2e = {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": GA * 3 * SEQ * MBS * 8,
+               "d2h_bytes_per_step": 8, "note": "the timed loop itself (stock Trainer.train_step)"}
         print(json.dumps({
             "impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 2),
@@ -408,6 +441,7 @@ def run_reference(args):
             "config": {"model": MODEL, "global_batch": MBS * GA * world, "seq_len": SEQ,
                        "parallelism": f"fsdp2 dp{world} (reference)", "attn_implementation": cfg.attn_implementation,
                        "e2e_note": "reference Trainer.train_step: host collate + H2D + loss readback each step"},
+            "e2e": e2e,
         }), flush=True)
     if world > 1:
         dist.barrier()

@@ -16,6 +16,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from micro_engram_fork_b200.ops import use_native
+from micro_engram_fork_b200.ops.linear import projection
 
 _PRIME = 2_147_483_647  # 2^31 - 1
 
@@ -288,8 +289,8 @@ class MicroEngram(nn.Module):
         if self.gate in self.SCALAR_GATES:
             if (use_native(hidden) and hidden.dtype == torch.bfloat16 and mem.dtype == torch.bfloat16
                     and self.key.weight.dtype == torch.bfloat16):
-                k = self.key(mem)
-                v = self.value(mem)
+                k = projection(mem, self.key.weight)
+                v = projection(mem, self.value.weight)
                 return self._gate_native(hidden, k, v, keep)
             if self.gate == "scalar_sqrt":
                 qs, ks = self.norm_scales()
@@ -331,8 +332,8 @@ class MicroEngram(nn.Module):
         flat = torch.stack([i.reshape(-1) for i in idx]) if isinstance(idx, (list, tuple)) else idx
         flat = flat.reshape(len(self.table_rows), -1).to(hidden.device).contiguous()
         mem = gather_rows(flat, self.row_store, torch.bfloat16, self.row_shards)
-        k = F.linear(mem, self.key.weight)
-        v = F.linear(mem, self.value.weight)
+        k = projection(mem, self.key.weight)
+        v = projection(mem, self.value.weight)
         return self._gate_native(hidden, k, v, keep)
 
     def forward(self, hidden, input_ids, position_ids=None):

@@ -179,65 +179,110 @@ def _dtensor(t, n_rows, world):
     return DTensor.from_local(t, _GROUPS[key], [Shard(0)], run_check=False, shape=shape, stride=stride)
 
 
-class RowTables:
-    """The row-sharded tables of every engram of a run: optimizer, clipping, save/load.
+class _TableRef:
+    """One table shard of one engram: its checkpoint key, full row count and Parameter."""
+    __slots__ = ("key", "rows", "param", "engram", "index")
 
-    entries: [(prefix, engram)] with prefixes like "model.language_model.layers.0.micro_engram.".
+    def __init__(self, key, rows, param, engram, index):
+        self.key, self.rows, self.param, self.engram, self.index = key, rows, param, engram, index
+
+    @property
+    def trains(self):
+        return any(p.requires_grad for p in self.engram.row_shards)
+
+
+def _grad_sq(p):
+    """Squared L2 norm of a table shard's gradient held outside a row store (dense .grad
+    and/or the coalesced sparse (rows, grads) pair), as a 1-element fp32 tensor."""
+    total = torch.zeros(1, dtype=torch.float32, device=p.device)
+    if p.grad is not None:
+        total += p.grad.float().square().sum()
+    sparse = getattr(p, "sparse_grad", None)
+    if sparse is not None:
+        total += sparse[1].square().sum()
+    return total
+
+
+def _scale_grad(p, coef):
+    if p.grad is not None:
+        p.grad.mul_(coef.to(p.grad.dtype))
+    sparse = getattr(p, "sparse_grad", None)
+    if sparse is not None:
+        sparse[1].mul_(coef)
+
+
+def _convert_second_moment(saved, target, p):
+    """Copy a loaded second moment written by the other lazy optimizer into `target`: per value
+    -> per row is the row mean (v is linear in g^2, so this is exact for a fresh row); per row ->
+    per value repeats the row's value."""
+    if saved.dim() > target.dim():
+        target.copy_(saved.flatten(1).mean(dim=1))
+    else:
+        target.copy_(saved.reshape(-1, *([1] * (p.dim() - 1))).expand_as(p))
+
+
+class RowTables:
+    """Every row-sharded table of a run: the optimizer over the shards, global-norm clipping,
+    and checkpoints (collective: every rank calls clip / save / load).
+
+    entries: [(prefix, engram)], prefix being the engram's module path plus a dot, e.g.
+    "model.language_model.layers.0.micro_engram.".
     """
 
     def __init__(self, entries, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, lazy=False,
                  rowwise=False, stochastic_rounding=True, sparse_grads=False):
+        if sparse_grads and not lazy:
+            raise ValueError("sparse row gradients need a lazy optimizer (lazy_adam or rowwise_adam); plain AdamW "
+                             "steps every row every step")
         self.entries = entries
         self.world = dist_rank_world()[1]
-        train = [p for _, e in entries for p in e.row_shards if p.requires_grad]
-        if sparse_grads and not lazy:
-            raise ValueError("sparse row gradients need a lazy optimizer (lazy_adam / rowwise_adam): "
-                             "plain AdamW updates every row every step")
         self.sparse = bool(sparse_grads)
-        for _, e in entries:
-            store = getattr(e, "row_store", None)
-            for k, p in enumerate(e.row_shards):
-                p._sparse_rows = self.sparse
-                if store is not None:
-                    p._row_store = (store, k)
-        self.optimizer = LazyAdamW([{"params": train, "lazy": lazy, "rowwise": rowwise}], lr=lr, betas=betas,
-                                   eps=eps, weight_decay=weight_decay,
-                                   stochastic_rounding=stochastic_rounding) if train else None
+        self.refs = [_TableRef(f"{prefix}tables.{k}.weight", e.table_rows[k], p, e, k)
+                     for prefix, e in entries for k, p in enumerate(e.row_shards)]
+        for ref in self.refs:
+            ref.param._sparse_rows = self.sparse
+            store = getattr(ref.engram, "row_store", None)
+            if store is not None:
+                ref.param._row_store = (store, ref.index)
+        trained = [r.param for r in self.refs if r.param.requires_grad]
+        self.optimizer = None
+        if trained:
+            self.optimizer = LazyAdamW([{"params": trained, "lazy": lazy, "rowwise": rowwise}], lr=lr, betas=betas,
+                                       eps=eps, weight_decay=weight_decay, stochastic_rounding=stochastic_rounding)
         self.last_grad_norm = None
         self.converted = 0
 
     def params(self):
-        return [p for _, e in self.entries for p in e.row_shards]
+        return [r.param for r in self.refs]
 
     def stores(self):
-        seen = []
-        for _, e in self.entries:
-            s = getattr(e, "row_store", None)
-            if s is not None and any(p.requires_grad for p in e.row_shards) and s not in seen:
-                seen.append(s)
-        return seen
+        """The row stores holding gradients of trained tables (each once)."""
+        out = []
+        for r in self.refs:
+            store = getattr(r.engram, "row_store", None)
+            if store is not None and r.trains and store not in out:
+                out.append(store)
+        return out
 
+    # ------------------------------------------------------------------ clipping
     def clip(self, max_norm):
-        """Global L2 norm of the table gradients (each row lives on one rank), scaled down to
-        max_norm when larger. Collective: every rank calls it."""
-        ps = [p for p in self.params() if p.requires_grad]
-        if not ps:
+        """Scale every table gradient by min(1, max_norm / global norm) and return the global
+        norm (a row lives on exactly one rank, so the squared norms add across ranks). On CUDA
+        the coefficient stays on the device and the touched-row update applies it."""
+        trained = [p for p in self.params() if p.requires_grad]
+        if not trained:
             return None
-        dev = ps[0].device
+        dev = trained[0].device
         sq = torch.zeros(1, dtype=torch.float32, device=dev)
         for store in self.stores():
             if store.pending:
                 store.sqnorm_into(sq)
-        for p in ps:
-            if getattr(p, "_row_store", None) is not None:
-                continue
-            if p.grad is not None:
-                sq += p.grad.float().pow(2).sum()
-            sg = getattr(p, "sparse_grad", None)
-            if sg is not None:
-                sq += sg[1].pow(2).sum()
+        loose = [p for p in trained if getattr(p, "_row_store", None) is None]
+        for p in loose:
+            sq += _grad_sq(p)
         if self.world > 1:
             dist.all_reduce(sq, group=_group(self.world))
+        clipping = bool(max_norm) and max_norm > 0
         if dev.type == "cuda" and self.stores():
             from micro_engram_fork_b200 import native
 
@@ -248,24 +293,18 @@ class RowTables:
                 store.coef = coef
         else:
             norm = sq.sqrt()
-            coef = (max_norm / (norm + 1e-6)).clamp(max=1.0) if (max_norm and max_norm > 0) else None
-        if max_norm and max_norm > 0:
-            for p in ps:
-                if getattr(p, "_row_store", None) is not None:
-                    continue
-                if p.grad is not None:
-                    p.grad.mul_(coef.to(p.grad.dtype))
-                sg = getattr(p, "sparse_grad", None)
-                if sg is not None:
-                    sg[1].mul_(coef)
-        self.last_grad_norm = float(norm)
-        return self.last_grad_norm
+            coef = torch.clamp(max_norm / (norm + 1e-6), max=1.0) if clipping else None
+        if clipping:
+            for p in loose:
+                _scale_grad(p, coef)
+        self.last_grad_norm = norm
+        return norm
 
     def step(self, lr):
         if self.optimizer is None:
             return
-        for g in self.optimizer.param_groups:
-            g["lr"] = lr
+        for group in self.optimizer.param_groups:
+            group["lr"] = lr
         self.optimizer.step()
         self.zero_grad()
 
@@ -279,96 +318,100 @@ class RowTables:
                 store.zero_grads()
             store.coef = None
 
-    # ------------------------------------------------------------------ checkpoints (collective)
-    def _table_items(self, frozen_too=False):
-        for prefix, e in self.entries:
-            if not frozen_too and not any(p.requires_grad for p in e.row_shards):
-                continue
-            for k, p in enumerate(e.row_shards):
-                yield f"{prefix}tables.{k}.weight", e.table_rows[k], p
+    # ------------------------------------------------------------------ checkpoints
+    def _trained_refs(self):
+        return [r for r in self.refs if r.trains]
 
     def save(self, folder, optim_folder=None):
-        """The complete engram (tables + dense weights + buffers) to `folder` and the tables'
-        optimizer state to `optim_folder`, as DCP. Frozen engrams are skipped."""
+        """DCP checkpoint of every trained engram: tables (as Shard(0) DTensors of the whole
+        table, reshardable to any world size), dense weights and buffers under their module
+        names in `folder`; the tables' optimizer moments and step in `optim_folder`."""
         import torch.distributed.checkpoint as dcp
 
-        sd = {}
+        trained = {id(e) for _, e in self.entries if any(p.requires_grad for p in e.row_shards)}
+        state = {}
         for prefix, e in self.entries:
-            if not any(p.requires_grad for p in e.row_shards):
-                continue
-            sd.update({prefix + k: v for k, v in e.state_dict().items()})
-        for key, rows, p in self._table_items():
-            sd[key] = _dtensor(p.detach(), rows, self.world)
-        if sd:
-            dcp.save(sd, checkpoint_id=folder)
+            if id(e) in trained:
+                state.update((prefix + k, v) for k, v in e.state_dict().items())
+        for r in self._trained_refs():
+            state[r.key] = _dtensor(r.param.detach(), r.rows, self.world)
+        if state:
+            dcp.save(state, checkpoint_id=folder)
         if optim_folder and self.optimizer is not None:
-            osd = {}
-            for key, rows, p in self._table_items():
-                st = self.optimizer.state.get(p)
-                if st:
-                    osd[f"{key}.exp_avg"] = _dtensor(st["exp_avg"], rows, self.world)
-                    osd[f"{key}.exp_avg_sq"] = _dtensor(st["exp_avg_sq"], rows, self.world)
-                    osd[f"{key}.step"] = st["step"].detach().clone().reshape(())
-            if osd:
-                dcp.save(osd, checkpoint_id=optim_folder)
+            moments = {}
+            for r in self._trained_refs():
+                st = self.optimizer.state.get(r.param)
+                if not st:
+                    continue
+                moments[f"{r.key}.exp_avg"] = _dtensor(st["exp_avg"], r.rows, self.world)
+                moments[f"{r.key}.exp_avg_sq"] = _dtensor(st["exp_avg_sq"], r.rows, self.world)
+                moments[f"{r.key}.step"] = st["step"].detach().clone().reshape(())
+            if moments:
+                dcp.save(moments, checkpoint_id=optim_folder)
 
-    def load(self, folder, optim_folder=None):
-        """Tables from a DCP folder (micro_engram_rows, or an FSDP checkpoint), resharded to this
-        run's world. Returns (tables loaded, whether optimizer state was loaded)."""
-        import torch.distributed.checkpoint as dcp
-
-        meta = dcp.FileSystemReader(folder).read_metadata().state_dict_metadata
-        by_name = {}
+    def _saved_table_keys(self, meta):
+        """{(layer or None, 'tables.k.weight'): saved key} of a DCP checkpoint's table tensors."""
+        found = {}
         for key in meta:
             local = _local_name(key)
             if local is not None and local.startswith("tables."):
-                by_name[(layer_of_key(key), local)] = key
-        want = {}
-        for prefix, e in self.entries:
-            layer = layer_of_key(prefix + "x")
-            for k, p in enumerate(e.row_shards):
-                found = by_name.get((layer, f"tables.{k}.weight")) or by_name.get((None, f"tables.{k}.weight"))
-                if found is None:
-                    raise ValueError(f"[micro_engram] {folder} has no tables.{k}.weight for {prefix.rstrip('.')}")
-                saved_rows = meta[found].size[0]
-                if saved_rows != e.table_rows[k]:
-                    raise ValueError(f"[micro_engram] {folder}: tables.{k}.weight has {saved_rows:,} rows, this "
-                                     f"engram's table {k} (order {e._table_orders[k]}) has {e.table_rows[k]:,}: "
-                                     f"different table sizes can't resume (start a new run, or keep the sizes)")
-                want[found] = (e.table_rows[k], p)
-        templ = {key: _dtensor(p.data, rows, self.world) for key, (rows, p) in want.items()}
-        dcp.load(templ, checkpoint_id=folder)
-        optim_loaded = False
+                found[(layer_of_key(key), local)] = key
+        return found
+
+    def load(self, folder, optim_folder=None):
+        """Load tables from a DCP folder (micro_engram_rows, or an FSDP checkpoint holding the
+        engram), resharded to this run's world size; then the optimizer moments when
+        `optim_folder` has them (converting between the two lazy optimizers' second-moment
+        shapes). Returns (number of tables loaded, whether optimizer state was loaded)."""
+        import torch.distributed.checkpoint as dcp
+
+        meta = dcp.FileSystemReader(folder).read_metadata().state_dict_metadata
+        saved = self._saved_table_keys(meta)
+        targets = {}
+        for r in self.refs:
+            layer = layer_of_key(r.key)
+            local = f"tables.{r.index}.weight"
+            key = saved.get((layer, local)) or saved.get((None, local))
+            if key is None:
+                raise ValueError(f"[micro_engram] {folder} holds no {local} for {r.key.rsplit('.tables.', 1)[0]}")
+            if meta[key].size[0] != r.rows:
+                raise ValueError(f"[micro_engram] {folder}: {local} was saved with {meta[key].size[0]:,} rows but "
+                                 f"table {r.index} (order {r.engram._table_orders[r.index]}) has {r.rows:,}; "
+                                 "a run cannot resume with other table sizes")
+            targets[key] = _dtensor(r.param.data, r.rows, self.world)
+        dcp.load(targets, checkpoint_id=folder)
+        loaded_optim = False
         if optim_folder and self.optimizer is not None and os.path.isdir(optim_folder):
-            ometa = dcp.FileSystemReader(optim_folder).read_metadata().state_dict_metadata
-            otempl, steps, convert = {}, {}, {}
-            group = self.optimizer.param_groups[0]
-            for key, rows, p in self._table_items():
-                if f"{key}.exp_avg" not in ometa:
-                    continue
-                st = self.optimizer.state[p]
-                if not st:
-                    LazyAdamW.init_state(st, p, group, self.optimizer._on_host(p, group))
-                otempl[f"{key}.exp_avg"] = _dtensor(st["exp_avg"], rows, self.world)
-                saved_dims = len(ometa[f"{key}.exp_avg_sq"].size)
-                sq = st["exp_avg_sq"]
-                if saved_dims != sq.dim():  # written by the other lazy optimizer
-                    sq = torch.zeros(p.shape if saved_dims == p.dim() else p.shape[:1], dtype=torch.float32,
-                                     device=p.device)
-                    convert[p] = sq
-                otempl[f"{key}.exp_avg_sq"] = _dtensor(sq, rows, self.world)
-                otempl[f"{key}.step"] = steps[p] = torch.zeros((), dtype=torch.float32)
-            if otempl:
-                dcp.load(otempl, checkpoint_id=optim_folder)
-                for p, s in steps.items():
-                    self.optimizer.state[p]["step"] = s
-                for p, sq in convert.items():
-                    st = self.optimizer.state[p]
-                    if sq.dim() > st["exp_avg_sq"].dim():
-                        # per value -> per row: v is linear in g^2, so the row mean is exact
-                        st["exp_avg_sq"].copy_(sq.flatten(1).mean(dim=1))
-                    else:  # per row -> per value
-                        st["exp_avg_sq"].copy_(sq.reshape(-1, *([1] * (p.dim() - 1))).expand_as(p))
-                self.converted = len(convert)
-                optim_loaded = True
-        return len(want), optim_loaded
+            loaded_optim = self._load_moments(optim_folder)
+        return len(targets), loaded_optim
+
+    def _load_moments(self, optim_folder):
+        import torch.distributed.checkpoint as dcp
+
+        ometa = dcp.FileSystemReader(optim_folder).read_metadata().state_dict_metadata
+        group = self.optimizer.param_groups[0]
+        targets, steps, foreign = {}, {}, {}
+        for r in self._trained_refs():
+            if f"{r.key}.exp_avg" not in ometa:
+                continue
+            p, st = r.param, self.optimizer.state[r.param]
+            if not st:
+                LazyAdamW.init_state(st, p, group, self.optimizer._on_host(p, group))
+            targets[f"{r.key}.exp_avg"] = _dtensor(st["exp_avg"], r.rows, self.world)
+            saved_ndim = len(ometa[f"{r.key}.exp_avg_sq"].size)
+            v = st["exp_avg_sq"]
+            if saved_ndim != v.dim():  # written by the other lazy optimizer: load, then convert
+                v = torch.zeros(p.shape if saved_ndim == p.dim() else p.shape[:1], dtype=torch.float32,
+                                device=p.device)
+                foreign[p] = v
+            targets[f"{r.key}.exp_avg_sq"] = _dtensor(v, r.rows, self.world)
+            steps[p] = targets[f"{r.key}.step"] = torch.zeros((), dtype=torch.float32)
+        if not targets:
+            return False
+        dcp.load(targets, checkpoint_id=optim_folder)
+        for p, step in steps.items():
+            self.optimizer.state[p]["step"] = step
+        for p, v in foreign.items():
+            _convert_second_moment(v, self.optimizer.state[p]["exp_avg_sq"], p)
+        self.converted = len(foreign)
+        return True

@@ -169,17 +169,9 @@ class TrainConfig(MicroEngramArgs):
 
     @model_validator(mode="after")
     def _check(self):
-        if self.fsdp_config.activation_checkpointing:
-            raise ValueError("fsdp_config.activation_checkpointing is not supported: use gradient_checkpointing: true "
-                             "(per-layer non-reentrant checkpointing, as Axolotl's hf implementation)")
-        if self.micro_engram_dense_lr is not None and self.micro_engram_dense_lr <= 0:
-            raise ValueError("micro_engram_dense_lr must be > 0 (freeze an engram with micro_engram_frozen instead)")
-        if self.liger_rope:
-            raise ValueError("liger_rope: Gemma 4 RoPE is already fused with the q/k norms (fused_attn_kernel)")
-        if (self.gradient_checkpointing_kwargs or {}).get("use_reentrant"):
-            raise ValueError("gradient_checkpointing_kwargs.use_reentrant must be false (frozen inputs get no grads)")
-        if self.micro_engram_sharding not in (None, "rows"):
-            raise ValueError("micro_engram_sharding must be rows (or unset, which means rows here)")
+        for broken, why in _CONFIG_ERRORS:
+            if broken(self):
+                raise ValueError(why)
         return self
 
     @property
@@ -193,30 +185,54 @@ class TrainConfig(MicroEngramArgs):
         return default if v is None else v
 
 
-def load_config(path_or_dict):
-    """TrainConfig from a YAML path or a dict; raises on LoRA and unknown keys."""
+# Combinations of valid keys that this trainer refuses, with the reason shown to the user.
+_CONFIG_ERRORS = (
+    (lambda c: bool(c.fsdp_config.activation_checkpointing),
+     "fsdp_config.activation_checkpointing: set gradient_checkpointing: true instead (this trainer "
+     "checkpoints each decoder layer itself, non-reentrant)"),
+    (lambda c: c.micro_engram_dense_lr is not None and c.micro_engram_dense_lr <= 0,
+     "micro_engram_dense_lr must be positive; to keep an engram fixed use micro_engram_frozen"),
+    (lambda c: c.liger_rope,
+     "liger_rope: RoPE is already applied inside the fused q/k/v norm kernel"),
+    (lambda c: bool((c.gradient_checkpointing_kwargs or {}).get("use_reentrant")),
+     "gradient_checkpointing_kwargs.use_reentrant: true is not supported (the frozen layers' inputs carry "
+     "no gradient, so reentrant checkpointing would drop the engram's)"),
+    (lambda c: c.micro_engram_sharding not in (None, "rows"),
+     "micro_engram_sharding: tables are always row-sharded here; use rows or leave it out"),
+)
+
+
+def _read(path_or_dict):
     if isinstance(path_or_dict, dict):
-        raw = dict(path_or_dict)
-    else:
-        with open(path_or_dict, encoding="utf-8") as f:
-            raw = yaml.safe_load(f) or {}
-    lora = sorted(k for k in raw if k in LORA_KEYS or k.startswith(LORA_PREFIX))
+        return dict(path_or_dict)
+    with open(path_or_dict, encoding="utf-8") as f:
+        return yaml.safe_load(f) or {}
+
+
+def _screen(raw, announce):
+    """Apply the key rules to a raw YAML mapping in place: LoRA keys, FSDP1 and 8-bit loading
+    are errors; Axolotl-only keys and loss-implementation keys are dropped with one warning
+    each (the loss here is always the fused, chunked, vocab-parallel one)."""
+    lora = [k for k in raw if k in LORA_KEYS or k.startswith(LORA_PREFIX)]
     if lora:
-        raise ValueError(f"remove {', '.join(lora)}: micro_engram.train loads a 4-bit base directly "
-                         "(load_in_4bit: true), with no placeholder LoRA, and trains only the engram "
-                         "(no unfrozen_parameters needed)")
-    if raw.get("fsdp_version") not in (None, 2, "2"):
-        raise ValueError("only FSDP2 is supported (fsdp_version: 2, or leave it out)")
-    first = os.environ.get("RANK", "0") == "0"
-    ignored = sorted(k for k in raw if k in IGNORED_KEYS)
-    if ignored and first:
-        LOG.warning(f"[micro_engram] ignoring Axolotl-only keys: {', '.join(ignored)}")
-    loss = sorted(k for k in raw if k in LOSS_KEYS)
-    if loss and first:
-        LOG.warning(f"[micro_engram] {', '.join(loss)}: not needed, the loss is always fused "
-                    f"(chunked, vocab-parallel; no full logits)")
-    for k in ignored + loss:
-        raw.pop(k)
-    if "load_in_8bit" in raw and raw.pop("load_in_8bit"):
-        raise ValueError("load_in_8bit is not supported (use load_in_4bit)")
+        raise ValueError(f"{', '.join(sorted(lora))}: no adapter is trained or needed; the base stays frozen "
+                         "(load_in_4bit: true quantizes it directly) and only the engram trains")
+    if raw.get("fsdp_version") is not None and str(raw["fsdp_version"]) != "2":
+        raise ValueError("fsdp_version: only 2 (FSDP2 semantics) is supported")
+    if raw.pop("load_in_8bit", False):
+        raise ValueError("load_in_8bit is not supported; use load_in_4bit (NF4)")
+    dropped = {"ignoring Axolotl-only keys": sorted(k for k in raw if k in IGNORED_KEYS),
+               "not needed (the loss is always fused, chunked and vocab-parallel)":
+                   sorted(k for k in raw if k in LOSS_KEYS)}
+    for what, keys in dropped.items():
+        for k in keys:
+            del raw[k]
+        if keys and announce:
+            LOG.warning(f"[micro_engram] {what}: {', '.join(keys)}")
+    return raw
+
+
+def load_config(path_or_dict):
+    """TrainConfig from a YAML file or a dict (unknown keys are errors)."""
+    raw = _screen(_read(path_or_dict), announce=os.environ.get("RANK", "0") == "0")
     return TrainConfig(**raw)

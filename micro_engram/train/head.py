@@ -42,14 +42,21 @@ class VocabShard:
             from micro_engram_fork_b200.parallel.symm import SymmBuffer
 
             esz = torch.empty((), dtype=dtype).element_size()
-            self._buf = SymmBuffer(self.per * self.d * esz, device, _group(world))
-            full = self._buf.view(0, (self.per, self.d), dtype)
+            per8 = -(-self.per // 8) * 8
+            self._buf = SymmBuffer(per8 * self.d * esz, device, _group(world))
+            full = self._buf.view(0, (per8, self.d), dtype)
+            full.zero_()
             full[:self.rows].copy_(local.to(device=device, dtype=dtype))
             self.weight = full[:self.rows]
+            # the tcgen05 head GEMMs read whole 16-byte rows of logits: rows padded with zeros
+            # to a multiple of 8 (zero rows add nothing to dH; the loss masks their columns)
+            self.gemm_weight = full[:-(-self.rows // 8) * 8]
             self._ptrs = torch.tensor(self._buf.ptrs, dtype=torch.int64, device=device)
         else:
             self.weight = local.to(device=device, dtype=dtype).clone()
             self._ptrs = None
+            pad = -(-self.rows // 8) * 8 - self.rows
+            self.gemm_weight = (torch.cat([self.weight, self.weight.new_zeros(pad, self.d)]) if pad else self.weight)
         self._per_t = None
         self.embed_scale = embed_scale
         self.softcap = softcap
@@ -190,45 +197,62 @@ class _VocabParallelCE(torch.autograd.Function):
 
 
 class _FusedVocabCE(torch.autograd.Function):
-    """CUDA path: bf16 logits GEMM + one-pass softcap/LSE row kernel, and, in the same pass over
-    each chunk, the gradient: the logits are overwritten in place with (softmax - onehot) *
-    softcap' (unscaled), multiplied into dH with fp32 output and reduce-scattered to the
-    token's rank. The backward only scales this rank's dH rows by the incoming gradient (the
-    loss is linear in it, and reduce-scatter keeps each token's row on its own rank), so the
-    logits GEMM runs once per chunk instead of twice."""
+    """CUDA path, per chunk of tokens (gathered from every rank):
+
+      1. one tcgen05 GEMM of the chunk against this rank's vocab rows whose epilogue softcaps
+         the bf16 logits and reduces each 256-column tile to a partial sum of exp(zc - cap) plus
+         the target logit (gemm_ce); with a softcap every partial shares the offset `cap`, so the
+         ranks combine by a plain sum: lse = cap + log(sum of partials). The bf16 logits are
+         kept only when a gradient is needed;
+      2. the logits are overwritten in place with (softmax - onehot) * softcap' (ce_bwd_inplace,
+         SFU exp/tanh, one pass), multiplied into dH on the tcgen05 GEMM with fp32 output
+         (gemm_f32) and reduce-scattered to the token's rank.
+
+    The backward only scales this rank's dH rows by the incoming gradient (the loss is linear
+    in it), so the logits GEMM runs once per chunk. Reference semantics:
+    micro_engram/train/head.py:76-165 (softcap as tanh(z/c)*c on the fp32 value of the bf16
+    logits; loss = sum over trained tokens of lse - target)."""
 
     @staticmethod
     def forward(ctx, hidden, labels, shard, need_grad):
         from micro_engram_fork_b200 import native
 
         C = native()
-        world, group, w = shard.world, shard.group, shard.weight
+        world, group, w = shard.world, shard.group, shard.gemm_weight
         N, c = hidden.shape[0], shard.chunk_bf16
         cap = float(shard.softcap or 0.0)
-        h = hidden.detach().to(w.dtype)
+        h = hidden.detach().to(w.dtype).contiguous()
         total = torch.zeros((), dtype=torch.float32, device=hidden.device)
         dh = torch.empty(N, shard.d, dtype=torch.float32, device=hidden.device) if need_grad else None
         for a in range(0, N, c):
             b = min(N, a + c)
+            n = b - a
             H = _gather(h[a:b], group, world)
             L = _gather(labels[a:b].contiguous(), group, world)
-            z = H @ w.t()
-            m, s, tgt = C.ce_fwd(z, L, shard.start, cap)
-            if world > 1:
-                M = m.clone()
-                dist.all_reduce(M, op=dist.ReduceOp.MAX, group=group)
-                st = torch.stack([s * torch.exp(m - M), tgt])
-                dist.all_reduce(st, group=group)
-                m, s, tgt = M, st[0], st[1]
-            lse = m + torch.log(s)
-            n = b - a
+            s_part, m_part, tgt, z = C.gemm_ce(H, w, L, shard.start, cap, need_grad, shard.rows)
+            if cap > 0:
+                s = s_part.sum(1)
+                if world > 1:
+                    st = torch.stack([s, tgt])
+                    dist.all_reduce(st, group=group)
+                    s, tgt = st[0], st[1]
+                lse = cap + torch.log(s)
+            else:
+                m = m_part.amax(1)
+                s = (s_part * torch.exp(m_part - m[:, None])).sum(1)
+                if world > 1:
+                    M = m.clone()
+                    dist.all_reduce(M, op=dist.ReduceOp.MAX, group=group)
+                    st = torch.stack([s * torch.exp(m - M), tgt])
+                    dist.all_reduce(st, group=group)
+                    m, s, tgt = M, st[0], st[1]
+                lse = m + torch.log(s)
             own = slice(shard.rank * n, (shard.rank + 1) * n)
             valid = L[own] != IGNORE
             total = total + torch.where(valid, lse[own] - tgt[own], torch.zeros_like(lse[own])).sum()
             if need_grad:
                 C.ce_bwd_inplace(z, L, shard.start, cap, lse, (L != IGNORE).float())
-                dH = torch.mm(z, w, out_dtype=torch.float32)
-                dh[a:b] = _reduce_scatter(dH, n, shard.d, group, world)
+                dh[a:b] = _reduce_scatter(C.gemm_f32(z, w), n, shard.d, group, world)
             del z
         ctx.dh, ctx.hdtype = dh, hidden.dtype
         return total

@@ -385,6 +385,7 @@ CUtensorMap make_tmap_thd(const void* ptr, int64_t T, int64_t H, int64_t D, int 
   cuuint64_t strides[2] = {(cuuint64_t)(D * 2), (cuuint64_t)(H * D * 2)};
   cuuint32_t box[3] = {64, 1, (cuuint32_t)rows};
   cuuint32_t estr[3] = {1, 1, 1};
+  bind_primary_context();
   CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);

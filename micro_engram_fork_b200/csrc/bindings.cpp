@@ -73,7 +73,15 @@ std::vector<torch::Tensor> attn_bwd_mat(torch::Tensor dout, torch::Tensor q, tor
                                         torch::Tensor o, torch::Tensor lse, torch::Tensor doc_start, int64_t window,
                                         double scale, int64_t tile_budget_bytes);
 // gemm.cu
-torch::Tensor gemm_tc(torch::Tensor A, torch::Tensor B, int64_t block_n);
+torch::Tensor gemm(torch::Tensor A, torch::Tensor W, bool b_kmajor, c10::optional<torch::Tensor> out);
+std::vector<torch::Tensor> gemm_geglu(torch::Tensor A, torch::Tensor Wgu, bool save_gu);
+torch::Tensor gemm_dgeglu(torch::Tensor dY, torch::Tensor Wdown, torch::Tensor gu);
+torch::Tensor gemm_f32(torch::Tensor A, torch::Tensor W);
+torch::Tensor gemm_tn_f32(torch::Tensor At, torch::Tensor Bt);
+void gemm_carry_copy(int64_t device, int64_t segs, int64_t nsegs, int64_t begin16, int64_t end16);
+void layer_gather(torch::Tensor segs, int64_t begin16, int64_t end16);
+std::vector<torch::Tensor> gemm_ce(torch::Tensor H, torch::Tensor E, torch::Tensor labels, int64_t lab_start,
+                                   double cap, bool keep_logits, int64_t n_valid);
 torch::Tensor gemm_status(int64_t device);
 // nf4.cu
 std::vector<torch::Tensor> nf4_quantize(torch::Tensor w);
@@ -117,7 +125,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd_tc", &attn_bwd_tc);
   m.def("attn_bwd_mat", &attn_bwd_mat);
   m.def("p2p_allreduce_mean", &p2p_allreduce_mean);
-  m.def("gemm_tc", &gemm_tc, py::arg("A"), py::arg("B"), py::arg("block_n") = 256);
+  m.def("gemm", &gemm, py::arg("A"), py::arg("W"), py::arg("b_kmajor") = true, py::arg("out") = py::none());
+  m.def("gemm_geglu", &gemm_geglu);
+  m.def("gemm_dgeglu", &gemm_dgeglu);
+  m.def("gemm_f32", &gemm_f32);
+  m.def("gemm_tn_f32", &gemm_tn_f32);
+  m.def("gemm_carry_copy", &gemm_carry_copy);
+  m.def("layer_gather", &layer_gather);
+  m.def("gemm_ce", &gemm_ce);
   m.def("gemm_status", &gemm_status);
   m.def("nf4_quantize", &nf4_quantize);
   m.def("nf4_dequant", &nf4_dequant);

@@ -12,6 +12,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include "act.cuh"
 #include "common.cuh"
 
 using namespace me;
@@ -20,7 +21,9 @@ namespace {
 using bf16 = __nv_bfloat16;
 constexpr int64_t kIgnore = -100;
 
-ME_DEVICE float capz(float z, float cap) { return cap > 0.f ? tanhf(z / cap) * cap : z; }
+// Same softcap evaluation as the tcgen05 head GEMM's CE epilogue (gemm.cu), so the backward's
+// probabilities use exactly the logits the forward's log-sum-exp saw.
+ME_DEVICE float capz(float z, float cap) { return cap > 0.f ? softcap_fast(z, cap) : z; }
 
 ME_DEVICE void merge(float& m, float& s, float m2, float s2) {
   if (m2 == -INFINITY) return;
@@ -30,7 +33,7 @@ ME_DEVICE void merge(float& m, float& s, float m2, float s2) {
     return;
   }
   const float mx = fmaxf(m, m2);
-  s = s * expf(m - mx) + s2 * expf(m2 - mx);
+  s = s * exp2_fast((m - mx) * kLog2e) + s2 * exp2_fast((m2 - mx) * kLog2e);
   m = mx;
 }
 
@@ -55,7 +58,7 @@ __global__ void ce_fwd_kernel(const bf16* __restrict__ z, int64_t M, int64_t V, 
       }
       float ls = 0.f;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ls += expf(c[e] - lm);
+      for (int e = 0; e < 8; ++e) ls += exp2_fast((c[e] - lm) * kLog2e);
       merge(m, s, lm, ls);
     }
     for (int64_t j = nvec * 8 + threadIdx.x; j < V; j += blockDim.x) merge(m, s, capz(bf2f(row[j]), cap), 1.f);
@@ -107,7 +110,7 @@ __global__ void ce_bwd_kernel(bf16* __restrict__ z, int64_t M, int64_t V, const 
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const float zc = capz(bf2f(x.h[e]), cap);
-        float p = expf(zc - l);
+        float p = exp2_fast((zc - l) * kLog2e);
         if (i * 8 + e == loc) p -= 1.f;
         float gr = p * w;
         if (cap > 0.f) {
@@ -120,7 +123,7 @@ __global__ void ce_bwd_kernel(bf16* __restrict__ z, int64_t M, int64_t V, const 
     }
     for (int64_t j = nvec * 8 + threadIdx.x; j < V; j += blockDim.x) {
       const float zc = capz(bf2f(row[j]), cap);
-      float p = expf(zc - l);
+      float p = exp2_fast((zc - l) * kLog2e);
       if (j == loc) p -= 1.f;
       float gr = p * w;
       if (cap > 0.f) {

@@ -1,221 +1,92 @@
-// tcgen05 GEMM for sm_100a: D[M, N] = A[M, K] . B[N, K]^T, bf16 operands, fp32 accumulation
-// in tensor memory, bf16 output.
-//
-// One CTA computes a 128 x BN tile with three warp roles (192 threads):
-//   warp 0      TMA producer: one elected thread streams 64-wide K blocks of A and B into a
-//               STAGES-deep ring of 128B-swizzled shared-memory stages (cp.async.bulk.tensor,
-//               no multicast), each stage guarded by a full/empty mbarrier pair
-//   warp 1      allocates the TMEM accumulator (BN fp32 columns x 128 lanes) and one elected
-//               thread issues tcgen05.mma (M=128, N=BN, K=16; 4 per stage) and tcgen05.commit
-//               to release each stage back to the producer and, at the end, to wake the epilogue
-//   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns at a time (each warp owns the TMEM
-//               lane quadrant warp%4), convert to bf16 and store
-// Every mbarrier wait is bounded (%globaltimer, 2 s); on expiry the kernel records
-// ME_ERR_TIMEOUT in the status word, the other roles stop, TMEM is freed and the kernel returns.
-#include <torch/extension.h>
-#include <ATen/cuda/CUDAContext.h>
-#include <c10/cuda/CUDAGuard.h>
+// Plain projections on the persistent tcgen05 GEMM (kernel and its design: gemm_kernel.cuh):
+// bf16 out for the decoder's forward and dX products, fp32 out for the LM head's dH.
+#include "gemm_kernel.cuh"
 
-#include <cudaTypedefs.h>
+using namespace me::gemm;
 
-#include <mutex>
-#include <unordered_map>
-
-#include "tc_common.cuh"
-
-using namespace me;
-using namespace me::tc;
-
-namespace {
-using bf16 = __nv_bfloat16;
-constexpr int BM = 128, BK = 64;
-
-template <int BN, int STAGES>
-struct GemmSmem {
-  static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
-  static constexpr int TILE_BYTES = STAGES * (A_BYTES + B_BYTES);
-  static constexpr int BYTES = TILE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
-  static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
-};
-
-template <int BN, int STAGES>
-__global__ void __launch_bounds__(192, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, bf16* __restrict__ D,
-                   int64_t ldd, int M, int N, int K, int* status) {
-  using S = GemmSmem<BN, STAGES>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * S::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::TILE_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* done = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-  const int nk = (K + BK - 1) / BK;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    mbar_init(done, 1);
-    *abort = 0;
-    fence_barrier_init();
-    prefetch_tmap(&ta);
-    prefetch_tmap(&tb);
-  }
-  if (warp == 1) tmem_alloc(tmem_slot, S::TMEM_COLS);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % STAGES, r = kb / STAGES;
-        if (r > 0 && !mbar_wait(&empty[s], (r - 1) & 1, status, 1, abort)) break;
-        mbar_expect_tx(&full[s], S::A_BYTES + S::B_BYTES);
-        tma_load_2d(sA + s * S::A_BYTES, &ta, &full[s], kb * BK, m0);
-        tma_load_2d(sB + s * S::B_BYTES, &tb, &full[s], kb * BK, n0);
-      }
-      // drain: make sure every issued copy has landed before the CTA can exit
-      const int first = nk > STAGES ? nk - STAGES : 0;
-      for (int kb = first; kb < nk; ++kb) mbar_wait(&full[kb % STAGES], (kb / STAGES) & 1, status, 4, nullptr);
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = idesc_bf16(BM, BN);
-      bool ok = true;
-      for (int kb = 0; kb < nk && ok; ++kb) {
-        const int s = kb % STAGES, r = kb / STAGES;
-        if (!mbar_wait(&full[s], r & 1, status, 2, abort)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t a0 = smem_addr(sA + s * S::A_BYTES), b0 = smem_addr(sB + s * S::B_BYTES);
-#pragma unroll
-        for (int k = 0; k < BK / 16; ++k)
-          umma_bf16(tmem, desc_sw128(a0 + k * 32), desc_sw128(b0 + k * 32), idesc, (kb | k) != 0);
-        umma_commit(&empty[s]);
-      }
-      if (ok) umma_commit(done);
-    }
-  } else {
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
-    if (mbar_wait(done, 0, status, 3, abort)) {
-      tc_fence_after();
-      const int row = m0 + q * 32 + lane;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        float v[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, v);
-        const int col = n0 + c * 32;
-        if (row < M) {
-          bf16* dst = D + (int64_t)row * ldd + col;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            if (col + j * 8 < N) {
-              BF16x8 o;
-#pragma unroll
-              for (int e = 0; e < 8; ++e) o.h[e] = f2bf(v[j * 8 + e]);
-              *reinterpret_cast<uint4*>(dst + j * 8) = o.u;
-            }
-          }
-        }
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, S::TMEM_COLS);
-  }
-}
-
-// ------------------------------------------------------------------ host: tensor maps
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    cudaDriverEntryPointQueryResult q;
-    void* p = nullptr;
-    cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
-    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  TORCH_CHECK(fn != nullptr, "cuTensorMapEncodeTiled is unavailable");
-  return fn;
-}
-
-// 2-D K-major bf16 operand [rows, K] (row stride ld elements), box 64 x box_rows, 128B swizzle.
-CUtensorMap make_tmap(const void* ptr, int64_t rows, int64_t K, int64_t ld, int box_rows) {
-  TORCH_CHECK(reinterpret_cast<uintptr_t>(ptr) % 16 == 0, "TMA operand base must be 16-byte aligned");
-  TORCH_CHECK((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
-  CUtensorMap map;
-  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
-  return map;
-}
-
-torch::Tensor& status_buffer(int dev) {
-  static std::unordered_map<int, torch::Tensor> bufs;
-  static std::mutex mu;
-  std::lock_guard<std::mutex> lk(mu);
-  auto it = bufs.find(dev);
-  if (it == bufs.end())
-    it = bufs.emplace(dev, torch::zeros({2}, torch::TensorOptions().dtype(torch::kInt32).device(torch::kCUDA, dev)))
-             .first;
-  return it->second;
-}
-
-template <int BN, int STAGES>
-void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, bf16* D, int64_t ldd, int M, int N, int K, int* st,
-                 cudaStream_t stream) {
-  using S = GemmSmem<BN, STAGES>;
-  auto kern = gemm_tc_kernel<BN, STAGES>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES);
-  dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
-  kern<<<grid, 192, S::BYTES, stream>>>(ta, tb, D, ldd, M, N, K, st);
-}
-
-}  // namespace
-
-// D = A . B^T (A [M, K], B [N, K], bf16, row-major) on the tcgen05 kernel.
-torch::Tensor gemm_tc(torch::Tensor A, torch::Tensor B, int64_t block_n) {
-  TORCH_CHECK(A.is_cuda() && B.is_cuda(), "gemm_tc: CUDA tensors");
-  TORCH_CHECK(A.scalar_type() == torch::kBFloat16 && B.scalar_type() == torch::kBFloat16, "gemm_tc: bf16");
-  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "gemm_tc: A [M,K], B [N,K]");
-  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1, "gemm_tc: K-major operands");
+// out[M, N] = A[M, K] . W^T, where W is [N, K] (b_kmajor) or W is [K, N] (the transposed use:
+// out = A . W). bf16 in, bf16 out, fp32 accumulation. `out` may be given (row stride >= N).
+torch::Tensor gemm(torch::Tensor A, torch::Tensor W, bool b_kmajor, c10::optional<torch::Tensor> out) {
+  check_operand(A, "A");
+  check_operand(W, "W");
   const at::cuda::CUDAGuard guard(A.device());
-  const int M = (int)A.size(0), N = (int)B.size(0), K = (int)A.size(1);
-  TORCH_CHECK(K % 8 == 0 && N % 8 == 0, "gemm_tc: K and N must be multiples of 8");
-  auto D = torch::empty({M, N}, A.options());
+  const int M = (int)A.size(0), K = (int)A.size(1);
+  const int N = (int)(b_kmajor ? W.size(0) : W.size(1));
+  TORCH_CHECK((b_kmajor ? W.size(1) : W.size(0)) == K, "gemm: inner dimensions differ");
+  TORCH_CHECK(N % 8 == 0 && K % 8 == 0, "gemm: N and K must be multiples of 8");
+  torch::Tensor D = out.has_value() ? *out : torch::empty({M, N}, A.options());
+  check_operand(D, "out");
+  TORCH_CHECK(D.size(0) == M && D.size(1) == N, "gemm: out shape");
   if (M == 0 || N == 0) return D;
+  if (K == 0) return D.zero_();
+  const int dev = A.get_device();
+  GemmArgs a = base_args(M, N, K, (N + BN - 1) / BN, dev);
+  a.D = reinterpret_cast<bf16*>(D.data_ptr());
+  a.ldd = D.stride(0);
   auto stream = at::cuda::getCurrentCUDAStream();
-  int* st = status_buffer(A.get_device()).data_ptr<int>();
-  auto* dp = reinterpret_cast<bf16*>(D.data_ptr());
-  const CUtensorMap ta = make_tmap(A.data_ptr(), M, K, A.stride(0), BM);
-  if (block_n == 128) {
-    const CUtensorMap tb = make_tmap(B.data_ptr(), N, K, B.stride(0), 128);
-    launch_gemm<128, 6>(ta, tb, dp, N, M, N, K, st, stream);
+  const CUtensorMap ta = make_tmap(A.data_ptr(), M, K, A.stride(0), BK, BM);
+  if (b_kmajor) {
+    const CUtensorMap tb = make_tmap(W.data_ptr(), N, K, W.stride(0), BK, BN / 2);
+    launch<EPI_STORE, false>(ta, tb, a, dev, stream);
   } else {
-    const CUtensorMap tb = make_tmap(B.data_ptr(), N, K, B.stride(0), 256);
-    launch_gemm<256, 4>(ta, tb, dp, N, M, N, K, st, stream);
+    const CUtensorMap tb = make_tmap(W.data_ptr(), K, N, W.stride(0), 64, BK);
+    launch<EPI_STORE, true>(ta, tb, a, dev, stream);
   }
   return D;
+}
+
+// out[M, N] (fp32) = A[M, K] . W, with W [K, N] read N-major (the LM head's dH = P . E).
+torch::Tensor gemm_f32(torch::Tensor A, torch::Tensor W) {
+  check_operand(A, "A");
+  check_operand(W, "W");
+  const at::cuda::CUDAGuard guard(A.device());
+  const int M = (int)A.size(0), K = (int)A.size(1), N = (int)W.size(1);
+  TORCH_CHECK(W.size(0) == K, "gemm_f32: inner dimensions differ");
+  TORCH_CHECK(N % 8 == 0 && K % 8 == 0, "gemm_f32: N and K must be multiples of 8");
+  auto D = torch::empty({M, N}, A.options().dtype(torch::kFloat32));
+  if (M == 0 || N == 0) return D;
+  if (K == 0) return D.zero_();
+  const int dev = A.get_device();
+  GemmArgs a = base_args(M, N, K, (N + BN - 1) / BN, dev);
+  a.Df = D.data_ptr<float>();
+  a.ldd = N;
+  const CUtensorMap ta = make_tmap(A.data_ptr(), M, K, A.stride(0), BK, BM);
+  const CUtensorMap tb = make_tmap(W.data_ptr(), K, N, W.stride(0), 64, BK);
+  launch<EPI_F32, true>(ta, tb, a, dev, at::cuda::getCurrentCUDAStream());
+  return D;
+}
+
+// out[M, N] (fp32) = At^T . Bt with At [K, M] and Bt [K, N] (both read with the reduction
+// dimension as rows): the weight gradient dW = dY^T . X of a projection y = x W^T.
+torch::Tensor gemm_tn_f32(torch::Tensor At, torch::Tensor Bt) {
+  check_operand(At, "At");
+  check_operand(Bt, "Bt");
+  const at::cuda::CUDAGuard guard(At.device());
+  const int K = (int)At.size(0), M = (int)At.size(1), N = (int)Bt.size(1);
+  TORCH_CHECK(Bt.size(0) == K, "gemm_tn_f32: At and Bt need the same number of rows");
+  TORCH_CHECK(M % 8 == 0 && N % 8 == 0, "gemm_tn_f32: M and N must be multiples of 8 (16-byte rows)");
+  auto D = torch::empty({M, N}, At.options().dtype(torch::kFloat32));
+  if (M == 0 || N == 0) return D;
+  if (K == 0) return D.zero_();
+  const int dev = At.get_device();
+  GemmArgs a = base_args(M, N, K, (N + BN - 1) / BN, dev);
+  a.Df = D.data_ptr<float>();
+  a.ldd = N;
+  const CUtensorMap ta = make_tmap(At.data_ptr(), K, M, At.stride(0), 64, BK);
+  const CUtensorMap tb = make_tmap(Bt.data_ptr(), K, N, Bt.stride(0), 64, BK);
+  launch<EPI_F32, true, true>(ta, tb, a, dev, at::cuda::getCurrentCUDAStream());
+  return D;
+}
+
+// The next GEMM launched on `device` also copies units [begin16, end16) of the segment table at
+// `segs` (int64 [nsegs, 4] on the device: src, dst, start16, n16) in its side-copy warp.
+void gemm_carry_copy(int64_t device, int64_t segs, int64_t nsegs, int64_t begin16, int64_t end16) {
+  TORCH_CHECK(nsegs >= 0 && begin16 >= 0 && end16 >= begin16, "gemm_carry_copy: bad range");
+  SideCopy& job = pending_copy((int)device);
+  job.segs = reinterpret_cast<const GatherSeg*>(segs);
+  job.nsegs = (int)nsegs;
+  job.begin16 = begin16;
+  job.end16 = end16;
 }
 
 torch::Tensor gemm_status(int64_t device) { return status_buffer((int)device); }

@@ -12,6 +12,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include "act.cuh"
 #include "common.cuh"
 
 using namespace me;
@@ -493,22 +494,6 @@ __global__ void __launch_bounds__(256, 4) qkv_norm_rope_bwd_kernel(
 
 // ---------------------------------------------------------------------------- GeGLU
 // gu [N, 2F] = [gate | up]; m = bf16(bf16(gelu_tanh(gate)) * up).
-// gelu_tanh(x) = 0.5 x (1 + tanh(y)), y = k0 (x + k1 x^3), evaluated as x * s with
-// s = 0.5 (1 + tanh(y)) = 1 / (1 + e^{-2y}): one exponential and one division per element
-// (and s -> 0 without cancellation for very negative x). Its derivative:
-// s + x * 0.5 (1 - tanh^2 y) y' = s + 2 x s (1 - s) k0 (1 + 3 k1 x^2).
-ME_DEVICE float gelu_gate(float x) {
-  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-  const float y = k0 * (x + k1 * x * x * x);
-  return __fdividef(1.f, 1.f + __expf(-2.f * y));
-}
-ME_DEVICE float gelu_tanh(float x) { return x * gelu_gate(x); }
-ME_DEVICE float gelu_tanh_grad(float x) {
-  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-  const float s = gelu_gate(x);
-  return s + 2.f * x * s * (1.f - s) * k0 * (1.f + 3.f * k1 * x * x);
-}
-
 // One block per row (grid-stride over rows), 16-byte vectors along the row: no index division.
 __global__ void geglu_fwd_kernel(const bf16* __restrict__ gu, int64_t N, int F, bf16* __restrict__ m) {
   const int fv = F / 8;

@@ -21,6 +21,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
+#include "gather.cuh"
 
 using namespace me;
 
@@ -100,7 +101,29 @@ __global__ void __launch_bounds__(256) p2p_allreduce_mean_kernel(const int64_t* 
   }
 }
 
+// The standalone form of a layer all-gather range: one warp per 32 threads, grid-strided.
+__global__ void __launch_bounds__(256) layer_gather_kernel(const GatherSeg* __restrict__ segs, int nsegs,
+                                                           int64_t begin16, int64_t end16) {
+  const int warps = blockDim.x / 32;
+  gather_range(segs, nsegs, begin16, end16, blockIdx.x * warps + threadIdx.x / 32, gridDim.x * warps,
+               threadIdx.x & 31);
+}
+
 }  // namespace
+
+// Copy units [begin16, end16) of a segment table (int64 [nsegs, 4] on the device: src, dst,
+// start16, n16) as a kernel of its own (the first layer of a pass, or what no GEMM carried).
+void layer_gather(torch::Tensor segs, int64_t begin16, int64_t end16) {
+  TORCH_CHECK(segs.is_cuda() && segs.scalar_type() == torch::kInt64 && segs.dim() == 2 && segs.size(1) == 4 &&
+                  segs.is_contiguous(), "layer_gather: segs must be a contiguous int64 [n, 4] CUDA tensor");
+  if (end16 <= begin16 || segs.size(0) == 0) return;
+  const at::cuda::CUDAGuard guard(segs.device());
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, segs.get_device());
+  layer_gather_kernel<<<sms * 2, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const GatherSeg*>(segs.data_ptr<int64_t>()), (int)segs.size(0), begin16, end16);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
 
 // out[n] fp32 = (sum over ranks of their stage[call & 1][:n]) * scale. `bases` [world] int64:
 // every rank's symmetric-buffer base address (this rank's own at index `rank`).

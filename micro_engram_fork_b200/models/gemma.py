@@ -31,6 +31,7 @@ import torch.nn.functional as F
 from ..ops import use_native
 from ..ops import norm as N
 from ..ops.attention import attention_torch, doc_starts
+from ..ops.linear import dgeglu_linear, geglu_linear, linear, linear_t
 
 
 # ----------------------------------------------------------------------------- config
@@ -303,35 +304,40 @@ def _ls(layer):
     return layer.layer_scalar.float().reshape(1).contiguous()
 
 
-def _materialize(layer):
-    """NF4 base: expand this layer's weights into the shared bf16 buffer before they are read."""
+def _materialize(layer, direction=1):
+    """Make this layer's full bf16 weights readable before it runs: an NF4 base expands them into
+    the shared buffer; a sharded base gathers them from the peers (what the previous GEMMs did
+    not already carry) and hands the next layer's gather (`direction` +1 forward, -1 backward)
+    to this layer's GEMMs."""
     if getattr(layer, "_nf4", None) is not None:
         from .nf4 import materialize
 
         materialize(layer)
+    sb = getattr(layer, "_sharded", None)
+    if sb is not None:
+        sb.materialize(layer, direction)
 
 
-def _layer_fwd(layer, x, pos, doc_start, keep=False):
+def _layer_fwd(layer, x, pos, doc_start, keep=False, direction=1):
     """Native forward of one layer; returns (out, saved dict or None)."""
     from ..ops.attention import attention_fwd
 
-    _materialize(layer)
+    _materialize(layer, direction)
     cfg = layer.cfg
     eps = cfg.rms_norm_eps
     T = x.shape[0]
     hd = layer.head_dim
     att = layer.self_attn
     h1, r_in = N.rmsnorm(x, layer.input_layernorm.weight, eps)
-    qkv = F.linear(h1, layer.qkv_weight)
+    qkv = linear(h1, layer.qkv_weight)
     q, k, v, r_qkv = N.qkv_norm_rope(qkv, att.q_norm.weight, att.k_norm.weight, layer.inv_freq, pos, layer.n_q,
                                      layer.n_kv, hd, layer.kv_eq, eps)
     a, lse = attention_fwd(q, k, v, doc_start, layer.window, 1.0)
-    o = F.linear(a.view(T, -1), att.o_proj.weight)
+    o = linear(a.view(T, -1), att.o_proj.weight)
     x2, h2, r_o, r_x2 = N.post_norm_add(x, o, layer.post_attention_layernorm.weight, None,
                                         layer.pre_feedforward_layernorm.weight, eps)
-    gu = F.linear(h2, layer.gate_up_weight)
-    m = N.geglu(gu)
-    dn = F.linear(m, layer.mlp.down_proj.weight)
+    m, gu = geglu_linear(h2, layer.gate_up_weight, save_gu=keep)
+    dn = linear(m, layer.mlp.down_proj.weight)
     x3, _, r_dn, _ = N.post_norm_add(x2, dn, layer.post_feedforward_layernorm.weight, _ls(layer), None, eps)
     saved = None
     if keep:
@@ -345,10 +351,10 @@ _SAVE_KEYS = ("r_in", "qkv", "q", "k", "v", "r_qkv", "a", "lse", "o", "x2", "r_o
 _SELECTIVE_KEYS = ("qkv", "a", "lse", "o")
 
 
-def _recompute_selective(layer, x, pos, kept):
+def _recompute_selective(layer, x, pos, kept, direction=-1):
     """Rebuild a layer's saved state from its input and the kept attention tensors: norms,
     RoPE and the MLP are recomputed; the q/k/v and o projections and attention are not."""
-    _materialize(layer)
+    _materialize(layer, direction)
     eps = layer.cfg.rms_norm_eps
     att = layer.self_attn
     _, r_in = N.rmsnorm(x, layer.input_layernorm.weight, eps)
@@ -356,8 +362,8 @@ def _recompute_selective(layer, x, pos, kept):
                                      layer.n_q, layer.n_kv, layer.head_dim, layer.kv_eq, eps)
     x2, h2, r_o, r_x2 = N.post_norm_add(x, kept["o"], layer.post_attention_layernorm.weight, None,
                                         layer.pre_feedforward_layernorm.weight, eps)
-    gu = F.linear(h2, layer.gate_up_weight)
-    dn = F.linear(N.geglu(gu), layer.mlp.down_proj.weight)
+    m, gu = geglu_linear(h2, layer.gate_up_weight, save_gu=True)
+    dn = linear(m, layer.mlp.down_proj.weight)
     _, _, r_dn, _ = N.post_norm_add(x2, dn, layer.post_feedforward_layernorm.weight, _ls(layer), None, eps)
     return dict(r_in=r_in, qkv=kept["qkv"], q=q, k=k, v=v, r_qkv=r_qkv, a=kept["a"], lse=kept["lse"], o=kept["o"],
                 x2=x2, r_o=r_o, r_x2=r_x2, gu=gu, dn=dn, r_dn=r_dn)
@@ -393,7 +399,7 @@ class _LayerFn(torch.autograd.Function):
         from ..ops.attention import attention_bwd
 
         layer = ctx.layer
-        _materialize(layer)
+        _materialize(layer, -1)
         cfg = layer.cfg
         att = layer.self_attn
         tensors = ctx.saved_tensors
@@ -411,7 +417,7 @@ class _LayerFn(torch.autograd.Function):
                     layer.head_dim, layer.kv_eq, cfg.rms_norm_eps)
         elif ctx.checkpoint:
             with torch.no_grad():
-                _, s = _layer_fwd(layer, x, pos, doc_start, keep=True)
+                _, s = _layer_fwd(layer, x, pos, doc_start, keep=True, direction=-1)
         else:
             s = dict(zip(_SAVE_KEYS, tensors[3:]))
         T = x.shape[0]
@@ -419,17 +425,16 @@ class _LayerFn(torch.autograd.Function):
         # MLP block: x3 = (x2 + n(dn)) * ls
         d_x2_res, d_dn = N.post_norm_add_bwd(g, None, s["dn"], s["dn"], layer.post_feedforward_layernorm.weight,
                                              _ls(layer), None, s["r_dn"], None)
-        d_m = torch.matmul(d_dn, layer.mlp.down_proj.weight)
-        d_gu = N.geglu_bwd(d_m, s["gu"])
-        d_h2 = torch.matmul(d_gu, layer.gate_up_weight)
+        d_gu = dgeglu_linear(d_dn, layer.mlp.down_proj.weight, s["gu"])
+        d_h2 = linear_t(d_gu, layer.gate_up_weight)
         # attention block: x2 = x + n(o); h2 = n(x2)
         d_x_res, d_o = N.post_norm_add_bwd(d_x2_res, d_h2, s["o"], s["x2"], layer.post_attention_layernorm.weight,
                                            None, layer.pre_feedforward_layernorm.weight, s["r_o"], s["r_x2"])
-        d_a = torch.matmul(d_o, att.o_proj.weight).view_as(s["a"])
+        d_a = linear_t(d_o, att.o_proj.weight).view_as(s["a"])
         dq, dk, dv = attention_bwd(d_a, s["q"], s["k"], s["v"], s["a"], s["lse"], doc_start, layer.window, 1.0)
         d_qkv = N.qkv_norm_rope_bwd(dq, dk, dv, s["qkv"], att.q_norm.weight, att.k_norm.weight, layer.inv_freq,
                                     pos, s["r_qkv"], layer.n_q, layer.n_kv, layer.head_dim, layer.kv_eq)
-        d_h1 = torch.matmul(d_qkv, layer.qkv_weight)
+        d_h1 = linear_t(d_qkv, layer.qkv_weight)
         dx = N.rmsnorm_bwd(d_h1, x, layer.input_layernorm.weight, s["r_in"], d_x_res)
         return dx, None, None, None, None
 

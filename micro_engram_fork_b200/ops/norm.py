@@ -47,6 +47,17 @@ def geglu_ref(gu):
     return F.gelu(g, approximate="tanh") * u
 
 
+def geglu_bwd_ref(dm, gu):
+    """d gu = [dm * u * gelu'(g) | dm * gelu(g)] (tanh GELU), computed in fp32."""
+    g, u = gu.float().chunk(2, dim=-1)
+    dm = dm.float()
+    k0, k1 = 0.7978845608028654, 0.044715
+    t = torch.tanh(k0 * (g + k1 * g * g * g))
+    gelu = 0.5 * g * (1.0 + t)
+    dgelu = 0.5 * (1.0 + t) + 0.5 * g * (1.0 - t * t) * k0 * (1.0 + 3.0 * k1 * g * g)
+    return torch.cat((dm * u * dgelu, dm * gelu), dim=-1).to(gu.dtype)
+
+
 # ------------------------------------------------------------------------- native entry points
 def rmsnorm(x, w=None, eps=1e-6):
     """(y, rstd) on CUDA."""

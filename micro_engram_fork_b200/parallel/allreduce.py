@@ -16,6 +16,13 @@ from .symm import SymmBuffer
 _FLAG_BYTES = 256  # flags [world <= 16] u32, padded
 
 
+def zero_on_error(out, status):
+    """A call whose bounded wait ran out leaves `out` unwritten, or partly written (stale or
+    uninitialised values). Replace it by zeros, decided on the device, so no step trains on
+    garbage before the host reads the status word at its next logging step and stops the run."""
+    return out.masked_fill_(status[:1] != 0, 0.0)
+
+
 class P2PAllReduce:
     def __init__(self, n, device, group=None, timeout_s=10.0):
         self.n = int(n)
@@ -51,7 +58,7 @@ class P2PAllReduce:
             raise ValueError(f"P2PAllReduce: got {k} values, built for {self.n}")
         native().p2p_allreduce_mean(self.bases, self.rank, self.stage_off, self.n, self.calls, 1.0 / self.world,
                                     self.timeout_s, self.out, self.status)
-        return self.out
+        return zero_on_error(self.out, self.status)
 
     def check_status(self):
         st = self.status.tolist()

@@ -45,16 +45,52 @@ def _docs(T, dev, lens=(2000, 3000, 1192, 2000)):
     return doc_starts(pos)
 
 
-def case_gemm(C, dev, it, pk):
-    """Engram key projection shape: [8192 tokens x 1536] x [5376 x 1536]^T."""
-    A = torch.randn(8192, 1536, device=dev).to(torch.bfloat16)
-    B = (torch.randn(5376, 1536, device=dev) / 40).to(torch.bfloat16)
-    flops = 2 * 8192 * 5376 * 1536
+GEMM_SHAPES = (
+    # name, N, K, kind: "nt" = x . W^T (W [N, K]), "nn" = g . W (W [K, N]), "geglu" (N = F), "dgeglu" (N = F)
+    ("qkv_sliding", 16384, 5376, "nt"), ("qkv_global", 18432, 5376, "nt"), ("o_sliding", 5376, 8192, "nt"),
+    ("o_global", 5376, 16384, "nt"), ("gate_up_geglu", 21504, 5376, "geglu"), ("down", 5376, 21504, "nt"),
+    ("d_down_dgeglu", 21504, 5376, "dgeglu"), ("d_gate_up", 5376, 43008, "nn"), ("d_o_sliding", 8192, 5376, "nn"),
+    ("d_qkv_sliding", 5376, 16384, "nn"), ("lm_head_chunk", 262144, 5376, "nt_m2048"),
+)
+
+
+def case_gemm(C, dev, it, pk, M=8192, only=None):
+    """The decoder's projections at 8192 tokens (and one 2048-token LM-head chunk): the
+    tcgen05 GEMM (with its fused GeGLU / GeGLU-backward epilogues) against cuBLAS
+    (torch.matmul, plus the separate GeGLU kernels where the epilogue is fused)."""
     out = {}
-    for name, fn in (("tcgen05 gemm_tc", lambda: C.gemm_tc(A, B, 256)), ("cuBLAS (torch.matmul)", lambda: A @ B.t())):
-        ms = _time(fn, it)
-        out[name] = {"ms": round(ms, 4), "tflops": round(flops / ms / 1e9, 1),
-                     "frac_of_peak": round(flops / ms / 1e9 / pk["bf16_tflops"], 3)}
+    for name, N, K, kind in GEMM_SHAPES:
+        if only and name not in only:
+            continue
+        m = 2048 if kind == "nt_m2048" else M
+        A = torch.randn(m, K, device=dev).to(torch.bfloat16)
+        if kind in ("nt", "nt_m2048"):
+            W = (torch.randn(N, K, device=dev) / K ** 0.5).to(torch.bfloat16)
+            ours, lib = (lambda: C.gemm(A, W, True, None)), (lambda: A @ W.t())
+            flops = 2 * m * N * K
+        elif kind == "nn":
+            W = (torch.randn(K, N, device=dev) / K ** 0.5).to(torch.bfloat16)
+            ours, lib = (lambda: C.gemm(A, W, False, None)), (lambda: A @ W)
+            flops = 2 * m * N * K
+        elif kind == "geglu":
+            W = (torch.randn(2 * N, K, device=dev) / K ** 0.5).to(torch.bfloat16)
+            ours = lambda: C.gemm_geglu(A, W, True)
+            lib = lambda: C.geglu_fwd(A @ W.t())
+            flops = 2 * m * 2 * N * K
+        else:  # dgeglu
+            W = (torch.randn(K, N, device=dev) / K ** 0.5).to(torch.bfloat16)
+            gu = torch.randn(m, 2 * N, device=dev).to(torch.bfloat16)
+            ours = lambda: C.gemm_dgeglu(A, W, gu)
+            lib = lambda: C.geglu_bwd(A @ W, gu)
+            flops = 2 * m * N * K
+        row = {"M": m, "N": N, "K": K, "kind": kind}
+        for tag, fn in (("tcgen05", ours), ("cublas", lib)):
+            ms = _time(fn, it)
+            row[tag] = {"ms": round(ms, 4), "tflops": round(flops / ms / 1e9, 1),
+                        "frac_of_peak": round(flops / ms / 1e9 / pk["bf16_tflops"], 3)}
+        row["speedup_vs_cublas"] = round(row["cublas"]["ms"] / row["tcgen05"]["ms"], 3)
+        out[name] = row
+        del A, W
     return out
 
 
@@ -190,6 +226,7 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default="all", choices=["all"] + list(CASES))
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--gemm-shapes", default="", help="comma-separated subset of GEMM_SHAPES names")
     args = ap.parse_args(argv)
     from .. import native
 
@@ -200,7 +237,10 @@ def main(argv=None):
     res = {"peaks": pk}
     for name, fn in CASES.items():
         if args.case in ("all", name):
-            res[name] = fn(C, dev, args.iters, pk)
+            if name == "gemm" and args.gemm_shapes:
+                res[name] = fn(C, dev, args.iters, pk, only=set(args.gemm_shapes.split(",")))
+            else:
+                res[name] = fn(C, dev, args.iters, pk)
     res["status"] = {"gemm": C.gemm_status(0).tolist(), "attn_tc": C.attn_tc_status(0).tolist()}
     print(json.dumps(res, indent=1))
 

@@ -146,7 +146,7 @@ def test_request_rules():
             "sequence_len": 32, "output_dir": "/tmp/x", "micro_engram_layer": 1, "micro_engram_table_size": 97,
             "micro_engram_table_sizes": {2: 97, 3: 131, 4: 0}}
     reqs = engram_requests(load_config({**base, "micro_engram_extra": [{"layer": 3}]}))
-    sizes = [r[0].get("table_sizes") for r in reqs]
+    sizes = [r.spec.get("table_sizes") for r in reqs]
     assert sizes[0] == sizes[1] and 4 not in (sizes[0] or {}) or not (sizes[0] or {}).get(4)
     with pytest.raises(ValueError):
         engram_requests(load_config({**base, "micro_engram_extra": [{"layer": 1}]}))

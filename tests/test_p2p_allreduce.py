@@ -50,9 +50,15 @@ def test_emulated_two_ranks_sum(n):
 
 @pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
 def test_missing_peer_times_out():
+    from micro_engram_fork_b200.parallel.allreduce import zero_on_error
+
     out, status, _ = _emulated(1024, False)
     assert status.tolist() == [1, 1]  # ME_ERR_TIMEOUT, waiting on rank 1
     assert bool(torch.isnan(out).all())  # nothing written
+    # what the trainer copies into the gradients after such a call: zeros, never the unwritten
+    # (here NaN) buffer or a previous call's result
+    guarded = zero_on_error(out, status)
+    assert bool((guarded == 0).all())
 
 
 def _worker(rank, world, port, q):
