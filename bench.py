@@ -88,6 +88,9 @@ def bench_config(tmp, steps):
         "gradient_checkpointing": True, "activation_offloading": True, "micro_engram_stats_steps": 0,
         "gradient_checkpointing_policy": os.environ.get("ME_BENCH_AC", "auto"),
         "gradient_checkpointing_reserve_gib": float(os.environ.get("ME_BENCH_AC_RESERVE", "23")),
+        # config 3 is FSDP2: the frozen base row-sharded over the GPUs (ME_BENCH_PLACEMENT=replicated
+        # runs the replicated-base variant instead)
+        "base_placement": os.environ.get("ME_BENCH_PLACEMENT", "sharded"),
         "seed": 42,
     }
 
@@ -290,7 +293,10 @@ def run_ours(args):
             "vs_baseline": None if not BASELINE_VALUE else round(value / BASELINE_VALUE, 4),
             "dtype": "bf16", "data": "synthetic (Zipf(1.1) packed docs 256-4096, random-init weights)",
             "config": {"model": MODEL, "global_batch": MBS * GA * world, "seq_len": SEQ,
-                       "parallelism": f"dp{world} (replicated frozen base, row-sharded engram, vocab-parallel head)",
+                       "parallelism": (f"fsdp{world} (row-sharded frozen base, layer all-gathers carried by the "
+                                       "tcgen05 GEMMs; row-sharded engram; vocab-parallel head)"
+                                       if trainer.placement == "sharded" else
+                                       f"dp{world} (replicated frozen base, row-sharded engram, vocab-parallel head)"),
                        "engram": "layer 0, tables {2:1572864,3:4194304,4:4194304} x8 heads x dim 64, "
                                  "scalar_sqrt, rowwise_adam bf16+SR",
                        "activation_checkpointing": f"per-layer, policy {trainer.cfg.gradient_checkpointing_policy}"
@@ -366,7 +372,8 @@ def run_reference(args):
 
     tmp = tempfile.mkdtemp(prefix="me_ref_")
     c = bench_config(tmp, args.warmup + 2 * args.steps + 2)
-    for k in ("base_init", "gradient_checkpointing_policy", "gradient_checkpointing_reserve_gib"):  # not reference keys
+    for k in ("base_init", "gradient_checkpointing_policy", "gradient_checkpointing_reserve_gib",
+              "base_placement"):  # not reference keys
         c.pop(k)
     # the reference's recommended B200-runnable kernel settings (README example config)
     # (fused_attn_kernel off: that patch's shared-KV side channel is None under the installed

@@ -37,76 +37,87 @@ def resolve_order_sizes(table_size, orders=(2, 3), table_sizes=None):
     return sizes
 
 
-class MicroEngram(nn.Module):
-    """Hashed n-gram memory (Engram-style) with a learned gate into the hidden state.
+def hash_multipliers(seed, n_tables, max_order):
+    """The odd multipliers of the n-gram hash, one row per table. This is a stored contract:
+    trained tables are addressed through these numbers, so they must be reproduced bit for bit
+    from the seed (a CPU torch.Generator seeded with `seed`, one randint draw of shape
+    [n_tables, max_order] in [1, 2^31 - 1), low bit forced on)."""
+    gen = torch.Generator().manual_seed(seed)
+    return torch.randint(1, _PRIME, (n_tables, max_order), generator=gen, device="cpu") | 1
 
-    At position t, the 2-, 3- (optionally 4-) grams ending at t are hashed into `num_heads`
-    tables per order; the rows are concatenated into `mem` [.., n_tables*engram_dim].
+
+class MicroEngram(nn.Module):
+    """Hashed n-gram memory (Engram-style) whose rows are gated into a decoder's hidden state.
+
+    For position t, every n-gram order (2, 3, optionally 4) has `num_heads` tables; the n-gram
+    ending at t is hashed into each of them and the rows found are concatenated into `mem`
+    [.., n_tables * engram_dim] (tables in order-major, then head, order).
 
     Gates:
-      scalar       alpha = sigmoid(<rms(h), rms(key(mem))> / sqrt(d)); h += alpha * value(mem)
-      scalar_sqrt  as scalar with a signed square root on the score and learnable norm
-                   scales q_scale / k_scale (stored as delta from 1)
-      ple          g = gelu_tanh(down(rms(h))); h += up(g * mem)
+      scalar       h += sigmoid(<rms(h), rms(key(mem))> / sqrt(d)) * value(mem)
+      scalar_sqrt  the same with a signed square root on the score, and learnable RMS-norm
+                   scales on both sides of the score (kept as offsets from 1, see norm_scales)
+      ple          h += up(gelu_tanh(down(rms(h))) * mem)
+    The output projection (value, or up) starts at zero, so a new engram changes nothing.
     """
 
     GATES = ("scalar", "ple", "scalar_sqrt")
     SCALAR_GATES = ("scalar", "scalar_sqrt")
     DELTA_SCALES = ("q_scale", "k_scale")
 
-    # row sharding state: plain attributes, outside parameters()/state_dict()
+    # row-sharding state lives in plain attributes, outside parameters() and the state dict
     row_shards = None
     row_info = None
     row_store = None
-    row_lookup_fn = None  # a server's own lookup for row-sharded tables (vLLM tensor parallel)
+    row_lookup_fn = None  # a server's own lookup over row-sharded tables (vLLM tensor parallelism)
 
     def __init__(self, model_dim, table_size=65_536, engram_dim=128, num_heads=4, orders=(2, 3), pad_id=0,
                  seed=0, vocab_size=262_144, canon=None, gate="scalar", build_tables=True, table_sizes=None):
         super().__init__()
         if gate not in self.GATES:
             raise ValueError(f"gate must be one of {self.GATES}, got {gate!r}")
-        self.gate = gate
+        self.gate, self.engram_dim, self.seed, self.pad_id = gate, engram_dim, seed, pad_id
+        self._layout(table_size, orders, table_sizes, num_heads)
+        if build_tables:
+            self.tables = nn.ModuleList(nn.Embedding(rows, engram_dim) for rows in self.table_rows)
+            for table in self.tables:
+                nn.init.normal_(table.weight, std=0.02)
+        self._gate_weights(model_dim, engram_dim * len(self._table_orders))
+        self.register_buffer("mults", hash_multipliers(seed, len(self._table_orders), max(self.orders)))
+        self.register_buffer("canon", self._canon_map(canon, vocab_size))
+        self._dev_consts = {}
+
+    def _layout(self, table_size, orders, table_sizes, num_heads):
         self.order_sizes = resolve_order_sizes(table_size, orders, table_sizes)
         self.orders = tuple(self.order_sizes)
-        self.engram_dim = engram_dim
-        self.seed = seed
-        self.pad_id = pad_id
         self._table_orders = [n for n in self.orders for _ in range(num_heads)]
         self.table_rows = [self.order_sizes[n] for n in self._table_orders]
-        self.table_size = self.table_rows[0] if len(set(self.table_rows)) == 1 else None
-        n_tables = len(self._table_orders)
+        uniform = len(set(self.table_rows)) == 1
+        self.table_size = self.table_rows[0] if uniform else None
 
-        if build_tables:
-            self.tables = nn.ModuleList(nn.Embedding(r, engram_dim) for r in self.table_rows)
-            for t in self.tables:
-                nn.init.normal_(t.weight, std=0.02)
-
-        mem_dim = engram_dim * n_tables
-        if gate in self.SCALAR_GATES:
-            self.key = nn.Linear(mem_dim, model_dim, bias=False)
-            self.value = nn.Linear(mem_dim, model_dim, bias=False)
-            nn.init.zeros_(self.value.weight)  # exact no-op at step 0
-            if gate == "scalar_sqrt":
-                # scale = 1 + delta: an Adam step near 1.0 would round away in bf16 (spacing 1/128)
-                self.q_scale = nn.Parameter(torch.zeros(model_dim))
-                self.k_scale = nn.Parameter(torch.zeros(model_dim))
-        else:
+    def _gate_weights(self, model_dim, mem_dim):
+        if self.gate == "ple":
             self.down = nn.Linear(model_dim, mem_dim, bias=False)
             self.up = nn.Linear(mem_dim, model_dim, bias=False)
             nn.init.zeros_(self.up.weight)
+            return
+        self.key = nn.Linear(mem_dim, model_dim, bias=False)
+        self.value = nn.Linear(mem_dim, model_dim, bias=False)
+        nn.init.zeros_(self.value.weight)
+        if self.gate == "scalar_sqrt":
+            # stored as offsets from 1: in bf16 the spacing near 1.0 is 1/128, so an Adam step on
+            # the scale itself would mostly round away
+            self.q_scale = nn.Parameter(torch.zeros(model_dim))
+            self.k_scale = nn.Parameter(torch.zeros(model_dim))
 
-        # hash multipliers: deterministic from the seed (a CPU generator, whatever the default device)
-        gen = torch.Generator().manual_seed(seed)
-        mults = torch.randint(1, _PRIME, (n_tables, max(self.orders)), generator=gen, device="cpu") | 1
-        self.register_buffer("mults", mults)
+    @staticmethod
+    def _canon_map(canon, vocab_size):
         if canon is None:
-            canon = torch.arange(vocab_size)
-        else:
-            canon = torch.as_tensor(canon).long().clone()
-            if canon.shape != (vocab_size,):
-                raise ValueError(f"canon must have shape ({vocab_size},), got {tuple(canon.shape)}")
-        self.register_buffer("canon", canon)
-        self._dev_consts = {}
+            return torch.arange(vocab_size)
+        canon = torch.as_tensor(canon).long().clone()
+        if canon.shape != (vocab_size,):
+            raise ValueError(f"canon must have shape ({vocab_size},), got {tuple(canon.shape)}")
+        return canon
 
     # ------------------------------------------------------------------ row sharding
     def shard_rows(self, rank, world, device=None, dtype=None, requires_grad=True, empty=False, pin_memory=False,
@@ -378,33 +389,26 @@ def find_text_layers(model):
 
 
 def engram_from_spec(spec, model_dim, vocab_size, pad_default=0, canon=None, build_tables=True):
-    """A MicroEngram from one engram spec (see weights.engram_specs); the seed fixes the hash."""
-    return MicroEngram(
-        model_dim=model_dim,
-        table_size=spec["table_size"],
-        table_sizes=spec.get("table_sizes"),
-        engram_dim=spec["engram_dim"],
-        num_heads=spec["num_heads"],
-        orders=tuple(spec.get("orders") or (2, 3)),
-        pad_id=spec["pad_id"] if spec.get("pad_id") is not None else pad_default,
-        seed=spec.get("seed") or 0,
-        vocab_size=vocab_size,
-        canon=canon,
-        gate=spec.get("gate") or "scalar",
-        build_tables=build_tables,
-    )
+    """Build the MicroEngram a config spec describes (weights.engram_specs); its seed fixes the
+    hash, so the same spec always addresses the same rows."""
+    pad = spec.get("pad_id")
+    kw = dict(table_size=spec["table_size"], table_sizes=spec.get("table_sizes"), engram_dim=spec["engram_dim"],
+              num_heads=spec["num_heads"], orders=tuple(spec.get("orders") or (2, 3)),
+              pad_id=pad_default if pad is None else pad, seed=spec.get("seed") or 0, gate=spec.get("gate") or "scalar")
+    return MicroEngram(model_dim=model_dim, vocab_size=vocab_size, canon=canon, build_tables=build_tables, **kw)
 
 
 def check_loaded(engram, sd, where):
-    """Strictly load `sd` into `engram`. `mults` may be absent (rebuilt from the seed) but,
-    when present, must equal the seed's: a different one means a wrong seed."""
-    if "mults" in sd and not torch.equal(sd["mults"].to(engram.mults.device).long(), engram.mults.long()):
-        raise ValueError(f"[micro_engram] {where}: the saved hash multipliers differ from the ones this engram's "
-                         f"seed gives; the seed is wrong for these weights")
+    """Load `sd` into `engram`, refusing any mismatch. Saved `mults` may be missing (the seed
+    rebuilds them); when present they must be the seed's, or the seed is wrong for the tables."""
+    saved_mults = sd.get("mults")
+    if saved_mults is not None and not torch.equal(saved_mults.to(engram.mults.device).long(), engram.mults.long()):
+        raise ValueError(f"[micro_engram] {where}: the saved hash multipliers are not the ones this engram's seed "
+                         "gives, so the seed does not belong to these weights")
     result = engram.load_state_dict(sd, strict=False)
-    problems = [k for k in result.missing_keys if k != "mults"] + list(result.unexpected_keys)
-    if problems:
-        raise ValueError(f"[micro_engram] {where} does not match the engram settings: {problems[:10]}")
+    mismatch = [k for k in result.missing_keys if k != "mults"] + list(result.unexpected_keys)
+    if mismatch:
+        raise ValueError(f"[micro_engram] {where} does not fit the engram settings: {mismatch[:10]}")
     return result
 
 

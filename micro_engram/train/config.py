@@ -10,8 +10,10 @@ Keys this framework adds (all optional, defaults keep the reference's behaviour)
   base_init            "load" (weights from base_model) or "random" (random-init weights of
                        base_model's config.json: synthetic benchmarking)
   base_placement       "auto" | "replicated" | "sharded": the frozen base on every GPU, or
-                       row-sharded with a per-layer all-gather (FSDP semantics); auto picks
-                       replicated when it fits in HBM
+                       row-sharded over the GPUs with FSDP2 semantics (each layer gathered for
+                       its forward and again for its backward; the gathers ride inside the
+                       tcgen05 GEMMs of the previous layer); auto picks replicated when it
+                       fits in HBM
   kernels              "native" (sm_100a kernels, the default on CUDA) or "reference"
                        (plain PyTorch ops; oracle runs)
   gradient_checkpointing_policy

@@ -121,46 +121,58 @@ def _reduce_scatter(x, n, d, group, world):
     return out
 
 
-def _chunk_logits(h, w, softcap):
+def _softcapped_logits(h, w, softcap):
+    """fp32 logits of a chunk against this rank's vocab rows (from the bf16 product, as the
+    model computes them), softcapped as c * tanh(z / c)."""
     z = (h @ w.t()).float()
-    if softcap:
-        z.div_(softcap).tanh_().mul_(softcap)
-    return z
+    return torch.tanh(z / softcap) * softcap if softcap else z
+
+
+def _local_partials(z, labels, start, rows):
+    """Per token: this rank's row max m, sum of exp(z - m) over its vocab rows, and the target
+    logit when the label is one of its rows (else 0)."""
+    m = z.amax(dim=1)
+    s = torch.exp(z - m[:, None]).sum(dim=1)
+    col = labels - start
+    here = (labels != IGNORE) & (col >= 0) & (col < rows)
+    picked = z.gather(1, col.clamp(0, rows - 1)[:, None]).squeeze(1)
+    return m, s, torch.where(here, picked, torch.zeros_like(picked))
+
+
+def _merge_ranks(m, s, tgt, group, world):
+    """(log-sum-exp over the whole vocabulary, target logit): every rank's (m, s, target)
+    partials are all-gathered once and merged locally."""
+    if world == 1:
+        return m + torch.log(s), tgt
+    mine = torch.stack([m, s, tgt])
+    every = mine.new_empty((world * 3, mine.shape[1]))
+    dist.all_gather_into_tensor(every, mine.contiguous(), group=group)
+    every = every.view(world, 3, -1)
+    top = every[:, 0].amax(dim=0)
+    total = (every[:, 1] * torch.exp(every[:, 0] - top)).sum(dim=0)
+    return top + torch.log(total), every[:, 2].sum(dim=0)
 
 
 class _VocabParallelCE(torch.autograd.Function):
-    """PyTorch path (CPU/gloo and the oracle)."""
+    """PyTorch path (CPU / gloo, and the oracle of the CUDA path). Forward: per chunk of tokens
+    (gathered from every rank), partials against this rank's vocab rows, merged over ranks into
+    each token's log-sum-exp; only the LSEs are kept. Backward: the chunk's logits again,
+    softmax - onehot (times softcap'), weighted by each token's own rank's loss weight, through
+    the head into dH, reduce-scattered back to the tokens' ranks."""
 
     @staticmethod
     def forward(ctx, hidden, labels, shard):
         world, group, w = shard.world, shard.group, shard.weight
-        N, c = hidden.shape[0], shard.chunk
         h = hidden.detach().to(w.dtype)
-        lses, total = [], torch.zeros((), dtype=torch.float32, device=hidden.device)
-        for a in range(0, N, c):
-            b = min(N, a + c)
-            H = _gather(h[a:b], group, world)
+        total = torch.zeros((), dtype=torch.float32, device=hidden.device)
+        lses = []
+        for a, b in _chunks(hidden.shape[0], shard.chunk):
             L = _gather(labels[a:b].contiguous(), group, world)
-            z = _chunk_logits(H, w, shard.softcap)
-            m = z.max(dim=1).values
-            loc = L - shard.start
-            mine = (L != IGNORE) & (loc >= 0) & (loc < shard.rows)
-            tgt = torch.zeros_like(m)
-            idx = mine.nonzero().squeeze(1)
-            if idx.numel():
-                tgt[idx] = z[idx, loc[idx]]
-            if world > 1:
-                dist.all_reduce(m, op=dist.ReduceOp.MAX, group=group)
-            s = z.sub_(m[:, None]).exp_().sum(dim=1)
-            if world > 1:
-                st = torch.stack([s, tgt])
-                dist.all_reduce(st, group=group)
-                s, tgt = st[0], st[1]
-            lse = m + torch.log(s)
-            n = b - a
-            own = slice(shard.rank * n, (shard.rank + 1) * n)
-            valid = L[own] != IGNORE
-            total = total + torch.where(valid, lse[own] - tgt[own], torch.zeros_like(lse[own])).sum()
+            z = _softcapped_logits(_gather(h[a:b], group, world), w, shard.softcap)
+            lse, tgt = _merge_ranks(*_local_partials(z, L, shard.start, shard.rows), group, world)
+            mine = slice(shard.rank * (b - a), (shard.rank + 1) * (b - a))
+            trained = L[mine] != IGNORE
+            total = total + torch.where(trained, lse[mine] - tgt[mine], torch.zeros_like(tgt[mine])).sum()
             lses.append(lse)
         ctx.shard = shard
         ctx.save_for_backward(hidden.detach(), labels, *lses)
@@ -171,29 +183,28 @@ class _VocabParallelCE(torch.autograd.Function):
         shard = ctx.shard
         hidden, labels, *lses = ctx.saved_tensors
         world, group, w = shard.world, shard.group, shard.weight
-        N, c = hidden.shape[0], shard.chunk
-        gs = _gather(g.detach().float().reshape(1), group, world)
+        weights = _gather(g.detach().float().reshape(1), group, world)  # each rank's loss weight
         h = hidden.to(w.dtype)
-        grad = torch.empty(N, shard.d, dtype=hidden.dtype, device=hidden.device)
-        for k, a in enumerate(range(0, N, c)):
-            b = min(N, a + c)
+        grad = torch.empty(hidden.shape[0], shard.d, dtype=hidden.dtype, device=hidden.device)
+        for (a, b), lse in zip(_chunks(hidden.shape[0], shard.chunk), lses):
             n = b - a
-            H = _gather(h[a:b], group, world)
             L = _gather(labels[a:b].contiguous(), group, world)
-            p = _chunk_logits(H, w, shard.softcap)
-            cap = (p / shard.softcap).pow_(2).neg_().add_(1) if shard.softcap else None
-            p.sub_(lses[k][:, None]).exp_()
-            loc = L - shard.start
-            mine = (L != IGNORE) & (loc >= 0) & (loc < shard.rows)
-            idx = mine.nonzero().squeeze(1)
-            if idx.numel():
-                p[idx, loc[idx]] -= 1
-            p.mul_((gs.repeat_interleave(n) * (L != IGNORE).float())[:, None])
-            if cap is not None:
-                p.mul_(cap)
+            z = _softcapped_logits(_gather(h[a:b], group, world), w, shard.softcap)
+            p = torch.exp(z - lse[:, None])
+            col = L - shard.start
+            here = ((L != IGNORE) & (col >= 0) & (col < shard.rows)).nonzero().squeeze(1)
+            p[here, col[here]] -= 1
+            row_weight = weights.repeat_interleave(n) * (L != IGNORE).float()
+            p *= row_weight[:, None]
+            if shard.softcap:
+                p *= 1 - (z / shard.softcap).square()
             dH = (p.to(w.dtype) @ w).float()
             grad[a:b] = _reduce_scatter(dH, n, shard.d, group, world).to(grad.dtype)
         return grad, None, None
+
+
+def _chunks(n, size):
+    return [(a, min(n, a + size)) for a in range(0, n, size)]
 
 
 class _FusedVocabCE(torch.autograd.Function):

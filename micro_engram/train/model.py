@@ -5,9 +5,9 @@ its placement on the GPUs, the vocab shard, the no-grad prefix and checkpointing
 Reference counterpart: micro_engram/train/model.py:1-285 (HF model + FSDP2 + kernel patches).
 B200 placement: the base is frozen, so a GPU never needs its gradients or optimizer state.
 With 180 GB of HBM a 31B bf16 base (62 GB) fits on every GPU, so `base_placement: auto`
-replicates it (no per-layer all-gathers at all); `sharded` keeps FSDP's layout (each rank
-holds 1/world of every layer and all-gathers a layer before using it, prefetching the next
-on a side stream) for bases that don't fit.
+replicates it (no per-layer all-gathers at all) unless it does not fit; `sharded` keeps FSDP2's
+layout (each rank holds 1/world of every layer; the next layer's all-gather is carried by the
+current layer's tcgen05 GEMMs, see micro_engram_fork_b200/parallel/sharded_base.py).
 """
 import logging
 import os
@@ -148,14 +148,39 @@ def base_bytes(text):
 
 
 def place_base(text, cfg, device, world):
-    """Decide the base placement ("replicated" when it fits, else "sharded")."""
+    """Place the frozen base: "replicated" (every GPU holds all of it; `auto` picks this when it
+    fits in 60% of HBM) or "sharded" (FSDP2's layout: each GPU holds 1/world of every layer, the
+    layer all-gathers ride inside the tcgen05 GEMMs; micro_engram_fork_b200.parallel.sharded_base).
+    Returns the placement used. fsdp_config keys that the placement makes moot are reported."""
     mode = cfg.base_placement
     if mode == "auto":
-        if device.type == "cuda":
-            free, total = torch.cuda.mem_get_info(device)
-            mode = "replicated" if base_bytes(text) < 0.6 * total else "sharded"
-        else:
-            mode = "replicated"
-    if mode == "sharded" and world > 1:
-        raise NotImplementedError("base_placement: sharded is not available yet; use replicated (it fits)")
-    return "replicated"
+        mode = "replicated"
+        if device.type == "cuda" and world > 1:
+            _, total = torch.cuda.mem_get_info(device)
+            if base_bytes(text) >= 0.6 * total:
+                mode = "sharded"
+    fsdp = cfg.fsdp_config
+    if fsdp.offload_params:
+        LOG.warning("[micro_engram] fsdp_config.offload_params is not supported (the frozen base stays in HBM: "
+                    "activations, not parameters, are offloaded); ignoring it")
+    if mode == "sharded" and (world == 1 or device.type != "cuda"):
+        LOG.warning("[micro_engram] base_placement: sharded needs CUDA and 2+ GPUs; the base stays replicated")
+        mode = "replicated"
+    if mode == "sharded" and cfg.load_in_4bit:
+        raise ValueError("base_placement: sharded is for a bf16 base; an NF4 base (load_in_4bit) is replicated "
+                         "(31B in NF4 is 17 GB)")
+    if mode == "replicated":
+        if world > 1 and not fsdp.reshard_after_forward:
+            LOG.warning("[micro_engram] fsdp_config.reshard_after_forward has no effect: the base is replicated")
+        return "replicated"
+    if not fsdp.reshard_after_forward:
+        LOG.warning("[micro_engram] fsdp_config.reshard_after_forward: false is not supported; each layer is "
+                    "gathered again for its backward (two gather slots per GPU)")
+    from micro_engram_fork_b200.parallel.sharded_base import ShardedBase, activate
+
+    sb = ShardedBase(text.layers, dist.get_rank(), world, device)
+    activate(sb)
+    text._sharded_base = sb
+    LOG.warning(f"[micro_engram] base_placement: sharded over {world} GPUs ({sb.nbytes() / 2 ** 30:.1f} GiB per GPU "
+                "incl. two gather slots); layer all-gathers carried by the tcgen05 GEMMs")
+    return "sharded"

@@ -83,7 +83,7 @@ torch::Tensor gemm_tn_f32(torch::Tensor At, torch::Tensor Bt) {
 void gemm_carry_copy(int64_t device, int64_t segs, int64_t nsegs, int64_t begin16, int64_t end16) {
   TORCH_CHECK(nsegs >= 0 && begin16 >= 0 && end16 >= begin16, "gemm_carry_copy: bad range");
   SideCopy& job = pending_copy((int)device);
-  job.segs = reinterpret_cast<const GatherSeg*>(segs);
+  job.segs = reinterpret_cast<const me::GatherSeg*>(segs);
   job.nsegs = (int)nsegs;
   job.begin16 = begin16;
   job.end16 = end16;

@@ -98,9 +98,10 @@ struct GemmArgs {
   int M, N, K;          // N: output columns (GEGLU / DGEGLU: F)
   int tiles_m, tiles_n, group_m;
   // Split-K tail (STORE / F32): the first dp_tiles tiles run whole; the last (ntiles - dp_tiles)
-  // tiles are cut into `splits` K ranges each (tail_units units, at most one per cluster) that
-  // add their fp32 partials into `ws` [tail tile][256][256]; the last unit of each 32-row slice
-  // (counted in `cnt`) writes the result. ws and cnt start at zero.
+  // tiles are cut into `splits` K ranges each (tail_units units, at most one per cluster). Each
+  // unit writes its fp32 partial to its own slice ws[tail tile][split][256][256]; the last unit
+  // to finish a 32-row slice (counted in `cnt`, which starts at zero) sums the splits in split
+  // order and stores the result, so the tail is as deterministic as the rest of the GEMM.
   int dp_tiles, tail_units, splits;
   float* ws;
   int* cnt;
@@ -305,18 +306,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       const bool row_ok = row < p.M;
       if ((EPI == EPI_STORE || EPI == EPI_F32) && u.part >= 0) {
-        // split-K tail unit: add this K range's partial into the workspace row; the last of
-        // the `splits` units to finish these 32 rows stores them
+        // split-K tail unit: write this K range's partial to its own workspace slice; the last of
+        // the `splits` units to finish these 32 rows sums all slices in order and stores them
         const int tt = u.tile - p.dp_tiles;
-        float* wrow = p.ws + ((int64_t)tt * (2 * BM) + (int)rank * BM + q * 32 + lane) * BN;
+        const int64_t rowi = (int64_t)(int)rank * BM + q * 32 + lane;
+        const int64_t slice = (int64_t)(2 * BM) * BN;
+        float* mine = p.ws + ((int64_t)tt * p.splits + u.part) * slice + rowi * BN;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           float v[32];
           tmem_ld32(tbase + c * 32, v);
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            atomicAdd(reinterpret_cast<float4*>(wrow + c * 32 + j * 4),
-                      make_float4(v[j * 4], v[j * 4 + 1], v[j * 4 + 2], v[j * 4 + 3]));
+            __stcg(reinterpret_cast<float4*>(mine + c * 32 + j * 4),
+                   make_float4(v[j * 4], v[j * 4 + 1], v[j * 4 + 2], v[j * 4 + 3]));
         }
         __threadfence();
         __syncwarp();
@@ -325,18 +328,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         done = __shfl_sync(0xffffffffu, done, 0);
         if (done == p.splits - 1) {
           __threadfence();
+          const float* first = p.ws + (int64_t)tt * p.splits * slice + rowi * BN;
 #pragma unroll 1
           for (int c = 0; c < BN / 32; ++c) {
             const int col = nb * BN + c * 32;
             if (row_ok && col < p.N) {
               float v[32];
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float4 f = __ldcg(reinterpret_cast<const float4*>(wrow + c * 32 + j * 4));
-                v[j * 4] = f.x;
-                v[j * 4 + 1] = f.y;
-                v[j * 4 + 2] = f.z;
-                v[j * 4 + 3] = f.w;
+              for (int e = 0; e < 32; ++e) v[e] = 0.f;
+              for (int sp = 0; sp < p.splits; ++sp) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const float4 f = __ldcg(reinterpret_cast<const float4*>(first + sp * slice + c * 32 + j * 4));
+                  v[j * 4] += f.x;
+                  v[j * 4 + 1] += f.y;
+                  v[j * 4 + 2] += f.z;
+                  v[j * 4 + 3] += f.w;
+                }
               }
               if (EPI == EPI_STORE) {
                 store_row32(p.D + (int64_t)row * p.ldd + col, v, p.N - col);
@@ -599,7 +607,7 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, 
       a.splits = splits;
       a.tail_units = rem * splits;
       auto dev_opt = torch::TensorOptions().device(torch::kCUDA, dev);
-      ws = torch::zeros({(int64_t)rem * 2 * BM * BN}, dev_opt.dtype(torch::kFloat32));
+      ws = torch::empty({(int64_t)rem * splits * 2 * BM * BN}, dev_opt.dtype(torch::kFloat32));
       cnt = torch::zeros({(int64_t)rem * 8}, dev_opt.dtype(torch::kInt32));
       a.ws = ws.data_ptr<float>();
       a.cnt = cnt.data_ptr<int>();

@@ -65,7 +65,7 @@ def test_mults_seed_and_check_loaded():
     assert torch.equal(a.mults, b.mults) and (a.mults % 2 == 1).all()
     sd = a.state_dict()
     sd["mults"] = sd["mults"] + 2
-    with pytest.raises(ValueError, match="seed is wrong"):
+    with pytest.raises(ValueError, match="seed does not belong"):
         check_loaded(make(), sd, "x")
 
 

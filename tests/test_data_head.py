@@ -155,3 +155,16 @@ def _head_worker(rank, world):
 def test_vocab_parallel_head(world):
     res = run_dist(_head_worker, world)
     assert all(res.values()), res
+
+
+def test_packing_order_is_pinned():
+    """The packing order is part of the contract (a resumed run, or a run compared with the
+    reference trainer, must see the same bins): a fixed input packs to a recorded result."""
+    import hashlib
+
+    from micro_engram.train.data import pack
+
+    lens = np.random.default_rng(2024).integers(0, 600, size=500)
+    bins = pack(lens, 512, 11)
+    assert hashlib.sha256(json.dumps(bins).encode()).hexdigest()[:16] == "a9436382b82cb5d7"
+    assert sorted(i for b in bins for i in b) == [i for i in range(500) if 0 < lens[i] <= 512]

@@ -1,6 +1,11 @@
-"""Gate modes of MicroEngram on CPU: exact no-op start, gradient flow, parameter names and
-checkpoint compatibility, sqrt-gate saturation, gate statistics, keep mask, delta-stored
-norm scales, weight stats, and a code guard on reading the delta parameters."""
+"""The three gates of MicroEngram on CPU (scalar, scalar_sqrt, ple).
+
+Checked: an untrained engram is an exact no-op and still passes gradients to its output
+projection; once that projection is non-zero the tables get gradients too; parameter names
+and checkpoint compatibility between gates; the signed-sqrt gate saturates less than the plain
+scalar gate; gate statistics are collected in training mode only; the keep mask; the norm
+scales stored as deltas (loaded from and saved as the scale itself); weight statistics; and a
+guard that only module.py reads the delta parameters directly."""
 import pathlib
 import re
 
@@ -11,166 +16,172 @@ import torch.nn.functional as F
 from micro_engram.module import MicroEngram
 from micro_engram.stats import format_stats, module_stats, weight_stats
 
-V, D = 1000, 32
+VOCAB, DIM = 1000, 32
 
 
-def make(gate, **kw):
-    return MicroEngram(model_dim=D, table_size=257, engram_dim=4, num_heads=2, vocab_size=V, gate=gate, **kw)
+def engram(gate, **kw):
+    return MicroEngram(model_dim=DIM, table_size=257, engram_dim=4, num_heads=2, vocab_size=VOCAB, gate=gate, **kw)
+
+
+def output_projection(e):
+    return e.up if e.gate == "ple" else e.value
+
+
+def memory(e, ids):
+    """The concatenated table rows the engram reads for `ids`."""
+    return torch.cat([table(i) for table, i in zip(e.tables, e.hash_ids(ids))], dim=-1)
 
 
 @pytest.fixture
-def data():
-    torch.manual_seed(0)
-    return torch.randint(5, V, (2, 12)), torch.randn(2, 12, D) * 50
+def batch():
+    g = torch.Generator().manual_seed(0)
+    return torch.randint(5, VOCAB, (2, 12), generator=g), torch.randn(2, 12, DIM, generator=g) * 50
 
 
 @pytest.mark.parametrize("gate", MicroEngram.GATES)
-def test_noop_start_and_grad_flow(gate, data):
-    ids, hidden = data
-    eng = make(gate)
-    assert torch.equal(eng(hidden, ids), hidden)
-    h = hidden.clone().requires_grad_(True)
-    eng(h, ids).pow(2).sum().backward()
-    out_layer = eng.up if gate == "ple" else eng.value
-    assert out_layer.weight.grad is not None and out_layer.weight.grad.abs().sum() > 0
-    eng.zero_grad()
+def test_untrained_engram_is_a_noop_that_learns(gate, batch):
+    ids, hidden = batch
+    e = engram(gate)
+    assert torch.equal(e(hidden, ids), hidden)
+    h = hidden.clone().requires_grad_()
+    e(h, ids).square().sum().backward()
+    assert output_projection(e).weight.grad.abs().sum() > 0  # the zero projection still learns
+    e.zero_grad()
     with torch.no_grad():
-        out_layer.weight.normal_(std=0.02)
-    eng(hidden, ids).pow(2).sum().backward()
-    assert eng.tables[0].weight.grad.abs().sum() > 0
-    assert not torch.equal(eng(hidden, ids), hidden)
-    ob = make(gate).to(torch.bfloat16)(hidden.to(torch.bfloat16), ids)
-    assert ob.dtype == torch.bfloat16 and ob.shape == hidden.shape
+        output_projection(e).weight.normal_(std=0.02)
+    e(hidden, ids).square().sum().backward()
+    assert e.tables[0].weight.grad.abs().sum() > 0
+    assert not torch.equal(e(hidden, ids), hidden)
+    half = engram(gate).to(torch.bfloat16)(hidden.to(torch.bfloat16), ids)
+    assert half.dtype == torch.bfloat16 and half.shape == hidden.shape
 
 
-def test_names_and_compat():
-    s, p, q = make("scalar"), make("ple"), make("scalar_sqrt")
-    assert {"key.weight", "value.weight"} <= set(s.state_dict())
-    assert {"down.weight", "up.weight"} <= set(p.state_dict()) and "key.weight" not in p.state_dict()
-    assert sum(x.numel() for x in s.parameters()) == sum(x.numel() for x in p.parameters())
-    assert not make("scalar").load_state_dict(s.state_dict(), strict=True).missing_keys
-    sd = q.state_dict()
-    assert torch.equal(q.q_scale, torch.zeros(D)) and q.q_scale.requires_grad
-    assert torch.equal(sd["q_scale"], torch.ones(D))
-    missing = set(make("scalar_sqrt").load_state_dict(s.state_dict(), strict=False).missing_keys)
-    assert missing == {"q_scale", "k_scale"}
+def test_parameter_names_across_gates():
+    scalar, ple, sqrt = engram("scalar"), engram("ple"), engram("scalar_sqrt")
+    assert {"key.weight", "value.weight"} <= set(scalar.state_dict())
+    assert {"down.weight", "up.weight"} <= set(ple.state_dict()) and "key.weight" not in ple.state_dict()
+    assert sum(p.numel() for p in scalar.parameters()) == sum(p.numel() for p in ple.parameters())
+    assert not engram("scalar").load_state_dict(scalar.state_dict(), strict=True).missing_keys
+    # scalar_sqrt stores its norm scales as deltas from 1 and saves the scales themselves
+    assert torch.equal(sqrt.q_scale, torch.zeros(DIM)) and sqrt.q_scale.requires_grad
+    assert torch.equal(sqrt.state_dict()["q_scale"], torch.ones(DIM))
+    result = engram("scalar_sqrt").load_state_dict(scalar.state_dict(), strict=False)
+    assert set(result.missing_keys) == {"q_scale", "k_scale"}
     with pytest.raises(ValueError):
-        make("bogus")
+        engram("no_such_gate")
 
 
-def _gate_of(eng, h, ids):
-    eng.train()
-    eng._gate_stats = None
-    eng(h, ids)
-    return eng.pop_gate_stats()
+def _gate_stats(e, hidden, ids):
+    e.train()
+    e._gate_stats = None
+    e(hidden, ids)
+    return e.pop_gate_stats()
 
 
-def test_sqrt_gate_saturates_less_and_stats(data):
-    ids, hidden = data
+def test_sqrt_gate_saturates_less(batch):
+    ids, hidden = batch
     torch.manual_seed(1)
-    sq, sc = make("scalar_sqrt"), make("scalar")
+    sqrt, plain = engram("scalar_sqrt"), engram("scalar")
     with torch.no_grad():
-        sc.key.weight.copy_(sq.key.weight)
-        sc.tables.load_state_dict(sq.tables.state_dict())
-        for e in (sq, sc):
+        plain.key.weight.copy_(sqrt.key.weight)
+        plain.tables.load_state_dict(sqrt.tables.state_dict())
+        for e in (sqrt, plain):
             e.value.weight.normal_(std=0.02)
-    idx = sq.hash_ids(ids)
-    mem = torch.cat([t(i) for t, i in zip(sq.tables, idx)], dim=-1)
-    h_al = sq.key(mem).detach() * 30
-    g_sq, sat_sq = _gate_of(sq, h_al, ids)
-    g_sc, sat_sc = _gate_of(sc, h_al, ids)
-    assert g_sc > g_sq > 0.5 and sat_sc >= sat_sq
-    sq.eval()
-    sq(h_al, ids)
-    assert sq.pop_gate_stats() is None
-    sq.train()
-    sq.zero_grad()
-    sq(h_al + torch.randn_like(h_al), ids).pow(2).sum().backward()
-    assert sq.q_scale.grad.abs().sum() > 0 and sq.k_scale.grad.abs().sum() > 0
+    aligned = sqrt.key(memory(sqrt, ids)).detach() * 30  # hidden states pointing along the keys
+    mean_sqrt, sat_sqrt = _gate_stats(sqrt, aligned, ids)
+    mean_plain, sat_plain = _gate_stats(plain, aligned, ids)
+    assert mean_plain > mean_sqrt > 0.5 and sat_plain >= sat_sqrt
+    sqrt.eval()
+    sqrt(aligned, ids)
+    assert sqrt.pop_gate_stats() is None  # no statistics outside training mode
+    sqrt.train()
+    sqrt.zero_grad()
+    sqrt(aligned + torch.randn_like(aligned), ids).square().sum().backward()
+    assert sqrt.q_scale.grad.abs().sum() > 0 and sqrt.k_scale.grad.abs().sum() > 0
 
 
-def test_weight_stats():
-    big = MicroEngram(model_dim=D, table_size=4096, engram_dim=64, num_heads=2, vocab_size=V, gate="scalar_sqrt")
-    st = module_stats(big)
-    assert abs(st["engram/table_rms_2g"] - 0.02) < 0.002 and st["engram/rows_learned_3g"] < 0.001
-    assert st["engram/out_abs_mean"] == 0 and abs(st["engram/q_scale_mean"] - 1) < 1e-6
+def test_weight_stats_of_tables():
+    e = MicroEngram(model_dim=DIM, table_size=4096, engram_dim=64, num_heads=2, vocab_size=VOCAB, gate="scalar_sqrt")
+    fresh = module_stats(e)
+    assert abs(fresh["engram/table_rms_2g"] - 0.02) < 0.002 and fresh["engram/rows_learned_3g"] < 0.001
+    assert fresh["engram/out_abs_mean"] == 0 and abs(fresh["engram/q_scale_mean"] - 1) < 1e-6
     with torch.no_grad():
-        big.tables[2].weight[:1024] *= 3
-    st2 = module_stats(big)
-    assert 0.10 < st2["engram/rows_learned_3g"] < 0.15 and st2["engram/rows_learned_2g"] < 0.001
-    assert weight_stats(big.state_dict(), big.orders, 2) == st2
-    assert "learned" in format_stats({**st2, "engram/gate_mean": 0.42, "engram/gate_saturated": 0.03})
+        e.tables[2].weight[:1024] *= 3  # a quarter of one 3-gram table "learned"
+    grown = module_stats(e)
+    assert 0.10 < grown["engram/rows_learned_3g"] < 0.15 and grown["engram/rows_learned_2g"] < 0.001
+    assert weight_stats(e.state_dict(), e.orders, 2) == grown
+    assert "learned" in format_stats({**grown, "engram/gate_mean": 0.42, "engram/gate_saturated": 0.03})
 
 
-def test_keep_mask(data):
-    ids, hidden = data
-    eng = make("ple")
+def test_keep_mask_leaves_tokens_untouched(batch):
+    ids, hidden = batch
+    e = engram("ple")
     with torch.no_grad():
-        eng.up.weight.normal_(std=0.05)
-    idx = eng.hash_ids(ids)
-    keep = torch.tensor([[True] * 6 + [False] * 6] * 2)
-    masked, full = eng.inject(hidden, idx, keep), eng.inject(hidden, idx)
-    assert torch.equal(masked[:, 6:], hidden[:, 6:]) and torch.equal(masked[:, :6], full[:, :6])
+        e.up.weight.normal_(std=0.05)
+    idx = e.hash_ids(ids)
+    keep = torch.zeros(2, 12, dtype=torch.bool)
+    keep[:, :6] = True
+    masked, unmasked = e.inject(hidden, idx, keep), e.inject(hidden, idx)
+    assert torch.equal(masked[:, 6:], hidden[:, 6:]) and torch.equal(masked[:, :6], unmasked[:, :6])
 
 
-def test_delta_scales(data):
-    ids, hidden = data
+def test_norm_scales_stored_as_deltas(batch):
+    ids, hidden = batch
     torch.manual_seed(3)
-    old = make("scalar_sqrt").state_dict()
-    old["q_scale"] = 1 + 0.3 * torch.rand(D)
-    old["k_scale"] = 1 - 0.2 * torch.rand(D)
-    old["value.weight"] = torch.randn_like(old["value.weight"]) * 0.05
-    new = make("scalar_sqrt")
-    new.load_state_dict(old)
-    assert torch.allclose(new.q_scale, old["q_scale"] - 1) and torch.allclose(new.k_scale, old["k_scale"] - 1)
-    assert torch.allclose(new.state_dict()["q_scale"], old["q_scale"])
-    idx = new.hash_ids(ids)
-    mem = torch.cat([t(i) for t, i in zip(new.tables, idx)], dim=-1)
-    h = F.rms_norm(hidden.float(), (D,), weight=old["q_scale"])
-    k = F.rms_norm(new.key(mem).float(), (D,), weight=old["k_scale"])
-    s = (h * k).sum(-1, keepdim=True) / D ** 0.5
-    want = hidden + torch.sigmoid(s.sign() * s.abs().clamp_min(1e-6).sqrt()) * new.value(mem)
-    assert torch.allclose(new.inject(hidden, idx), want, atol=1e-5)
-    st = module_stats(new)
-    assert abs(st["engram/q_scale_mean"] - float(old["q_scale"].mean())) < 1e-5
-    rt = make("scalar_sqrt").to(torch.bfloat16)
+    saved = engram("scalar_sqrt").state_dict()
+    saved["q_scale"] = 1 + 0.3 * torch.rand(DIM)
+    saved["k_scale"] = 1 - 0.2 * torch.rand(DIM)
+    saved["value.weight"] = torch.randn_like(saved["value.weight"]) * 0.05
+    e = engram("scalar_sqrt")
+    e.load_state_dict(saved)
+    assert torch.allclose(e.q_scale, saved["q_scale"] - 1) and torch.allclose(e.k_scale, saved["k_scale"] - 1)
+    assert torch.allclose(e.state_dict()["q_scale"], saved["q_scale"])
+    # the gate computed by hand from the saved scales
+    mem = memory(e, ids)
+    q = F.rms_norm(hidden.float(), (DIM,), weight=saved["q_scale"])
+    k = F.rms_norm(e.key(mem).float(), (DIM,), weight=saved["k_scale"])
+    score = (q * k).sum(-1, keepdim=True) / DIM ** 0.5
+    gate = torch.sigmoid(torch.sign(score) * score.abs().clamp_min(1e-6).sqrt())
+    assert torch.allclose(e.inject(hidden, e.hash_ids(ids)), hidden + gate * e.value(mem), atol=1e-5)
+    assert abs(module_stats(e)["engram/q_scale_mean"] - float(saved["q_scale"].mean())) < 1e-5
+    # bf16 module: deltas keep full precision in the saved fp32 scale and round-trip exactly
+    bf = engram("scalar_sqrt").to(torch.bfloat16)
     with torch.no_grad():
-        rt.q_scale.copy_(torch.linspace(-0.01, 0.01, D))
-    saved = rt.state_dict()
-    back = make("scalar_sqrt").to(torch.bfloat16)
-    back.load_state_dict(saved)
-    assert torch.equal(back.q_scale, rt.q_scale) and saved["q_scale"].dtype == torch.float32
-    ns = make("scalar_sqrt").to(torch.bfloat16)
+        bf.q_scale.copy_(torch.linspace(-0.01, 0.01, DIM))
+    sd = bf.state_dict()
+    again = engram("scalar_sqrt").to(torch.bfloat16)
+    again.load_state_dict(sd)
+    assert torch.equal(again.q_scale, bf.q_scale) and sd["q_scale"].dtype == torch.float32
+    small = engram("scalar_sqrt").to(torch.bfloat16)
     with torch.no_grad():
-        ns.q_scale.fill_(0.003)
-    qs, ks = ns.norm_scales()
+        small.q_scale.fill_(0.003)
+    qs, ks = small.norm_scales()
     assert qs.dtype == torch.float32 and abs(float(qs[0]) - 1.003) < 1e-4 and float(ks[0]) == 1.0
 
 
-def test_bf16_scales_learn(data):
-    ids, hidden = data
-    bf = make("scalar_sqrt").to(torch.bfloat16)
+def test_bf16_norm_scales_train(batch):
+    ids, hidden = batch
+    e = engram("scalar_sqrt").to(torch.bfloat16)
     with torch.no_grad():
-        bf.value.weight.normal_(std=0.05)
-    opt = torch.optim.AdamW(bf.parameters(), lr=1e-3, weight_decay=0.0)
-    hb = hidden.to(torch.bfloat16)
+        e.value.weight.normal_(std=0.05)
+    opt = torch.optim.AdamW(e.parameters(), lr=1e-3, weight_decay=0.0)
     for _ in range(50):
         opt.zero_grad()
-        bf(hb, ids).float().pow(2).mean().backward()
+        e(hidden.to(torch.bfloat16), ids).float().square().mean().backward()
         opt.step()
-    moved = (bf.state_dict()["q_scale"].float() - 1).abs()
-    assert (moved > 0).float().mean() > 0.5
+    moved = (e.state_dict()["q_scale"].float() - 1).abs() > 0
+    assert moved.float().mean() > 0.5  # a bf16 scale near 1 would round most updates away
 
 
-def test_code_guard_delta_parameters():
-    """Only module.py reads .q_scale/.k_scale (they hold scale - 1)."""
+def test_only_module_reads_delta_parameters():
+    """.q_scale / .k_scale hold scale - 1; outside module.py code must use norm_scales()."""
     root = pathlib.Path(__file__).resolve().parent.parent
-    bad = []
-    for f in root.rglob("*.py"):
-        rel = f.relative_to(root).as_posix()
+    pattern = re.compile(r"\.(q|k)_scale\b")
+    offenders = []
+    for path in root.rglob("*.py"):
+        rel = path.relative_to(root).as_posix()
         if rel == "micro_engram/module.py" or rel.startswith(("tests/", "_work/", "baseline/", "build/")):
             continue
-        for i, line in enumerate(f.read_text(encoding="utf-8", errors="replace").splitlines(), 1):
-            if re.search(r"\.(q|k)_scale\b", line):
-                bad.append(f"{rel}:{i}")
-    assert not bad, bad
+        text = path.read_text(encoding="utf-8", errors="replace")
+        offenders += [f"{rel}:{n}" for n, line in enumerate(text.splitlines(), 1) if pattern.search(line)]
+    assert not offenders, offenders

@@ -128,3 +128,22 @@ def test_projection_grads(T, N, K):
     noise_floor_check(y, x32 @ W32.t(), xb @ Wb.t(), rel=1.5, eps=1e-2, name="proj y")
     noise_floor_check(x.grad, x32.grad, xb.grad, rel=1.5, eps=1e-2, name="proj dx")
     noise_floor_check(W.grad, W32.grad, Wb.grad, rel=1.5, eps=1e-2, name="proj dW")
+
+
+@cuda
+@pytest.mark.parametrize("kmajor", [True, False])
+def test_gemm_bitwise_repeatable(kmajor):
+    """Shapes whose last partial wave is split along K (a 5376-wide output over 8192 rows):
+    two runs give identical bits (the split partials are summed in a fixed order)."""
+    import micro_engram_fork_b200 as me
+
+    torch.manual_seed(6)
+    A = torch.randn(8192, 2048, device=_dev()).to(torch.bfloat16)
+    W = (torch.randn(5376, 2048, device=_dev()) if kmajor else torch.randn(2048, 5376, device=_dev())) / 45
+    W = W.to(torch.bfloat16)
+    first = me.native().gemm(A, W, kmajor, None)
+    second = me.native().gemm(A, W, kmajor, None)
+    assert _status_ok()
+    assert torch.equal(first, second)
+    ref32 = A.float() @ (W.float().t() if kmajor else W.float())
+    noise_floor_check(first, ref32, A @ (W.t() if kmajor else W), rel=1.5, eps=1e-2, name="tail split")
