@@ -250,14 +250,17 @@ class MicroEngram(nn.Module):
             pos = position_ids.to(ids.device).expand_as(ids)
             back = [b if i == 0 else torch.where(pos >= i, b, torch.full_like(b, self.pad_id))
                     for i, b in enumerate(back)]
-        mults = self.mults.to(ids.device)
-        out = []
-        for k, n in enumerate(self._table_orders):
-            x = back[0] * mults[k, 0]
-            for i in range(1, n):
-                x = x + back[i] * mults[k, i]
-            out.append((x % _PRIME) % self.table_rows[k])
-        return out
+        return self._combine(back)
+
+    def _combine(self, back):
+        """Row ids per table from token columns back[i] = canonical token at t - i (pad where
+        there is none): (sum_i back[i] * mults[k, i]) mod p mod rows_k, int64 arithmetic."""
+        mults = self.mults.to(back[0].device)
+        rows = []
+        for k, order in enumerate(self._table_orders):
+            terms = [back[i] * mults[k, i] for i in range(order)]
+            rows.append((torch.stack(terms).sum(0) % _PRIME) % self.table_rows[k])
+        return rows
 
     def hash_prev(self, ids):
         """Hashes from [N, max_order] histories: column i = token at t-i, -1 = none."""
@@ -268,16 +271,9 @@ class MicroEngram(nn.Module):
             canon, mults, orders, rows = self._consts(ids.device)
             return list(_hash_prev(ids.contiguous(), canon, mults, orders, rows, self.pad_id).unbind(0))
         canon = self.canon.to(ids.device)
-        merged = canon[ids.clamp(0, canon.numel() - 1)]
-        merged = torch.where(ids >= 0, merged, torch.full_like(merged, self.pad_id))
-        mults = self.mults.to(ids.device)
-        out = []
-        for k, n in enumerate(self._table_orders):
-            x = merged[:, 0] * mults[k, 0]
-            for i in range(1, n):
-                x = x + merged[:, i] * mults[k, i]
-            out.append((x % _PRIME) % self.table_rows[k])
-        return out
+        known = ids >= 0
+        cols = canon[ids.clamp(0, canon.numel() - 1)].masked_fill(~known, self.pad_id)
+        return self._combine(list(cols.unbind(1)))
 
     # ------------------------------------------------------------------ injection
     def _fused_ok(self, hidden):
@@ -293,37 +289,36 @@ class MicroEngram(nn.Module):
         if self._fused_ok(hidden):
             return self._inject_fused(hidden, idx, keep)
         mem = torch.cat(self.lookup(idx), dim=-1)
-        if self.row_shards is not None:
-            reader = self.key if self.gate in self.SCALAR_GATES else self.up
-            mem = mem.to(reader.weight.dtype)
-        d = hidden.shape[-1]
-        if self.gate in self.SCALAR_GATES:
-            if (use_native(hidden) and hidden.dtype == torch.bfloat16 and mem.dtype == torch.bfloat16
-                    and self.key.weight.dtype == torch.bfloat16):
-                k = projection(mem, self.key.weight)
-                v = projection(mem, self.value.weight)
-                return self._gate_native(hidden, k, v, keep)
-            if self.gate == "scalar_sqrt":
-                qs, ks = self.norm_scales()
-                h = F.rms_norm(hidden.float(), (d,), weight=qs)
-                k = F.rms_norm(self.key(mem).float(), (d,), weight=ks)
-            else:
-                h = F.rms_norm(hidden.float(), (d,))
-                k = F.rms_norm(self.key(mem).float(), (d,))
-            s = (h * k).sum(-1, keepdim=True) / d ** 0.5
-            if self.gate == "scalar_sqrt":
-                s = s.sign() * s.abs().clamp_min(1e-6).sqrt()
-            alpha = torch.sigmoid(s)
-            if self.training:
-                self._record_gate(alpha)
-            out = alpha * self.value(mem).float()
-        else:
-            h = F.rms_norm(hidden.float(), (d,))
-            g = F.gelu(self.down(h.to(self.down.weight.dtype)), approximate="tanh")
-            out = self.up(g * mem).float()
+        scalar = self.gate in self.SCALAR_GATES
+        if self.row_shards is not None:  # gathered rows arrive in the table dtype
+            mem = mem.to((self.key if scalar else self.up).weight.dtype)
+        if scalar and (use_native(hidden) and hidden.dtype == torch.bfloat16 and mem.dtype == torch.bfloat16
+                       and self.key.weight.dtype == torch.bfloat16):
+            return self._gate_native(hidden, projection(mem, self.key.weight), projection(mem, self.value.weight),
+                                     keep)
+        added = self._scalar_gate_torch(hidden, mem) if scalar else self._ple_gate_torch(hidden, mem)
         if keep is not None:
-            out = out * keep.reshape(*out.shape[:-1], 1).to(out.dtype)
-        return hidden + out.to(hidden.dtype)
+            added = added * keep.reshape(*added.shape[:-1], 1).to(added.dtype)
+        return hidden + added.to(hidden.dtype)
+
+    def _scalar_gate_torch(self, hidden, mem):
+        """sigmoid(<rms(h) q, rms(key(mem)) k> / sqrt(d)) * value(mem) in fp32; the scalar_sqrt gate
+        takes the signed square root of the score and uses the learned norm scales."""
+        d = hidden.shape[-1]
+        qs, ks = self.norm_scales() if self.gate == "scalar_sqrt" else (None, None)
+        score = (F.rms_norm(hidden.float(), (d,), weight=qs) * F.rms_norm(self.key(mem).float(), (d,), weight=ks))
+        score = score.sum(-1, keepdim=True) / d ** 0.5
+        if self.gate == "scalar_sqrt":
+            score = torch.sign(score) * torch.sqrt(score.abs().clamp_min(1e-6))
+        alpha = torch.sigmoid(score)
+        if self.training:
+            self._record_gate(alpha)
+        return self.value(mem).float() * alpha
+
+    def _ple_gate_torch(self, hidden, mem):
+        """up(gelu_tanh(down(rms(h))) * mem) in fp32 (the per-layer-embedding style gate)."""
+        normed = F.rms_norm(hidden.float(), (hidden.shape[-1],)).to(self.down.weight.dtype)
+        return self.up(F.gelu(self.down(normed), approximate="tanh") * mem).float()
 
     def _gate_native(self, hidden, k, v, keep):
         from micro_engram_fork_b200.ops.engram import gate
@@ -377,15 +372,25 @@ class MicroEngram(nn.Module):
 
 
 def find_text_layers(model):
-    """(name, ModuleList) of the language model's decoder layers (not a vision/audio tower)."""
-    cands = [(n, m) for n, m in model.named_modules() if isinstance(m, nn.ModuleList) and n.endswith("layers")]
-    for n, m in cands:
-        if "language_model" in n:
-            return n, m
-    for n, m in cands:
-        if "vision" not in n and "audio" not in n:
-            return n, m
-    raise RuntimeError("Could not find text decoder layers; print(model) and set the path by hand.")
+    """(name, ModuleList) of the language model's decoder layers (not a vision/audio tower).
+
+    Preference order: a `...layers` list under a `language_model` module, then any `...layers`
+    list outside a vision or audio tower."""
+    def rank(name):
+        if "language_model" in name:
+            return 0
+        return 1 if ("vision" not in name and "audio" not in name) else None
+
+    best = None
+    for name, mod in model.named_modules():
+        if not (isinstance(mod, nn.ModuleList) and name.endswith("layers")):
+            continue
+        r = rank(name)
+        if r is not None and (best is None or r < best[0]):
+            best = (r, name, mod)
+    if best is None:
+        raise RuntimeError("Could not find text decoder layers; print(model) and set the path by hand.")
+    return best[1], best[2]
 
 
 def engram_from_spec(spec, model_dim, vocab_size, pad_default=0, canon=None, build_tables=True):
@@ -418,17 +423,15 @@ _QUANTIZED_PARAMS = ("Params4bit", "Int8Params", "NF4Weight")
 def layer_device_dtype(layer):
     """(device, compute dtype) for an engram placed in `layer`: the first real floating-point
     weight, else a quantized module's compute dtype, else bf16."""
-    params = list(layer.parameters())
-    if not params:
+    weights = list(layer.parameters())
+    if not weights:
         raise RuntimeError("decoder layer has no parameters")
-    for p in params:
-        if p.is_floating_point() and type(p).__name__ not in _QUANTIZED_PARAMS:
-            return p.device, p.dtype
-    for m in layer.modules():
-        cd = getattr(m, "compute_dtype", None)
-        if isinstance(cd, torch.dtype) and cd.is_floating_point:
-            return params[0].device, cd
-    return params[0].device, torch.bfloat16
+    plain = [w for w in weights if w.is_floating_point() and type(w).__name__ not in _QUANTIZED_PARAMS]
+    if plain:
+        return plain[0].device, plain[0].dtype
+    declared = (getattr(m, "compute_dtype", None) for m in layer.modules())
+    dtype = next((d for d in declared if isinstance(d, torch.dtype) and d.is_floating_point), torch.bfloat16)
+    return weights[0].device, dtype
 
 
 def attach_engram(model, engram, layer_idx, dtype=None, get_ids=None):
@@ -443,22 +446,22 @@ def attach_engram(model, engram, layer_idx, dtype=None, get_ids=None):
     device, layer_dtype = layer_device_dtype(target)
     engram.to(device=device, dtype=dtype or layer_dtype)
     target.add_module("micro_engram", engram)
-    seen = {}
+    seen = {"input_ids": None, "position_ids": None}
 
     def capture(_mod, args, kwargs):
-        ids = kwargs.get("input_ids")
-        if ids is None and args:
-            ids = args[0]
-        seen["input_ids"] = ids
+        seen["input_ids"] = kwargs.get("input_ids", args[0] if args else None)
         seen["position_ids"] = kwargs.get("position_ids")
 
+    def current_ids():
+        return get_ids() if get_ids is not None else (seen["input_ids"], seen["position_ids"])
+
     def inject(_mod, _args, output):
-        ids, pos = get_ids() if get_ids is not None else (seen.get("input_ids"), seen.get("position_ids"))
+        ids, pos = current_ids()
         if ids is None:
             return output
-        if isinstance(output, tuple):
-            return (engram(output[0], ids, pos),) + tuple(output[1:])
-        return engram(output, ids, pos)
+        hidden = output[0] if isinstance(output, tuple) else output
+        mixed = engram(hidden, ids, pos)
+        return (mixed, *output[1:]) if isinstance(output, tuple) else mixed
 
     handles = [target.register_forward_hook(inject)]
     if get_ids is None:

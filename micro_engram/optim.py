@@ -39,6 +39,29 @@ def stochastic_bf16(x):
 _SEED_BASE = 0x5EED
 
 
+def _evaluate(closure):
+    if closure is None:
+        return None
+    with torch.enable_grad():
+        return closure()
+
+
+class _Hyper:
+    """One group's AdamW constants at a given step (bias corrections included)."""
+
+    __slots__ = ("lr", "beta1", "beta2", "eps", "wd", "bc1", "bc2", "sr", "step")
+
+    @classmethod
+    def of(cls, group, step):
+        h = cls()
+        h.beta1, h.beta2 = group["betas"]
+        h.lr, h.eps, h.wd = group["lr"], group["eps"], group["weight_decay"]
+        h.bc1, h.bc2 = 1 - h.beta1 ** step, 1 - h.beta2 ** step
+        h.sr = bool(group.get("stochastic_rounding", True))
+        h.step = int(step)
+        return h
+
+
 class LazyAdamW(torch.optim.Optimizer):
     def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, lazy=False, rowwise=False,
                  stochastic_rounding=True):
@@ -104,54 +127,48 @@ class LazyAdamW(torch.optim.Optimizer):
 
     @torch.no_grad()
     def step(self, closure=None):
-        loss = None
-        if closure is not None:
-            with torch.enable_grad():
-                loss = closure()
-        stores = []
-        for group in self.param_groups:
-            for p in group["params"]:
-                rs = getattr(p, "_row_store", None)
-                if rs is not None:
-                    self._step_store(p, group)
-                    if rs[0] not in stores:
-                        stores.append(rs[0])
-                else:
-                    self._step_param(p, group)
-        for store in stores:  # every touched row was consumed (and cleared) by the kernels
-            store.pending = False
-            store.coef = None
+        loss = _evaluate(closure)
+        done = {}  # row stores whose touched rows the kernels consumed (and cleared) this step
+        for group, p in ((g, p) for g in self.param_groups for p in g["params"]):
+            owner = getattr(p, "_row_store", None)
+            if owner is None:
+                self._step_param(p, group)
+                continue
+            self._step_store(p, group)
+            done[id(owner[0])] = owner[0]
+        for store in done.values():
+            store.pending, store.coef = False, None
         return loss
+
+    def _advance(self, p, group, on_host=False):
+        """Create the state on first use, count the step and return the update's constants."""
+        state = self.state[p]
+        if not state:
+            self.init_state(state, p, group, on_host)
+        state["step"] += 1
+        return state, _Hyper.of(group, float(state["step"]))
 
     # ------------------------------------------------------------------ row-store tables (CUDA)
     def _step_store(self, p, group):
         store, k = p._row_store
         if not store.pending:
             return
-        state = self.state[p]
-        if not state:
-            self.init_state(state, p, group, self._on_host(p, group))
-        state["step"] += 1
-        step = float(state["step"])
-        beta1, beta2 = group["betas"]
-        lr, eps, wd = group["lr"], group["eps"], group["weight_decay"]
-        bc1, bc2 = 1 - beta1 ** step, 1 - beta2 ** step
-        sr = bool(group.get("stochastic_rounding", True))
+        state, h = self._advance(p, group, self._on_host(p, group))
         seed = (_SEED_BASE + 7919 * store.rank + 104729 * getattr(store, "salt", 0)) & 0x7FFFFFFF
         from micro_engram_fork_b200.ops.engram import adam_dense, adam_touched
 
         coef = getattr(store, "coef", None)
         if group["lazy"]:
             adam_touched(p.data, state["exp_avg"], state["exp_avg_sq"], store.acc[k], store.pos[k],
-                         store.list[k], store.count[k], coef, lr, beta1, beta2, eps, wd, bc1, bc2, sr, seed,
-                         int(step), k)
+                         store.list[k], store.count[k], coef, h.lr, h.beta1, h.beta2, h.eps, h.wd, h.bc1, h.bc2,
+                         h.sr, seed, h.step, k)
         else:  # every row steps: densify the compact accumulator for this table
             n = p.shape[0]
             g = store.dense_grad(k)[:n]
             if coef is not None:
                 g.mul_(coef)
-            adam_dense(p.data, g, state["exp_avg"], state["exp_avg_sq"], lr, beta1, beta2, eps, wd, bc1, bc2,
-                       1.0, sr, seed, int(step))
+            adam_dense(p.data, g, state["exp_avg"], state["exp_avg_sq"], h.lr, h.beta1, h.beta2, h.eps, h.wd, h.bc1,
+                       h.bc2, 1.0, h.sr, seed, h.step)
             del g
             used = min(int(store.count[k][0]), store.cap[k])
             rows = store.list[k][:used].long()
@@ -162,28 +179,20 @@ class LazyAdamW(torch.optim.Optimizer):
     # ------------------------------------------------------------------ everything else
     def _step_param(self, p, group):
         sparse = getattr(p, "sparse_grad", None)
-        if p.grad is None and sparse is None:
+        if sparse is None and p.grad is None:
             return
-        state = self.state[p]
-        if not state:
-            self.init_state(state, p, group)
-        state["step"] += 1
-        step = float(state["step"])
-        beta1, beta2 = group["betas"]
-        lr, eps, wd = group["lr"], group["eps"], group["weight_decay"]
-        bc1, bc2 = 1 - beta1 ** step, 1 - beta2 ** step
-        sr = group.get("stochastic_rounding", True)
-        P = _local(p)
-        M, V = _local(state["exp_avg"]), _local(state["exp_avg_sq"])
-        if (sparse is None and not group["lazy"] and use_native(P) and M.dim() == V.dim()
-                and P.dtype in (torch.bfloat16, torch.float32) and P.is_contiguous()):
+        state, h = self._advance(p, group)
+        lr, beta1, beta2, eps, wd, bc1, bc2, sr = h.lr, h.beta1, h.beta2, h.eps, h.wd, h.bc1, h.bc2, h.sr
+        P, M, V = _local(p), _local(state["exp_avg"]), _local(state["exp_avg_sq"])
+        fused = (sparse is None and not group["lazy"] and use_native(P) and M.dim() == V.dim()
+                 and P.dtype in (torch.bfloat16, torch.float32) and P.is_contiguous())
+        if fused:
             from micro_engram_fork_b200.ops.engram import adam_dense
 
             G = _local(p.grad)
-            if G.dtype not in (torch.float32, P.dtype):
-                G = G.float()
+            G = G if G.dtype in (torch.float32, P.dtype) else G.float()
             adam_dense(P, G.contiguous(), M, V, lr, beta1, beta2, eps, wd, bc1, bc2, 1.0,
-                       bool(sr) and P.dtype == torch.bfloat16, _SEED_BASE ^ (id(p) & 0xFFFF), int(step))
+                       sr and P.dtype == torch.bfloat16, _SEED_BASE ^ (id(p) & 0xFFFF), h.step)
             return
         rows = None
         if sparse is not None:

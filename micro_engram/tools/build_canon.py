@@ -90,7 +90,7 @@ def build(pieces, protected, vocab_size, merge_space=False, accents=False, white
     return canon, classes
 
 
-def main(argv=None):
+def _parser():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--tokenizer", required=True)
     ap.add_argument("--out", required=True)
@@ -100,43 +100,61 @@ def main(argv=None):
     ap.add_argument("--merge-whitespace", action="store_true")
     ap.add_argument("--paper", action="store_true", help="all three merges")
     ap.add_argument("--protect", action="append", default=[], metavar="FILE")
-    args = ap.parse_args(argv)
-    if args.paper:
-        args.merge_space = args.strip_accents = args.merge_whitespace = True
-    chosen = (args.merge_space, args.strip_accents, args.merge_whitespace)
+    return ap
 
+
+def _tokenizer_pieces(path, vocab_size):
+    """(pieces of the first min(len, vocab_size) ids, ids of special and added tokens)."""
     from transformers import AutoTokenizer
 
-    tok = AutoTokenizer.from_pretrained(args.tokenizer)
-    n = min(len(tok), args.vocab_size)
-    pieces = tok.convert_ids_to_tokens(list(range(n)))
-    protected = set(tok.get_added_vocab().values()) | set(tok.all_special_ids)
-    print(f"tokenizer pieces: {n:,} | protected (special/added): {len(protected):,}")
-    for path in args.protect:
-        ids, single, split = name_token_ids(read_names(path), pieces)
-        protected |= ids
-        print(f"{path}: {len(single)} names kept apart ({len(ids)} tokens)")
+    tok = AutoTokenizer.from_pretrained(path)
+    count = min(len(tok), vocab_size)
+    keep = set(tok.all_special_ids).union(tok.get_added_vocab().values())
+    return tok.convert_ids_to_tokens(list(range(count))), keep
+
+
+def _protect_names(files, pieces, protected):
+    for path in files:
+        hit, kept, split = name_token_ids(read_names(path), pieces)
+        protected.update(hit)
+        print(f"{path}: {len(kept)} names kept apart ({len(hit)} tokens)")
         if split:
             print(f"  split by the tokenizer, left alone ({len(split)}): {', '.join(split)}")
+
+
+def _report(pieces, protected, vocab_size, chosen):
+    """The class count of every rung of the option ladder, the chosen one marked."""
+    n = len(pieces)
     for label, flags in _LADDER:
-        canon, _ = build(pieces, protected, args.vocab_size, *flags)
-        k = len(set(canon[:n]))
-        print(f"{label:22s}: {n:,} tokens -> {k:,} classes ({1 - k / n:.1%} fewer)"
-              + ("  <- chosen" if flags == chosen else ""))
-    canon, classes = build(pieces, protected, args.vocab_size, *chosen)
-    print(f"\nchosen: merge_space={args.merge_space} strip_accents={args.strip_accents} "
-          f"merge_whitespace={args.merge_whitespace}")
-    if WHITESPACE_CLASS in classes:
-        ws = classes[WHITESPACE_CLASS]
+        classes = len(set(build(pieces, protected, vocab_size, *flags)[0][:n]))
+        mark = "  <- chosen" if flags == chosen else ""
+        print(f"{label:22s}: {n:,} tokens -> {classes:,} classes ({1 - classes / n:.1%} fewer){mark}")
+
+
+def _show_classes(pieces, classes):
+    ws = classes.get(WHITESPACE_CLASS)
+    if ws:
         print(f"whitespace class: {len(ws)} pieces, e.g. {[pieces[i] for i in ws[:8]]}")
-    big = [ids for key, ids in classes.items() if len(ids) >= 3 and key != WHITESPACE_CLASS]
+    merged = [ids for key, ids in classes.items() if key != WHITESPACE_CLASS and len(ids) >= 3]
     print("\nsample of merged classes:")
-    for ids in random.Random(0).sample(big, min(12, len(big))):
+    for ids in random.Random(0).sample(merged, min(12, len(merged))):
         print("   ", [pieces[i] for i in ids[:8]])
-    t = torch.tensor(canon, dtype=torch.long)
-    if not torch.equal(t[t], t):
+
+
+def main(argv=None):
+    args = _parser().parse_args(argv)
+    chosen = (True, True, True) if args.paper else (args.merge_space, args.strip_accents, args.merge_whitespace)
+    pieces, protected = _tokenizer_pieces(args.tokenizer, args.vocab_size)
+    print(f"tokenizer pieces: {len(pieces):,} | protected (special/added): {len(protected):,}")
+    _protect_names(args.protect, pieces, protected)
+    _report(pieces, protected, args.vocab_size, chosen)
+    canon, classes = build(pieces, protected, args.vocab_size, *chosen)
+    print(f"\nchosen: merge_space={chosen[0]} strip_accents={chosen[1]} merge_whitespace={chosen[2]}")
+    _show_classes(pieces, classes)
+    table = torch.tensor(canon, dtype=torch.long)
+    if not torch.equal(table[table], table):
         raise SystemExit("internal error: the map is not idempotent")
-    torch.save(t, args.out)
+    torch.save(table, args.out)
     print(f"\nsaved {args.out}")
 
 

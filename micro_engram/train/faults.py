@@ -66,6 +66,9 @@ def check_device(trainer):
     ar = getattr(trainer, "_p2p_ar", None)
     if ar is not None:
         ar.check_status()
+    vocab = getattr(trainer, "vocab", None)
+    if vocab is not None:
+        vocab.check_status()
     if trainer.device.type == "cuda":
         from micro_engram_fork_b200 import native
 

@@ -8,9 +8,10 @@ Each rank keeps row_range(V) of the tied embedding / output head (outside the ba
   loss   per chunk of tokens, the chunk's hidden states are gathered from all ranks, each rank
          computes logits against its own vocab rows (bf16 GEMM, fp32 softcap), and the
          per-row (max, sum-exp, target logit) partials are combined across ranks into the LSE.
-         CUDA: one row kernel produces the partials in a single pass over the bf16 logits,
-         and the backward overwrites the recomputed logits in place with
-         (softmax - onehot) * w * softcap' before the dH GEMM and the reduce-scatter.
+         CUDA: the logits GEMM's epilogue produces the partials, the logits are overwritten in
+         place with (softmax - onehot) * w * softcap', and the dH GEMM's epilogue stores each
+         token's rows on its owner's GPU; every exchange between ranks goes through peer
+         memory (micro_engram_fork_b200/parallel/vocab_comm.py), none through NCCL.
 
 Every rank runs the same chunk count: the chunk size comes from ceil(V/world), never from
 this rank's own row count (micro_engram/train/head.py:38-42 of the reference). Loss terms
@@ -36,6 +37,7 @@ class VocabShard:
         device = torch.device(device) if device is not None else weight.device
         dtype = dtype or weight.dtype
         self._buf = None
+        self._comm = None
         local = weight[self.start:self.start + self.rows].detach()
         if device.type == "cuda" and world > 1 and use_native(torch.empty(0, device=device)):
             # peer-mapped shard (padded to `per` rows, same layout on every rank)
@@ -70,6 +72,21 @@ class VocabShard:
     @property
     def group(self):
         return _group(self.world)
+
+    def comm(self):
+        """The peer-memory exchange of the CUDA loss (built on first use; collective)."""
+        if self._comm is None:
+            import os
+
+            from micro_engram_fork_b200.parallel.vocab_comm import VocabComm
+
+            timeout = float(os.environ.get("MICRO_ENGRAM_PEER_TIMEOUT_S", "10"))
+            self._comm = VocabComm(self.chunk_bf16, self.d, self.weight.device, self.group, timeout_s=timeout)
+        return self._comm
+
+    def check_status(self):
+        if self._comm is not None:
+            self._comm.check_status()
 
     @torch.no_grad()
     def embed(self, ids):
@@ -216,8 +233,12 @@ class _FusedVocabCE(torch.autograd.Function):
          ranks combine by a plain sum: lse = cap + log(sum of partials). The bf16 logits are
          kept only when a gradient is needed;
       2. the logits are overwritten in place with (softmax - onehot) * softcap' (ce_bwd_inplace,
-         SFU exp/tanh, one pass), multiplied into dH on the tcgen05 GEMM with fp32 output
-         (gemm_f32) and reduce-scattered to the token's rank.
+         SFU exp/tanh, one pass) and multiplied into dH on the tcgen05 GEMM with fp32 output,
+         whose epilogue stores each token's rows straight into its owner's receive slot.
+
+    Across ranks every exchange goes through peer memory (VocabComm: the chunk's hidden states
+    and labels, the (max, sum, target) partials, dH), with no NCCL call; the partials are
+    merged in rank order, so the loss is the same on every run.
 
     The backward only scales this rank's dH rows by the incoming gradient (the loss is linear
     in it), so the logits GEMM runs once per chunk. Reference semantics:
@@ -229,41 +250,36 @@ class _FusedVocabCE(torch.autograd.Function):
         from micro_engram_fork_b200 import native
 
         C = native()
-        world, group, w = shard.world, shard.group, shard.gemm_weight
+        world, w = shard.world, shard.gemm_weight
         N, c = hidden.shape[0], shard.chunk_bf16
         cap = float(shard.softcap or 0.0)
+        comm = shard.comm() if world > 1 else None
         h = hidden.detach().to(w.dtype).contiguous()
         total = torch.zeros((), dtype=torch.float32, device=hidden.device)
         dh = torch.empty(N, shard.d, dtype=torch.float32, device=hidden.device) if need_grad else None
         for a in range(0, N, c):
             b = min(N, a + c)
             n = b - a
-            H = _gather(h[a:b], group, world)
-            L = _gather(labels[a:b].contiguous(), group, world)
+            H, L = comm.gather(h[a:b], labels[a:b].contiguous()) if comm else (h[a:b], labels[a:b].contiguous())
             s_part, m_part, tgt, z = C.gemm_ce(H, w, L, shard.start, cap, need_grad, shard.rows)
-            if cap > 0:
-                s = s_part.sum(1)
-                if world > 1:
-                    st = torch.stack([s, tgt])
-                    dist.all_reduce(st, group=group)
-                    s, tgt = st[0], st[1]
-                lse = cap + torch.log(s)
+            if cap > 0:  # every partial shares the offset cap
+                m, s = torch.full_like(tgt, cap), s_part.sum(1)
             else:
                 m = m_part.amax(1)
                 s = (s_part * torch.exp(m_part - m[:, None])).sum(1)
-                if world > 1:
-                    M = m.clone()
-                    dist.all_reduce(M, op=dist.ReduceOp.MAX, group=group)
-                    st = torch.stack([s * torch.exp(m - M), tgt])
-                    dist.all_reduce(st, group=group)
-                    m, s, tgt = M, st[0], st[1]
+            if comm:
+                lse, tgt = comm.merge(m, s, tgt)
+            else:
                 lse = m + torch.log(s)
             own = slice(shard.rank * n, (shard.rank + 1) * n)
             valid = L[own] != IGNORE
             total = total + torch.where(valid, lse[own] - tgt[own], torch.zeros_like(lse[own])).sum()
             if need_grad:
                 C.ce_bwd_inplace(z, L, shard.start, cap, lse, (L != IGNORE).float())
-                dh[a:b] = _reduce_scatter(C.gemm_f32(z, w), n, shard.d, group, world)
+                if comm:
+                    comm.scatter_sum(z, w, dh[a:b])
+                else:
+                    dh[a:b] = C.gemm_f32(z, w)
             del z
         ctx.dh, ctx.hdtype = dh, hidden.dtype
         return total

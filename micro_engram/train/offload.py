@@ -2,74 +2,103 @@
 per-layer checkpointing, each layer's input) go to pinned host memory on a side stream and
 come back for the backward.
 
-Pinned buffers are pooled by (numel, dtype) and reused every step (pinning is slow);
-each copy is one cudaMemcpyAsync on the offload stream, ordered after the producer with an
-event, and the device tensor is kept alive until its copy finished (record_stream).
-Same mechanism as the reference (micro_engram/train/offload.py:1-66).
+Design:
+  * a pool of pinned host buffers keyed by (numel, dtype), reused every step (pinning is
+    slow); a buffer returns to the pool when the micro-batch's backward is over;
+  * every saved tensor becomes a _Saved record: its host buffer, the event that marks the
+    end of its device->host copy, and (once fetched) its device copy and that copy's event;
+  * device->host copies are ordered after the producer by a stream wait and keep the source
+    alive with record_stream; host->device copies run on the same side stream;
+  * the backward visits layers in reverse forward order, so fetching record i also starts
+    the fetch of record i-1: its copy overlaps the backward of the current layer.
+
+Behaviour of the reference: micro_engram/train/offload.py:1-66 (saved-tensor hooks, pinned
+copies on a side stream).
 """
 import torch
 
-MIN_BYTES = 1 << 20
+MIN_BYTES = 1 << 20  # smaller tensors stay on the device
+
+
+class _Saved:
+    __slots__ = ("host", "shape", "device", "copied", "index", "on_device", "arrived")
+
+    def __init__(self, host, shape, device, copied, index):
+        self.host, self.shape, self.device, self.copied, self.index = host, shape, device, copied, index
+        self.on_device = None  # device tensor once fetched (until handed to autograd)
+        self.arrived = None    # event: its host->device copy finished
+
+
+class _PinnedPool:
+    def __init__(self):
+        self.free = {}
+        self.lent = []
+
+    def take(self, numel, dtype):
+        key = (numel, dtype)
+        stack = self.free.setdefault(key, [])
+        buf = stack.pop() if stack else torch.empty(numel, dtype=dtype, pin_memory=True)
+        self.lent.append((key, buf))
+        return buf
+
+    def give_back_all(self):
+        for key, buf in self.lent:
+            self.free[key].append(buf)
+        self.lent = []
+
+    def nbytes(self):
+        held = [b for bufs in self.free.values() for b in bufs] + [b for _, b in self.lent]
+        return sum(b.numel() * b.element_size() for b in held)
 
 
 class ActivationOffload:
     def __init__(self, device):
         self.device = device
-        self.pool = {}
-        self.in_use = []
-        self.order = []  # packed entries of this micro-batch, in forward order
         self.stream = torch.cuda.Stream(device) if device.type == "cuda" else None
+        self._pool = _PinnedPool()
+        self.order = []  # _Saved records of this micro-batch, in forward order
 
-    def _buffer(self, t):
-        key = (t.numel(), t.dtype)
-        free = self.pool.setdefault(key, [])
-        buf = free.pop() if free else torch.empty(t.numel(), dtype=t.dtype, pin_memory=True)
-        self.in_use.append((key, buf))
-        return buf
+    @staticmethod
+    def _worth_moving(t):
+        return t.device.type == "cuda" and t.is_contiguous() and t.numel() * t.element_size() >= MIN_BYTES
 
     def pack(self, t):
-        if t.device.type != "cuda" or t.numel() * t.element_size() < MIN_BYTES or not t.is_contiguous():
+        if not self._worth_moving(t):
             return t
-        buf = self._buffer(t)
-        self.stream.wait_stream(torch.cuda.current_stream(t.device))
-        with torch.cuda.stream(self.stream):
-            buf.copy_(t.view(-1), non_blocking=True)
-            ev = torch.cuda.Event()
-            ev.record(self.stream)
-        t.record_stream(self.stream)
-        entry = {"buf": buf, "shape": t.shape, "device": t.device, "ev": ev, "dev": None, "ready": None}
-        self.order.append(entry)
-        return entry
+        host = self._pool.take(t.numel(), t.dtype)
+        side = self.stream
+        side.wait_stream(torch.cuda.current_stream(t.device))
+        copied = torch.cuda.Event()
+        with torch.cuda.stream(side):
+            host.copy_(t.view(-1), non_blocking=True)
+            copied.record(side)
+        t.record_stream(side)  # the device tensor stays allocated until the copy is done
+        rec = _Saved(host, t.shape, t.device, copied, len(self.order))
+        self.order.append(rec)
+        return rec
 
-    def _fetch(self, e):
-        """Start the host->device copy of entry e on the side stream (once)."""
-        if e["dev"] is not None:
+    def _fetch(self, rec):
+        """Start the host->device copy of `rec` on the side stream (at most once)."""
+        if rec.on_device is not None:
             return
-        self.stream.wait_event(e["ev"])
-        with torch.cuda.stream(self.stream):
-            e["dev"] = e["buf"].to(e["device"], non_blocking=True)
-            e["ready"] = torch.cuda.Event()
-            e["ready"].record(self.stream)
+        side = self.stream
+        side.wait_event(rec.copied)
+        rec.arrived = torch.cuda.Event()
+        with torch.cuda.stream(side):
+            rec.on_device = rec.host.to(rec.device, non_blocking=True)
+            rec.arrived.record(side)
 
     def unpack(self, packed):
-        if isinstance(packed, torch.Tensor):
+        if not isinstance(packed, _Saved):
             return packed
-        e = packed
-        self._fetch(e)
-        # the backward visits layers in reverse: start copying the previous layer's input now,
-        # so it overlaps this layer's backward
-        try:
-            i = next(j for j in range(len(self.order) - 1, -1, -1) if self.order[j] is e)
-        except StopIteration:
-            i = -1
-        if i > 0:
-            self._fetch(self.order[i - 1])
-        cur = torch.cuda.current_stream(e["device"])
-        cur.wait_event(e["ready"])
-        out = e["dev"]
-        out.record_stream(cur)
-        e["dev"] = None  # the caller owns it now
-        return out.view(e["shape"])
+        self._fetch(packed)
+        if packed.index > 0:  # prefetch the input of the layer the backward visits next
+            self._fetch(self.order[packed.index - 1])
+        consumer = torch.cuda.current_stream(packed.device)
+        consumer.wait_event(packed.arrived)
+        out, packed.on_device = packed.on_device, None  # autograd owns the device copy now
+        out.record_stream(consumer)
+        return out.view(packed.shape)
 
     def context(self):
         return torch.autograd.graph.saved_tensors_hooks(self.pack, self.unpack)
@@ -78,11 +107,8 @@ class ActivationOffload:
         """After the backward: every pinned buffer of this micro-batch can be reused."""
         if self.device.type == "cuda":
             torch.cuda.current_stream(self.device).synchronize()
-        for key, buf in self.in_use:
-            self.pool[key].append(buf)
-        self.in_use = []
+        self._pool.give_back_all()
         self.order = []
 
     def pinned_bytes(self):
-        return (sum(b.numel() * b.element_size() for bs in self.pool.values() for b in bs)
-                + sum(b.numel() * b.element_size() for _, b in self.in_use))
+        return self._pool.nbytes()

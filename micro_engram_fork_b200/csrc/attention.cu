@@ -647,14 +647,46 @@ thread_local const char* g_noalloc_err = "no error";
 
 size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
-// doc_end[s] = last token of s's document: each document's last token writes its range.
+// doc_end[t] = last token of t's document. Document starts are non-decreasing along the packed
+// row, so the end is the last position whose start equals ds[t]: one binary search per token
+// (O(log T) work each, all tokens in parallel, whatever the document lengths).
 __global__ void doc_end_from_start_kernel(const int* __restrict__ ds, int T, int* __restrict__ de) {
   for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < T; t += gridDim.x * blockDim.x) {
-    if (t == T - 1 || ds[t + 1] == t + 1) {
-      for (int s = ds[t]; s <= t; ++s) de[s] = t;
+    const int s = ds[t];
+    int lo = t, hi = T - 1;  // invariant: ds[lo] == s; the answer lies in [lo, hi]
+    while (lo < hi) {
+      const int mid = lo + (hi - lo + 1) / 2;
+      if (ds[mid] == s) lo = mid;
+      else hi = mid - 1;
     }
+    de[t] = lo;
   }
 }
+
+// launch_bwd with every step checked, for the allocation-free entry point: the shared-memory
+// opt-in of each kernel and each launch report their own failure.
+template <int D>
+const char* launch_bwd_checked(const bf16* q, const bf16* k, const bf16* v, const bf16* dout, const float* lse,
+                               const float* delta, const int* ds, const int* de, int T, int Hq, int Hk, int window,
+                               float scale, bf16* dq, bf16* dk, bf16* dv, cudaStream_t stream) {
+  constexpr int BN = D > 256 ? 32 : 64;
+  const size_t smem_kv = (size_t)(2 * BN * D + 2 * 64 * D + 2 * BN * 64) * 2 + 2 * 64 * sizeof(float);
+  const size_t smem_q = (size_t)(2 * 64 * D + 2 * BN * D + 64 * BN) * 2;
+  auto kv = attn_bwd_dkdv_kernel<D, BN>;
+  auto qk = attn_bwd_dq_kernel<D, BN>;
+  if (cudaFuncSetAttribute(kv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_kv) != cudaSuccess)
+    return "me_attn_bwd_noalloc: cudaFuncSetAttribute (shared memory) failed for the dK/dV kernel";
+  if (cudaFuncSetAttribute(qk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_q) != cudaSuccess)
+    return "me_attn_bwd_noalloc: cudaFuncSetAttribute (shared memory) failed for the dQ kernel";
+  kv<<<dim3((T + BN - 1) / BN, Hk), 256, smem_kv, stream>>>(q, k, v, dout, lse, delta, ds, de, T, Hq, Hk, window,
+                                                             scale, dk, dv);
+  if (cudaGetLastError() != cudaSuccess) return "me_attn_bwd_noalloc: the dK/dV kernel failed to launch";
+  qk<<<dim3((T + 63) / 64, Hq), 256, smem_q, stream>>>(q, k, v, dout, lse, delta, ds, T, Hq, Hk, window, scale, dq);
+  if (cudaGetLastError() != cudaSuccess) return "me_attn_bwd_noalloc: the dQ kernel failed to launch";
+  return nullptr;
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 // Device address of the scratch array on the current device (looked up once per device).
 void* scratch_on_current_device(int* err) {
@@ -690,6 +722,23 @@ extern "C" __attribute__((visibility("default"))) int me_attn_bwd_noalloc(
                     "not in {64, 128, 256, 512}";
     return ME_NOALLOC_ERR_ARGS;
   }
+  // the kernels read and write the bf16 tensors 16 bytes at a time, lse and doc_start 4 at a time
+  for (const void* p : {dout, q, k, v, o, (const void*)dq, (const void*)dk, (const void*)dv}) {
+    if (!aligned(p, 16)) {
+      g_noalloc_err = "me_attn_bwd_noalloc: dout, q, k, v, o, dq, dk and dv must start on 16-byte boundaries";
+      return ME_NOALLOC_ERR_ARGS;
+    }
+  }
+  if (!aligned(lse, 4) || !aligned(doc_start, 4)) {
+    g_noalloc_err = "me_attn_bwd_noalloc: lse and doc_start must start on 4-byte boundaries";
+    return ME_NOALLOC_ERR_ARGS;
+  }
+  if (cudaPeekAtLastError() != cudaSuccess) {
+    // an earlier, unrelated launch left an error: report it as such and leave it pending for its owner
+    g_noalloc_err = "me_attn_bwd_noalloc: a CUDA error from earlier work is pending (cudaPeekAtLastError); "
+                    "nothing was launched";
+    return ME_NOALLOC_ERR_LAUNCH;
+  }
   const size_t delta_bytes = align256((size_t)Hq * (size_t)T * sizeof(float));
   const size_t need = delta_bytes + align256((size_t)T * sizeof(int));
   if (need > (size_t)ME_ATTN_BWD_NOALLOC_SCRATCH_BYTES) {
@@ -710,7 +759,15 @@ extern "C" __attribute__((visibility("default"))) int me_attn_bwd_noalloc(
     const int grid = (int)std::min<int64_t>((rows + 7) / 8, 148 * 32);
     attn_bwd_pre_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const bf16*>(o), reinterpret_cast<const bf16*>(dout),
                                                   T, Hq, D, delta);
+    if (cudaGetLastError() != cudaSuccess) {
+      g_noalloc_err = "me_attn_bwd_noalloc: the softmax-correction kernel failed to launch";
+      return ME_NOALLOC_ERR_LAUNCH;
+    }
     doc_end_from_start_kernel<<<(T + 255) / 256, 256, 0, stream>>>(doc_start, T, doc_end);
+    if (cudaGetLastError() != cudaSuccess) {
+      g_noalloc_err = "me_attn_bwd_noalloc: the document-end kernel failed to launch";
+      return ME_NOALLOC_ERR_LAUNCH;
+    }
   }
   const bf16* qp = reinterpret_cast<const bf16*>(q);
   const bf16* kp = reinterpret_cast<const bf16*>(k);
@@ -719,14 +776,15 @@ extern "C" __attribute__((visibility("default"))) int me_attn_bwd_noalloc(
   bf16* dqp = reinterpret_cast<bf16*>(dq);
   bf16* dkp = reinterpret_cast<bf16*>(dk);
   bf16* dvp = reinterpret_cast<bf16*>(dv);
+  const char* failed = nullptr;
   switch (D) {
-    case 64: launch_bwd<64>(qp, kp, vp, gp, lse, delta, doc_start, doc_end, T, Hq, Hk, window, scale, dqp, dkp, dvp, stream); break;
-    case 128: launch_bwd<128>(qp, kp, vp, gp, lse, delta, doc_start, doc_end, T, Hq, Hk, window, scale, dqp, dkp, dvp, stream); break;
-    case 256: launch_bwd<256>(qp, kp, vp, gp, lse, delta, doc_start, doc_end, T, Hq, Hk, window, scale, dqp, dkp, dvp, stream); break;
-    default: launch_bwd<512>(qp, kp, vp, gp, lse, delta, doc_start, doc_end, T, Hq, Hk, window, scale, dqp, dkp, dvp, stream); break;
+    case 64: failed = launch_bwd_checked<64>(qp, kp, vp, gp, lse, delta, doc_start, doc_end, T, Hq, Hk, window, scale, dqp, dkp, dvp, stream); break;
+    case 128: failed = launch_bwd_checked<128>(qp, kp, vp, gp, lse, delta, doc_start, doc_end, T, Hq, Hk, window, scale, dqp, dkp, dvp, stream); break;
+    case 256: failed = launch_bwd_checked<256>(qp, kp, vp, gp, lse, delta, doc_start, doc_end, T, Hq, Hk, window, scale, dqp, dkp, dvp, stream); break;
+    default: failed = launch_bwd_checked<512>(qp, kp, vp, gp, lse, delta, doc_start, doc_end, T, Hq, Hk, window, scale, dqp, dkp, dvp, stream); break;
   }
-  if (cudaGetLastError() != cudaSuccess) {
-    g_noalloc_err = "me_attn_bwd_noalloc: a kernel launch failed";
+  if (failed != nullptr) {
+    g_noalloc_err = failed;
     return ME_NOALLOC_ERR_LAUNCH;
   }
   g_noalloc_err = "no error";

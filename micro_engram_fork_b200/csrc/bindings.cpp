@@ -80,6 +80,12 @@ torch::Tensor gemm_f32(torch::Tensor A, torch::Tensor W);
 torch::Tensor gemm_tn_f32(torch::Tensor At, torch::Tensor Bt);
 void gemm_carry_copy(int64_t device, int64_t segs, int64_t nsegs, int64_t begin16, int64_t end16);
 void layer_gather(torch::Tensor segs, int64_t begin16, int64_t end16);
+void gemm_f32_scatter(torch::Tensor A, torch::Tensor W, torch::Tensor recv_ptrs, int64_t rows_per_rank,
+                      int64_t slot, int64_t slot_elems);
+void p2p_gather(torch::Tensor bases, int64_t rank, int64_t call, int64_t stage_off, int64_t half_bytes, int64_t n16,
+                torch::Tensor out, double timeout_s, torch::Tensor status);
+void p2p_sum_slots(torch::Tensor bases, int64_t rank, int64_t call, int64_t recv_off, int64_t slot_elems,
+                   torch::Tensor out, double timeout_s, torch::Tensor status);
 std::vector<torch::Tensor> gemm_ce(torch::Tensor H, torch::Tensor E, torch::Tensor labels, int64_t lab_start,
                                    double cap, bool keep_logits, int64_t n_valid);
 torch::Tensor gemm_status(int64_t device);
@@ -132,6 +138,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_tn_f32", &gemm_tn_f32);
   m.def("gemm_carry_copy", &gemm_carry_copy);
   m.def("layer_gather", &layer_gather);
+  m.def("gemm_f32_scatter", &gemm_f32_scatter);
+  m.def("p2p_gather", &p2p_gather);
+  m.def("p2p_sum_slots", &p2p_sum_slots);
   m.def("gemm_ce", &gemm_ce);
   m.def("gemm_status", &gemm_status);
   m.def("nf4_quantize", &nf4_quantize);

@@ -35,6 +35,33 @@ torch::Tensor gemm(torch::Tensor A, torch::Tensor W, bool b_kmajor, c10::optiona
   return D;
 }
 
+// dH rows scattered to their owners: rows [r * rows_per_rank, (r + 1) * rows_per_rank) of
+// A . W (fp32, W [K, N] read N-major) are stored into rank r's receive buffer recv_ptrs[r], in
+// slot `slot` (slots of slot_elems floats; rows of N floats). The caller signals the peers after
+// this launch (p2p_sum_slots) so the owners can sum their slots.
+void gemm_f32_scatter(torch::Tensor A, torch::Tensor W, torch::Tensor recv_ptrs, int64_t rows_per_rank,
+                      int64_t slot, int64_t slot_elems) {
+  check_operand(A, "A");
+  check_operand(W, "W");
+  TORCH_CHECK(recv_ptrs.is_cuda() && recv_ptrs.scalar_type() == torch::kInt64, "gemm_f32_scatter: recv_ptrs");
+  const at::cuda::CUDAGuard guard(A.device());
+  const int M = (int)A.size(0), K = (int)A.size(1), N = (int)W.size(1);
+  TORCH_CHECK(W.size(0) == K && N % 8 == 0 && K % 8 == 0, "gemm_f32_scatter: W must be [K, N], N % 8 == 0");
+  TORCH_CHECK(rows_per_rank > 0 && M == rows_per_rank * recv_ptrs.numel(), "gemm_f32_scatter: M != world * rows");
+  TORCH_CHECK(slot_elems >= rows_per_rank * N, "gemm_f32_scatter: slots too small");
+  if (M == 0 || N == 0) return;
+  const int dev = A.get_device();
+  GemmArgs a = base_args(M, N, K, (N + BN - 1) / BN, dev);
+  a.ldd = N;
+  a.peer_out = recv_ptrs.data_ptr<int64_t>();
+  a.peer_rows = (int)rows_per_rank;
+  a.peer_slot = (int)slot;
+  a.peer_slot_elems = slot_elems;
+  const CUtensorMap ta = make_tmap(A.data_ptr(), M, K, A.stride(0), BK, BM);
+  const CUtensorMap tb = make_tmap(W.data_ptr(), K, N, W.stride(0), 64, BK);
+  launch<EPI_F32, true>(ta, tb, a, dev, at::cuda::getCurrentCUDAStream());
+}
+
 // out[M, N] (fp32) = A[M, K] . W, with W [K, N] read N-major (the LM head's dH = P . E).
 torch::Tensor gemm_f32(torch::Tensor A, torch::Tensor W) {
   check_operand(A, "A");

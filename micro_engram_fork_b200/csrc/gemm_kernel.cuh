@@ -36,7 +36,8 @@
 //            for the backward.
 //   DGEGLU   acc = dL/dm for 256 features; reads gu of the row and writes
 //            d_gu = [bf16(dm * u * gelu'(g)) | bf16(dm * bf16(gelu(g)))].
-//   F32      D = acc in fp32 (the LM head's dH, reduced across ranks in fp32).
+//   F32      D = acc in fp32 (the LM head's dH, reduced across ranks in fp32); with peer_out set,
+//            each row is stored straight into its token owner's receive slot on that GPU.
 //   CE       logits of the tied head against this rank's vocab rows: z = bf16(acc) (stored only
 //            when the backward needs it), zc = softcap(z); per (row, tile) the partial sum of
 //            exp(zc - m) with m = the cap itself when softcapping (|zc| <= cap, so no running max
@@ -89,6 +90,13 @@ struct GemmArgs {
   const bf16* aux;      // DGEGLU: gu [M, 2F]
   int64_t ld_aux;
   float* Df;            // F32: [M, N]
+  // F32 with a peer-scattered output (the fused reduce-scatter of the LM head's dH): row r of D
+  // belongs to rank r / peer_rows and goes to that rank's receive buffer peer_out[rank] at slot
+  // `peer_slot` (this rank), row r % peer_rows; plain 16-byte stores over NVLink
+  const int64_t* peer_out;
+  int peer_rows;
+  int64_t peer_slot_elems;
+  int peer_slot;
   const int64_t* labels;  // CE: [M]
   int64_t lab_start;    // CE: first vocab id of this rank's rows
   float cap;            // CE: softcap (0 = none)
@@ -147,6 +155,14 @@ ME_DEVICE void tile_coords(int t, const GemmArgs& p, int& mb, int& nb) {
   const int r = t - g * per_group;
   mb = first + r % gsz;
   nb = r / gsz;
+}
+
+// Destination of row `row` of an fp32 output: local, or a peer's receive slot.
+ME_DEVICE float* f32_row(const GemmArgs& p, int row) {
+  if (p.peer_out == nullptr) return p.Df + (int64_t)row * p.ldd;
+  const int owner = row / p.peer_rows;
+  float* base = reinterpret_cast<float*>(p.peer_out[owner]) + (int64_t)p.peer_slot * p.peer_slot_elems;
+  return base + (int64_t)(row - owner * p.peer_rows) * p.ldd;
 }
 
 ME_DEVICE void store_row32(bf16* dst, const float (&v)[32], int valid_cols) {
@@ -349,7 +365,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               if (EPI == EPI_STORE) {
                 store_row32(p.D + (int64_t)row * p.ldd + col, v, p.N - col);
               } else {
-                float* dst = p.Df + (int64_t)row * p.ldd + col;
+                float* dst = f32_row(p, row) + col;
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
                   if (col + j * 4 < p.N)
@@ -396,7 +412,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           tmem_ld32(tbase + c * 32, v);
           const int col = nb * BN + c * 32;
           if (row_ok && col < p.N) {
-            float* dst = p.Df + (int64_t)row * p.ldd + col;
+            float* dst = f32_row(p, row) + col;
 #pragma unroll
             for (int j = 0; j < 8; ++j)
               if (col + j * 4 < p.N)

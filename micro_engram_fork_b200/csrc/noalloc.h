@@ -21,6 +21,11 @@
 //    two host threads on one device) race on it. Serialize them.
 //  * The array keeps the previous call's contents; every element a call reads is written by
 //    that call first, so nothing needs clearing between calls.
+//  * dout, q, k, v, o, dq, dk and dv must start on 16-byte boundaries (the kernels move them 16
+//    bytes at a time) and lse and doc_start on 4-byte boundaries; other pointers are refused with
+//    ME_NOALLOC_ERR_ARGS. doc_start must be non-decreasing (packed documents), as from doc_starts.
+//  * A CUDA error already pending when the call starts (from earlier, unrelated work) is left
+//    pending and reported as ME_NOALLOC_ERR_LAUNCH; nothing is launched then.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -29,10 +34,10 @@
 
 enum {
   ME_NOALLOC_OK = 0,
-  ME_NOALLOC_ERR_ARGS = -1,       // a null pointer, a non-positive size or an unsupported head_dim
+  ME_NOALLOC_ERR_ARGS = -1,       // a null or misaligned pointer, a bad size or an unsupported head_dim
   ME_NOALLOC_ERR_TOO_LARGE = -2,  // the problem needs more scratch than the fixed array holds
   ME_NOALLOC_ERR_SETUP = -3,      // cudaGetSymbolAddress failed on this device
-  ME_NOALLOC_ERR_LAUNCH = -4,     // a kernel launch failed
+  ME_NOALLOC_ERR_LAUNCH = -4,     // an earlier error was pending, a shared-memory opt-in or a launch failed
 };
 
 #ifdef __cplusplus

@@ -101,6 +101,64 @@ __global__ void __launch_bounds__(256) p2p_allreduce_mean_kernel(const int64_t* 
   }
 }
 
+// ------------------------------------------------------------------ exchanges of the vocab loss
+// Every block signals `call` into flag[rank] of every peer and waits (acquire, bounded) until
+// all flags have reached it: each rank's data staged before its launch is then readable.
+ME_DEVICE bool flags_barrier(const int64_t* __restrict__ bases, int world, int rank, uint32_t call,
+                             uint64_t timeout_ns, int* status) {
+  __shared__ int failed;
+  if (threadIdx.x == 0) failed = 0;
+  __syncthreads();
+  if (threadIdx.x < world) {
+    st_release_sys(reinterpret_cast<uint32_t*>(bases[threadIdx.x]) + rank, call);
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(bases[rank]) + threadIdx.x;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 0;; ++it) {
+      if ((int32_t)(ld_acquire_sys(mine) - call) >= 0) break;
+      if ((it & 63u) == 63u && globaltimer_ns() - t0 > timeout_ns) {
+        report(status, ME_ERR_TIMEOUT, threadIdx.x);
+        failed = 1;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  return failed == 0;
+}
+
+// out[r * n16 ...] = rank r's stage (n16 16-byte units at stage_off + parity * half) for every r.
+__global__ void __launch_bounds__(256) p2p_gather_kernel(const int64_t* __restrict__ bases, int world, int rank,
+                                                         uint32_t call, int64_t stage_off, int64_t half_bytes,
+                                                         int64_t n16, uint4* __restrict__ out, uint64_t timeout_ns,
+                                                         int* status) {
+  if (!flags_barrier(bases, world, rank, call, timeout_ns, status)) return;
+  const int64_t off = stage_off + (int64_t)(call & 1u) * half_bytes;
+  const int64_t total = n16 * world;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / n16);
+    out[i] = __ldcg(reinterpret_cast<const uint4*>(bases[r] + off) + (i - (int64_t)r * n16));
+  }
+}
+
+// out[i] = sum over slots s of this rank's recv[parity][s][i] (fp32), after every peer signalled
+// that its scattered stores into those slots are done.
+__global__ void __launch_bounds__(256) p2p_sum_slots_kernel(const int64_t* __restrict__ bases, int world, int rank,
+                                                            uint32_t call, int64_t recv_off, int64_t slot_elems,
+                                                            int64_t n4, float4* __restrict__ out, uint64_t timeout_ns,
+                                                            int* status) {
+  if (!flags_barrier(bases, world, rank, call, timeout_ns, status)) return;
+  const float* recv = reinterpret_cast<const float*>(bases[rank] + recv_off) +
+                      (int64_t)(call & 1u) * world * slot_elems;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sl = 0; sl < world; ++sl) {  // fixed order: the sum is the same on every run
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(recv + (int64_t)sl * slot_elems) + i);
+      acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
+    }
+    out[i] = acc;
+  }
+}
+
 // The standalone form of a layer all-gather range: one warp per 32 threads, grid-strided.
 __global__ void __launch_bounds__(256) layer_gather_kernel(const GatherSeg* __restrict__ segs, int nsegs,
                                                            int64_t begin16, int64_t end16) {
@@ -122,6 +180,43 @@ void layer_gather(torch::Tensor segs, int64_t begin16, int64_t end16) {
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, segs.get_device());
   layer_gather_kernel<<<sms * 2, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const GatherSeg*>(segs.data_ptr<int64_t>()), (int)segs.size(0), begin16, end16);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+int grid_for(int64_t units, int dev) {
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return (int)std::max<int64_t>(1, std::min<int64_t>((units + 255) / 256, (int64_t)sms * 4));
+}
+
+// Gather every rank's staged bytes (n16 16-byte units each) into out [world * n16 * 16 bytes].
+void p2p_gather(torch::Tensor bases, int64_t rank, int64_t call, int64_t stage_off, int64_t half_bytes, int64_t n16,
+                torch::Tensor out, double timeout_s, torch::Tensor status) {
+  const int world = (int)bases.numel();
+  TORCH_CHECK(world >= 1 && world <= MAX_RANKS && out.is_cuda() && out.nbytes() >= (size_t)(world * n16 * 16),
+              "p2p_gather: bad arguments");
+  TORCH_CHECK(stage_off % 16 == 0 && half_bytes % 16 == 0 && reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
+              "p2p_gather: 16-byte alignment");
+  const at::cuda::CUDAGuard guard(out.device());
+  p2p_gather_kernel<<<grid_for(world * n16, out.get_device()), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      bases.data_ptr<int64_t>(), world, (int)rank, (uint32_t)call, stage_off, half_bytes, n16,
+      reinterpret_cast<uint4*>(out.data_ptr()), (uint64_t)(timeout_s * 1e9), status.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// out[n] (fp32) = sum of this rank's `world` receive slots of the parity of `call`.
+void p2p_sum_slots(torch::Tensor bases, int64_t rank, int64_t call, int64_t recv_off, int64_t slot_elems,
+                   torch::Tensor out, double timeout_s, torch::Tensor status) {
+  const int world = (int)bases.numel();
+  TORCH_CHECK(world >= 1 && world <= MAX_RANKS && out.is_cuda() && out.scalar_type() == torch::kFloat32 &&
+                  out.is_contiguous() && out.numel() % 4 == 0 && out.numel() <= slot_elems,
+              "p2p_sum_slots: bad arguments");
+  TORCH_CHECK(recv_off % 16 == 0 && slot_elems % 4 == 0, "p2p_sum_slots: 16-byte alignment");
+  const at::cuda::CUDAGuard guard(out.device());
+  const int64_t n4 = out.numel() / 4;
+  p2p_sum_slots_kernel<<<grid_for(n4, out.get_device()), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      bases.data_ptr<int64_t>(), world, (int)rank, (uint32_t)call, recv_off, slot_elems, n4,
+      reinterpret_cast<float4*>(out.data_ptr()), (uint64_t)(timeout_s * 1e9), status.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -3,7 +3,8 @@ events (warm-up, synchronize on both sides) and reported against the measured ro
 (MEASURED_PEAKS.json: cuBLAS bf16 burst TFLOP/s and copy bandwidth; the recipe's fallback
 figures otherwise). Also the workload that the committed ncu summaries in profiles/ capture.
 
-  python -m micro_engram_fork_b200.utils.kernel_bench [--case all|gemm|attn_fwd|attn_bwd|gate|ce|qkv|geglu] [--iters N]
+  python -m micro_engram_fork_b200.utils.kernel_bench [--case all|gemm|attn_fwd|attn_bwd|gate|ce|qkv|geglu|rows|
+                                                       norms|ce_bwd|nf4] [--iters N] [--small]
 """
 import argparse
 import json
@@ -145,9 +146,10 @@ def case_attn_bwd(C, dev, it, pk):
     return out
 
 
-def case_gate(C, dev, it, pk):
-    """Fused scalar_sqrt gate at the microbenchmark size: 65536 tokens x d 5376."""
-    N, d = 65536, 5376
+def case_gate(C, dev, it, pk, small=False):
+    """Fused scalar_sqrt gate at the microbenchmark size: 65536 tokens x d 5376 (16384 with
+    --small, the size an ncu capture replays)."""
+    N, d = (16384 if small else 65536), 5376
     h = torch.randn(N, d, device=dev).to(torch.bfloat16)
     k = torch.randn_like(h)
     v = torch.randn_like(h) * 0.1
@@ -218,8 +220,111 @@ def case_geglu(C, dev, it, pk):
     return r
 
 
+def _hbm(name, nbytes, ms, pk):
+    return {name: {"ms": round(ms, 4), "gbs": round(nbytes / ms / 1e6, 1),
+                   "frac_of_hbm": round(nbytes / ms / 1e6 / pk["hbm_gbs"], 3)}}
+
+
+def case_rows(C, dev, it, pk, small=False):
+    """The engram row path of one GPU at the module benchmark's size (65536 tokens, 24 tables of
+    {1.57M, 4.19M, 4.19M} rows x dim 64 bf16, Zipf(1.1) ids): hash, gather, row-gradient push into
+    the compact accumulator, touched-row Adam. Bytes count what each kernel must move: the ids
+    and rows it reads, the rows it writes (scatter: fp32 row gradients added; Adam: per touched
+    row, the bf16 row and moment read and written, the fp32 accumulator read). --small divides the
+    table rows by 8 (still above L2) for ncu captures."""
+    import numpy as np
+
+    from micro_engram.module import MicroEngram
+
+    from ..parallel.row_store import RowStore
+
+    tables, N, dim = {2: 1572864, 3: 4194304, 4: 4194304}, 65536, 64
+    if small:
+        tables = {k: v // 8 for k, v in tables.items()}
+    e = MicroEngram(model_dim=256, engram_dim=dim, num_heads=8, orders=(2, 3, 4), table_sizes=tables,
+                    vocab_size=262144, gate="scalar_sqrt", build_tables=False, seed=0)
+    rng = np.random.default_rng(0)
+    p = np.arange(1, 262145, dtype=np.float64) ** -1.1
+    ids = torch.from_numpy(np.searchsorted(np.cumsum(p / p.sum()), rng.random(N)).astype(np.int64)).to(dev)
+    pos = torch.cat([torch.arange(n) for n in (2000, 3000, 1192, 2000)] * 8).to(dev)[None]
+    canon, mults, orders, rows_t = e._consts(dev)
+    nt = len(e.table_rows)
+    r = {}
+    ms = _time(lambda: C.engram_hash(ids[None], pos, canon, mults, orders, rows_t, 0), it)
+    r.update(_hbm("hash", N * 16 + nt * N * 8, ms, pk))
+    idx = C.engram_hash(ids[None], pos, canon, mults, orders, rows_t, 0).reshape(nt, N).contiguous()
+    store = RowStore(e.table_rows, dim, torch.bfloat16, 0, 1, dev, capacity=N)
+    for w in store.weights:
+        w.normal_(0, 0.02)
+    ms = _time(lambda: store.gather(idx, torch.bfloat16), it)
+    r.update(_hbm("gather", nt * N * (8 + 2 * dim * 2), ms, pk))
+    g = torch.randn(N, nt * dim, device=dev).to(torch.bfloat16)
+    uniq = sum(int(torch.unique(idx[k]).numel()) for k in range(nt))
+    m = [torch.zeros_like(w) for w in store.weights]
+    v = [torch.zeros(w.shape[0], device=dev) for w in store.weights]
+
+    def push_and_step():
+        store.push_grads(g, idx, 1.0)
+        for k in range(nt):
+            C.engram_adam_touched(store.weights[k], m[k], v[k], store.acc[k], store.pos[k], store.list[k],
+                                  store.count[k], None, 1e-3, 0.9, 0.999, 1e-8, 0.0, 0.1, 0.001, True, 0, 1, k)
+        for c in store.count:
+            c.zero_()
+
+    ms = _time(push_and_step, it)
+    r.update(_hbm("scatter+adam", nt * N * (8 + dim * 2) + uniq * dim * (4 + 4 * 2 + 4), ms, pk))
+    r["unique_rows"] = uniq
+    r["lookups"] = nt * N
+    return r
+
+
+def case_norms(C, dev, it, pk):
+    """The decoder's row norms on one 8192-token step at d 5376: RMSNorm forward/backward and the
+    fused post-norm + residual add (+ the next layer's input norm) forward/backward."""
+    T, d = 8192, 5376
+    x = torch.randn(T, d, device=dev).to(torch.bfloat16)
+    a = torch.randn_like(x)
+    w = torch.rand(d, device=dev) + 0.5
+    ls = torch.rand(1, device=dev) + 0.5
+    y, rstd = C.rmsnorm_fwd(x, w, 1e-6)
+    r = {}
+    ms = _time(lambda: C.rmsnorm_fwd(x, w, 1e-6), it)
+    r.update(_hbm("rmsnorm fwd", 2 * T * d * 2, ms, pk))
+    ms = _time(lambda: C.rmsnorm_bwd(y, x, w, rstd, None), it)
+    r.update(_hbm("rmsnorm bwd", 3 * T * d * 2, ms, pk))
+    outs = C.post_norm_add(x, a, w, ls, w, 1e-6)
+    ms = _time(lambda: C.post_norm_add(x, a, w, ls, w, 1e-6), it)
+    r.update(_hbm("post_norm_add fwd", 4 * T * d * 2, ms, pk))
+    xo, hn, ra, rx = outs[0], outs[1], outs[2], outs[3]
+    ms = _time(lambda: C.post_norm_add_bwd(y, y, a, xo, w, ls, w, ra, rx), it)
+    r.update(_hbm("post_norm_add bwd", 6 * T * d * 2, ms, pk))
+    return r
+
+
+def case_ce_bwd(C, dev, it, pk):
+    """The in-place loss gradient of one 2048-token chunk against 262144 vocab rows (bf16 logits
+    read and overwritten)."""
+    z = torch.randn(2048, 262144, device=dev).to(torch.bfloat16)
+    lab = torch.randint(0, 262144, (2048,), device=dev)
+    lse = torch.full((2048,), 40.0, device=dev)
+    wr = torch.ones(2048, device=dev)
+    ms = _time(lambda: C.ce_bwd_inplace(z, lab, 0, 30.0, lse, wr), it)
+    return _hbm("ce_bwd_inplace 2048x262144", 2 * z.numel() * 2, ms, pk)
+
+
+def case_nf4(C, dev, it, pk):
+    """NF4 dequantisation of one 31B-class MLP weight (gate|up, 43008 x 5376, block 64)."""
+    w = (torch.randn(43008, 5376, device=dev) * 0.02).to(torch.bfloat16)
+    codes, absmax = C.nf4_quantize(w)[:2]
+    out = torch.empty_like(w)
+    ms = _time(lambda: C.nf4_dequant(codes, absmax, out), it)
+    return _hbm("nf4_dequant 43008x5376", codes.numel() * codes.element_size() + absmax.numel() * 4 + out.numel() * 2,
+                ms, pk)
+
+
 CASES = {"gemm": case_gemm, "attn_fwd": case_attn_fwd, "attn_bwd": case_attn_bwd, "gate": case_gate, "ce": case_ce,
-         "qkv": case_qkv, "geglu": case_geglu}
+         "qkv": case_qkv, "geglu": case_geglu, "rows": case_rows, "norms": case_norms, "ce_bwd": case_ce_bwd,
+         "nf4": case_nf4}
 
 
 def main(argv=None):
@@ -227,6 +332,7 @@ def main(argv=None):
     ap.add_argument("--case", default="all", choices=["all"] + list(CASES))
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--gemm-shapes", default="", help="comma-separated subset of GEMM_SHAPES names")
+    ap.add_argument("--small", action="store_true", help="smaller gate/rows problems (for ncu captures)")
     args = ap.parse_args(argv)
     from .. import native
 
@@ -239,6 +345,8 @@ def main(argv=None):
         if args.case in ("all", name):
             if name == "gemm" and args.gemm_shapes:
                 res[name] = fn(C, dev, args.iters, pk, only=set(args.gemm_shapes.split(",")))
+            elif name in ("gate", "rows"):
+                res[name] = fn(C, dev, args.iters, pk, small=args.small)
             else:
                 res[name] = fn(C, dev, args.iters, pk)
     res["status"] = {"gemm": C.gemm_status(0).tolist(), "attn_tc": C.attn_tc_status(0).tolist()}
