@@ -4,6 +4,8 @@ decoder at seq 8192, on N GPUs of one node.
   python bench.py --gpus N --steps K --warmup W          (N=1)
   torchrun --nproc-per-node N bench.py --gpus N ...       (N>1, one rank per GPU)
   python bench.py --impl reference ...                    (the unmodified reference)
+  python bench.py --config 4 ...                          (NF4 base, engrams at
+                                                           layers 0 and 29, synthetic 10% canon)
 
 Config: 60 layers, d 5376, FFN 21504, 32 q heads, sliding-1024 layers (16 KV heads, head_dim
 256) interleaved 5:1 with global layers (4 KV heads, head_dim 512, v = k), vocab 262144 tied
@@ -71,11 +73,36 @@ def synthetic_samples(n_bins, vocab, seed=1234, min_len=256, max_len=4096, seq=S
     return Samples.from_list(items)
 
 
-def bench_config(tmp, steps):
+METRIC4 = "train tokens/s (31B-class NF4, 2 engrams, seq 8192)"
+MODEL4 = MODEL.replace("stage-1 engram", "NF4 frozen base (block 64, fp32 absmax), engrams at layers 0 and 29")
+
+
+def synthetic_canon(path, vocab=262144, share=0.10, seed=1):
+    """Config 4's canon map: a random `share` of the vocabulary ids (seed 1) is paired up, and
+    each pair shares one canonical id (the smaller of the two). Idempotent."""
+    import numpy as np
+    import torch
+
+    rng = np.random.default_rng(seed)
+    n = int(share * vocab) // 2 * 2
+    pairs = rng.choice(vocab, size=n, replace=False).reshape(-1, 2)
+    canon = np.arange(vocab, dtype=np.int64)
+    canon[pairs.max(1)] = pairs.min(1)
+    torch.save(torch.from_numpy(canon), path)
+    return path
+
+
+def bench_config(tmp, steps, config=3):
     base = os.path.join(tmp, "base")
     os.makedirs(base, exist_ok=True)
     with open(os.path.join(base, "config.json"), "w") as f:
         json.dump(base_config_31b(), f)
+    if config == 4:  # NF4 base, a second engram at layer 29, a synthetic 10% canon
+        c = bench_config(tmp, steps)
+        c.update({"load_in_4bit": True, "base_placement": "replicated",
+                  "micro_engram_extra": [{"layer": 29}],
+                  "micro_engram_canon_path": synthetic_canon(os.path.join(tmp, "canon.pt"))})
+        return c
     return {
         "base_model": base, "base_init": "random",
         "datasets": [{"path": os.path.join(tmp, "unused.jsonl"), "type": "completion"}],
@@ -215,7 +242,7 @@ def run_ours(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     steps_total = args.warmup + 2 * args.steps + 1
     tmp = tempfile.mkdtemp(prefix="me_bench_")
-    cfg = load_config(bench_config(tmp, steps_total))
+    cfg = load_config(bench_config(tmp, steps_total, args.config))
     trainer = Trainer(cfg)
     rank, device = trainer.rank, trainer.device
     n_bins = steps_total * GA * MBS * world + 8
@@ -286,19 +313,21 @@ def run_ours(args):
     value = tokens * world / (dev_ms / 1e3)
     e2e_value = tokens * world / (e2e_ms / 1e3)
     if rank == 0:
+        parallelism = (f"fsdp{world} (row-sharded frozen base, layer all-gathers carried by the tcgen05 GEMMs; "
+                       "row-sharded engram; vocab-parallel head)" if trainer.placement == "sharded" else
+                       f"dp{world} (replicated frozen base, row-sharded engram, vocab-parallel head)")
+        engram = ("layer 0, tables {2:1572864,3:4194304,4:4194304} x8 heads x dim 64, scalar_sqrt, "
+                  "rowwise_adam bf16+SR")
+        if args.config == 4:
+            engram = "layers 0 and 29 (same tables each), synthetic canon pairing 10% of the vocabulary; " + engram
         line = {
-            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+            "metric": METRIC if args.config == 3 else METRIC4, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 2),
             "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None if not BASELINE_VALUE else round(value / BASELINE_VALUE, 4),
             "dtype": "bf16", "data": "synthetic (Zipf(1.1) packed docs 256-4096, random-init weights)",
-            "config": {"model": MODEL, "global_batch": MBS * GA * world, "seq_len": SEQ,
-                       "parallelism": (f"fsdp{world} (row-sharded frozen base, layer all-gathers carried by the "
-                                       "tcgen05 GEMMs; row-sharded engram; vocab-parallel head)"
-                                       if trainer.placement == "sharded" else
-                                       f"dp{world} (replicated frozen base, row-sharded engram, vocab-parallel head)"),
-                       "engram": "layer 0, tables {2:1572864,3:4194304,4:4194304} x8 heads x dim 64, "
-                                 "scalar_sqrt, rowwise_adam bf16+SR",
+            "config": {"model": MODEL if args.config == 3 else MODEL4, "global_batch": MBS * GA * world,
+                       "seq_len": SEQ, "baseline_config": args.config, "parallelism": parallelism, "engram": engram,
                        "activation_checkpointing": f"per-layer, policy {trainer.cfg.gradient_checkpointing_policy}"
                                                    " (HBM-budgeted: selective = q/k/v projection, attention output"
                                                    " and o-proj kept on the GPU, norms/RoPE/MLP recomputed; none ="
@@ -371,7 +400,7 @@ def run_reference(args):
     from transformers.models.gemma4.configuration_gemma4 import Gemma4TextConfig
 
     tmp = tempfile.mkdtemp(prefix="me_ref_")
-    c = bench_config(tmp, args.warmup + 2 * args.steps + 2)
+    c = bench_config(tmp, args.warmup + 2 * args.steps + 2, 3)
     for k in ("base_init", "gradient_checkpointing_policy", "gradient_checkpointing_reserve_gib",
               "base_placement"):  # not reference keys
         c.pop(k)
@@ -461,11 +490,16 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, choices=[3, 4], default=3,
+                    help="BASELINE config: 3 = bf16 base, one engram (headline); 4 = NF4 base, two engrams")
     args = ap.parse_args()
     if args.warmup < 3:
         print("bench: at least 3 warm-up steps", file=sys.stderr)
         args.warmup = 3
-    if args.impl == "reference":
+    if args.impl == "reference" and args.config == 4:
+        print(json.dumps({"impl": "reference", "metric": METRIC4, "unavailable":
+                          "the reference's NF4 base needs bitsandbytes and accelerate, neither installed offline"}))
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

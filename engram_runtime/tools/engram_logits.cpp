@@ -22,7 +22,9 @@
 #include <string>
 #include <vector>
 
+#ifndef ME_RT_NO_CUDA
 #include <cuda_runtime.h>
+#endif
 
 #include "engram_runtime.h"
 
@@ -56,6 +58,7 @@ void ubatch(Run& r, const std::vector<int32_t>& seq, const std::vector<int64_t>&
   if (me_rt_hash(r.rt, r.e, tok.data(), prev.data(), n, rows.data())) die("hash");
   std::vector<float> h((size_t)n * r.d);
   for (int64_t i = 0; i < n; ++i) std::memcpy(h.data() + i * r.d, rows_h[i], r.d * 4);
+#ifndef ME_RT_NO_CUDA
   if (r.gpu) {
     if (r.d_cap < n) {
       cudaFree(r.d_hidden);
@@ -67,7 +70,9 @@ void ubatch(Run& r, const std::vector<int32_t>& seq, const std::vector<int64_t>&
     cudaMemcpy(r.d_rows, rows.data(), n * r.nt * 4, cudaMemcpyHostToDevice);
     if (me_rt_cuda_inject(r.rt, r.e, r.d_hidden, r.d_rows, nullptr, n, nullptr)) die("cuda_inject");
     cudaMemcpy(h.data(), r.d_hidden, n * r.d * 4, cudaMemcpyDeviceToHost);
-  } else if (me_rt_inject_cpu(r.rt, r.e, h.data(), rows.data(), nullptr, n)) {
+  } else
+#endif
+  if (me_rt_inject_cpu(r.rt, r.e, h.data(), rows.data(), nullptr, n)) {
     die("inject_cpu");
   }
   const bool dump = std::getenv("ENGRAM_DUMP") != nullptr;
@@ -135,6 +140,12 @@ int main(int argc, char** argv) {
   r.d = me_rt_n_embd(r.rt);
   r.n_prev = me_rt_max_order(r.rt) - 1;
   if (me_rt_engram_info(r.rt, e, nullptr, nullptr, &r.nt, nullptr, nullptr)) die("engram_info");
+#ifdef ME_RT_NO_CUDA
+  if (gpu) {
+    std::fprintf(stderr, "engram_logits: --gpu needs the CUDA build (make, not make cpu)\n");
+    return 2;
+  }
+#endif
   if (gpu && me_rt_cuda_upload(r.rt, e, 0)) die("cuda_upload");
   if (me_rt_hist_new(&r.hist)) die("hist_new");
   auto tok = read_file<int32_t>(tokens_path.c_str(), (size_t)S * T);
@@ -189,10 +200,12 @@ int main(int argc, char** argv) {
     return 1;
   }
   std::fclose(f);
+#ifndef ME_RT_NO_CUDA
   if (gpu) {
     cudaFree(r.d_hidden);
     cudaFree(r.d_rows);
   }
+#endif
   me_rt_hist_free(r.hist);
   me_rt_close(r.rt);
   return 0;

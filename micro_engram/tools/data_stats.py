@@ -91,38 +91,46 @@ def report(keys, sup, sizes, out=print):
         out("")
 
 
+def _ints(text):
+    return tuple(int(x) for x in text.split(","))
+
+
+def _load_canon(path):
+    if not path:
+        return None
+    import torch
+
+    return torch.load(path, map_location="cpu").long().numpy()
+
+
+def _prepared_rows(path):
+    """(input_ids, labels) of every sample of a prepared dataset folder (its train split), shuffled."""
+    from datasets import DatasetDict, load_from_disk
+
+    ds = load_from_disk(path)
+    if isinstance(ds, DatasetDict):
+        ds = ds["train" if "train" in ds else next(iter(ds.keys()))]
+    missing = {"input_ids", "labels"} - set(ds.column_names)
+    if missing:
+        raise SystemExit(f"need columns input_ids and labels, found {ds.column_names}")
+    ds = ds.select_columns(["input_ids", "labels"]).shuffle(seed=0)
+    for batch in ds.iter(batch_size=1000):
+        yield from zip(batch["input_ids"], batch["labels"])
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("path")
     ap.add_argument("--max-tokens", type=int, default=50_000_000)
-    ap.add_argument("--orders", default="2,3")
-    ap.add_argument("--sizes", default=",".join(map(str, TABLE_SIZES)))
+    ap.add_argument("--orders", default="2,3", type=_ints)
+    ap.add_argument("--sizes", default=",".join(map(str, TABLE_SIZES)), type=_ints)
     ap.add_argument("--canon", default=None)
     args = ap.parse_args(argv)
-    orders = tuple(int(x) for x in args.orders.split(","))
-    sizes = tuple(int(x) for x in args.sizes.split(","))
-    canon = None
-    if args.canon:
-        import torch
-
-        canon = torch.load(args.canon, map_location="cpu").long().numpy()
-    from datasets import DatasetDict, load_from_disk
-
-    ds = load_from_disk(args.path)
-    if isinstance(ds, DatasetDict):
-        ds = ds["train"] if "train" in ds else ds[next(iter(ds.keys()))]
-    if "input_ids" not in ds.column_names or "labels" not in ds.column_names:
-        raise SystemExit(f"need columns input_ids and labels, found {ds.column_names}")
-    ds = ds.select_columns(["input_ids", "labels"]).shuffle(seed=0)
-
-    def rows():
-        for batch in ds.iter(batch_size=1000):
-            yield from zip(batch["input_ids"], batch["labels"])
-
-    keys, sup, total, trained, used = collect(rows(), args.max_tokens, orders, canon)
+    keys, sup, total, trained, used = collect(_prepared_rows(args.path), args.max_tokens, args.orders,
+                                              _load_canon(args.canon))
     print(f"\nsampled {used:,} samples, {total:,} tokens")
     print(f"positions with a trained next token: {trained / max(total, 1):.1%}\n")
-    report(keys, sup, sizes)
+    report(keys, sup, args.sizes)
     print("Counts come from the sample (a bigger sample finds more distinct n-grams). About 1 per row or fewer "
           "is light sharing, 5+ heavy.")
 

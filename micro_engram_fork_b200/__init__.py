@@ -8,7 +8,9 @@ Layout:
   parallel/  symmetric peer memory over NVLink (CUDA IPC), the row store of the
              row-sharded engram tables, P2P collectives
   models/    the Gemma-4-style decoder (frozen base) built from the ops above
-  utils/     device timers, NVTX ranges, the device status word, environment helpers
+  utils/     per-phase CUDA-event timers with NVTX ranges (timers.py) and the benchmarks:
+             kernel microbenchmarks (kernel_bench), the engram module benchmark (engram_bench),
+             the peer-memory all-reduce against NCCL (p2p_bench)
 
 The native extension is `micro_engram_fork_b200._C`, built in-tree by
 ``python setup.py build_ext --inplace`` for sm_100a only.

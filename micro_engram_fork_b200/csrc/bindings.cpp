@@ -11,6 +11,15 @@ torch::Tensor engram_gather(torch::Tensor idx, torch::Tensor ptrs, torch::Tensor
 void engram_scatter_grad(torch::Tensor g, torch::Tensor idx, torch::Tensor acc_ptrs, torch::Tensor pos_ptrs,
                          torch::Tensor list_ptrs, torch::Tensor cnt_ptrs, torch::Tensor per, torch::Tensor caps,
                          int64_t world, double scale, c10::optional<torch::Tensor> status, int64_t my_rank);
+void engram_push_grads(torch::Tensor g, torch::Tensor idx, torch::Tensor acc_ptrs, torch::Tensor pos_ptrs,
+                       torch::Tensor list_ptrs, torch::Tensor cnt_ptrs, torch::Tensor per, torch::Tensor caps,
+                       torch::Tensor xbases, int64_t me, double scale, int64_t cap_e, int64_t region_bytes,
+                       int64_t rows_off, int64_t call, double timeout_s, torch::Tensor status);
+void engram_accumulate_grads(torch::Tensor acc_ptrs, torch::Tensor pos_ptrs, torch::Tensor list_ptrs,
+                             torch::Tensor cnt_ptrs, torch::Tensor per, torch::Tensor caps, torch::Tensor xbases,
+                             int64_t n_tables, int64_t dim, int64_t me, double scale, int64_t cap_e,
+                             int64_t region_bytes, int64_t rows_off, int64_t call, double timeout_s,
+                             torch::Tensor status);
 void engram_touched_sqnorm(torch::Tensor acc_ptrs, torch::Tensor cnt_ptrs, torch::Tensor caps, int64_t dim,
                            torch::Tensor sq);
 void engram_clip_coef(torch::Tensor sq, double max_norm, torch::Tensor coef, torch::Tensor norm);
@@ -89,6 +98,13 @@ void p2p_sum_slots(torch::Tensor bases, int64_t rank, int64_t call, int64_t recv
 std::vector<torch::Tensor> gemm_ce(torch::Tensor H, torch::Tensor E, torch::Tensor labels, int64_t lab_start,
                                    double cap, bool keep_logits, int64_t n_valid);
 torch::Tensor gemm_status(int64_t device);
+// gemm_nf4.cu
+torch::Tensor gemm_nf4(torch::Tensor A, torch::Tensor codes, torch::Tensor absmax, int64_t rows, int64_t cols,
+                       bool b_kmajor, c10::optional<torch::Tensor> out);
+std::vector<torch::Tensor> gemm_geglu_nf4(torch::Tensor A, torch::Tensor codes, torch::Tensor absmax, int64_t rows,
+                                          int64_t cols, bool save_gu);
+torch::Tensor gemm_dgeglu_nf4(torch::Tensor dY, torch::Tensor codes, torch::Tensor absmax, int64_t rows,
+                              int64_t cols, torch::Tensor gu);
 // nf4.cu
 std::vector<torch::Tensor> nf4_quantize(torch::Tensor w);
 void nf4_dequant(torch::Tensor codes, torch::Tensor absmax, torch::Tensor out);
@@ -107,6 +123,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("engram_hash_prev", &engram_hash_prev);
   m.def("engram_gather", &engram_gather);
   m.def("engram_scatter_grad", &engram_scatter_grad);
+  m.def("engram_push_grads", &engram_push_grads);
+  m.def("engram_accumulate_grads", &engram_accumulate_grads);
   m.def("engram_touched_sqnorm", &engram_touched_sqnorm);
   m.def("engram_clip_coef", &engram_clip_coef);
   m.def("engram_adam_touched", &engram_adam_touched);
@@ -143,6 +161,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_sum_slots", &p2p_sum_slots);
   m.def("gemm_ce", &gemm_ce);
   m.def("gemm_status", &gemm_status);
+  m.def("gemm_nf4", &gemm_nf4);
+  m.def("gemm_geglu_nf4", &gemm_geglu_nf4);
+  m.def("gemm_dgeglu_nf4", &gemm_dgeglu_nf4);
   m.def("nf4_quantize", &nf4_quantize);
   m.def("nf4_dequant", &nf4_dequant);
   m.def("symm_alloc", &symm_alloc);

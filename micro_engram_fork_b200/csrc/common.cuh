@@ -161,4 +161,26 @@ ME_DEVICE uint64_t globaltimer_ns() {
   return t;
 }
 
+// ---------------------------------------------------------------- flags between GPUs
+// A flag word in (possibly peer) global memory, published with release semantics at system
+// scope and read with acquire semantics: everything written before the release store is
+// visible to a reader that saw the value.
+ME_DEVICE void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+ME_DEVICE uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Spin (bounded) until the flag reaches `want` (wrap-around compare). False on timeout.
+ME_DEVICE bool wait_flag_geq(const uint32_t* flag, uint32_t want, uint64_t timeout_ns) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 0;; ++it) {
+    if ((int32_t)(ld_acquire_sys(flag) - want) >= 0) return true;
+    if ((it & 63u) == 63u && globaltimer_ns() - t0 > timeout_ns) return false;
+  }
+}
+
 }  // namespace me

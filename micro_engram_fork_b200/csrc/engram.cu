@@ -228,6 +228,208 @@ __global__ void scatter_grad_kernel(const Tg* __restrict__ g, const int64_t* __r
   }
 }
 
+// ------------------------------------------------------------------------------ row-grad exchange
+// The multi-GPU return of row gradients without remote atomics, in two kernels per backward
+// call (both on every rank, in the same order):
+//
+//   push        every (token, table) event whose row this rank owns is added into the local
+//               compact accumulator at once (local float4 atomics). An event owned by rank o is
+//               appended to o's inbox region for this rank: the entry index comes from a LOCAL
+//               counter, the (table, local row) header and the bf16 row gradient go over NVLink
+//               as plain 16-byte stores. The last block to finish publishes, per owner, the entry
+//               count and then ready[this rank] = call (release, system scope).
+//   accumulate  waits (bounded) until every peer's ready flag reached `call`, then adds every
+//               entry of every inbox region into the local accumulator (local atomics), scaled.
+//               Its last block tells each peer consumed[this rank] = call.
+//
+// A push writes into an owner's inbox only after that owner's accumulate of the previous call
+// has finished (push waits, bounded, until consumed[o] >= call - 1), so one inbox per (owner,
+// source) suffices. Exchange buffer, same offsets on every rank:
+//   [0, 64)     ready[16]     u32    written by the sources
+//   [64, 128)   consumed[16]  u32    written by the owners
+//   [128, 192)  counts[16]    i32    entries source s wrote for the current call
+//   [192, 256)  outcnt[16]    i32    this rank's entries per owner during a push
+//   [256, 264)  done[2]       i32    blocks finished (push, accumulate)
+//   [512, ...)  region[s] for every source s: hdr [cap_e] int2 (table, local row) at 0,
+//               rows [cap_e, dim] bf16 at rows_off; regions region_bytes apart.
+constexpr int kXReady = 0, kXConsumed = 64, kXCounts = 128, kXOut = 192, kXDone = 256, kXRegions = 512;
+
+ME_DEVICE int claim_slot(int* pos, int* cnt, int* list, int64_t cap, int local, int* status, int k) {
+  int s = *reinterpret_cast<volatile int*>(pos + local);
+  if (s != 0) return s;
+  const int t = atomicAdd(cnt, 1);
+  if (t < cap) {
+    const int old = atomicCAS(pos + local, 0, t + 1);
+    list[t] = old == 0 ? local : -1;
+    return old == 0 ? t + 1 : old;
+  }
+  s = atomicAdd(pos + local, 0);  // another event may have installed a slot meanwhile
+  if (s == 0) report(status, ME_ERR_CAPACITY, k);
+  return s;
+}
+
+// 8 bf16 (one 16-byte chunk) * scale added into acc[0..8) with two local float4 atomics.
+ME_DEVICE void add_chunk(float* acc, uint4 raw, float scale) {
+  BF16x8 x;
+  x.u = raw;
+  float f[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) f[j] = bf2f(x.h[j]) * scale;
+  atomicAdd(reinterpret_cast<float4*>(acc), make_float4(f[0], f[1], f[2], f[3]));
+  atomicAdd(reinterpret_cast<float4*>(acc + 4), make_float4(f[4], f[5], f[6], f[7]));
+}
+
+struct RowTablesArgs {
+  const int64_t* acc_ptrs;   // [world * n_tables]: (rank, table) -> accumulator base
+  const int64_t* pos_ptrs;
+  const int64_t* list_ptrs;
+  const int64_t* cnt_ptrs;
+  const int64_t* per;        // [n_tables] rows per shard
+  const int64_t* caps;       // [n_tables] slots per accumulator
+  const int64_t* xbases;     // [world] exchange buffer base of every rank
+  int n_tables, dim, world, me;
+  int64_t cap_e, region_bytes, rows_off;
+  uint32_t call;
+  uint64_t timeout_ns;
+  int* status;
+};
+
+// Whether every block's stores are done: the last block to arrive on `done` returns true (and
+// resets the counter for the next call).
+ME_DEVICE bool last_block(int* done) {
+  __shared__ bool last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    last = atomicAdd(done, 1) == (int)gridDim.x - 1;
+    if (last) {
+      __threadfence();
+      *reinterpret_cast<volatile int*>(done) = 0;
+    }
+  }
+  __syncthreads();
+  return last;
+}
+
+// groups of 8 threads; one (token, table) event per group
+__global__ void __launch_bounds__(256) row_push_kernel(const __nv_bfloat16* __restrict__ g,
+                                                       const int64_t* __restrict__ idx, int64_t N, RowTablesArgs a,
+                                                       float scale) {
+  __shared__ int failed;
+  uint8_t* mine = reinterpret_cast<uint8_t*>(a.xbases[a.me]);
+  if (threadIdx.x == 0) failed = 0;
+  __syncthreads();
+  if (threadIdx.x < a.world && (int)threadIdx.x != a.me) {
+    const uint32_t* consumed = reinterpret_cast<const uint32_t*>(mine + kXConsumed) + threadIdx.x;
+    if (!wait_flag_geq(consumed, a.call - 1u, a.timeout_ns)) {
+      report(a.status, ME_ERR_TIMEOUT, 100 + (int)threadIdx.x);
+      failed = 1;
+    }
+  }
+  __syncthreads();
+  const int sub = threadIdx.x & 7;
+  const unsigned gmask = 0xFFu << (threadIdx.x & 24);
+  const int chunks = a.dim / 8;
+  const int64_t events = N * a.n_tables;
+  const int64_t groups = (int64_t)gridDim.x * (blockDim.x >> 3);
+  int* outcnt = reinterpret_cast<int*>(mine + kXOut);
+  for (int64_t e = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3; !failed && e < events; e += groups) {
+    const int k = (int)(e % a.n_tables);
+    const int64_t n = e / a.n_tables;
+    const int64_t row = idx[(int64_t)k * N + n];
+    const int64_t pk = a.per[k];
+    const int owner = (int)(row / pk);
+    const int local = (int)(row - (int64_t)owner * pk);
+    const __nv_bfloat16* src = g + n * (int64_t)a.n_tables * a.dim + (int64_t)k * a.dim;
+    if (owner == a.me) {
+      const int t = a.me * a.n_tables + k;
+      int s = 0;
+      if (sub == 0)
+        s = claim_slot(reinterpret_cast<int*>(a.pos_ptrs[t]), reinterpret_cast<int*>(a.cnt_ptrs[t]),
+                       reinterpret_cast<int*>(a.list_ptrs[t]), a.caps[k], local, a.status, k);
+      s = __shfl_sync(gmask, s, 0, 8);
+      if (s <= 0) continue;
+      float* acc = reinterpret_cast<float*>(a.acc_ptrs[t]) + (int64_t)(s - 1) * a.dim;
+      for (int c = sub; c < chunks; c += 8)
+        add_chunk(acc + c * 8, *reinterpret_cast<const uint4*>(src + c * 8), scale);
+    } else {
+      int slot = 0;
+      if (sub == 0) slot = atomicAdd(outcnt + owner, 1);
+      slot = __shfl_sync(gmask, slot, 0, 8);
+      if (slot >= a.cap_e) {
+        if (sub == 0) report(a.status, ME_ERR_CAPACITY, 200 + owner);
+        continue;
+      }
+      uint8_t* region = reinterpret_cast<uint8_t*>(a.xbases[owner]) + kXRegions + (int64_t)a.me * a.region_bytes;
+      if (sub == 0) reinterpret_cast<int2*>(region)[slot] = make_int2(k, local);
+      uint4* dst = reinterpret_cast<uint4*>(region + a.rows_off + (int64_t)slot * a.dim * 2);
+      for (int c = sub; c < chunks; c += 8) dst[c] = *reinterpret_cast<const uint4*>(src + c * 8);
+    }
+  }
+  if (last_block(reinterpret_cast<int*>(mine + kXDone))) {
+    if ((int)threadIdx.x < a.world && (int)threadIdx.x != a.me) {
+      const int o = threadIdx.x;
+      const int n_o = atomicExch(outcnt + o, 0);
+      uint8_t* peer = reinterpret_cast<uint8_t*>(a.xbases[o]);
+      reinterpret_cast<volatile int*>(peer + kXCounts)[a.me] = (int)min((int64_t)n_o, a.cap_e);
+      st_release_sys(reinterpret_cast<uint32_t*>(peer + kXReady) + a.me, a.call);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) row_accumulate_kernel(RowTablesArgs a, float scale) {
+  __shared__ int failed;
+  __shared__ int count[16];
+  uint8_t* mine = reinterpret_cast<uint8_t*>(a.xbases[a.me]);
+  if (threadIdx.x == 0) failed = 0;
+  __syncthreads();
+  if ((int)threadIdx.x < a.world) {
+    int c = 0;
+    if ((int)threadIdx.x != a.me) {
+      const uint32_t* ready = reinterpret_cast<const uint32_t*>(mine + kXReady) + threadIdx.x;
+      if (wait_flag_geq(ready, a.call, a.timeout_ns)) {
+        c = __ldcg(reinterpret_cast<const int*>(mine + kXCounts) + threadIdx.x);
+      } else {
+        report(a.status, ME_ERR_TIMEOUT, 300 + (int)threadIdx.x);
+        failed = 1;
+      }
+    }
+    count[threadIdx.x] = c;
+  }
+  __syncthreads();
+  const int sub = threadIdx.x & 7;
+  const unsigned gmask = 0xFFu << (threadIdx.x & 24);
+  const int chunks = a.dim / 8;
+  const int64_t groups = (int64_t)gridDim.x * (blockDim.x >> 3);
+  const int64_t first = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3;
+  for (int src = 0; !failed && src < a.world; ++src) {
+    const uint8_t* region = mine + kXRegions + (int64_t)src * a.region_bytes;
+    const int2* hdr = reinterpret_cast<const int2*>(region);
+    for (int64_t i = first; i < count[src]; i += groups) {
+      int s = 0, k = 0;
+      if (sub == 0) {
+        const int2 h = __ldcg(hdr + i);
+        k = h.x;
+        const int t = a.me * a.n_tables + k;
+        s = claim_slot(reinterpret_cast<int*>(a.pos_ptrs[t]), reinterpret_cast<int*>(a.cnt_ptrs[t]),
+                       reinterpret_cast<int*>(a.list_ptrs[t]), a.caps[k], h.y, a.status, k);
+      }
+      s = __shfl_sync(gmask, s, 0, 8);
+      k = __shfl_sync(gmask, k, 0, 8);
+      if (s <= 0) continue;
+      float* acc = reinterpret_cast<float*>(a.acc_ptrs[a.me * a.n_tables + k]) + (int64_t)(s - 1) * a.dim;
+      const uint4* rowp = reinterpret_cast<const uint4*>(region + a.rows_off + i * a.dim * 2);
+      for (int c = sub; c < chunks; c += 8) add_chunk(acc + c * 8, __ldcg(rowp + c), scale);
+    }
+  }
+  if (last_block(reinterpret_cast<int*>(mine + kXDone) + 1)) {
+    if ((int)threadIdx.x < a.world && (int)threadIdx.x != a.me)
+      st_release_sys(reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(a.xbases[threadIdx.x]) + kXConsumed) +
+                         a.me,
+                     a.call);
+  }
+}
+
 // Sum of squares of the touched rows' accumulated gradients (every row lives on exactly one
 // rank, so the sum over ranks is the global table norm^2): the first min(count, cap) slots of
 // each compact accumulator (holes are zero). counts are read on the device.
@@ -864,6 +1066,73 @@ void engram_scatter_grad(torch::Tensor g, torch::Tensor idx, torch::Tensor acc_p
         pos_ptrs.data_ptr<int64_t>(), list_ptrs.data_ptr<int64_t>(), cnt_ptrs.data_ptr<int64_t>(),
         per.data_ptr<int64_t>(), caps.data_ptr<int64_t>(), world, (float)scale, st, (int)my_rank);
   }
+}
+
+// The exchange form of engram_scatter_grad for world > 1 (row_push_kernel, then
+// row_accumulate_kernel; see the kernels). `x` holds the exchange layout: xbases [world] int64,
+// and the sizes cap_e (entries per inbox region), region_bytes, rows_off.
+static RowTablesArgs row_tables_args(const torch::Tensor& acc_ptrs, const torch::Tensor& pos_ptrs,
+                              const torch::Tensor& list_ptrs, const torch::Tensor& cnt_ptrs,
+                              const torch::Tensor& per, const torch::Tensor& caps, const torch::Tensor& xbases,
+                              int64_t n_tables, int64_t dim, int64_t me, int64_t cap_e, int64_t region_bytes,
+                              int64_t rows_off, int64_t call, double timeout_s, torch::Tensor& status) {
+  const int world = (int)xbases.numel();
+  TORCH_CHECK(world >= 2 && world <= 16, "row exchange: 2..16 ranks");
+  TORCH_CHECK(dim % 8 == 0 && rows_off % 16 == 0 && region_bytes % 256 == 0, "row exchange: alignment");
+  TORCH_CHECK(acc_ptrs.numel() == world * n_tables && per.numel() == n_tables && caps.numel() == n_tables,
+              "row exchange: pointer tables");
+  RowTablesArgs a;
+  a.acc_ptrs = acc_ptrs.data_ptr<int64_t>();
+  a.pos_ptrs = pos_ptrs.data_ptr<int64_t>();
+  a.list_ptrs = list_ptrs.data_ptr<int64_t>();
+  a.cnt_ptrs = cnt_ptrs.data_ptr<int64_t>();
+  a.per = per.data_ptr<int64_t>();
+  a.caps = caps.data_ptr<int64_t>();
+  a.xbases = xbases.data_ptr<int64_t>();
+  a.n_tables = (int)n_tables;
+  a.dim = (int)dim;
+  a.world = world;
+  a.me = (int)me;
+  a.cap_e = cap_e;
+  a.region_bytes = region_bytes;
+  a.rows_off = rows_off;
+  a.call = (uint32_t)call;
+  a.timeout_ns = (uint64_t)(timeout_s * 1e9);
+  a.status = status.data_ptr<int>();
+  return a;
+}
+
+void engram_push_grads(torch::Tensor g, torch::Tensor idx, torch::Tensor acc_ptrs, torch::Tensor pos_ptrs,
+                       torch::Tensor list_ptrs, torch::Tensor cnt_ptrs, torch::Tensor per, torch::Tensor caps,
+                       torch::Tensor xbases, int64_t me, double scale, int64_t cap_e, int64_t region_bytes,
+                       int64_t rows_off, int64_t call, double timeout_s, torch::Tensor status) {
+  check_cuda(g, "g");
+  check_cuda(idx, "idx");
+  TORCH_CHECK(g.scalar_type() == torch::kBFloat16 && g.is_contiguous(), "row exchange: bf16 contiguous grads");
+  const at::cuda::CUDAGuard guard(g.device());
+  const int64_t nt = idx.size(0), N = idx.size(1);
+  const int64_t dim = N ? g.size(1) / nt : 8;
+  TORCH_CHECK(N == 0 || (g.size(0) == N && g.size(1) == nt * dim), "row exchange: g must be [N, n_tables * dim]");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(g.data_ptr()) % 16 == 0, "row exchange: 16-byte aligned grads");
+  RowTablesArgs a = row_tables_args(acc_ptrs, pos_ptrs, list_ptrs, cnt_ptrs, per, caps, xbases, nt, dim, me, cap_e,
+                                    region_bytes, rows_off, call, timeout_s, status);
+  // every launch signals its peers, also with no events (their accumulate waits for it)
+  const int grid = grid_for(std::max<int64_t>(1, N * nt * 8), 256);
+  row_push_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), idx.data_ptr<int64_t>(), N, a, (float)scale);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void engram_accumulate_grads(torch::Tensor acc_ptrs, torch::Tensor pos_ptrs, torch::Tensor list_ptrs,
+                             torch::Tensor cnt_ptrs, torch::Tensor per, torch::Tensor caps, torch::Tensor xbases,
+                             int64_t n_tables, int64_t dim, int64_t me, double scale, int64_t cap_e,
+                             int64_t region_bytes, int64_t rows_off, int64_t call, double timeout_s,
+                             torch::Tensor status) {
+  const at::cuda::CUDAGuard guard(status.device());
+  RowTablesArgs a = row_tables_args(acc_ptrs, pos_ptrs, list_ptrs, cnt_ptrs, per, caps, xbases, n_tables, dim, me,
+                                    cap_e, region_bytes, rows_off, call, timeout_s, status);
+  row_accumulate_kernel<<<sm_count() * 4, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a, (float)scale);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 // sq (fp32 [1], accumulated into) += sum over the local touched rows of acc^2.

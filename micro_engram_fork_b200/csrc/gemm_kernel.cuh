@@ -21,6 +21,14 @@
 //   warp 6     side copy (optional): a range of a peer-to-local copy job (the next frozen layer's
 //              all-gather under base_placement: sharded, gather.cuh) runs here while the tensor
 //              cores work, so the layer's all-gather costs no separate kernel and no idle SMs
+//   warps 7-10 NF4 B producer (B_NF4 only, 352 threads per CTA): the frozen weight stays in NF4
+//              (4-bit codes, one fp32 absmax per 64 weights along its rows) and these 128 threads
+//              dequantise this CTA's B half of every stage straight into the 128-byte-swizzled
+//              layout the TMA would have written (one 128-byte row each: 32 code bytes + 1
+//              absmax -> 64 bf16, bf16(level * absmax) exactly as the standalone dequant kernel
+//              rounds), fence the generic-proxy stores for the tensor core, and arrive on the
+//              leader's `full` barrier (which then counts 3 arrivals: the A expect_tx + one per
+//              CTA). Loads run two stages ahead of the stores. So the bf16 weight never exists.
 //   warps 2-5  epilogue (each warp owns the TMEM lane quarter warp % 4 = 32 rows): wait for
 //              `acc_full`, tcgen05.ld 32 columns at a time, apply the epilogue, store, then
 //              arrive on the leader's `acc_empty` so the next-but-one tile can reuse the
@@ -74,6 +82,7 @@ constexpr int BM = 128;  // A rows per CTA (256 per pair)
 constexpr int BN = 256;  // accumulator columns per tile
 constexpr int BK = 64;   // K per stage (one 128-byte swizzle row of bf16)
 constexpr int NTHREADS = 224;
+constexpr int NTHREADS_NF4 = 352;  // + 4 warps dequantising the NF4 B operand
 constexpr uint32_t TMEM_COLS = 512;  // two accumulators
 constexpr int A_BYTES = BM * BK * 2;        // 16 KB
 constexpr int B_BYTES = (BN / 2) * BK * 2;  // 16 KB: this CTA's half of B
@@ -118,7 +127,20 @@ struct GemmArgs {
   int gnsegs;
   int64_t gbegin16, gend16;
   int* status;
+  // B_NF4: the weight W [q_rows, q_cols] (row-major, two 4-bit codes per byte, low nibble first,
+  // one fp32 absmax per 64 consecutive weights of a row; q_cols % 64 == 0). K-major B reads W's
+  // rows as B rows (y = x . W^T); N-major B reads W's rows as the reduction dimension (dX = g . W).
+  const uint8_t* q_codes;
+  const float* q_absmax;
+  int64_t q_rows, q_cols;
 };
+
+// The 16 NF4 levels (QLoRA, Dettmers et al. 2023, appendix E), the table nf4.cu quantises with.
+static __constant__ float kNF4Levels[16] = {-1.0f, -0.6961928009986877f, -0.5250730514526367f, -0.39491748809814453f,
+                                     -0.28444138169288635f, -0.18477343022823334f, -0.09105003625154495f, 0.0f,
+                                     0.07958029955625534f, 0.16093020141124725f, 0.24611230194568634f,
+                                     0.33791524171829224f, 0.44070982933044434f, 0.5626170039176941f,
+                                     0.7229568362236023f, 1.0f};
 
 struct Unit {
   int tile, kb0, kb1, part;  // part < 0: the whole tile
@@ -177,8 +199,34 @@ ME_DEVICE void store_row32(bf16* dst, const float (&v)[32], int valid_cols) {
   }
 }
 
-template <int EPI, bool B_NMAJOR, bool A_MMAJOR, int STAGES>
-__global__ void __launch_bounds__(NTHREADS, 1)
+// One 64-weight NF4 segment of a B row (32 code bytes and its absmax), fetched ahead of use.
+struct Nf4Seg {
+  uint4 lo, hi;
+  float scale;
+  bool valid;
+};
+
+// The k-block sequence of this cluster (same order as the producer and the MMA issuer).
+struct KCursor {
+  int w, kb;
+  Unit u;
+  bool have;
+  ME_DEVICE void start(int cluster, const GemmArgs& p, int nk) {
+    w = cluster;
+    have = unit_at(w, p, nk, u);
+    kb = have ? u.kb0 : 0;
+  }
+  ME_DEVICE void next(int nclusters, const GemmArgs& p, int nk) {
+    if (++kb >= u.kb1) {
+      w += nclusters;
+      have = unit_at(w, p, nk, u);
+      kb = have ? u.kb0 : 0;
+    }
+  }
+};
+
+template <int EPI, bool B_NMAJOR, bool A_MMAJOR, int STAGES, bool B_NF4 = false>
+__global__ void __launch_bounds__(B_NF4 ? NTHREADS_NF4 : NTHREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                      const GemmArgs p) {
   extern __shared__ uint8_t smem_raw[];
@@ -192,6 +240,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint64_t* mma_done = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* nf4_stop = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  float* nf4_lut = reinterpret_cast<float*>(smem + Smem<STAGES>::TILES + 256);  // 16 levels
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();  // 0 = leader, 1 = peer
@@ -201,7 +251,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], B_NF4 ? 3 : 1);  // NF4: + one arrival per CTA's dequantising warps
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -240,7 +290,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             ok = false;
             break;
           }
-          if (leader) mbar_expect_tx(&full[s], 2 * STAGE_BYTES);
+          if (leader) mbar_expect_tx(&full[s], B_NF4 ? 2 * A_BYTES : 2 * STAGE_BYTES);
           const uint32_t bar = full_leader + (uint32_t)(s * 8);
           if (A_MMAJOR) {  // A stored [K, M]: two 64-row (M) x 64 (K) boxes per half
             tma_load_2d_pair(sA + s * A_BYTES, &ta, bar, a_row, kb * BK);
@@ -248,7 +298,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           } else {
             tma_load_2d_pair(sA + s * A_BYTES, &ta, bar, kb * BK, a_row);
           }
-          if (B_NMAJOR) {
+          if (B_NF4) {
+            // B comes from the dequantising warps
+          } else if (B_NMAJOR) {
             tma_load_2d_pair(sB + s * B_BYTES, &tb, bar, b_row, kb * BK);
             tma_load_2d_pair(sB + s * B_BYTES + B_BYTES / 2, &tb, bar, b_row + 64, kb * BK);
           } else {
@@ -304,6 +356,89 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   } else if (warp == 6) {
     // ------------------------------------------------------------------ side copy
     if (p.gnsegs > 0) gather_range(p.gsegs, p.gnsegs, p.gbegin16, p.gend16, blockIdx.x, gridDim.x, lane);
+  } else if (B_NF4 && warp >= 7) {
+    // ------------------------------------------------------------------ NF4 B producer
+    const int t = threadIdx.x - 7 * 32;  // 0..127: one 128-byte row of this CTA's B half
+    if (t < 16) nf4_lut[t] = kNF4Levels[t];
+    if (t == 0) *nf4_stop = 0;
+    named_sync(1, 128);
+    const uint32_t full_leader = mapa_shared(smem_addr(full), 0);
+    const int64_t cbytes = p.q_cols / 2, blocks = p.q_cols / 64;
+    // where this thread's row of the stage comes from (W row, first column) and goes to
+    int srow_in_atom;
+    uint32_t dst_off;
+    if (B_NMAJOR) {
+      srow_in_atom = t & 63;
+      dst_off = (uint32_t)((t >> 6) * (B_BYTES / 2) + (t & 63) * 128);
+    } else {
+      srow_in_atom = t;
+      dst_off = (uint32_t)(t * 128);
+    }
+    auto fetch = [&](const KCursor& c, Nf4Seg& g) {
+      int mb, nb;
+      tile_coords(c.u.tile, p, mb, nb);
+      int64_t row, col;
+      if (B_NMAJOR) {
+        row = (int64_t)c.kb * BK + (t & 63);
+        col = (int64_t)nb * BN + (int64_t)rank * (BN / 2) + (t >> 6) * 64;
+      } else {
+        row = EPI == EPI_GEGLU ? (int64_t)rank * p.N + (int64_t)nb * (BN / 2) + t
+                               : (int64_t)nb * BN + (int64_t)rank * (BN / 2) + t;
+        col = (int64_t)c.kb * BK;
+      }
+      g.valid = row < p.q_rows && col < p.q_cols;
+      if (g.valid) {
+        const uint4* src = reinterpret_cast<const uint4*>(p.q_codes + row * cbytes + col / 2);
+        g.lo = __ldg(src);
+        g.hi = __ldg(src + 1);
+        g.scale = __ldg(p.q_absmax + row * blocks + col / 64);
+      }
+    };
+    KCursor ld, use;
+    ld.start(cluster, p, nk);
+    use.start(cluster, p, nk);
+    Nf4Seg s0{}, s1{};
+    if (ld.have) {
+      fetch(ld, s0);
+      ld.next(nclusters, p, nk);
+    }
+    if (ld.have) {
+      fetch(ld, s1);
+      ld.next(nclusters, p, nk);
+    }
+    for (int it = 0; use.have; use.next(nclusters, p, nk), ++it) {
+      const Nf4Seg cur = s0;
+      s0 = s1;
+      if (ld.have) {
+        fetch(ld, s1);
+        ld.next(nclusters, p, nk);
+      }
+      const int s = it % STAGES, r = it / STAGES;
+      if (t == 0 && r > 0 && !mbar_wait(&empty[s], (r - 1) & 1, p.status, 16, abort)) *nf4_stop = 1;
+      named_sync(1, 128);
+      if (*nf4_stop) break;
+      uint8_t* dst = sB + s * B_BYTES + dst_off;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint4 out = make_uint4(0u, 0u, 0u, 0u);
+        if (cur.valid) {
+          const uint32_t w4 = c < 4 ? (&cur.lo.x)[c] : (&cur.hi.x)[c - 4];
+          uint32_t packed[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t byte = (w4 >> (8 * j)) & 0xFFu;
+            const __nv_bfloat162 two = __floats2bfloat162_rn(nf4_lut[byte & 15u] * cur.scale,
+                                                             nf4_lut[byte >> 4] * cur.scale);
+            packed[j] = *reinterpret_cast<const uint32_t*>(&two);
+          }
+          out = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        }
+        *reinterpret_cast<uint4*>(dst + ((c ^ (srow_in_atom & 7)) * 16)) = out;
+      }
+      fence_async_smem();  // the tensor core reads these stores through the async proxy
+      named_sync(1, 128);
+      if (t == 0) mbar_arrive_cluster(full_leader + (uint32_t)(s * 8));
+    }
   } else {
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may read
@@ -564,9 +699,10 @@ inline SideCopy& pending_copy(int dev) {
   return jobs[dev & 63];
 }
 
-template <int EPI, bool B_NMAJOR, bool A_MMAJOR = false>
+template <int EPI, bool B_NMAJOR, bool A_MMAJOR = false, bool B_NF4 = false>
 void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int dev, cudaStream_t stream) {
-  auto kern = gemm_pair_kernel<EPI, B_NMAJOR, A_MMAJOR, STAGES>;
+  auto kern = gemm_pair_kernel<EPI, B_NMAJOR, A_MMAJOR, STAGES, B_NF4>;
+  constexpr int nthreads = B_NF4 ? NTHREADS_NF4 : NTHREADS;
   constexpr int smem = Smem<STAGES>::BYTES;
   // max resident clusters of this kernel on this device, computed once per (kernel, device)
   static std::mutex mu;
@@ -587,7 +723,7 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, 
       int sms = 0;
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
       cfg.gridDim = dim3(sms & ~1);
-      cfg.blockDim = dim3(NTHREADS);
+      cfg.blockDim = dim3(nthreads);
       cfg.dynamicSmemBytes = smem;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
@@ -637,7 +773,7 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, 
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.gridDim = dim3(2 * grid_clusters);
-  cfg.blockDim = dim3(NTHREADS);
+  cfg.blockDim = dim3(nthreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cfg.attrs = attr;

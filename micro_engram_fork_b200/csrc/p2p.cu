@@ -27,15 +27,6 @@ using namespace me;
 
 namespace {
 
-ME_DEVICE void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-ME_DEVICE uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 constexpr int MAX_RANKS = 16;
 
 __global__ void __launch_bounds__(256) p2p_allreduce_mean_kernel(const int64_t* __restrict__ bases, int world,

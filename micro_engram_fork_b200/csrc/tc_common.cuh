@@ -108,6 +108,8 @@ ME_DEVICE void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* b
 }
 // Generic-proxy shared-memory writes (st.shared) -> visible to the tensor cores' async proxy.
 ME_DEVICE void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Barrier among `nthreads` threads (whole warps) of the CTA on named barrier `id` (1..15).
+ME_DEVICE void named_sync(int id, int nthreads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory"); }
 ME_DEVICE void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

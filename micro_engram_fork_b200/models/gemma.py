@@ -277,7 +277,7 @@ class GemmaLayer(nn.Module):
         return N.rmsnorm_ref(x, None if w_none else norm.weight, self.cfg.rms_norm_eps)
 
     def _forward_torch(self, x, pos, doc_start):
-        _materialize(self)
+        _materialize(self, force=True)
         cfg, att = self.cfg, self.self_attn
         T = x.shape[0]
         hd = self.head_dim
@@ -304,7 +304,62 @@ def _ls(layer):
     return layer.layer_scalar.float().reshape(1).contiguous()
 
 
-def _materialize(layer, direction=1):
+# ------------------------------------------------------------------ projections of a layer
+# bf16 weights go through ops.linear; an NF4 base with the fused path hands the codes to the
+# GEMM that dequantises them in-kernel (micro_engram_fork_b200/csrc/gemm_nf4.cu).
+def _nf4_fused(layer):
+    nf = getattr(layer, "_nf4", None)
+    return nf if nf is not None and nf.fused else None
+
+
+def _weight(layer, name):
+    return {"qkv": layer.qkv_weight, "gate_up": layer.gate_up_weight, "o": layer.self_attn.o_proj.weight,
+            "down": layer.mlp.down_proj.weight}[name]
+
+
+def _proj(layer, name, x):
+    """x . W^T for one of the layer's projections."""
+    nf = _nf4_fused(layer)
+    if nf is None:
+        return linear(x, _weight(layer, name))
+    from .. import native
+
+    x2 = x.reshape(-1, x.shape[-1]).contiguous()
+    return native().gemm_nf4(x2, *nf.operand(name), True, None).view(*x.shape[:-1], -1)
+
+
+def _proj_t(layer, name, g):
+    """g . W: the input gradient of _proj."""
+    nf = _nf4_fused(layer)
+    if nf is None:
+        return linear_t(g, _weight(layer, name))
+    from .. import native
+
+    g2 = g.reshape(-1, g.shape[-1]).contiguous()
+    return native().gemm_nf4(g2, *nf.operand(name), False, None).view(*g.shape[:-1], -1)
+
+
+def _geglu_proj(layer, h, save_gu):
+    nf = _nf4_fused(layer)
+    if nf is None:
+        return geglu_linear(h, layer.gate_up_weight, save_gu=save_gu)
+    from .. import native
+
+    m, gu = native().gemm_geglu_nf4(h.reshape(-1, h.shape[-1]).contiguous(), *nf.operand("gate_up"), save_gu)
+    return m, (gu if save_gu else None)
+
+
+def _dgeglu_proj(layer, g, gu):
+    nf = _nf4_fused(layer)
+    if nf is None:
+        return dgeglu_linear(g, layer.mlp.down_proj.weight, gu)
+    from .. import native
+
+    return native().gemm_dgeglu_nf4(g.reshape(-1, g.shape[-1]).contiguous(), *nf.operand("down"),
+                                    gu.reshape(-1, gu.shape[-1]))
+
+
+def _materialize(layer, direction=1, force=False):
     """Make this layer's full bf16 weights readable before it runs: an NF4 base expands them into
     the shared buffer; a sharded base gathers them from the peers (what the previous GEMMs did
     not already carry) and hands the next layer's gather (`direction` +1 forward, -1 backward)
@@ -312,7 +367,7 @@ def _materialize(layer, direction=1):
     if getattr(layer, "_nf4", None) is not None:
         from .nf4 import materialize
 
-        materialize(layer)
+        materialize(layer, force)
     sb = getattr(layer, "_sharded", None)
     if sb is not None:
         sb.materialize(layer, direction)
@@ -329,15 +384,15 @@ def _layer_fwd(layer, x, pos, doc_start, keep=False, direction=1):
     hd = layer.head_dim
     att = layer.self_attn
     h1, r_in = N.rmsnorm(x, layer.input_layernorm.weight, eps)
-    qkv = linear(h1, layer.qkv_weight)
+    qkv = _proj(layer, "qkv", h1)
     q, k, v, r_qkv = N.qkv_norm_rope(qkv, att.q_norm.weight, att.k_norm.weight, layer.inv_freq, pos, layer.n_q,
                                      layer.n_kv, hd, layer.kv_eq, eps)
     a, lse = attention_fwd(q, k, v, doc_start, layer.window, 1.0)
-    o = linear(a.view(T, -1), att.o_proj.weight)
+    o = _proj(layer, "o", a.view(T, -1))
     x2, h2, r_o, r_x2 = N.post_norm_add(x, o, layer.post_attention_layernorm.weight, None,
                                         layer.pre_feedforward_layernorm.weight, eps)
-    m, gu = geglu_linear(h2, layer.gate_up_weight, save_gu=keep)
-    dn = linear(m, layer.mlp.down_proj.weight)
+    m, gu = _geglu_proj(layer, h2, keep)
+    dn = _proj(layer, "down", m)
     x3, _, r_dn, _ = N.post_norm_add(x2, dn, layer.post_feedforward_layernorm.weight, _ls(layer), None, eps)
     saved = None
     if keep:
@@ -362,8 +417,8 @@ def _recompute_selective(layer, x, pos, kept, direction=-1):
                                      layer.n_q, layer.n_kv, layer.head_dim, layer.kv_eq, eps)
     x2, h2, r_o, r_x2 = N.post_norm_add(x, kept["o"], layer.post_attention_layernorm.weight, None,
                                         layer.pre_feedforward_layernorm.weight, eps)
-    m, gu = geglu_linear(h2, layer.gate_up_weight, save_gu=True)
-    dn = linear(m, layer.mlp.down_proj.weight)
+    m, gu = _geglu_proj(layer, h2, True)
+    dn = _proj(layer, "down", m)
     _, _, r_dn, _ = N.post_norm_add(x2, dn, layer.post_feedforward_layernorm.weight, _ls(layer), None, eps)
     return dict(r_in=r_in, qkv=kept["qkv"], q=q, k=k, v=v, r_qkv=r_qkv, a=kept["a"], lse=kept["lse"], o=kept["o"],
                 x2=x2, r_o=r_o, r_x2=r_x2, gu=gu, dn=dn, r_dn=r_dn)
@@ -425,16 +480,16 @@ class _LayerFn(torch.autograd.Function):
         # MLP block: x3 = (x2 + n(dn)) * ls
         d_x2_res, d_dn = N.post_norm_add_bwd(g, None, s["dn"], s["dn"], layer.post_feedforward_layernorm.weight,
                                              _ls(layer), None, s["r_dn"], None)
-        d_gu = dgeglu_linear(d_dn, layer.mlp.down_proj.weight, s["gu"])
-        d_h2 = linear_t(d_gu, layer.gate_up_weight)
+        d_gu = _dgeglu_proj(layer, d_dn, s["gu"])
+        d_h2 = _proj_t(layer, "gate_up", d_gu)
         # attention block: x2 = x + n(o); h2 = n(x2)
         d_x_res, d_o = N.post_norm_add_bwd(d_x2_res, d_h2, s["o"], s["x2"], layer.post_attention_layernorm.weight,
                                            None, layer.pre_feedforward_layernorm.weight, s["r_o"], s["r_x2"])
-        d_a = linear_t(d_o, att.o_proj.weight).view_as(s["a"])
+        d_a = _proj_t(layer, "o", d_o).view_as(s["a"])
         dq, dk, dv = attention_bwd(d_a, s["q"], s["k"], s["v"], s["a"], s["lse"], doc_start, layer.window, 1.0)
         d_qkv = N.qkv_norm_rope_bwd(dq, dk, dv, s["qkv"], att.q_norm.weight, att.k_norm.weight, layer.inv_freq,
                                     pos, s["r_qkv"], layer.n_q, layer.n_kv, layer.head_dim, layer.kv_eq)
-        d_h1 = linear_t(d_qkv, layer.qkv_weight)
+        d_h1 = _proj_t(layer, "qkv", d_qkv)
         dx = N.rmsnorm_bwd(d_h1, x, layer.input_layernorm.weight, s["r_in"], d_x_res)
         return dx, None, None, None, None
 

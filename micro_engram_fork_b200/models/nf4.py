@@ -55,8 +55,17 @@ def dequant_into(codes, absmax, out):
 
 
 # ------------------------------------------------------------------ model integration
+def fused_enabled(device):
+    """Whether CUDA layers run their projections on the GEMM that dequantises NF4 in-kernel
+    (MICRO_ENGRAM_NF4_FUSED=0 falls back to expanding into the shared bf16 buffer first)."""
+    import os
+
+    return device.type == "cuda" and os.environ.get("MICRO_ENGRAM_NF4_FUSED", "1") != "0"
+
+
 class NF4Weights:
-    """The NF4 copies of one layer's projections and the shared expansion buffer they use."""
+    """The NF4 copies of one layer's projections and the shared expansion buffer they use.
+    With `fused` the tcgen05 GEMM reads the codes directly and the buffer is never filled."""
 
     NAMES = ("qkv", "gate_up", "o", "down")
 
@@ -67,6 +76,13 @@ class NF4Weights:
         for name, w in zip(self.NAMES, _weights(layer)):
             self.shapes[name] = tuple(w.shape)
             self.packed[name] = quantize(w)
+        self.fused = fused_enabled(_weights(layer)[0].device)
+
+    def operand(self, name):
+        """(codes, absmax, rows, cols) of one projection, the NF4 GEMM's B operand."""
+        codes, absmax = self.packed[name]
+        rows, cols = self.shapes[name]
+        return codes, absmax, rows, cols
 
     def nbytes(self):
         return sum(c.numel() + a.numel() * 4 for c, a in self.packed.values())
@@ -100,10 +116,11 @@ def _need(shapes):
     return sum((-(-s[0] * s[1] // 8)) * 8 + 8 for s in shapes.values())
 
 
-def materialize(layer):
-    """Expand this layer's NF4 weights into the shared buffer (no-op if it already holds them)."""
+def materialize(layer, force=False):
+    """Expand this layer's NF4 weights into the shared buffer (no-op if it already holds them,
+    or if the layer's GEMMs read the NF4 codes themselves, unless `force`: the PyTorch path)."""
     nf = getattr(layer, "_nf4", None)
-    if nf is None or nf.scratch.owner is layer:
+    if nf is None or (nf.fused and not force) or nf.scratch.owner is layer:
         return
     views = nf.scratch.views(nf.shapes)
     for name in NF4Weights.NAMES:

@@ -18,7 +18,6 @@ import logging
 from typing import Callable, Optional, Sequence
 
 import torch
-import torch.nn.functional as F
 
 from .. import native
 
@@ -91,8 +90,8 @@ def serve_inject(hidden: torch.Tensor, hist: torch.Tensor, canon: torch.Tensor, 
     n = hidden.shape[0]
     idx = C.engram_hash_prev(hist[:n].long().contiguous(), canon, mults, orders, rows, pad_id)
     mem = C.engram_gather(idx, w_ptrs, per, world, dim, src_dtype, torch.bfloat16, status)
-    k = F.linear(mem, key_w)
-    v = F.linear(mem, value_w)
+    k = C.gemm(mem, key_w.contiguous(), True, None)  # the tcgen05 GEMM, no library GEMM on this path
+    v = C.gemm(mem, value_w.contiguous(), True, None)
     keep_u8 = keep.reshape(-1).to(torch.uint8).contiguous() if keep is not None else None
     out, _stats = C.engram_gate_fwd(hidden.contiguous(), k, v, q_scale, k_scale, keep_u8, sqrt_gate, None)
     return out

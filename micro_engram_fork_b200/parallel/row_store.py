@@ -11,14 +11,14 @@ layout), in ONE buffer laid out identically on every rank so a peer's row is at
                   list   [cap_k] i32                   slot -> row (-1: a slot lost to a race)
                   count  [4] i32                       slots handed out this step
 
-cap_k = min(per_k, capacity): `capacity` is the number of (token, table) lookups one
-optimizer step can push to a rank (tokens per step per rank x ranks); every lookup takes at
-most one slot, so the compact accumulator cannot overflow, and it replaces a dense fp32
-accumulator as large as the table (2x the bf16 table) with a few hundred MB. Without a
-capacity (inference, tests) cap_k = per_k.
+cap_k = capacity: the number of (token, table) lookups one optimizer step can push to a rank
+(tokens per step per rank x ranks); every lookup takes at most one slot, so the compact
+accumulator cannot overflow, and it replaces a dense fp32 accumulator as large as the table
+(2x the bf16 table) with a few hundred MB. Without a capacity (inference, tests) cap_k = per_k.
 
 With world > 1 the buffer is a SymmBuffer (CUDA IPC over NVLink); kernels index it
-through device tables of per-rank addresses. The optimizer moments live in ordinary local
+through device tables of per-rank addresses. Row gradients return to their owners through a
+second symmetric buffer of per-source inbox regions (no remote atomics; see push_grads). The optimizer moments live in ordinary local
 memory (only the owner touches them).
 """
 import torch
@@ -46,7 +46,9 @@ class RowStore:
         self.device = torch.device(device)
         self.nt = len(self.table_rows)
         self.per = [-(-r // self.world) for r in self.table_rows]
-        self.cap = [p if capacity is None else max(1, min(p, int(capacity))) for p in self.per]
+        # every lookup event reserves at most one slot (a race loser leaves a hole), so `capacity`
+        # events per step always fit; capping at the shard's rows could overflow through holes
+        self.cap = [p if capacity is None else max(1, int(capacity)) for p in self.per]
         self.counts = []
         for r, p in zip(self.table_rows, self.per):
             start = min(self.rank * p, r)
@@ -113,6 +115,34 @@ class RowStore:
         self.cap_t = torch.tensor(self.cap, dtype=torch.int64, device=self.device)
         self.status = torch.zeros(2, dtype=torch.int32, device=self.device)
         self.pending = False  # row gradients were pushed since the last optimizer step
+        self._setup_exchange(capacity, group)
+
+    # ---------------------------------------------------------------- multi-GPU gradient return
+    def _setup_exchange(self, capacity, group):
+        """With world > 1 and a capacity, row gradients return to their owners through inbox
+        regions (engram_push_grads / engram_accumulate_grads: plain NVLink stores, owner-side
+        local atomics). An inbox region holds what one rank can send one owner in a backward
+        call: capacity / world tokens x n_tables events of (table, row) + dim bf16 values."""
+        self.x = None
+        if self.world == 1 or capacity is None or self.dim % 8:
+            return
+        import os
+
+        import torch.distributed as dist
+
+        from .symm import SymmBuffer
+
+        self.x_tokens = max(1, int(capacity) // self.world)
+        self.cap_e = self.x_tokens * self.nt
+        self.x_rows_off = _align(self.cap_e * 8)
+        self.x_region = _align(self.x_rows_off + self.cap_e * self.dim * 2)
+        self.x = SymmBuffer(512 + self.world * self.x_region, self.device, group)
+        self.x.view(0, (128,), torch.int32).zero_()  # flags and counters
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=group)  # every rank's flags are zero before anyone signals
+        self.xbases = torch.tensor(self.x.ptrs, dtype=torch.int64, device=self.device)
+        self.x_calls = 0
+        self.x_timeout = float(os.environ.get("MICRO_ENGRAM_PEER_TIMEOUT_S", "10"))
 
     # ---------------------------------------------------------------- views
     def shard(self, k):
@@ -143,10 +173,23 @@ class RowStore:
                                       self.status)
 
     def push_grads(self, g, idx, scale):
-        """Row gradients g [N, n_tables*dim] of the looked-up rows -> the owners' accumulators."""
-        native().engram_scatter_grad(g.contiguous(), idx, self.acc_ptrs, self.pos_ptrs, self.list_ptrs,
-                                     self.cnt_ptrs, self.per_t, self.cap_t, self.world, float(scale), self.status,
-                                     self.rank)
+        """Row gradients g [N, n_tables*dim] of the looked-up rows -> the owners' accumulators.
+
+        world > 1 with an exchange buffer: collective (every rank calls it in the same order);
+        otherwise one kernel of atomics into the owners' accumulators."""
+        C = native()
+        g = g.contiguous()
+        if self.x is not None and g.dtype == torch.bfloat16 and idx.shape[1] <= self.x_tokens:
+            self.x_calls += 1
+            C.engram_push_grads(g, idx, self.acc_ptrs, self.pos_ptrs, self.list_ptrs, self.cnt_ptrs, self.per_t,
+                                self.cap_t, self.xbases, self.rank, float(scale), self.cap_e, self.x_region,
+                                self.x_rows_off, self.x_calls, self.x_timeout, self.status)
+            C.engram_accumulate_grads(self.acc_ptrs, self.pos_ptrs, self.list_ptrs, self.cnt_ptrs, self.per_t,
+                                      self.cap_t, self.xbases, self.nt, self.dim, self.rank, float(scale), self.cap_e,
+                                      self.x_region, self.x_rows_off, self.x_calls, self.x_timeout, self.status)
+        else:
+            C.engram_scatter_grad(g, idx, self.acc_ptrs, self.pos_ptrs, self.list_ptrs, self.cnt_ptrs, self.per_t,
+                                  self.cap_t, self.world, float(scale), self.status, self.rank)
         self.pending = True
 
     def sqnorm_into(self, sq):
@@ -177,3 +220,6 @@ class RowStore:
         if self.buf is not None:
             self.buf.close()
             self.buf = None
+        if getattr(self, "x", None) is not None:
+            self.x.close()
+            self.x = None

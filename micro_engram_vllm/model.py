@@ -130,6 +130,15 @@ def _uva_views(shards):
     return [get_accelerator_view_from_cpu_tensor(p.data) for p in shards]
 
 
+def _dummy_rows(engram, seed):
+    """load_format="dummy" (random weights for benchmarking) never calls load_weights, so the
+    row shards, allocated empty, get N(0, 0.02) rows here instead of whatever memory held."""
+    with torch.no_grad():
+        for shard in engram.row_shards:
+            g = torch.Generator(device=shard.device).manual_seed(seed)
+            shard.copy_(torch.randn(shard.shape, generator=g, device=shard.device).to(shard.dtype) * 0.02)
+
+
 # ============================================================================ the layer
 class EngramGemma4DecoderLayer(Gemma4DecoderLayer):
     """Gemma 4 decoder layer that adds its engram's gated memory to the layer output."""
@@ -237,6 +246,8 @@ class EngramGemma4ForCausalLM(Gemma4ForCausalLM):
             group = get_tp_group().cpu_group if tp_size > 1 else None
             engram.shard_rows(tp_rank, tp_size, device=ref.device, dtype=ref.dtype, requires_grad=False,
                               empty=True, group=group)
+        if getattr(getattr(vllm_config, "load_config", None), "load_format", None) == "dummy":
+            _dummy_rows(engram, spec["seed"] * 1_000_003 + tp_rank)
         layer.add_module("micro_engram", engram)
         if self._micro_engram_ids is None:
             rows = vllm_config.scheduler_config.max_num_batched_tokens

@@ -22,7 +22,7 @@ if os.environ.get("ME_BOUNDS_CHECK") == "1":
 CXX = ["-O3", "-std=c++17"]
 
 SOURCES = [os.path.join(CSRC, f) for f in (
-    "bindings.cpp", "symm.cpp", "engram.cu", "norm.cu", "ce.cu", "attention.cu", "attention_tc.cu", "gemm.cu", "gemm_fused.cu",
+    "bindings.cpp", "symm.cpp", "engram.cu", "norm.cu", "ce.cu", "attention.cu", "attention_tc.cu", "gemm.cu", "gemm_fused.cu", "gemm_nf4.cu",
     "p2p.cu", "nf4.cu",
 )]
 

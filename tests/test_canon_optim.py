@@ -78,17 +78,27 @@ def test_position_ids_stop_ngrams():
     assert same([h[:, 3:] for h in h_split], h_doc2)
 
 
-def _run(opt_cls, grads, init, lazy=True, wd=0.0, dtype=torch.float32, **kw):
-    p = nn.Parameter(init.clone().to(dtype))
-    if opt_cls is LazyAdamW:
-        kw["lazy"] = lazy
-    kw.setdefault("lr", 1e-2)
-    opt = opt_cls([p], betas=(0.9, 0.999), eps=1e-8, weight_decay=wd, **kw)
+def train_param(make_opt, grads, init, dtype=torch.float32):
+    """A fresh parameter (init, in dtype) stepped once per gradient by make_opt([param])."""
+    param = nn.Parameter(init.clone().to(dtype))
+    opt = make_opt([param])
     for g in grads:
         opt.zero_grad()
-        p.grad = g.clone().to(dtype)
+        param.grad = g.clone().to(dtype)
         opt.step()
-    return p.detach().float(), opt
+    return param.detach().float(), opt
+
+
+def adamw(wd=0.0):
+    return lambda ps: torch.optim.AdamW(ps, lr=1e-2, betas=(0.9, 0.999), eps=1e-8, weight_decay=wd, foreach=False)
+
+
+def lazy_adamw(wd=0.0, **kw):
+    return lambda ps: LazyAdamW(ps, lr=1e-2, betas=(0.9, 0.999), eps=1e-8, weight_decay=wd, **kw)
+
+
+def only_state(opt):
+    return next(iter(opt.state.values()))
 
 
 R, C = 16, 8
@@ -96,128 +106,124 @@ R, C = 16, 8
 
 @pytest.fixture
 def grads():
+    """(init [R, C], 5 dense gradients, 5 gradients touching rows 0-3 only, row 0 only in the first)."""
     torch.manual_seed(0)
     init = torch.randn(R, C)
     dense = [torch.randn(R, C) for _ in range(5)]
     sparse = []
-    for i in range(5):
+    for step in range(5):
         g = torch.randn(R, C)
-        g[4:] = 0
-        if i > 0:
-            g[0] = 0
+        g[4:].zero_()
+        g[0].mul_(float(step == 0))
         sparse.append(g)
     return init, dense, sparse
 
 
 def test_lazy_adam_vs_adamw(grads):
     init, dense, sparse = grads
-    for wd in (0.0, 0.1):
-        a, _ = _run(torch.optim.AdamW, dense, init, wd=wd, foreach=False)
-        b, _ = _run(LazyAdamW, dense, init, wd=wd, lazy=True)
-        assert torch.allclose(a, b, atol=1e-6)
-    a, _ = _run(torch.optim.AdamW, sparse, init, foreach=False)
-    b, _ = _run(LazyAdamW, sparse, init, lazy=False)
-    assert torch.allclose(a, b, atol=1e-6)
-    c, opt = _run(LazyAdamW, sparse, init, lazy=True)
-    after1, _ = _run(LazyAdamW, sparse[:1], init, lazy=True)
-    assert torch.equal(c[4:], init[4:])
-    assert torch.equal(c[0], after1[0]) and not torch.allclose(a[0], after1[0])
-    assert torch.allclose(c[1:4], a[1:4], atol=1e-6)
-    st = opt.state[opt.param_groups[0]["params"][0]]
-    assert set(st) == {"step", "exp_avg", "exp_avg_sq"}
-    assert torch.equal(st["exp_avg"][4:], torch.zeros(R - 4, C))
-    d, optb = _run(LazyAdamW, sparse, init, lazy=True, dtype=torch.bfloat16)
-    stb = optb.state[optb.param_groups[0]["params"][0]]
-    assert torch.equal(d[4:], init[4:].bfloat16().float()) and stb["exp_avg"].dtype == torch.bfloat16
+    for wd in (0.0, 0.1):  # lazy on dense gradients is plain AdamW
+        assert torch.allclose(train_param(adamw(wd), dense, init)[0],
+                              train_param(lazy_adamw(wd, lazy=True), dense, init)[0], atol=1e-6)
+    eager_ref = train_param(adamw(), sparse, init)[0]
+    assert torch.allclose(eager_ref, train_param(lazy_adamw(lazy=False), sparse, init)[0], atol=1e-6)
+    lazy, opt = train_param(lazy_adamw(lazy=True), sparse, init)
+    row0_once = train_param(lazy_adamw(lazy=True), sparse[:1], init)[0][0]
+    assert torch.equal(lazy[4:], init[4:]), "untouched rows moved"
+    assert torch.equal(lazy[0], row0_once), "a row moved on steps where its gradient was zero"
+    assert not torch.allclose(eager_ref[0], row0_once), "the eager optimizer should keep moving row 0"
+    assert torch.allclose(lazy[1:4], eager_ref[1:4], atol=1e-6)
+    st = only_state(opt)
+    assert sorted(st) == ["exp_avg", "exp_avg_sq", "step"] and not st["exp_avg"][4:].any()
+    low, opt_bf = train_param(lazy_adamw(lazy=True), sparse, init, dtype=torch.bfloat16)
+    assert torch.equal(low[4:], init[4:].bfloat16().float()) and only_state(opt_bf)["exp_avg"].dtype == torch.bfloat16
 
 
 def test_rowwise(grads):
     init, _, sparse = grads
-    row_scale = torch.rand(R, 1) + 0.5
-    uniform = [row_scale * torch.sign(torch.randn(R, C)) * (i + 1) for i in range(5)]
-    a, _ = _run(torch.optim.AdamW, uniform, init, wd=0.1, foreach=False)
-    b, opt = _run(LazyAdamW, uniform, init, wd=0.1, lazy=False, rowwise=True)
-    assert torch.allclose(a, b, atol=1e-6)
-    st = opt.state[opt.param_groups[0]["params"][0]]
-    assert st["exp_avg_sq"].shape == (R,) and st["exp_avg_sq"].dtype == torch.float32
-    c, optl = _run(LazyAdamW, sparse, init, lazy=True, rowwise=True)
-    stl = optl.state[optl.param_groups[0]["params"][0]]
-    assert torch.equal(c[4:], init[4:]) and torch.equal(stl["exp_avg_sq"][4:], torch.zeros(R - 4))
+    # gradients with one magnitude per row: the row mean of g^2 equals every element's g^2,
+    # so row-wise Adam reduces to AdamW exactly
+    scale = torch.rand(R, 1) + 0.5
+    uniform = [scale * torch.randn(R, C).sign() * (k + 1) for k in range(5)]
+    ref = train_param(adamw(0.1), uniform, init)[0]
+    got, opt = train_param(lazy_adamw(0.1, lazy=False, rowwise=True), uniform, init)
+    assert torch.allclose(ref, got, atol=1e-6)
+    v = only_state(opt)["exp_avg_sq"]
+    assert tuple(v.shape) == (R,) and v.dtype == torch.float32
+    lazy, opt_l = train_param(lazy_adamw(lazy=True, rowwise=True), sparse, init)
+    assert torch.equal(lazy[4:], init[4:]) and not only_state(opt_l)["exp_avg_sq"][4:].any()
 
 
 def test_bf16_second_moment_freeze(grads):
+    """With g = 1 the bias-corrected second moment tends to 1. A bf16 one rounded to nearest
+    stalls far below (each 0.001 step is under half an ulp); stochastic rounding and the fp32
+    row-wise moment get there."""
     init, _, _ = grads
-    pb, ps, pr = (nn.Parameter(init.clone().bfloat16()) for _ in range(3))
-    ob = LazyAdamW([pb], lr=0.0, stochastic_rounding=False)
-    osr = LazyAdamW([ps], lr=0.0)
-    orw = LazyAdamW([pr], lr=0.0, rowwise=True)
-    for _ in range(1500):
-        for p_, o_ in ((pb, ob), (ps, osr), (pr, orw)):
-            p_.grad = torch.ones_like(p_)
-            o_.step()
-    bc2 = 1 - 0.999 ** 1500
-    v_bf = float(ob.state[pb]["exp_avg_sq"].float().mean()) / bc2
-    v_sr = float(osr.state[ps]["exp_avg_sq"].float().mean()) / bc2
-    v_rw = float(orw.state[pr]["exp_avg_sq"].mean()) / bc2
-    assert v_bf < 0.5 and abs(v_sr - 1) < 0.02 and abs(v_rw - 1) < 1e-4
+    steps = 1500
+    settings = {"bf16 nearest": dict(stochastic_rounding=False), "bf16 stochastic": {}, "row-wise fp32": dict(rowwise=True)}
+    params = {name: nn.Parameter(init.clone().bfloat16()) for name in settings}
+    opts = {name: LazyAdamW([params[name]], lr=0.0, **kw) for name, kw in settings.items()}
+    for _ in range(steps):
+        for name, opt in opts.items():
+            params[name].grad = torch.ones_like(params[name])
+            opt.step()
+    corrected = {name: float(only_state(o)["exp_avg_sq"].float().mean()) / (1 - 0.999 ** steps)
+                 for name, o in opts.items()}
+    assert corrected["bf16 nearest"] < 0.5, corrected
+    assert abs(corrected["bf16 stochastic"] - 1) < 0.02, corrected
+    assert abs(corrected["row-wise fp32"] - 1) < 1e-4, corrected
 
 
 def test_stochastic_rounding():
-    x = torch.full((100_000,), 1.00149)
-    assert abs(float(stochastic_bf16(x).float().mean()) - 1.00149) < 2e-5
-    assert abs(float(stochastic_bf16(-x).float().mean()) + 1.00149) < 2e-5
+    target = 1.00149  # between two bf16 values
+    for sign in (1, -1):
+        x = torch.full((100_000,), sign * target)
+        assert abs(float(stochastic_bf16(x).float().mean()) - sign * target) < 2e-5
     assert torch.isinf(stochastic_bf16(torch.tensor([float("inf")]))).all()
-    for lr in (2.5e-5, 6.25e-5):
-        moved = {}
-        for name, dtype, sr in (("fp32", torch.float32, True), ("plain", torch.bfloat16, False),
-                                ("sr", torch.bfloat16, True)):
-            torch.manual_seed(5)
-            w = nn.Parameter(torch.full((2000, 8), 0.03, dtype=dtype))
-            opt = LazyAdamW([{"params": [w], "lazy": True, "rowwise": True}], lr=lr, stochastic_rounding=sr)
-            for _ in range(300):
-                w.grad = torch.ones_like(w)
-                opt.step()
-            moved[name] = float((0.03 - w.float()).mean())
-        assert abs(moved["plain"] / moved["fp32"] - 1) > 0.2
-        assert abs(moved["sr"] / moved["fp32"] - 1) < 0.03
+
+    def drift(lr, dtype, sr):
+        torch.manual_seed(5)
+        w = nn.Parameter(torch.full((2000, 8), 0.03, dtype=dtype))
+        opt = LazyAdamW([{"params": [w], "lazy": True, "rowwise": True}], lr=lr, stochastic_rounding=sr)
+        for _ in range(300):
+            w.grad = torch.ones_like(w)
+            opt.step()
+        return float((0.03 - w.float()).mean())
+
+    for lr in (2.5e-5, 6.25e-5):  # updates below half a bf16 ulp of 0.03
+        exact = drift(lr, torch.float32, True)
+        assert abs(drift(lr, torch.bfloat16, False) / exact - 1) > 0.2
+        assert abs(drift(lr, torch.bfloat16, True) / exact - 1) < 0.03
 
 
 def test_fsdp2_lazy_and_state(dist_env):
+    """LazyAdamW on FSDP2 DTensor parameters: lazy rows stay put, and the optimizer state survives
+    the distributed-checkpoint state-dict round trip."""
     import torch.distributed as dist
     from torch.distributed.checkpoint.state_dict import get_optimizer_state_dict, set_optimizer_state_dict
     from torch.distributed.fsdp import fully_shard
 
     dist.init_process_group("gloo", rank=0, world_size=1)
-
-    class Block(nn.Module):
-        def __init__(self):
-            super().__init__()
-            self.lin = nn.Linear(C, C)
-            self.tables = nn.Embedding(R, C)
-
-        def forward(self, ids):
-            return self.lin(self.tables(ids))
-
     torch.manual_seed(1)
-    blk = Block()
-    fully_shard(blk)
-    groups = [{"params": [blk.tables.weight], "lazy": True}, {"params": [blk.lin.weight, blk.lin.bias]}]
-    opt = LazyAdamW(groups, lr=1e-2)
-    before = blk.tables.weight.full_tensor().clone()
-    row1 = None
-    for i in range(3):
+    model = nn.Sequential(nn.Embedding(R, C), nn.Linear(C, C))
+    fully_shard(model)
+    table = model[0].weight
+
+    def make():
+        return LazyAdamW([{"params": [table], "lazy": True}, {"params": list(model[1].parameters())}], lr=1e-2)
+
+    opt = make()
+    start = table.full_tensor().clone()
+    snapshots = []
+    for ids in ([1, 2, 3], [2, 3], [2, 3]):
         opt.zero_grad()
-        ids = [[1, 2, 3]] if i == 0 else [[2, 3]]
-        blk(torch.tensor(ids)).pow(2).sum().backward()
+        model(torch.tensor([ids])).square().sum().backward()
         opt.step()
-        if i == 0:
-            row1 = blk.tables.weight.full_tensor()[1].clone()
-    w = blk.tables.weight.full_tensor()
-    assert not torch.equal(w[2:4], before[2:4]) and torch.equal(w[4:], before[4:]) and torch.equal(w[0], before[0])
-    assert torch.equal(w[1], row1)
-    sd = get_optimizer_state_dict(blk, opt)
-    opt2 = LazyAdamW([{"params": [blk.tables.weight], "lazy": True}, {"params": [blk.lin.weight, blk.lin.bias]}],
-                     lr=1e-2)
-    set_optimizer_state_dict(blk, opt2, sd)
-    s1, s2 = opt.state[blk.tables.weight], opt2.state[blk.tables.weight]
-    assert torch.equal(s1["exp_avg"].full_tensor(), s2["exp_avg"].full_tensor()) and float(s2["step"]) == 3
+        snapshots.append(table.full_tensor().clone())
+    end = snapshots[-1]
+    assert not torch.equal(end[2:4], start[2:4])
+    assert torch.equal(end[4:], start[4:]) and torch.equal(end[0], start[0])
+    assert torch.equal(end[1], snapshots[0][1]), "row 1 moved after its last lookup"
+    restored = make()
+    set_optimizer_state_dict(model, restored, get_optimizer_state_dict(model, opt))
+    a, b = opt.state[table], restored.state[table]
+    assert torch.equal(a["exp_avg"].full_tensor(), b["exp_avg"].full_tensor()) and float(b["step"]) == 3

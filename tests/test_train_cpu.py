@@ -18,52 +18,68 @@ WORDS = [f"w{i}" for i in range(123)]
 V = len(SPECIAL) + len(WORDS)
 
 
-def make_assets(root):
+def _tokenizer():
     from tokenizers import Tokenizer, models, pre_tokenizers
-    from transformers import Gemma4ForCausalLM, PreTrainedTokenizerFast
+    from transformers import PreTrainedTokenizerFast
+
+    vocab = {t: i for i, t in enumerate(SPECIAL + WORDS)}
+    core = Tokenizer(models.WordLevel(vocab, unk_token="<pad>"))
+    core.pre_tokenizer = pre_tokenizers.WhitespaceSplit()
+    return PreTrainedTokenizerFast(tokenizer_object=core, pad_token="<pad>", eos_token="<eos>", bos_token="<bos>")
+
+
+def _tiny_gemma():
+    """4 layers (2 sliding, 2 global), d 64, norm weights moved off 1 so that they matter."""
+    from transformers import Gemma4ForCausalLM
     from transformers.models.gemma4.configuration_gemma4 import Gemma4TextConfig
 
-    tk = Tokenizer(models.WordLevel({t: i for i, t in enumerate(SPECIAL + WORDS)}, unk_token="<pad>"))
-    tk.pre_tokenizer = pre_tokenizers.WhitespaceSplit()
-    tok = PreTrainedTokenizerFast(tokenizer_object=tk, pad_token="<pad>", eos_token="<eos>", bos_token="<bos>")
+    layer_types = ["sliding_attention"] * 2 + ["full_attention"] * 2
     cfg = Gemma4TextConfig(vocab_size=V, hidden_size=64, intermediate_size=128, num_hidden_layers=4,
                            num_attention_heads=4, num_key_value_heads=2, head_dim=16, global_head_dim=32,
-                           layer_types=["sliding_attention", "sliding_attention", "full_attention", "full_attention"],
-                           sliding_window=8, hidden_size_per_layer_input=0, max_position_embeddings=1024,
-                           final_logit_softcapping=30.0, pad_token_id=0, eos_token_id=1, bos_token_id=2)
+                           layer_types=layer_types, sliding_window=8, hidden_size_per_layer_input=0,
+                           max_position_embeddings=1024, final_logit_softcapping=30.0, pad_token_id=0,
+                           eos_token_id=1, bos_token_id=2)
     cfg.architectures = ["Gemma4ForCausalLM"]
     torch.manual_seed(0)
-    m = Gemma4ForCausalLM(cfg)
+    model = Gemma4ForCausalLM(cfg)
+    norms = [p for p in model.parameters() if p.dim() == 1]
     with torch.no_grad():
-        for n, p in m.named_parameters():
-            if p.dim() == 1:
-                p.copy_(1 + 0.2 * torch.randn_like(p))
-    model_dir = os.path.join(root, "base")
-    m.to(torch.bfloat16).save_pretrained(model_dir)
-    tok.save_pretrained(model_dir)
+        for p in norms:
+            p.copy_(1 + 0.2 * torch.randn_like(p))
+    return model
+
+
+def _corpus(path, docs=40):
     g = torch.Generator().manual_seed(1)
-    rows = []
-    for _ in range(40):
-        n = int(torch.randint(5, 60, (1,), generator=g))
-        rows.append({"text": "<bos> " + " ".join(WORDS[int(i)] for i in torch.randint(0, len(WORDS), (n,), generator=g))})
-    data = os.path.join(root, "cpt.jsonl")
-    with open(data, "w") as f:
-        f.write("\n".join(json.dumps(r) for r in rows))
+    lines = []
+    for _ in range(docs):
+        length = int(torch.randint(5, 60, (1,), generator=g))
+        words = [WORDS[int(i)] for i in torch.randint(0, len(WORDS), (length,), generator=g)]
+        lines.append(json.dumps({"text": "<bos> " + " ".join(words)}))
+    with open(path, "w") as f:
+        f.write("\n".join(lines))
+    return path
+
+
+def make_assets(root):
+    """(model folder with tokenizer, completion JSONL); also canon.pt merging every even/odd id pair."""
+    model_dir = os.path.join(root, "base")
+    _tiny_gemma().to(torch.bfloat16).save_pretrained(model_dir)
+    _tokenizer().save_pretrained(model_dir)
     torch.save(torch.arange(V) & ~1, os.path.join(root, "canon.pt"))
-    return model_dir, data
+    return model_dir, _corpus(os.path.join(root, "cpt.jsonl"))
 
 
 def base_cfg(root, model_dir, data, out, **over):
-    c = {"base_model": model_dir, "datasets": [{"path": data, "type": "completion"}], "sequence_len": 32,
-         "output_dir": out, "micro_batch_size": 1, "gradient_accumulation_steps": 2, "num_epochs": 1,
-         "learning_rate": 5e-3, "lr_scheduler": "constant", "max_grad_norm": 2.0, "seed": 7,
-         "gradient_checkpointing": True, "micro_engram_layer": 1, "micro_engram_table_size": 97,
-         "micro_engram_dim": 8, "micro_engram_heads": 2, "micro_engram_gate": "scalar_sqrt",
-         "micro_engram_extra": [{"layer": 3}], "micro_engram_optimizer": "rowwise_adam",
-         "micro_engram_dtype": "fp32", "micro_engram_canon_path": os.path.join(root, "canon.pt"),
-         "micro_engram_stats_steps": 1, "loss_chunk_tokens": 16, "save_steps": None}
-    c.update(over)
-    return c
+    engram = {"micro_engram_layer": 1, "micro_engram_table_size": 97, "micro_engram_dim": 8, "micro_engram_heads": 2,
+              "micro_engram_gate": "scalar_sqrt", "micro_engram_extra": [{"layer": 3}],
+              "micro_engram_optimizer": "rowwise_adam", "micro_engram_dtype": "fp32",
+              "micro_engram_canon_path": os.path.join(root, "canon.pt"), "micro_engram_stats_steps": 1}
+    run = {"base_model": model_dir, "datasets": [{"path": data, "type": "completion"}], "sequence_len": 32,
+           "output_dir": out, "micro_batch_size": 1, "gradient_accumulation_steps": 2, "num_epochs": 1,
+           "learning_rate": 5e-3, "lr_scheduler": "constant", "max_grad_norm": 2.0, "seed": 7,
+           "gradient_checkpointing": True, "loss_chunk_tokens": 16, "save_steps": None}
+    return {**run, **engram, **over}
 
 
 def _trainer(cfg):
@@ -78,140 +94,167 @@ def _trainer(cfg):
 def _randomize_dense(t):
     g = torch.Generator().manual_seed(5)
     with torch.no_grad():
-        for s in t.slots:
-            for _, p in s.engram.named_parameters():
-                p.copy_(torch.randn(p.shape, generator=g) * 0.05)
+        for p in (p for s in t.slots for p in s.engram.parameters()):
+            p.copy_(torch.randn(p.shape, generator=g) * 0.05)
 
 
-def _state(t):
-    out = {}
+def snapshot(t):
+    """Every engram weight of the trainer (dense parameters and table row shards), cloned."""
+    named = {}
     for s in t.slots:
-        for n, p in s.engram.named_parameters():
-            out[f"{s.layer}.{n}"] = p.detach().clone()
-        for k, p in enumerate(s.engram.row_shards):
-            out[f"{s.layer}.rows{k}"] = p.detach().clone()
-    return out
+        named.update({f"{s.layer}.{n}": p for n, p in s.engram.named_parameters()})
+        named.update({f"{s.layer}.rows{k}": p for k, p in enumerate(s.engram.row_shards)})
+    return {k: p.detach().clone() for k, p in named.items()}
 
 
-def _dense_grad(p):
-    sg = getattr(p, "sparse_grad", None)
-    if sg is not None:
-        g = torch.zeros(p.shape, dtype=torch.float32)
-        g.index_add_(0, sg[0], sg[1].float())
-        return g
-    return None if p.grad is None else p.grad.float().clone()
+def grad_as_dense(p):
+    """A table shard's gradient as a dense fp32 tensor, whether it is sparse (rows, values) or not."""
+    sparse = getattr(p, "sparse_grad", None)
+    if sparse is None:
+        return None if p.grad is None else p.grad.float().clone()
+    rows, vals = sparse
+    return torch.zeros(p.shape, dtype=torch.float32).index_add_(0, rows, vals.float())
 
 
-def _hf_loss(ref, batches):
+def hf_token_mean_loss(ref, batches):
+    """Cross-entropy of the HF model, summed over every rank's batches and divided by the trained tokens."""
     import torch.distributed as dist
 
-    s, c = torch.zeros(()), torch.zeros(())
+    tot = torch.zeros(2)
     with torch.no_grad():
         for b in batches:
-            logits = ref(input_ids=b["input_ids"], position_ids=b["position_ids"]).logits.float()
-            s += torch.nn.functional.cross_entropy(logits.reshape(-1, V), b["labels"].reshape(-1), ignore_index=-100,
-                                                   reduction="sum")
-            c += (b["labels"] != -100).sum()
-    dist.all_reduce(s)
-    dist.all_reduce(c)
-    return float(s / c)
+            logits = ref(input_ids=b["input_ids"], position_ids=b["position_ids"]).logits.float().reshape(-1, V)
+            labels = b["labels"].reshape(-1)
+            tot[0] += torch.nn.functional.cross_entropy(logits, labels, ignore_index=-100, reduction="sum")
+            tot[1] += (labels != -100).sum()
+    dist.all_reduce(tot)
+    return float(tot[0] / tot[1])
+
+
+def _clear_grads(t):
+    for p in t.dense:
+        p.grad = None
+    t.rows.zero_grad()
+
+
+def check_first_step(t, ref, rank):
+    micro = t.plan.micro_batches(0, 0, rank)
+    return {"ref_loss": hf_token_mean_loss(ref, [t._micro_batch(b) for b in micro]),
+            "loss": t.train_step(micro)["loss"]}
+
+
+def check_prefix(t, rank):
+    """The no-grad prefix (layers before the first engram run without autograd) leaves every engram
+    gradient as a full backward gives it."""
+    _randomize_dense(t)
+    batch = t._micro_batch(t.plan.micro_batches(0, 1, rank)[0])
+    runs = {}
+    for prefix in (True, False):
+        t.cfg.no_grad_prefix = prefix
+        _clear_grads(t)
+        t.forward_loss(batch, 1.0)
+        runs[prefix] = [None if p.grad is None else p.grad.clone() for p in t.dense] + \
+            [grad_as_dense(p) for p in t.rows.params()]
+
+    def same(a, c):
+        return (a is None) == (c is None) and (a is None or torch.allclose(a, c, atol=1e-6))
+
+    t.cfg.no_grad_prefix = True
+    _clear_grads(t)
+    return {"prefix_same": all(same(a, c) for a, c in zip(runs[True], runs[False])),
+            "prefix_nonzero": any(a is not None and bool(a.abs().sum() > 0) for a in runs[True])}
+
+
+def check_resume(t, cfg, out, rank):
+    """save -> resume -> next step gives what the uninterrupted run gives."""
+    t.global_step, t.step_in_epoch = 1, 1
+    t.save_checkpoint()
+    t.train_step(t.plan.micro_batches(0, 1, rank))
+    straight = snapshot(t)
+    again = _trainer({**cfg, "resume_from_checkpoint": os.path.join(out, "checkpoint-1")})
+    again._maybe_resume()
+    again.train_step(again.plan.micro_batches(0, again.step_in_epoch, rank))
+    resumed = snapshot(again)
+    return {"resume_same": all(torch.allclose(straight[k], resumed[k], atol=1e-6) for k in straight),
+            "resume_step": again.global_step}
+
+
+def check_meta_loading(cfg, root, rank):
+    """cpu_ram_efficient_loading: rank 0 reads the weights, the other ranks get a broadcast."""
+    t = _trainer({**cfg, "output_dir": os.path.join(root, "run_b"), "fsdp_config": {"cpu_ram_efficient_loading": True}})
+    return {"meta_loss": t.train_step(t.plan.micro_batches(0, 0, rank))["loss"]}
+
+
+def check_sparse(cfg, root, rank):
+    """Sparse (touched rows only) and dense table gradients give the same 3 clipped steps."""
+    runs = []
+    for sparse in (True, False):
+        t = _trainer({**cfg, "output_dir": os.path.join(root, f"run_sp{int(sparse)}"), "sparse_row_grads": sparse,
+                      "max_grad_norm": 0.05})
+        _randomize_dense(t)
+        norms = [t.train_step(t.plan.micro_batches(0, k, rank))["table_grad_norm"] for k in range(3)]
+        runs.append((snapshot(t), norms))
+    (wa, na), (wb, nb) = runs
+    same_w = all(torch.allclose(wa[k], wb[k], atol=1e-6) for k in wa)
+    same_n = all(abs(x - y) < 1e-5 * max(1, abs(y)) for x, y in zip(na, nb))
+    return {"sparse_same": same_w and same_n, "sparse_norms": na}
+
+
+def check_mb2(cfg, root, ref, rank):
+    """micro_batch_size 2 packs both rows into one; the loss still matches HF on both rows."""
+    t = _trainer({**cfg, "output_dir": os.path.join(root, "run_mb2"), "micro_batch_size": 2,
+                  "gradient_accumulation_steps": 1})
+    micro = t.plan.micro_batches(0, 0, rank)
+    return {"mb2": (t.train_step(micro)["loss"], hf_token_mean_loss(ref, [t._micro_batch(x) for x in micro]))}
+
+
+def check_dense_lr(cfg, root, rank):
+    """micro_engram_dense_lr follows the tables' schedule; a new value takes effect on resume."""
+    lc = {**cfg, "output_dir": os.path.join(root, "run_lr"), "learning_rate": 5e-3, "micro_engram_dense_lr": 1e-3,
+          "lr_scheduler": "cosine", "warmup_steps": 2}
+    t = _trainer(lc)
+    logs = [t.train_step(t.plan.micro_batches(0, k, rank)) for k in range(3)]
+    t.global_step = t.step_in_epoch = 3
+    t.save_checkpoint()
+    t = _trainer({**lc, "micro_engram_dense_lr": 2e-4, "resume_from_checkpoint": os.path.join(root, "run_lr",
+                                                                                               "checkpoint-3")})
+    t._maybe_resume()
+    logs.append(t.train_step(t.plan.micro_batches(0, 3, rank)))
+    return {"lr_ratio": [x["learning_rate"] / x["dense_lr"] if x["dense_lr"] else None for x in logs],
+            "lr_seq": [x["learning_rate"] for x in logs]}
+
+
+def check_train_scales(cfg, root, rank):
+    """micro_engram_train_scales: false freezes the scalar_sqrt gate's norm scales."""
+    res = {}
+    for train in (False, True):
+        t = _trainer({**cfg, "output_dir": os.path.join(root, f"run_sc{int(train)}"),
+                      "micro_engram_train_scales": train})
+        _randomize_dense(t)
+        start = {s.layer: s.engram.q_scale.detach().clone() for s in t.slots}
+        for k in range(2):
+            t.train_step(t.plan.micro_batches(0, k, rank))
+        res[f"scales_moved{int(train)}"] = any(not torch.equal(start[s.layer], s.engram.q_scale) for s in t.slots)
+        res[f"scales_grad{int(train)}"] = all(s.engram.q_scale.requires_grad == train for s in t.slots)
+    return res
 
 
 def _worker(rank, world, root, model_dir, data):
     from transformers import Gemma4ForCausalLM
 
-    res = {}
     out = os.path.join(root, "run_a")
     cfg = base_cfg(root, model_dir, data, out)
     t = _trainer(cfg)
-    micro = t.plan.micro_batches(0, 0, rank)
     ref = Gemma4ForCausalLM.from_pretrained(model_dir, dtype=torch.bfloat16, attn_implementation="eager")
-    res["ref_loss"] = _hf_loss(ref, [t._micro_batch(b) for b in micro])
-    res["loss"] = t.train_step(micro)["loss"]
-    # no-grad prefix: the engram gradients equal a full backward's
-    _randomize_dense(t)
-    b = t._micro_batch(t.plan.micro_batches(0, 1, rank)[0])
-
-    def grads(prefix):
-        t.cfg.no_grad_prefix = prefix
-        for p in t.dense:
-            p.grad = None
-        t.rows.zero_grad()
-        t.forward_loss(b, 1.0)
-        return [None if p.grad is None else p.grad.clone() for p in t.dense] + [_dense_grad(p) for p in t.rows.params()]
-
-    g1, g0 = grads(True), grads(False)
-    res["prefix_same"] = all((a is None and c is None) or (a is not None and c is not None and
-                                                          torch.allclose(a, c, atol=1e-6)) for a, c in zip(g1, g0))
-    res["prefix_nonzero"] = any(a is not None and a.abs().sum() > 0 for a in g1)
-    t.cfg.no_grad_prefix = True
-    for p in t.dense:
-        p.grad = None
-    t.rows.zero_grad()
-    # save -> resume -> next step == the uninterrupted run
-    t.global_step, t.step_in_epoch = 1, 1
-    t.save_checkpoint()
-    t.train_step(t.plan.micro_batches(0, 1, rank))
-    after = _state(t)
+    res = check_first_step(t, ref, rank)
+    res.update(check_prefix(t, rank))
+    res.update(check_resume(t, cfg, out, rank))
     del t
-    t2 = _trainer({**cfg, "resume_from_checkpoint": os.path.join(out, "checkpoint-1")})
-    t2._maybe_resume()
-    t2.train_step(t2.plan.micro_batches(0, t2.step_in_epoch, rank))
-    after2 = _state(t2)
-    res["resume_same"] = all(torch.allclose(after[k], after2[k], atol=1e-6) for k in after)
-    res["resume_step"] = t2.global_step
-    del t2
-    # cpu_ram_efficient_loading: rank 0 loads, the others receive a broadcast
-    t3 = _trainer({**cfg, "output_dir": os.path.join(root, "run_b"), "fsdp_config": {"cpu_ram_efficient_loading": True}})
-    res["meta_loss"] = t3.train_step(t3.plan.micro_batches(0, 0, rank))["loss"]
-    del t3
-    # sparse row gradients == dense ones (3 clipped steps)
-    states = []
-    for sparse in (True, False):
-        tt = _trainer({**cfg, "output_dir": os.path.join(root, f"run_sp{int(sparse)}"), "sparse_row_grads": sparse,
-                       "max_grad_norm": 0.05})
-        _randomize_dense(tt)
-        norms = [tt.train_step(tt.plan.micro_batches(0, k, rank))["table_grad_norm"] for k in range(3)]
-        states.append((_state(tt), norms))
-        del tt
-    (a, na), (b2, nb) = states
-    res["sparse_same"] = all(torch.allclose(a[k], b2[k], atol=1e-6) for k in a) and \
-        all(abs(x - y) < 1e-5 * max(1, abs(y)) for x, y in zip(na, nb))
-    res["sparse_norms"] = na
-    # micro_batch_size 2: rows flattened into one packed row; same loss as HF on both rows
-    tm = _trainer({**cfg, "output_dir": os.path.join(root, "run_mb2"), "micro_batch_size": 2,
-                   "gradient_accumulation_steps": 1})
-    mb = tm.plan.micro_batches(0, 0, rank)
-    res["mb2"] = (tm.train_step(mb)["loss"], _hf_loss(ref, [tm._micro_batch(x) for x in mb]))
-    del tm
-    # micro_engram_dense_lr: same schedule as the tables; a new value applies on resume
-    lc = {**cfg, "output_dir": os.path.join(root, "run_lr"), "learning_rate": 5e-3, "micro_engram_dense_lr": 1e-3,
-          "lr_scheduler": "cosine", "warmup_steps": 2}
-    tl = _trainer(lc)
-    l1 = [tl.train_step(tl.plan.micro_batches(0, k, rank)) for k in range(3)]
-    tl.global_step = tl.step_in_epoch = 3
-    tl.save_checkpoint()
-    del tl
-    tl = _trainer({**lc, "micro_engram_dense_lr": 2e-4,
-                   "resume_from_checkpoint": os.path.join(root, "run_lr", "checkpoint-3")})
-    tl._maybe_resume()
-    l2 = tl.train_step(tl.plan.micro_batches(0, 3, rank))
-    res["lr_ratio"] = [x["learning_rate"] / x["dense_lr"] if x["dense_lr"] else None for x in l1] + \
-        [l2["learning_rate"] / l2["dense_lr"]]
-    res["lr_seq"] = [x["learning_rate"] for x in l1] + [l2["learning_rate"]]
-    del tl
-    # micro_engram_train_scales
-    for train_scales in (False, True):
-        ts = _trainer({**cfg, "output_dir": os.path.join(root, f"run_sc{int(train_scales)}"),
-                       "micro_engram_train_scales": train_scales})
-        _randomize_dense(ts)
-        before = {s.layer: s.engram.q_scale.detach().clone() for s in ts.slots}
-        for k in range(2):
-            ts.train_step(ts.plan.micro_batches(0, k, rank))
-        res[f"scales_moved{int(train_scales)}"] = any(not torch.equal(before[s.layer], s.engram.q_scale)
-                                                     for s in ts.slots)
-        res[f"scales_grad{int(train_scales)}"] = all(s.engram.q_scale.requires_grad == train_scales for s in ts.slots)
-        del ts
+    res.update(check_meta_loading(cfg, root, rank))
+    res.update(check_sparse(cfg, root, rank))
+    res.update(check_mb2(cfg, root, ref, rank))
+    res.update(check_dense_lr(cfg, root, rank))
+    res.update(check_train_scales(cfg, root, rank))
     return res
 
 

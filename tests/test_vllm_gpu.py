@@ -4,7 +4,10 @@ kernel, V2 runner), must give the prompt log-probs and the greedy continuation o
 transformers model with the same engram attached (micro_engram.module.attach_engram).
 
 The vLLM engine runs in a child process (in-process engine core, so the plugin registered
-there is the one the model runner sees)."""
+there is the one the model runner sees). With tensor parallelism 2 the table rows are split
+over the two GPUs' row stores and the fused op reads the other GPU's rows over NVLink; the
+TP worker processes find the plugin through the `vllm.general_plugins` entry point of the
+in-tree egg-info (`setup.py egg_info`), as an installed package would provide it."""
 import json
 import os
 import subprocess
@@ -64,16 +67,20 @@ def _hf_logprobs(hf, eng, ids):
     return plain, withe
 
 
-def _serve(folder, prompt, n_new):
+def _serve(folder, prompt, n_new, tp=1):
     os.environ["VLLM_ENABLE_V1_MULTIPROCESSING"] = "0"
     os.environ["VLLM_USE_V2_MODEL_RUNNER"] = "1"
+    if tp > 1:
+        os.environ["VLLM_WORKER_MULTIPROC_METHOD"] = "fork"
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     import micro_engram_vllm
     from vllm import LLM, SamplingParams
 
     micro_engram_vllm.register()
+    extra = {"tensor_parallel_size": tp, "distributed_executor_backend": "mp"} if tp > 1 else {}
     llm = LLM(model=folder, skip_tokenizer_init=True, dtype="bfloat16", enforce_eager=True, max_model_len=256,
               gpu_memory_utilization=0.2, max_num_seqs=4,
-              additional_config={"micro_engram": os.path.join(folder, "engram_config.json")})
+              additional_config={"micro_engram": os.path.join(folder, "engram_config.json")}, **extra)
     sp = SamplingParams(max_tokens=n_new, temperature=0.0, prompt_logprobs=0, logprobs=0, detokenize=False)
     out = llm.generate([{"prompt_token_ids": prompt}], sp)[0]
     prompt_lp = [None] + [next(iter(d.values())).logprob for d in out.prompt_logprobs[1:]]
@@ -82,21 +89,28 @@ def _serve(folder, prompt, n_new):
     return prompt_lp, gen, gen_lp
 
 
-def _main(folder):
+def _main(folder, tp):
     torch.manual_seed(3)
     prompt = torch.randint(3, V, (40,)).tolist()
-    prompt_lp, gen, gen_lp = _serve(folder, prompt, 8)
+    prompt_lp, gen, gen_lp = _serve(folder, prompt, 8, tp)
     with open(os.path.join(folder, "served.json"), "w") as f:
         json.dump({"prompt": prompt, "prompt_lp": prompt_lp, "gen": gen, "gen_lp": gen_lp}, f)
 
 
-def test_vllm_serves_engram_like_hf(tmp_path):
+@pytest.mark.parametrize("tp", [1, 2])
+def test_vllm_serves_engram_like_hf(tmp_path, tp):
     pytest.importorskip("vllm")
+    if torch.cuda.device_count() < tp:
+        pytest.skip(f"needs {tp} GPUs")
     folder = str(tmp_path)
+    if tp > 1:  # TP workers load plugins through entry points: an in-tree egg-info declares ours
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        subprocess.run([sys.executable, "setup.py", "-q", "egg_info"], cwd=root, check=True, capture_output=True)
     hf, eng = _build(folder)
     env = dict(os.environ, PYTHONPATH=os.pathsep.join([os.path.dirname(os.path.dirname(__file__)),
                                                        os.environ.get("PYTHONPATH", "")]))
-    r = subprocess.run([sys.executable, __file__, folder], env=env, capture_output=True, text=True, timeout=900)
+    r = subprocess.run([sys.executable, __file__, folder, str(tp)], env=env, capture_output=True, text=True,
+                       timeout=900)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-6000:]
     with open(os.path.join(folder, "served.json")) as f:
         s = json.load(f)
@@ -120,4 +134,4 @@ def test_vllm_serves_engram_like_hf(tmp_path):
 
 
 if __name__ == "__main__":
-    _main(sys.argv[1])
+    _main(sys.argv[1], int(sys.argv[2]) if len(sys.argv) > 2 else 1)
