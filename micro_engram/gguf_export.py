@@ -38,27 +38,35 @@ def find_config(path):
     return conf
 
 
+def _trained_engram(spec, conf, src, n_embd, several):
+    """The MicroEngram of one spec with the weights found at `src` (the canon map from the
+    weights when they carry one, else from the spec's canon_path when it merged tokens)."""
+    sd = load_engram_weights(src, layer=spec["layer"] if several else None)
+    if not any(k.startswith("tables.") for k in sd):
+        raise SystemExit(f"no engram weights for layer {spec['layer']} in {src}")
+    if "canon" in sd:
+        vocab, canon = int(sd["canon"].numel()), None
+    else:
+        vocab = int(conf.get("vocab_size") or 262144)
+        canon = torch.load(spec["canon_path"], map_location="cpu") if spec.get("token_merge") else None
+    eng = engram_from_spec(spec, n_embd, vocab, conf.get("pad_id") or 0, canon)
+    check_loaded(eng, sd, src)
+    return eng
+
+
 def load_engrams(conf_path, n_embd):
     """[(spec, MicroEngram with its trained weights)] in layer order."""
     with open(conf_path) as f:
         conf = json.load(f)
-    specs = sorted(engram_specs(conf, conf_path), key=lambda s: s["layer"])
-    out = []
+    specs = sorted(engram_specs(conf, conf_path), key=lambda sp: sp["layer"])
+    loaded = []
     for spec in specs:
         src = spec["weights"] or os.path.dirname(conf_path)
-        sd = load_engram_weights(src, layer=spec["layer"] if len(specs) > 1 else None)
-        if not any(k.startswith("tables.") for k in sd):
-            raise SystemExit(f"no engram weights for layer {spec['layer']} in {src}")
-        vocab = int(sd["canon"].numel()) if "canon" in sd else int(conf.get("vocab_size") or 262144)
-        canon = None
-        if "canon" not in sd and spec.get("token_merge"):
-            canon = torch.load(spec["canon_path"], map_location="cpu")
-        eng = engram_from_spec(spec, n_embd, vocab, conf.get("pad_id") or 0, canon)
-        check_loaded(eng, sd, src)
-        out.append((spec, eng))
+        eng = _trained_engram(spec, conf, src, n_embd, len(specs) > 1)
         print(f"layer {spec['layer']}: {spec['gate']} gate, {len(eng.tables)} tables, rows per order "
               f"{eng.order_sizes} x {eng.engram_dim}, seed {spec['seed']}, from {src}")
-    return out
+        loaded.append((spec, eng))
+    return loaded
 
 
 def _array(t, dtype):

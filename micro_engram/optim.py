@@ -12,8 +12,9 @@ torch.optim.AdamW (step, exp_avg, exp_avg_sq). Per parameter group:
 bf16 weights and states are written back with stochastic rounding when enabled.
 
 On CUDA the update runs in the sm_100a kernels: row-sharded tables with a RowStore are
-updated on their touched rows only (one warp per row, Philox4x32-10 rounding bits, the
-accumulator cleared in the same pass); other CUDA parameters use a fused elementwise AdamW.
+updated on their touched rows only, every lazy table of a store in one launch (8 lanes per
+row with 16-byte accesses, Philox4x32-10 rounding bits, the accumulator cleared in the same
+pass); other CUDA parameters use a fused elementwise AdamW.
 """
 import torch
 
@@ -37,6 +38,12 @@ def stochastic_bf16(x):
 
 
 _SEED_BASE = 0x5EED
+
+
+def _batchable(p):
+    """Row-store tables the batched touched-row kernel takes: bf16 or fp32, width a multiple of 8."""
+    return p.is_cuda and p.dtype in (torch.bfloat16, torch.float32) and p.dim() == 2 and p.shape[1] % 8 == 0 \
+        and p.shape[1] <= 256
 
 
 def _evaluate(closure):
@@ -129,13 +136,20 @@ class LazyAdamW(torch.optim.Optimizer):
     def step(self, closure=None):
         loss = _evaluate(closure)
         done = {}  # row stores whose touched rows the kernels consumed (and cleared) this step
+        batches = {}  # (store, group) -> lazy tables updated by one batched launch
         for group, p in ((g, p) for g in self.param_groups for p in g["params"]):
             owner = getattr(p, "_row_store", None)
             if owner is None:
                 self._step_param(p, group)
                 continue
-            self._step_store(p, group)
-            done[id(owner[0])] = owner[0]
+            store = owner[0]
+            if group["lazy"] and store.pending and _batchable(p):
+                batches.setdefault((id(store), id(group)), (store, group, []))[2].append(p)
+            else:
+                self._step_store(p, group)
+            done[id(store)] = store
+        for store, group, params in batches.values():
+            self._step_store_batch(store, group, params)
         for store in done.values():
             store.pending, store.coef = False, None
         return loss
@@ -175,6 +189,25 @@ class LazyAdamW(torch.optim.Optimizer):
             store.pos[k].index_fill_(0, rows[rows >= 0], 0)
             store.acc[k][:used].zero_()
         store.count[k].zero_()
+
+    def _step_store_batch(self, store, group, params):
+        """The lazy update of several tables of one row store in one kernel launch."""
+        from micro_engram_fork_b200 import native
+
+        seed = (_SEED_BASE + 7919 * store.rank + 104729 * getattr(store, "salt", 0)) & 0x7FFFFFFF
+        cols = {key: [] for key in ("p", "m", "v", "acc", "pos", "list", "cnt", "k", "bc1", "bc2", "step")}
+        h = None
+        for p in params:
+            k = p._row_store[1]
+            state, h = self._advance(p, group, self._on_host(p, group))
+            for key, val in (("p", p.data), ("m", state["exp_avg"]), ("v", state["exp_avg_sq"]), ("acc", store.acc[k]),
+                             ("pos", store.pos[k]), ("list", store.list[k]), ("cnt", store.count[k]), ("k", k),
+                             ("bc1", h.bc1), ("bc2", h.bc2), ("step", h.step)):
+                cols[key].append(val)
+        native().engram_adam_rows(cols["p"], cols["m"], cols["v"], cols["acc"], cols["pos"], cols["list"], cols["cnt"],
+                                  cols["k"], cols["bc1"], cols["bc2"], cols["step"], getattr(store, "coef", None),
+                                  h.lr, h.beta1, h.beta2, h.eps, h.wd, h.sr, seed)
+        torch._foreach_zero_(cols["cnt"])
 
     # ------------------------------------------------------------------ everything else
     def _step_param(self, p, group):

@@ -16,6 +16,7 @@ averaging), clipping uses the global norm over all tables, and checkpoints are D
 holding the complete engram under its usual names (reshardable to any world size).
 Reference: micro_engram/rows.py:1-343.
 """
+import itertools
 import os
 
 import torch
@@ -133,13 +134,11 @@ class _RowLookup(torch.autograd.Function):
 
 def add_sparse_grad(p, rows, g):
     """Accumulate fp32 row gradients into p.sparse_grad = (unique rows, summed grads)."""
-    cur = getattr(p, "sparse_grad", None)
-    if cur is not None:
-        rows, g = torch.cat([cur[0], rows]), torch.cat([cur[1], g])
-    u, inv = torch.unique(rows, return_inverse=True)
-    acc = torch.zeros(u.numel(), g.shape[1], dtype=torch.float32, device=g.device)
-    acc.index_add_(0, inv, g.float())
-    p.sparse_grad = (u, acc)
+    pending = getattr(p, "sparse_grad", None)
+    all_rows = rows if pending is None else torch.cat([pending[0], rows])
+    all_g = g.float() if pending is None else torch.cat([pending[1], g.float()])
+    uniq, where = torch.unique(all_rows, return_inverse=True)
+    p.sparse_grad = (uniq, all_g.new_zeros(uniq.numel(), all_g.shape[1]).index_add_(0, where, all_g))
 
 
 def row_lookup(engram, idx):
@@ -155,13 +154,12 @@ def row_lookup(engram, idx):
         dim = engram.engram_dim
         return [mem[:, k * dim:(k + 1) * dim].reshape(*idx[0].shape, dim) for k in range(len(shards))]
     rank, world, _starts, pers = engram.row_info
-    offsets = [0]
-    for rows in engram.table_rows:
-        offsets.append(offsets[-1] + rows)
+    # one flat id space over all tables: table k's rows start at the sum of the earlier tables
+    offsets = [0, *itertools.accumulate(engram.table_rows)]
     dev = shards[0].device
-    flat = torch.cat([i.reshape(-1).to(dev) + offsets[k] for k, i in enumerate(idx)])
-    out = _RowLookup.apply(flat, (offsets, pers, rank, world), *shards)
-    return [out[k * m:(k + 1) * m].reshape(*idx[0].shape, -1) for k in range(len(shards))]
+    flat = torch.cat([ids.reshape(-1).to(dev) + offsets[k] for k, ids in enumerate(idx)])
+    rows = _RowLookup.apply(flat, (offsets, pers, rank, world), *shards)
+    return [part.reshape(*idx[0].shape, -1) for part in rows.split(m)]
 
 
 # ----------------------------------------------------------------------------- training side
@@ -301,22 +299,24 @@ class RowTables:
         return norm
 
     def step(self, lr):
-        if self.optimizer is None:
-            return
-        for group in self.optimizer.param_groups:
-            group["lr"] = lr
-        self.optimizer.step()
-        self.zero_grad()
+        """One table update at learning rate `lr`, then the gradients are dropped."""
+        if self.optimizer is not None:
+            for group in self.optimizer.param_groups:
+                group["lr"] = lr
+            self.optimizer.step()
+            self.zero_grad()
 
     def zero_grad(self):
+        """Drop every pending table gradient: dense .grad, sparse (rows, grads) and the row
+        stores' used slots (a step consumes them already; this covers a skipped step)."""
         if self.optimizer is not None:
             self.optimizer.zero_grad(set_to_none=True)
         for p in self.params():
             p.sparse_grad = None
         for store in self.stores():
+            store.coef = None
             if store.pending:
                 store.zero_grads()
-            store.coef = None
 
     # ------------------------------------------------------------------ checkpoints
     def _trained_refs(self):

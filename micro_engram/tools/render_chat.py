@@ -42,17 +42,10 @@ def render_rows(convs, render, roles, eot, no_spans=False):
 
 def read_conversations(path):
     """(conversations, lines without one)."""
-    convs, skipped = [], 0
     with open(path, encoding="utf-8") as f:
-        for line in f:
-            if not line.strip():
-                continue
-            msgs = messages_of(json.loads(line))
-            if msgs is None:
-                skipped += 1
-            else:
-                convs.append(msgs)
-    return convs, skipped
+        parsed = [messages_of(json.loads(line)) for line in f if line.strip()]
+    found = [m for m in parsed if m is not None]
+    return found, len(parsed) - len(found)
 
 
 def main(argv=None):

@@ -297,28 +297,27 @@ class Handler(BaseHTTPRequestHandler):
     def log_message(self, fmt, *a):
         pass
 
-    def _cors(self):
-        for key, value in (("Access-Control-Allow-Origin", "*"), ("Access-Control-Allow-Headers", "*"),
-                           ("Access-Control-Allow-Methods", "GET, POST, OPTIONS")):
+    _CORS = (("Access-Control-Allow-Origin", "*"), ("Access-Control-Allow-Headers", "*"),
+             ("Access-Control-Allow-Methods", "GET, POST, OPTIONS"))
+
+    def _head(self, code, headers=()):
+        """Status line, the given headers and the CORS headers, then the blank line."""
+        self.send_response(code)
+        for key, value in (*headers, *self._CORS):
             self.send_header(key, value)
+        self.end_headers()
 
     def _json(self, obj, code=200):
-        data = json.dumps(obj).encode()
-        self.send_response(code)
-        self.send_header("Content-Type", "application/json")
-        self.send_header("Content-Length", str(len(data)))
-        self._cors()
-        self.end_headers()
-        self.wfile.write(data)
+        body = json.dumps(obj).encode()
+        self._head(code, (("Content-Type", "application/json"), ("Content-Length", str(len(body)))))
+        self.wfile.write(body)
 
     def _event(self, obj):
         self.wfile.write(f"data: {json.dumps(obj)}\n\n".encode())
         self.wfile.flush()
 
     def do_OPTIONS(self):
-        self.send_response(204)
-        self._cors()
-        self.end_headers()
+        self._head(204)
 
     def do_GET(self):
         path = self.path.rstrip("/")
@@ -359,11 +358,7 @@ class Handler(BaseHTTPRequestHandler):
             pieces = SERVER.stream(body, input_ids, engram_on, cancel, max_new, chat)
             try:
                 if streaming:
-                    self.send_response(200)
-                    self.send_header("Content-Type", "text/event-stream")
-                    self.send_header("Cache-Control", "no-cache")
-                    self._cors()
-                    self.end_headers()
+                    self._head(200, (("Content-Type", "text/event-stream"), ("Cache-Control", "no-cache")))
                     if chat:
                         self._event(reply.chunk("", first=True))
                 for kind, text in pieces:

@@ -28,17 +28,18 @@ IGNORE = -100
 
 
 class VocabShard:
+    """This rank's rows of the tied embedding / output head and the loss over them."""
+
     def __init__(self, weight, rank, world, embed_scale=None, softcap=None, chunk_tokens=2048,
                  chunk_bytes=256 << 20, device=None, dtype=None):
-        self.V, self.d = int(weight.shape[0]), int(weight.shape[1])
-        self.rank, self.world = rank, world
+        V, d = weight.shape
+        self.V, self.d, self.rank, self.world = int(V), int(d), rank, world
+        self.per = -(-self.V // world)  # rows per rank (the last ranks may hold fewer real ones)
         self.start, self.rows = row_range(self.V, rank, world)
-        self.per = -(-self.V // world)
-        device = torch.device(device) if device is not None else weight.device
+        device = weight.device if device is None else torch.device(device)
         dtype = dtype or weight.dtype
-        self._buf = None
-        self._comm = None
-        local = weight[self.start:self.start + self.rows].detach()
+        self._buf = self._comm = None
+        local = weight.detach()[self.start:self.start + self.rows]
         if device.type == "cuda" and world > 1 and use_native(torch.empty(0, device=device)):
             # peer-mapped shard (padded to `per` rows, same layout on every rank)
             from micro_engram_fork_b200.parallel.symm import SymmBuffer

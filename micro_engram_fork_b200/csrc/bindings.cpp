@@ -20,6 +20,12 @@ void engram_accumulate_grads(torch::Tensor acc_ptrs, torch::Tensor pos_ptrs, tor
                              int64_t n_tables, int64_t dim, int64_t me, double scale, int64_t cap_e,
                              int64_t region_bytes, int64_t rows_off, int64_t call, double timeout_s,
                              torch::Tensor status);
+void engram_fetch_serve(torch::Tensor fbases, torch::Tensor wptrs, torch::Tensor per, int64_t me, int64_t n_tables,
+                        int64_t row_bytes, int64_t ntok, int64_t cap_tok, int64_t recv_off, int64_t call,
+                        double timeout_s, torch::Tensor status);
+void engram_fetch_collect(torch::Tensor fbases, torch::Tensor wptrs, torch::Tensor per, int64_t me, int64_t n_tables,
+                          int64_t row_bytes, int64_t ntok, int64_t cap_tok, int64_t recv_off, int64_t call,
+                          double timeout_s, torch::Tensor status, torch::Tensor out);
 void engram_touched_sqnorm(torch::Tensor acc_ptrs, torch::Tensor cnt_ptrs, torch::Tensor caps, int64_t dim,
                            torch::Tensor sq);
 void engram_clip_coef(torch::Tensor sq, double max_norm, torch::Tensor coef, torch::Tensor norm);
@@ -27,6 +33,11 @@ void engram_adam_touched(torch::Tensor p, torch::Tensor m, torch::Tensor v, torc
                          torch::Tensor list, torch::Tensor cnt, c10::optional<torch::Tensor> coef, double lr,
                          double beta1, double beta2, double eps, double wd, double bc1, double bc2, bool sr,
                          int64_t seed, int64_t step, int64_t table_id);
+void engram_adam_rows(std::vector<torch::Tensor> p, std::vector<torch::Tensor> m, std::vector<torch::Tensor> v,
+                      std::vector<torch::Tensor> acc, std::vector<torch::Tensor> pos, std::vector<torch::Tensor> list,
+                      std::vector<torch::Tensor> cnt, std::vector<int64_t> table_ids, std::vector<double> bc1,
+                      std::vector<double> bc2, std::vector<int64_t> steps, c10::optional<torch::Tensor> coef,
+                      double lr, double beta1, double beta2, double eps, double wd, bool sr, int64_t seed);
 void adam_dense(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, double lr, double beta1,
                 double beta2, double eps, double wd, double bc1, double bc2, double gscale, bool sr, int64_t seed,
                 int64_t step);
@@ -125,6 +136,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("engram_scatter_grad", &engram_scatter_grad);
   m.def("engram_push_grads", &engram_push_grads);
   m.def("engram_accumulate_grads", &engram_accumulate_grads);
+  m.def("engram_adam_rows", &engram_adam_rows);
+  m.def("engram_fetch_serve", &engram_fetch_serve);
+  m.def("engram_fetch_collect", &engram_fetch_collect);
   m.def("engram_touched_sqnorm", &engram_touched_sqnorm);
   m.def("engram_clip_coef", &engram_clip_coef);
   m.def("engram_adam_touched", &engram_adam_touched);

@@ -311,7 +311,7 @@ ME_DEVICE bool last_block(int* done) {
   return last;
 }
 
-// groups of 8 threads; one (token, table) event per group
+// a warp takes 32 (token, table) events at a time; each is then handled by a group of 8 lanes
 __global__ void __launch_bounds__(256) row_push_kernel(const __nv_bfloat16* __restrict__ g,
                                                        const int64_t* __restrict__ idx, int64_t N, RowTablesArgs a,
                                                        float scale) {
@@ -327,43 +327,70 @@ __global__ void __launch_bounds__(256) row_push_kernel(const __nv_bfloat16* __re
     }
   }
   __syncthreads();
-  const int sub = threadIdx.x & 7;
-  const unsigned gmask = 0xFFu << (threadIdx.x & 24);
+  const int lane = threadIdx.x & 31, sub = lane & 7, grp = lane >> 3;
+  const unsigned gmask = 0xFFu << (lane & 24);
   const int chunks = a.dim / 8;
   const int64_t events = N * a.n_tables;
-  const int64_t groups = (int64_t)gridDim.x * (blockDim.x >> 3);
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   int* outcnt = reinterpret_cast<int*>(mine + kXOut);
-  for (int64_t e = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3; !failed && e < events; e += groups) {
-    const int k = (int)(e % a.n_tables);
-    const int64_t n = e / a.n_tables;
-    const int64_t row = idx[(int64_t)k * N + n];
-    const int64_t pk = a.per[k];
-    const int owner = (int)(row / pk);
-    const int local = (int)(row - (int64_t)owner * pk);
-    const __nv_bfloat16* src = g + n * (int64_t)a.n_tables * a.dim + (int64_t)k * a.dim;
-    if (owner == a.me) {
-      const int t = a.me * a.n_tables + k;
-      int s = 0;
-      if (sub == 0)
-        s = claim_slot(reinterpret_cast<int*>(a.pos_ptrs[t]), reinterpret_cast<int*>(a.cnt_ptrs[t]),
-                       reinterpret_cast<int*>(a.list_ptrs[t]), a.caps[k], local, a.status, k);
-      s = __shfl_sync(gmask, s, 0, 8);
-      if (s <= 0) continue;
-      float* acc = reinterpret_cast<float*>(a.acc_ptrs[t]) + (int64_t)(s - 1) * a.dim;
-      for (int c = sub; c < chunks; c += 8)
-        add_chunk(acc + c * 8, *reinterpret_cast<const uint4*>(src + c * 8), scale);
-    } else {
-      int slot = 0;
-      if (sub == 0) slot = atomicAdd(outcnt + owner, 1);
-      slot = __shfl_sync(gmask, slot, 0, 8);
-      if (slot >= a.cap_e) {
-        if (sub == 0) report(a.status, ME_ERR_CAPACITY, 200 + owner);
-        continue;
+  for (int64_t base = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 32; !failed && base < events;
+       base += warps * 32) {
+    // one event per lane (table-major: the 32 row ids read are contiguous)
+    const int64_t e = base + lane;
+    int k = 0, owner = a.me, local = 0, slot = -1;
+    int64_t n = 0;
+    const bool valid = e < events;
+    if (valid) {
+      k = (int)(e / N);
+      n = e - (int64_t)k * N;
+      const int64_t row = idx[e];
+      const int64_t pk = a.per[k];
+      owner = (int)(row / pk);
+      local = (int)(row - (int64_t)owner * pk);
+    }
+    // entries for other owners: one counter atomic per owner per warp, then each lane's place
+    const bool remote = valid && owner != a.me;
+    const unsigned rmask = __ballot_sync(0xffffffffu, remote);
+    if (remote) {
+      const unsigned same = __match_any_sync(rmask, owner);
+      const int leader = __ffs(same) - 1;
+      int first = 0;
+      if (lane == leader) first = atomicAdd(outcnt + owner, __popc(same));
+      first = __shfl_sync(same, first, leader);
+      slot = first + __popc(same & ((1u << lane) - 1u));
+    }
+    // the 32 events, four at a time, 8 lanes each
+#pragma unroll 1
+    for (int j = 0; j < 8; ++j) {
+      const int src_lane = j * 4 + grp;
+      const bool v = __shfl_sync(0xffffffffu, valid, src_lane);
+      const int kk = __shfl_sync(0xffffffffu, k, src_lane);
+      const int oo = __shfl_sync(0xffffffffu, owner, src_lane);
+      const int lo = __shfl_sync(0xffffffffu, local, src_lane);
+      const int sl = __shfl_sync(0xffffffffu, slot, src_lane);
+      const int64_t nn = __shfl_sync(0xffffffffu, n, src_lane);
+      if (!v) continue;
+      const __nv_bfloat16* src = g + nn * (int64_t)a.n_tables * a.dim + (int64_t)kk * a.dim;
+      if (oo == a.me) {
+        const int t = a.me * a.n_tables + kk;
+        int s = 0;
+        if (sub == 0)
+          s = claim_slot(reinterpret_cast<int*>(a.pos_ptrs[t]), reinterpret_cast<int*>(a.cnt_ptrs[t]),
+                         reinterpret_cast<int*>(a.list_ptrs[t]), a.caps[kk], lo, a.status, kk);
+        s = __shfl_sync(gmask, s, 0, 8);
+        if (s <= 0) continue;
+        float* acc = reinterpret_cast<float*>(a.acc_ptrs[t]) + (int64_t)(s - 1) * a.dim;
+        for (int c = sub; c < chunks; c += 8) add_chunk(acc + c * 8, *reinterpret_cast<const uint4*>(src + c * 8), scale);
+      } else {
+        if (sl >= a.cap_e) {
+          if (sub == 0) report(a.status, ME_ERR_CAPACITY, 200 + oo);
+          continue;
+        }
+        uint8_t* region = reinterpret_cast<uint8_t*>(a.xbases[oo]) + kXRegions + (int64_t)a.me * a.region_bytes;
+        if (sub == 0) reinterpret_cast<int2*>(region)[sl] = make_int2(kk, lo);
+        uint4* dst = reinterpret_cast<uint4*>(region + a.rows_off + (int64_t)sl * a.dim * 2);
+        for (int c = sub; c < chunks; c += 8) dst[c] = *reinterpret_cast<const uint4*>(src + c * 8);
       }
-      uint8_t* region = reinterpret_cast<uint8_t*>(a.xbases[owner]) + kXRegions + (int64_t)a.me * a.region_bytes;
-      if (sub == 0) reinterpret_cast<int2*>(region)[slot] = make_int2(k, local);
-      uint4* dst = reinterpret_cast<uint4*>(region + a.rows_off + (int64_t)slot * a.dim * 2);
-      for (int c = sub; c < chunks; c += 8) dst[c] = *reinterpret_cast<const uint4*>(src + c * 8);
     }
   }
   if (last_block(reinterpret_cast<int*>(mine + kXDone))) {
@@ -430,6 +457,135 @@ __global__ void __launch_bounds__(256) row_accumulate_kernel(RowTablesArgs a, fl
   }
 }
 
+// ------------------------------------------------------------------------------ owner-served fetch
+// The multi-GPU forward fetch, inverted so that no GPU reads another GPU's tables: random reads
+// of peer memory are bound by address translation (a measured 18 ms for 1.57M random 128-byte
+// remote rows against 0.1 ms locally, 0.3 ms when the same rows sit in a small window). Each rank
+// publishes its lookups; each OWNER reads the rows it holds from its own tables (random local
+// reads) and writes them into the requester's receive buffer (one window of N x n_tables x dim
+// bf16 per requester), then the requester copies the buffer out. Two kernels per call, on every
+// rank, in the same order:
+//
+//   serve    prologue: this rank's lookups for `call` are in its fetch buffer and its receive
+//            buffer is free, so it tells every owner (ntok, then ready = call, release). Then, for
+//            every requester r (bounded wait for r's ready flag in this rank's buffer): scan r's
+//            lookups 32 at a time (coalesced), and for those this rank owns, copy the row from the
+//            local shard into r's receive buffer (16-byte stores, 8 lanes per row). The last block
+//            tells every requester done = call.
+//   collect  waits (bounded) until every owner's done flag reached `call`, then copies the
+//            receive buffer into the output (the output outlives the next call).
+//
+// Fetch buffer layout (same offsets on every rank):
+//   [0, 64)    ready[16] u32   requester r set it (at this owner) for the call it published
+//   [64, 128)  ntok[16]  i32   that requester's token count
+//   [128, 192) done[16]  u32   owner o set it (at this requester) when its rows are written
+//   [192, 200) blocks finished (serve)
+//   [256, ...) idx [n_tables, cap_tok] int64 of this rank's lookups, then recv [cap_tok, n_tables, row]
+//              (rows as stored in the tables, row16 16-byte units each)
+constexpr int kFReady = 0, kFNtok = 64, kFDone = 128, kFBlocks = 192, kFIdx = 256;
+
+struct FetchArgs {
+  const int64_t* fbases;  // [world] fetch buffer of every rank
+  const int64_t* wptrs;   // [world * n_tables] table base of (rank, table); only this rank's are read
+  const int64_t* per;     // [n_tables] rows per shard
+  int n_tables, row16, world, me;  // row16: 16-byte units per table row (dim x element size / 16)
+  int64_t cap_tok, recv_off;  // recv offset in the fetch buffer (16-byte aligned)
+  uint32_t call;
+  uint64_t timeout_ns;
+  int* status;
+};
+
+__global__ void __launch_bounds__(256) rows_serve_kernel(FetchArgs a, int ntok_me) {
+  __shared__ int failed;
+  __shared__ int ntok[16];
+  uint8_t* mine = reinterpret_cast<uint8_t*>(a.fbases[a.me]);
+  if (threadIdx.x == 0) failed = 0;
+  if ((int)threadIdx.x < a.world) {  // publish: this rank's lookups are ready at every owner
+    uint8_t* owner = reinterpret_cast<uint8_t*>(a.fbases[threadIdx.x]);
+    reinterpret_cast<volatile int*>(owner + kFNtok)[a.me] = ntok_me;
+    st_release_sys(reinterpret_cast<uint32_t*>(owner + kFReady) + a.me, a.call);
+  }
+  __syncthreads();
+  if ((int)threadIdx.x < a.world) {
+    const uint32_t* ready = reinterpret_cast<const uint32_t*>(mine + kFReady) + threadIdx.x;
+    if (wait_flag_geq(ready, a.call, a.timeout_ns)) {
+      ntok[threadIdx.x] = __ldcg(reinterpret_cast<const int*>(mine + kFNtok) + threadIdx.x);
+    } else {
+      report(a.status, ME_ERR_TIMEOUT, 400 + (int)threadIdx.x);
+      failed = 1;
+    }
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, sub = lane & 7, grp = lane >> 3;
+  const int chunks = a.row16;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t w0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  for (int r = 0; !failed && r < a.world; ++r) {
+    const int n = ntok[r];
+    const int64_t events = (int64_t)n * a.n_tables;
+    const uint8_t* req = reinterpret_cast<const uint8_t*>(a.fbases[r]);
+    const int64_t* ridx = reinterpret_cast<const int64_t*>(req + kFIdx);
+    uint4* recv = reinterpret_cast<uint4*>(const_cast<uint8_t*>(req) + a.recv_off);
+    for (int64_t base = w0 * 32; base < events; base += warps * 32) {
+      // one event per lane: table-major order, so the 32 lookups read are contiguous
+      const int64_t e = base + lane;
+      int k = 0, t = 0;
+      int64_t local = -1;
+      if (e < events) {
+        k = (int)(e / n);
+        t = (int)(e - (int64_t)k * n);
+        const int64_t row = __ldcg(ridx + (int64_t)k * a.cap_tok + t);
+        const int64_t pk = a.per[k];
+        if (row / pk == a.me) local = row - (int64_t)a.me * pk;
+      }
+      unsigned own = __ballot_sync(0xffffffffu, local >= 0);
+      while (own) {  // four owned events at a time, 8 lanes each
+        int pick = -1;
+        unsigned rest = own;
+        for (int q = 0; q <= grp && rest; ++q) {
+          pick = __ffs(rest) - 1;
+          rest &= rest - 1;
+          if (q < grp) pick = -1;
+        }
+        const int64_t lo = __shfl_sync(0xffffffffu, local, pick < 0 ? 0 : pick);
+        const int kk = __shfl_sync(0xffffffffu, k, pick < 0 ? 0 : pick);
+        const int tt = __shfl_sync(0xffffffffu, t, pick < 0 ? 0 : pick);
+        if (pick >= 0) {
+          const uint4* src = reinterpret_cast<const uint4*>(a.wptrs[a.me * a.n_tables + kk]) + lo * chunks;
+          uint4* dst = recv + ((int64_t)tt * a.n_tables + kk) * chunks;
+          for (int c = sub; c < chunks; c += 8) dst[c] = src[c];
+        }
+        for (int q = 0; q < 4 && own; ++q) own &= own - 1;  // the four handled this round
+      }
+    }
+  }
+  if (last_block(reinterpret_cast<int*>(mine + kFBlocks))) {
+    if ((int)threadIdx.x < a.world)
+      st_release_sys(reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(a.fbases[threadIdx.x]) + kFDone) + a.me,
+                     a.call);
+  }
+}
+
+// Wait until every owner wrote this call's rows, then copy n16 16-byte units of recv to out.
+__global__ void __launch_bounds__(256) rows_collect_kernel(FetchArgs a, int64_t n16, uint4* __restrict__ out) {
+  __shared__ int failed;
+  const uint8_t* mine = reinterpret_cast<const uint8_t*>(a.fbases[a.me]);
+  if (threadIdx.x == 0) failed = 0;
+  __syncthreads();
+  if ((int)threadIdx.x < a.world) {
+    const uint32_t* done = reinterpret_cast<const uint32_t*>(mine + kFDone) + threadIdx.x;
+    if (!wait_flag_geq(done, a.call, a.timeout_ns)) {
+      report(a.status, ME_ERR_TIMEOUT, 500 + (int)threadIdx.x);
+      failed = 1;
+    }
+  }
+  __syncthreads();
+  if (failed) return;
+  const uint4* recv = reinterpret_cast<const uint4*>(mine + a.recv_off);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = __ldcg(recv + i);
+}
+
 // Sum of squares of the touched rows' accumulated gradients (every row lives on exactly one
 // rank, so the sum over ranks is the global table norm^2): the first min(count, cap) slots of
 // each compact accumulator (holes are zero). counts are read on the device.
@@ -466,6 +622,161 @@ __global__ void clip_coef_kernel(const float* sq, float max_norm, float* coef, f
 // rounding (Philox4x32-10 keyed by seed/step, counter = row, column block). The
 // accumulator slot and the row's pos entry are cleared for the next step. One warp per slot
 // of the compact accumulator (holes, list = -1, are only cleared).
+// The touched-row AdamW of several tables in ONE launch (same semantics as adam_touched_kernel):
+// a group of 8 lanes per touched row, each lane 8 consecutive values per 16-byte chunk, so a
+// 64-wide bf16 row is one 16-byte load per lane of the weight and of the moment; 4 rows per warp
+// are in flight at once. Rounding bits: Philox4x32-10 keyed by (seed, step), counter (row, table,
+// chunk, 0/1): 16 bits per rounded value.
+constexpr int kAdamMaxTables = 32;
+
+struct AdamTable {
+  void* p;          // weights [rows, dim] (bf16 or fp32)
+  void* m;          // first moment, weight dtype (device or mapped pinned host memory)
+  float* v_row;     // rowwise: fp32 [rows], else nullptr
+  void* v_val;      // per-value second moment, weight dtype (when v_row is null)
+  float* acc;       // compact fp32 accumulator [cap, dim]
+  int* pos;         // row -> slot + 1
+  const int* list;  // slot -> row (-1: hole)
+  const int* cnt;   // slots handed out
+  int cap;
+  uint32_t table_id, step;
+  float bc1, bc2_sqrt;
+};
+
+struct AdamTables {
+  AdamTable t[kAdamMaxTables];
+  int n;
+};
+
+ME_DEVICE float group8_sum(float x, unsigned mask) {
+  x += __shfl_xor_sync(mask, x, 4, 8);
+  x += __shfl_xor_sync(mask, x, 2, 8);
+  x += __shfl_xor_sync(mask, x, 1, 8);
+  return x;
+}
+
+template <typename T>
+ME_DEVICE void load8(const T* src, float (&v)[8]) {
+  if constexpr (sizeof(T) == 2) {
+    BF16x8 x;
+    x.u = *reinterpret_cast<const uint4*>(src);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = bf2f(x.h[j]);
+  } else {
+    const float4 a = *reinterpret_cast<const float4*>(src), b = *reinterpret_cast<const float4*>(src + 4);
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+  }
+}
+
+// 8 values to T (stochastic rounding with 16 bits each of rnd[0..3] when sr and T is bf16)
+template <typename T>
+ME_DEVICE void store8(T* dst, const float (&v)[8], bool sr, const uint32_t (&rnd)[4]) {
+  if constexpr (sizeof(T) == 2) {
+    BF16x8 x;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t bits = (j & 1) ? (rnd[j >> 1] >> 16) : rnd[j >> 1];
+      x.h[j] = sr ? sr_bf16(v[j], bits) : f2bf(v[j]);
+    }
+    *reinterpret_cast<uint4*>(dst) = x.u;
+  } else {
+    *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(dst + 4) = make_float4(v[4], v[5], v[6], v[7]);
+  }
+}
+
+// CPL: 16-byte chunks per lane (dim <= 64 * CPL). The (table, slot) pairs of all tables form one
+// index space, split evenly over the groups of 8 lanes (prefix sums of the tables' counts).
+template <typename T, int CPL>
+__global__ void __launch_bounds__(256, 4) adam_rows_kernel(const __grid_constant__ AdamTables tabs, int dim,
+                                                        const float* coef_ptr, float lr, float beta1, float beta2,
+                                                        float eps, float wd, int sr, uint32_t seed) {
+  __shared__ int64_t first[kAdamMaxTables + 1];
+  if (threadIdx.x == 0) {
+    int64_t run = 0;
+    for (int k = 0; k < tabs.n; ++k) {
+      first[k] = run;
+      run += min(*tabs.t[k].cnt, tabs.t[k].cap);
+    }
+    first[tabs.n] = run;
+  }
+  __syncthreads();
+  const int sub = threadIdx.x & 7;
+  const unsigned gmask = 0xFFu << (threadIdx.x & 24);
+  const int64_t groups = (int64_t)gridDim.x * (blockDim.x >> 3);
+  const float coef = coef_ptr ? *coef_ptr : 1.f;
+  const int chunks = dim / 8;
+  int k = 0;
+  for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3; i < first[tabs.n]; i += groups) {
+    while (i >= first[k + 1]) ++k;  // i only grows, so the table index only moves forward
+    const AdamTable& t = tabs.t[k];
+    const int64_t r = i - first[k];
+    const int row = t.list[r];
+    float* a = t.acc + r * dim;
+    float g[CPL][8];
+    float gsq = 0.f;
+    bool nz = false;
+#pragma unroll
+    for (int q = 0; q < CPL; ++q) {
+      const int c = sub + 8 * q;
+      if (c < chunks) {
+        const float4 x = *reinterpret_cast<const float4*>(a + c * 8), y = *reinterpret_cast<const float4*>(a + c * 8 + 4);
+        const float raw[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          nz |= raw[j] != 0.f;
+          g[q][j] = raw[j] * coef;
+          gsq += g[q][j] * g[q][j];
+        }
+        *reinterpret_cast<float4*>(a + c * 8) = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(a + c * 8 + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    if (row < 0) continue;  // a hole: only cleared
+    if (sub == 0) t.pos[row] = 0;
+    if (!__any_sync(gmask, nz)) continue;  // lazy: an all-zero row is left as it is
+    float vr = 0.f;
+    if (t.v_row) vr = t.v_row[row] * beta2 + (1.f - beta2) * (group8_sum(gsq, gmask) / (float)dim);
+    T* P = reinterpret_cast<T*>(t.p);
+    T* M = reinterpret_cast<T*>(t.m);
+    T* VV = reinterpret_cast<T*>(t.v_val);
+#pragma unroll
+    for (int q = 0; q < CPL; ++q) {
+      const int c = sub + 8 * q;
+      if (c >= chunks) break;
+      const int64_t o = (int64_t)row * dim + c * 8;
+      float pw[8], mw[8], vv[8];
+      load8(P + o, pw);
+      load8(M + o, mw);
+      if (!t.v_row) load8(VV + o, vv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (wd != 0.f) pw[j] *= (1.f - lr * wd);
+        mw[j] = mw[j] * beta1 + (1.f - beta1) * g[q][j];
+        float denom;
+        if (t.v_row) {
+          denom = sqrtf(vr) / t.bc2_sqrt + eps;
+        } else {
+          vv[j] = vv[j] * beta2 + (1.f - beta2) * g[q][j] * g[q][j];
+          denom = sqrtf(vv[j]) / t.bc2_sqrt + eps;
+        }
+        pw[j] = pw[j] + (-lr / t.bc1) * mw[j] / denom;
+      }
+      const Philox4 r0 = philox4x32_10((uint32_t)row, t.table_id, (uint32_t)c, 0u, seed, t.step);
+      const Philox4 r1 = philox4x32_10((uint32_t)row, t.table_id, (uint32_t)c, 1u, seed, t.step);
+      const uint32_t rp[4] = {r0.c[0], r0.c[1], r0.c[2], r0.c[3]};
+      const uint32_t rm[4] = {r1.c[0], r1.c[1], r1.c[2], r1.c[3]};
+      store8(P + o, pw, sr != 0, rp);
+      store8(M + o, mw, sr != 0, rm);
+      if (!t.v_row) {
+        const uint32_t rv[4] = {rp[0] ^ rm[1], rp[1] ^ rm[2], rp[2] ^ rm[3], rp[3] ^ rm[0]};
+        store8(VV + o, vv, sr != 0, rv);
+      }
+    }
+    if (t.v_row && sub == 0) t.v_row[row] = vr;
+  }
+}
+
 template <typename Tp, typename Tm>
 __global__ void adam_touched_kernel(Tp* __restrict__ p, Tm* __restrict__ m, float* __restrict__ v_row,
                                     Tm* __restrict__ v_val, float* __restrict__ acc,
@@ -1135,6 +1446,57 @@ void engram_accumulate_grads(torch::Tensor acc_ptrs, torch::Tensor pos_ptrs, tor
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// The owner-served fetch (rows_serve_kernel, then rows_collect_kernel; RowStore.gather calls both
+// in turn): `idx` [n_tables, N] int64 must already be in this rank's fetch buffer (its idx
+// region, row stride cap_tok); `out` receives the N x n_tables rows in the tables' dtype.
+// Collective: every rank makes the same calls in the same order.
+static FetchArgs fetch_args(const torch::Tensor& fbases, const torch::Tensor& wptrs, const torch::Tensor& per,
+                            int64_t me, int64_t n_tables, int64_t row_bytes, int64_t cap_tok, int64_t recv_off,
+                            int64_t call, double timeout_s, torch::Tensor& status) {
+  const int world = (int)fbases.numel();
+  TORCH_CHECK(world >= 2 && world <= 16, "engram_fetch: 2..16 ranks");
+  TORCH_CHECK(row_bytes % 16 == 0 && recv_off % 16 == 0, "engram_fetch: 16-byte rows and receive buffer");
+  TORCH_CHECK(wptrs.numel() == world * n_tables && per.numel() == n_tables, "engram_fetch: tables");
+  FetchArgs a;
+  a.fbases = fbases.data_ptr<int64_t>();
+  a.wptrs = wptrs.data_ptr<int64_t>();
+  a.per = per.data_ptr<int64_t>();
+  a.n_tables = (int)n_tables;
+  a.row16 = (int)(row_bytes / 16);
+  a.world = world;
+  a.me = (int)me;
+  a.cap_tok = cap_tok;
+  a.recv_off = recv_off;
+  a.call = (uint32_t)call;
+  a.timeout_ns = (uint64_t)(timeout_s * 1e9);
+  a.status = status.data_ptr<int>();
+  return a;
+}
+
+void engram_fetch_serve(torch::Tensor fbases, torch::Tensor wptrs, torch::Tensor per, int64_t me, int64_t n_tables,
+                        int64_t row_bytes, int64_t ntok, int64_t cap_tok, int64_t recv_off, int64_t call,
+                        double timeout_s, torch::Tensor status) {
+  TORCH_CHECK(ntok >= 0 && ntok <= cap_tok, "engram_fetch: more tokens than the fetch buffer holds");
+  const at::cuda::CUDAGuard guard(status.device());
+  FetchArgs a = fetch_args(fbases, wptrs, per, me, n_tables, row_bytes, cap_tok, recv_off, call, timeout_s, status);
+  rows_serve_kernel<<<sm_count() * 8, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a, (int)ntok);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void engram_fetch_collect(torch::Tensor fbases, torch::Tensor wptrs, torch::Tensor per, int64_t me, int64_t n_tables,
+                          int64_t row_bytes, int64_t ntok, int64_t cap_tok, int64_t recv_off, int64_t call,
+                          double timeout_s, torch::Tensor status, torch::Tensor out) {
+  TORCH_CHECK(out.is_cuda() && out.is_contiguous() && (int64_t)out.nbytes() >= ntok * n_tables * row_bytes &&
+                  reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
+              "engram_fetch: out must hold the rows (16-byte aligned)");
+  const at::cuda::CUDAGuard guard(out.device());
+  FetchArgs a = fetch_args(fbases, wptrs, per, me, n_tables, row_bytes, cap_tok, recv_off, call, timeout_s, status);
+  const int64_t n16 = ntok * n_tables * (row_bytes / 16);
+  rows_collect_kernel<<<grid_for(std::max<int64_t>(1, n16), 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      a, n16, reinterpret_cast<uint4*>(out.data_ptr()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 // sq (fp32 [1], accumulated into) += sum over the local touched rows of acc^2.
 void engram_touched_sqnorm(torch::Tensor acc_ptrs, torch::Tensor cnt_ptrs, torch::Tensor caps, int64_t dim,
                            torch::Tensor sq) {
@@ -1149,6 +1511,84 @@ void engram_clip_coef(torch::Tensor sq, double max_norm, torch::Tensor coef, tor
   const at::cuda::CUDAGuard guard(sq.device());
   clip_coef_kernel<<<1, 1, 0, at::cuda::getCurrentCUDAStream()>>>(
       sq.data_ptr<float>(), (float)max_norm, coef.data_ptr<float>(), norm.data_ptr<float>());
+}
+
+// Touched-row AdamW of up to kAdamMaxTables tables of one row store in one launch per 32 tables.
+// Per table: weights p, moments m and v (v fp32 [rows] when row-wise), compact accumulator acc,
+// pos, list, cnt, and its own table id, bias corrections and step (rounding-bit key).
+void engram_adam_rows(std::vector<torch::Tensor> p, std::vector<torch::Tensor> m, std::vector<torch::Tensor> v,
+                      std::vector<torch::Tensor> acc, std::vector<torch::Tensor> pos, std::vector<torch::Tensor> list,
+                      std::vector<torch::Tensor> cnt, std::vector<int64_t> table_ids, std::vector<double> bc1,
+                      std::vector<double> bc2, std::vector<int64_t> steps, c10::optional<torch::Tensor> coef,
+                      double lr, double beta1, double beta2, double eps, double wd, bool sr, int64_t seed) {
+  const size_t n = p.size();
+  TORCH_CHECK(m.size() == n && v.size() == n && acc.size() == n && pos.size() == n && list.size() == n &&
+                  cnt.size() == n && table_ids.size() == n && bc1.size() == n && bc2.size() == n && steps.size() == n,
+              "engram_adam_rows: one entry per table in every list");
+  if (n == 0) return;
+  check_cuda(p[0], "p");
+  const at::cuda::CUDAGuard guard(p[0].device());
+  const auto dtype = p[0].scalar_type();
+  const int dim = (int)p[0].size(1);
+  TORCH_CHECK(dim % 8 == 0 && dim <= 256, "engram_adam_rows: dim must be a multiple of 8, at most 256");
+  TORCH_CHECK(dtype == torch::kBFloat16 || dtype == torch::kFloat32, "engram_adam_rows: bf16 or fp32 tables");
+  auto device_view = [](const torch::Tensor& t, const char* name) -> void* {
+    if (t.is_cuda()) return t.data_ptr();
+    TORCH_CHECK(t.is_pinned(), name, " must live on the GPU or in pinned host memory");
+    cudaPointerAttributes attr;
+    C10_CUDA_CHECK(cudaPointerGetAttributes(&attr, t.data_ptr()));
+    TORCH_CHECK(attr.type == cudaMemoryTypeHost && attr.devicePointer != nullptr, name,
+                ": pinned host memory without a device mapping");
+    return attr.devicePointer;
+  };
+  const float* cp = coef.has_value() ? coef->data_ptr<float>() : nullptr;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  for (size_t a = 0; a < n; a += kAdamMaxTables) {
+    AdamTables tabs{};
+    tabs.n = (int)std::min<size_t>(kAdamMaxTables, n - a);
+    for (int i = 0; i < tabs.n; ++i) {
+      const size_t k = a + i;
+      TORCH_CHECK(p[k].scalar_type() == dtype && p[k].size(1) == dim && p[k].is_contiguous(),
+                  "engram_adam_rows: tables of one dtype and width");
+      TORCH_CHECK(m[k].scalar_type() == dtype && m[k].numel() == p[k].numel(), "engram_adam_rows: exp_avg");
+      TORCH_CHECK(acc[k].dim() == 2 && acc[k].size(1) == dim && pos[k].numel() >= p[k].size(0) &&
+                      list[k].numel() >= acc[k].size(0),
+                  "engram_adam_rows: compact accumulator shapes");
+      const bool rowwise = v[k].dim() == 1;
+      TORCH_CHECK(rowwise ? (v[k].is_cuda() && v[k].scalar_type() == torch::kFloat32) : v[k].scalar_type() == dtype,
+                  "engram_adam_rows: exp_avg_sq");
+      AdamTable& t = tabs.t[i];
+      t.p = p[k].data_ptr();
+      t.m = device_view(m[k], "exp_avg");
+      t.v_row = rowwise ? v[k].data_ptr<float>() : nullptr;
+      t.v_val = rowwise ? nullptr : device_view(v[k], "exp_avg_sq");
+      t.acc = acc[k].data_ptr<float>();
+      t.pos = pos[k].data_ptr<int>();
+      t.list = list[k].data_ptr<int>();
+      t.cnt = cnt[k].data_ptr<int>();
+      t.cap = (int)acc[k].size(0);
+      t.table_id = (uint32_t)table_ids[k];
+      t.step = (uint32_t)steps[k];
+      t.bc1 = (float)bc1[k];
+      t.bc2_sqrt = (float)std::sqrt(bc2[k]);
+    }
+    const int grid = sm_count() * 8;
+    auto run = [&](auto type_tag, auto cpl_tag) {
+      using T = decltype(type_tag);
+      constexpr int CPL = decltype(cpl_tag)::value;
+      adam_rows_kernel<T, CPL><<<grid, 256, 0, stream>>>(tabs, dim, cp, (float)lr, (float)beta1, (float)beta2,
+                                                          (float)eps, (float)wd, sr && sizeof(T) == 2 ? 1 : 0,
+                                                          (uint32_t)seed);
+    };
+    auto by_width = [&](auto type_tag) {
+      if (dim <= 64) run(type_tag, std::integral_constant<int, 1>{});
+      else if (dim <= 128) run(type_tag, std::integral_constant<int, 2>{});
+      else run(type_tag, std::integral_constant<int, 4>{});
+    };
+    if (dtype == torch::kBFloat16) by_width(__nv_bfloat16{});
+    else by_width(float{});
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
 }
 
 void engram_adam_touched(torch::Tensor p, torch::Tensor m, torch::Tensor v, torch::Tensor acc,

@@ -17,8 +17,11 @@ accumulator cannot overflow, and it replaces a dense fp32 accumulator as large a
 (2x the bf16 table) with a few hundred MB. Without a capacity (inference, tests) cap_k = per_k.
 
 With world > 1 the buffer is a SymmBuffer (CUDA IPC over NVLink); kernels index it
-through device tables of per-rank addresses. Row gradients return to their owners through a
-second symmetric buffer of per-source inbox regions (no remote atomics; see push_grads). The optimizer moments live in ordinary local
+through device tables of per-rank addresses. With a capacity, the forward fetch is served by
+the owners (each owner reads its rows locally and writes them into the requester's receive
+buffer: random reads of peer memory are slow, writes into one window are not) and row
+gradients return through per-source inbox regions (no remote atomics); see gather and
+push_grads. The optimizer moments live in ordinary local
 memory (only the owner touches them).
 """
 import torch
@@ -143,6 +146,17 @@ class RowStore:
         self.xbases = torch.tensor(self.x.ptrs, dtype=torch.int64, device=self.device)
         self.x_calls = 0
         self.x_timeout = float(os.environ.get("MICRO_ENGRAM_PEER_TIMEOUT_S", "10"))
+        # the owner-served forward fetch: this rank's lookups, then the rows its owners send it
+        esz = torch.empty((), dtype=self.dtype).element_size()
+        self.f_row_bytes = self.dim * esz
+        self.f_recv_off = _align(256 + self.nt * self.x_tokens * 8)
+        self.f = SymmBuffer(self.f_recv_off + self.x_tokens * self.nt * self.f_row_bytes, self.device, group)
+        self.f.view(0, (64,), torch.int32).zero_()
+        self.f_idx = self.f.view(256, (self.nt, self.x_tokens), torch.int64)
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=group)
+        self.fbases = torch.tensor(self.f.ptrs, dtype=torch.int64, device=self.device)
+        self.f_calls = 0
 
     # ---------------------------------------------------------------- views
     def shard(self, k):
@@ -167,7 +181,20 @@ class RowStore:
 
     # ---------------------------------------------------------------- kernels
     def gather(self, idx, out_dtype):
-        """idx [n_tables, N] global rows -> mem [N, n_tables*dim] from the owners' shards."""
+        """idx [n_tables, N] global rows -> mem [N, n_tables*dim] from the owners' shards.
+
+        world > 1 with a fetch buffer: the owners serve the rows (engram_fetch; collective, every
+        rank calls it in the same order); otherwise one kernel reads them where they live."""
+        n = idx.shape[1]
+        if getattr(self, "x", None) is not None and n <= self.x_tokens:
+            self.f_calls += 1
+            self.f_idx[:, :n].copy_(idx)
+            rows = torch.empty(n, self.nt * self.dim, dtype=self.dtype, device=self.device)
+            args = (self.fbases, self.w_ptrs, self.per_t, self.rank, self.nt, self.f_row_bytes, n, self.x_tokens,
+                    self.f_recv_off, self.f_calls, self.x_timeout, self.status)
+            native().engram_fetch_serve(*args)
+            native().engram_fetch_collect(*args, rows)
+            return rows if rows.dtype == out_dtype else rows.to(out_dtype)
         src = 0 if self.dtype == torch.bfloat16 else 1
         return native().engram_gather(idx, self.w_ptrs, self.per_t, self.world, self.dim, src, out_dtype,
                                       self.status)
@@ -222,4 +249,5 @@ class RowStore:
             self.buf = None
         if getattr(self, "x", None) is not None:
             self.x.close()
+            self.f.close()
             self.x = None

@@ -477,3 +477,49 @@ def test_attention_fwd_tcgen05_rescale(D, Hq, Hk, window):
     ob, _ = attention_ref(q, k, v, ds, window, 1.0)
     noise_floor_check(o, o32, ob.to(torch.bfloat16), rel=2.0, eps=2e-3, name="attn tc out (rescale)")
     torch.testing.assert_close(lse, lse32, rtol=1e-3, atol=1e-2)
+
+
+@cuda
+@pytest.mark.parametrize("dtype,rowwise", [(torch.float32, True), (torch.bfloat16, True), (torch.bfloat16, False)])
+def test_adam_rows_batched_matches_per_table(dtype, rowwise):
+    """The batched touched-row AdamW (all tables of a store in one launch, 8 lanes per row) against
+    the per-table kernel, without stochastic rounding: same updates up to the order of the
+    row-mean reduction; accumulators, pos entries cleared in both."""
+    from micro_engram_fork_b200 import native
+    from micro_engram_fork_b200.ops.engram import adam_touched
+    from micro_engram_fork_b200.parallel.row_store import RowStore
+
+    torch.manual_seed(3)
+    rows, dim, n = [1500, 2600, 999], 64, 800
+    idx = torch.stack([torch.randint(0, r, (n,)) for r in rows]).to(_dev())
+    g = torch.randn(n, len(rows) * dim, device=_dev()).to(dtype)
+    results = []
+    for batched in (False, True):
+        st = RowStore(rows, dim, dtype, 0, 1, _dev(), capacity=n)
+        gen = torch.Generator().manual_seed(1)
+        for k in range(len(rows)):
+            st.shard(k).copy_(torch.randn(rows[k], dim, generator=gen) * 0.02)
+        ms = [torch.zeros(r, dim, device=_dev(), dtype=dtype) for r in rows]
+        vs = [torch.zeros(r, device=_dev()) if rowwise else torch.zeros(r, dim, device=_dev(), dtype=dtype)
+              for r in rows]
+        for step in (1, 2):
+            st.push_grads(g, idx, 1.0)
+            bc1, bc2 = 1 - 0.9 ** step, 1 - 0.999 ** step
+            if batched:
+                native().engram_adam_rows([st.shard(k) for k in range(3)], ms, vs, st.acc, st.pos, st.list, st.count,
+                                          [0, 1, 2], [bc1] * 3, [bc2] * 3, [step] * 3, None, 1e-2, 0.9, 0.999, 1e-8,
+                                          0.01, False, 5)
+            else:
+                for k in range(3):
+                    adam_touched(st.shard(k), ms[k], vs[k], st.acc[k], st.pos[k], st.list[k], st.count[k], None, 1e-2,
+                                 0.9, 0.999, 1e-8, 0.01, bc1, bc2, False, 5, step, k)
+            for c in st.count:
+                c.zero_()
+        torch.cuda.synchronize()
+        results.append(([st.shard(k).float().cpu() for k in range(3)], [m.float().cpu() for m in ms],
+                        [v.float().cpu() for v in vs]))
+        assert all(float(a.abs().sum()) == 0.0 for a in st.acc) and all(int(p.abs().sum()) == 0 for p in st.pos)
+    tol = 1e-6 if dtype == torch.float32 else 1e-2
+    for a_list, b_list in zip(results[0], results[1]):
+        for a, b in zip(a_list, b_list):
+            torch.testing.assert_close(b, a, rtol=tol, atol=tol * float(a.abs().max()) + 1e-12)

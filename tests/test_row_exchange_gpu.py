@@ -114,3 +114,73 @@ def test_row_exchange_two_emulated_ranks():
                               r0.region, r0.rows_off, 3, 0.2, r0.status)
     torch.cuda.synchronize()
     assert r0.status.tolist() == [1, 301]  # ME_ERR_TIMEOUT, waiting on rank 1
+
+
+_F_READY, _F_NTOK, _F_IDX = 0, 64, 256
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+def test_owner_served_fetch_two_emulated_ranks():
+    """engram_fetch_serve / engram_fetch_collect with two ranks emulated on one GPU: every owner
+    copies the rows it holds into each requester's receive buffer; the oracle is indexing the
+    full tables. The ready flags and token counts are published by the test before the launches
+    (as each rank's serve kernel does for itself), and the launch order serve(0), serve(1),
+    collect(0), collect(1) makes every wait one that an earlier launch satisfied. A third call
+    in which rank 1 never serves must end rank 0's collect with a timeout status."""
+    from micro_engram_fork_b200 import native
+
+    C = native()
+    dev = torch.device("cuda", 0)
+    per = [-(-r // WORLD) for r in ROWS]
+    g = torch.Generator(device=dev).manual_seed(4)
+    full = [torch.randn(r, DIM, device=dev, generator=g).to(torch.bfloat16) for r in ROWS]
+    shards = []  # per rank: its tables, padded to `per` rows
+    for rk in range(WORLD):
+        shards.append([torch.zeros(p, DIM, device=dev, dtype=torch.bfloat16) for p in per])
+        for k, t in enumerate(full):
+            part = t[rk * per[k]:(rk + 1) * per[k]]
+            shards[rk][k][:part.shape[0]] = part
+    cap, row_bytes = N, DIM * 2
+    recv_off = _align(_F_IDX + len(ROWS) * cap * 8)
+    bufs = [torch.zeros(recv_off + cap * len(ROWS) * row_bytes, dtype=torch.uint8, device=dev) for _ in range(WORLD)]
+    fb = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device=dev)
+    wp = torch.tensor([t.data_ptr() for rk in range(WORLD) for t in shards[rk]], dtype=torch.int64, device=dev)
+    per_t = torch.tensor(per, dtype=torch.int64, device=dev)
+    status = [torch.zeros(2, dtype=torch.int32, device=dev) for _ in range(WORLD)]
+
+    def publish(call, ntoks):
+        for o in range(WORLD):
+            words = bufs[o][:256].view(torch.int32)
+            for r in range(WORLD):
+                words[_F_NTOK // 4 + r] = ntoks[r]
+                words[_F_READY // 4 + r] = call
+
+    def args(me, n, call, timeout=5.0):
+        return (fb, wp, per_t, me, len(ROWS), row_bytes, n, cap, recv_off, call, timeout, status[me])
+
+    for call, ntoks in ((1, (N, N - 123)), (2, (N - 7, N))):
+        idxs = []
+        for me in range(WORLD):
+            gi = torch.Generator().manual_seed(10 * call + me)
+            idx = torch.stack([torch.randint(0, r, (ntoks[me],), generator=gi) for r in ROWS]).to(dev)
+            bufs[me][_F_IDX:_F_IDX + len(ROWS) * cap * 8].view(torch.int64).view(len(ROWS), cap)[:, :ntoks[me]] = idx
+            idxs.append(idx)
+        publish(call, ntoks)
+        outs = [torch.full((ntoks[me], len(ROWS) * DIM), float("nan"), device=dev, dtype=torch.bfloat16)
+                for me in range(WORLD)]
+        for me in range(WORLD):
+            C.engram_fetch_serve(*args(me, ntoks[me], call))
+        for me in range(WORLD):
+            C.engram_fetch_collect(*args(me, ntoks[me], call), outs[me])
+        torch.cuda.synchronize()
+        for me in range(WORLD):
+            assert status[me].tolist() == [0, 0]
+            want = torch.cat([full[k][idxs[me][k]] for k in range(len(ROWS))], dim=1)
+            assert torch.equal(outs[me], want), f"call {call} rank {me}"
+    # call 3: rank 1 never serves its rows, so rank 0's collect must time out and say so
+    publish(3, (N, N))
+    out = torch.empty(N, len(ROWS) * DIM, device=dev, dtype=torch.bfloat16)
+    C.engram_fetch_serve(*args(0, N, 3))
+    C.engram_fetch_collect(*args(0, N, 3, timeout=0.2), out)
+    torch.cuda.synchronize()
+    assert status[0].tolist() == [1, 501]  # ME_ERR_TIMEOUT, waiting on rank 1's rows
