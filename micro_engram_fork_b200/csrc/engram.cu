@@ -688,7 +688,7 @@ ME_DEVICE void store8(T* dst, const float (&v)[8], bool sr, const uint32_t (&rnd
 // CPL: 16-byte chunks per lane (dim <= 64 * CPL). The (table, slot) pairs of all tables form one
 // index space, split evenly over the groups of 8 lanes (prefix sums of the tables' counts).
 template <typename T, int CPL>
-__global__ void __launch_bounds__(256, 4) adam_rows_kernel(const __grid_constant__ AdamTables tabs, int dim,
+__global__ void __launch_bounds__(256, CPL == 1 ? 4 : 2) adam_rows_kernel(const __grid_constant__ AdamTables tabs, int dim,
                                                         const float* coef_ptr, float lr, float beta1, float beta2,
                                                         float eps, float wd, int sr, uint32_t seed) {
   __shared__ int64_t first[kAdamMaxTables + 1];
@@ -713,19 +713,39 @@ __global__ void __launch_bounds__(256, 4) adam_rows_kernel(const __grid_constant
     const int64_t r = i - first[k];
     const int row = t.list[r];
     float* a = t.acc + r * dim;
-    float g[CPL][8];
+    T* P = reinterpret_cast<T*>(t.p);
+    T* M = reinterpret_cast<T*>(t.m);
+    T* VV = reinterpret_cast<T*>(t.v_val);
+    // every load of the row first (accumulator slot, weights, moments), then the stores: the loads
+    // are independent once the row is known, so they are in flight together
+    float g[CPL][8], pw[CPL][8], mw[CPL][8], vv[CPL][8];
+    float v_old = 0.f;
+#pragma unroll
+    for (int q = 0; q < CPL; ++q) {
+      const int c = sub + 8 * q;
+      if (c < chunks) {
+        const float4 x = *reinterpret_cast<const float4*>(a + c * 8), y = *reinterpret_cast<const float4*>(a + c * 8 + 4);
+        g[q][0] = x.x, g[q][1] = x.y, g[q][2] = x.z, g[q][3] = x.w;
+        g[q][4] = y.x, g[q][5] = y.y, g[q][6] = y.z, g[q][7] = y.w;
+        if (row >= 0) {
+          const int64_t o = (int64_t)row * dim + c * 8;
+          load8(P + o, pw[q]);
+          load8(M + o, mw[q]);
+          if (!t.v_row) load8(VV + o, vv[q]);
+        }
+      }
+    }
+    if (row >= 0 && t.v_row) v_old = t.v_row[row];
     float gsq = 0.f;
     bool nz = false;
 #pragma unroll
     for (int q = 0; q < CPL; ++q) {
       const int c = sub + 8 * q;
       if (c < chunks) {
-        const float4 x = *reinterpret_cast<const float4*>(a + c * 8), y = *reinterpret_cast<const float4*>(a + c * 8 + 4);
-        const float raw[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          nz |= raw[j] != 0.f;
-          g[q][j] = raw[j] * coef;
+          nz |= g[q][j] != 0.f;
+          g[q][j] *= coef;
           gsq += g[q][j] * g[q][j];
         }
         *reinterpret_cast<float4*>(a + c * 8) = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -736,41 +756,34 @@ __global__ void __launch_bounds__(256, 4) adam_rows_kernel(const __grid_constant
     if (sub == 0) t.pos[row] = 0;
     if (!__any_sync(gmask, nz)) continue;  // lazy: an all-zero row is left as it is
     float vr = 0.f;
-    if (t.v_row) vr = t.v_row[row] * beta2 + (1.f - beta2) * (group8_sum(gsq, gmask) / (float)dim);
-    T* P = reinterpret_cast<T*>(t.p);
-    T* M = reinterpret_cast<T*>(t.m);
-    T* VV = reinterpret_cast<T*>(t.v_val);
+    if (t.v_row) vr = v_old * beta2 + (1.f - beta2) * (group8_sum(gsq, gmask) / (float)dim);
 #pragma unroll
     for (int q = 0; q < CPL; ++q) {
       const int c = sub + 8 * q;
       if (c >= chunks) break;
       const int64_t o = (int64_t)row * dim + c * 8;
-      float pw[8], mw[8], vv[8];
-      load8(P + o, pw);
-      load8(M + o, mw);
-      if (!t.v_row) load8(VV + o, vv);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        if (wd != 0.f) pw[j] *= (1.f - lr * wd);
-        mw[j] = mw[j] * beta1 + (1.f - beta1) * g[q][j];
+        if (wd != 0.f) pw[q][j] *= (1.f - lr * wd);
+        mw[q][j] = mw[q][j] * beta1 + (1.f - beta1) * g[q][j];
         float denom;
         if (t.v_row) {
           denom = sqrtf(vr) / t.bc2_sqrt + eps;
         } else {
-          vv[j] = vv[j] * beta2 + (1.f - beta2) * g[q][j] * g[q][j];
-          denom = sqrtf(vv[j]) / t.bc2_sqrt + eps;
+          vv[q][j] = vv[q][j] * beta2 + (1.f - beta2) * g[q][j] * g[q][j];
+          denom = sqrtf(vv[q][j]) / t.bc2_sqrt + eps;
         }
-        pw[j] = pw[j] + (-lr / t.bc1) * mw[j] / denom;
+        pw[q][j] = pw[q][j] + (-lr / t.bc1) * mw[q][j] / denom;
       }
       const Philox4 r0 = philox4x32_10((uint32_t)row, t.table_id, (uint32_t)c, 0u, seed, t.step);
       const Philox4 r1 = philox4x32_10((uint32_t)row, t.table_id, (uint32_t)c, 1u, seed, t.step);
       const uint32_t rp[4] = {r0.c[0], r0.c[1], r0.c[2], r0.c[3]};
       const uint32_t rm[4] = {r1.c[0], r1.c[1], r1.c[2], r1.c[3]};
-      store8(P + o, pw, sr != 0, rp);
-      store8(M + o, mw, sr != 0, rm);
+      store8(P + o, pw[q], sr != 0, rp);
+      store8(M + o, mw[q], sr != 0, rm);
       if (!t.v_row) {
         const uint32_t rv[4] = {rp[0] ^ rm[1], rp[1] ^ rm[2], rp[2] ^ rm[3], rp[3] ^ rm[0]};
-        store8(VV + o, vv, sr != 0, rv);
+        store8(VV + o, vv[q], sr != 0, rv);
       }
     }
     if (t.v_row && sub == 0) t.v_row[row] = vr;

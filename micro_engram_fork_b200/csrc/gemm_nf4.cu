@@ -5,6 +5,11 @@
 //
 // The weight W is [rows, cols] with cols % 64 == 0 (blocks of 64 along each row), stored as
 // codes uint8 [rows * cols / 2] (low nibble first) and absmax fp32 [rows * cols / 64].
+//
+// Use: small M. Every 256-row M tile dequantises its B tiles again and the 16-level lookup costs
+// several instructions per weight, so at training-size M (8192 tokens) the dequantising warps,
+// not the tensor cores, set the pace; the decoder then expands a layer once into bf16 scratch
+// (models/nf4.py) and runs the bf16 GEMM instead.
 #include "gemm_kernel.cuh"
 
 using namespace me::gemm;

@@ -367,7 +367,7 @@ def _materialize(layer, direction=1, force=False):
     if getattr(layer, "_nf4", None) is not None:
         from .nf4 import materialize
 
-        materialize(layer, force)
+        materialize(layer, force, direction)
     sb = getattr(layer, "_sharded", None)
     if sb is not None:
         sb.materialize(layer, direction)

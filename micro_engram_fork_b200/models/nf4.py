@@ -57,10 +57,14 @@ def dequant_into(codes, absmax, out):
 # ------------------------------------------------------------------ model integration
 def fused_enabled(device):
     """Whether CUDA layers run their projections on the GEMM that dequantises NF4 in-kernel
-    (MICRO_ENGRAM_NF4_FUSED=0 falls back to expanding into the shared bf16 buffer first)."""
+    (MICRO_ENGRAM_NF4_FUSED=1). Off by default: with training-size M (8192 tokens) every 256-row
+    M tile dequantises the same weights again and the 16-level lookup costs several instructions
+    per weight, far more than the tensor cores' appetite, so the layer is expanded once instead
+    (into a double-buffered scratch, the next layer on a side stream; see Scratch). The in-kernel
+    form pays off for small M (a few hundred tokens), where one pass over the weights dominates."""
     import os
 
-    return device.type == "cuda" and os.environ.get("MICRO_ENGRAM_NF4_FUSED", "1") != "0"
+    return device.type == "cuda" and os.environ.get("MICRO_ENGRAM_NF4_FUSED", "0") == "1"
 
 
 class NF4Weights:
@@ -89,23 +93,38 @@ class NF4Weights:
 
 
 class Scratch:
-    """One expansion buffer per device (the weights' dtype, bf16 in training), big enough for the
-    largest layer."""
+    """Expansion buffers per device (the weights' dtype, bf16 in training), each big enough for
+    the largest layer. On CUDA there are two: a layer runs out of one while the next layer (in the
+    direction of travel: +1 forward, -1 backward) is expanded into the other on a side stream, so
+    the expansion overlaps the running layer's GEMMs. `owner[slot]` is the layer a slot holds
+    (a layer never runs on another layer's weights) and `ready[slot]` the event of an expansion
+    still pending on the side stream."""
 
     def __init__(self, device, numel, dtype=torch.bfloat16):
-        self.buf = torch.empty(numel, dtype=dtype, device=device)
-        self.owner = None
+        slots = 2 if device.type == "cuda" else 1
+        self.bufs = [torch.empty(numel, dtype=dtype, device=device) for _ in range(slots)]
+        self.owner = [None] * slots
+        self.ready = [None] * slots
+        self.layers = []  # every quantized layer, in model order
+        self.stream = torch.cuda.Stream(device) if device.type == "cuda" else None
 
-    def views(self, shapes):
+    @property
+    def buf(self):
+        return self.bufs[0]
+
+    def views(self, shapes, slot=0):
         out, off = {}, 0
         for name in NF4Weights.NAMES:
             n = 1
             for s in shapes[name]:
                 n *= s
             off = (off + 7) // 8 * 8  # 16-byte aligned starts for the vector kernel
-            out[name] = self.buf[off:off + n].view(shapes[name])
+            out[name] = self.bufs[slot][off:off + n].view(shapes[name])
             off += n
         return out
+
+    def slot_of(self, layer):
+        return next((i for i, o in enumerate(self.owner) if o is layer), None)
 
 
 def _weights(layer):
@@ -116,17 +135,57 @@ def _need(shapes):
     return sum((-(-s[0] * s[1] // 8)) * 8 + 8 for s in shapes.values())
 
 
-def materialize(layer, force=False):
-    """Expand this layer's NF4 weights into the shared buffer (no-op if it already holds them,
-    or if the layer's GEMMs read the NF4 codes themselves, unless `force`: the PyTorch path)."""
-    nf = getattr(layer, "_nf4", None)
-    if nf is None or (nf.fused and not force) or nf.scratch.owner is layer:
-        return
-    views = nf.scratch.views(nf.shapes)
-    for name in NF4Weights.NAMES:
+def _link(layer, views):
+    layer.qkv_weight = views["qkv"]
+    layer.gate_up_weight = views["gate_up"]
+    layer.self_attn.o_proj.weight.data = views["o"]
+    layer.mlp.down_proj.weight.data = views["down"]
+    layer._relink()
+
+
+def _expand(nf, layer, slot):
+    for name, view in nf.scratch.views(nf.shapes, slot).items():
         codes, absmax = nf.packed[name]
-        dequant_into(codes, absmax, views[name])
-    nf.scratch.owner = layer
+        dequant_into(codes, absmax, view)
+    nf.scratch.owner[slot] = layer
+
+
+def materialize(layer, force=False, direction=1):
+    """Make this layer's bf16 weights readable (its weight attributes point at the slot that holds
+    them), expanding them now unless a prefetch already did; then start expanding the next layer
+    in `direction` into the other slot on the side stream. No-op when the layer's GEMMs read the
+    NF4 codes themselves, unless `force` (the PyTorch path)."""
+    nf = getattr(layer, "_nf4", None)
+    if nf is None or (nf.fused and not force):
+        return
+    sc = nf.scratch
+    slot = sc.slot_of(layer)
+    if slot is None:  # not prefetched: expand in order on the current stream
+        slot = 1 if len(sc.bufs) > 1 and sc.ready[1] is None and sc.owner[0] is not None else 0
+        if sc.ready[slot] is not None:  # a prefetch into this slot is still pending
+            torch.cuda.current_stream().wait_event(sc.ready[slot])
+        _expand(nf, layer, slot)
+        sc.ready[slot] = None
+    elif sc.ready[slot] is not None:
+        torch.cuda.current_stream().wait_event(sc.ready[slot])
+        sc.ready[slot] = None
+    _link(layer, sc.views(nf.shapes, slot))
+    if sc.stream is None or len(sc.bufs) < 2:
+        return
+    nxt_i = nf.index + direction
+    if not 0 <= nxt_i < len(sc.layers):
+        return
+    nxt, other = sc.layers[nxt_i], 1 - slot
+    if sc.owner[other] is nxt:
+        return
+    # every kernel of the layer that last used the other slot is queued on the current stream
+    # before this point; the side stream starts after them
+    sc.stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(sc.stream):
+        _expand(nxt._nf4, nxt, other)
+        ev = torch.cuda.Event()
+        ev.record(sc.stream)
+    sc.ready[other] = ev
 
 
 def quantize_model_nf4(model):
@@ -146,20 +205,16 @@ def quantize_model_nf4(model):
                 raise ValueError(f"NF4 needs weights with a multiple of 64 elements; {n} is {shp}")
     scratch = Scratch(dev, max(_need(s) for s in shapes), layers[0].qkv_weight.dtype)
     stored = freed = 0
-    for layer, s in zip(layers, shapes):
+    for i, (layer, s) in enumerate(zip(layers, shapes)):
         nf = NF4Weights(layer, scratch)
+        nf.index = i
         stored += nf.nbytes()
         freed += sum(w.numel() * w.element_size() for w in _weights(layer))
-        views = scratch.views(s)
-        # the layer's weight attributes now alias the shared buffer; _relink keeps q/k/v and
+        # the layer's weight attributes now alias a shared buffer; _relink keeps q/k/v and
         # gate/up views into the fused buffers
-        layer.qkv_weight = views["qkv"]
-        layer.gate_up_weight = views["gate_up"]
-        layer.self_attn.o_proj.weight.data = views["o"]
-        layer.mlp.down_proj.weight.data = views["down"]
-        layer._relink()
+        _link(layer, scratch.views(s))
         layer._nf4 = nf
-    scratch.owner = None
+        scratch.layers.append(layer)
     if dev.type == "cuda":
         torch.cuda.empty_cache()
     return stored, freed

@@ -271,8 +271,16 @@ def case_rows(C, dev, it, pk, small=False):
         for c in store.count:
             c.zero_()
 
-    ms = _time(push_and_step, it)
-    r.update(_hbm("scatter+adam", nt * N * (8 + dim * 2) + uniq * dim * (4 + 4 * 2 + 4), ms, pk))
+    def push_and_batched_step():
+        store.push_grads(g, idx, 1.0)
+        C.engram_adam_rows(store.weights, m, v, store.acc, store.pos, store.list, store.count, list(range(nt)),
+                           [0.1] * nt, [0.001] * nt, [1] * nt, None, 1e-3, 0.9, 0.999, 1e-8, 0.0, True, 0)
+        for c in store.count:
+            c.zero_()
+
+    moved = nt * N * (8 + dim * 2) + uniq * dim * (4 + 4 * 2 + 4)
+    r.update(_hbm("scatter+adam (one launch per table)", moved, _time(push_and_step, it), pk))
+    r.update(_hbm("scatter+adam_rows (all tables, one launch)", moved, _time(push_and_batched_step, it), pk))
     r["unique_rows"] = uniq
     r["lookups"] = nt * N
     return r
