@@ -4,7 +4,7 @@ events (warm-up, synchronize on both sides) and reported against the measured ro
 figures otherwise). Also the workload that the committed ncu summaries in profiles/ capture.
 
   python -m micro_engram_fork_b200.utils.kernel_bench [--case all|gemm|attn_fwd|attn_bwd|gate|ce|qkv|geglu|rows|
-                                                       norms|ce_bwd|nf4] [--iters N] [--small]
+                                                       norms|ce_bwd|nf4|ce_gemm] [--iters N] [--small]
 """
 import argparse
 import json
@@ -177,6 +177,24 @@ def case_ce(C, dev, it, pk):
                                    "frac_of_hbm": round(nbytes / ms / 1e6 / pk["hbm_gbs"], 3)}}
 
 
+def case_ce_gemm(C, dev, it, pk):
+    """The loss's logits GEMM of one 2048-token chunk against 262144 tied-head rows (d 5376) with the
+    softcapped-CE epilogue (per-tile partial sums and the target logit; logits kept for the
+    backward), against the plain GEMM of the same shape."""
+    H = torch.randn(2048, 5376, device=dev).to(torch.bfloat16)
+    E = (torch.randn(262144, 5376, device=dev) * 0.02).to(torch.bfloat16)
+    lab = torch.randint(0, 262144, (2048,), device=dev)
+    flops = 2 * 2048 * 262144 * 5376
+    r = {}
+    for name, fn in (("gemm_ce (softcap 30, logits kept)", lambda: C.gemm_ce(H, E, lab, 0, 30.0, True, 262144)),
+                     ("gemm_ce (softcap 30, no logits)", lambda: C.gemm_ce(H, E, lab, 0, 30.0, False, 262144)),
+                     ("plain gemm", lambda: C.gemm(H, E, True, None))):
+        ms = _time(fn, it)
+        r[name] = {"ms": round(ms, 4), "tflops": round(flops / ms / 1e9, 1),
+                   "frac_of_peak": round(flops / ms / 1e9 / pk["bf16_tflops"], 3)}
+    return r
+
+
 def case_qkv(C, dev, it, pk):
     """q/k/v RMSNorm + RoPE, forward and backward, on one packed 8192-token step: a sliding layer
     (32 q heads, 16 k + 16 v heads of 256) and a global one (32 q heads of 512, 4 k heads, v = k)."""
@@ -332,7 +350,7 @@ def case_nf4(C, dev, it, pk):
 
 CASES = {"gemm": case_gemm, "attn_fwd": case_attn_fwd, "attn_bwd": case_attn_bwd, "gate": case_gate, "ce": case_ce,
          "qkv": case_qkv, "geglu": case_geglu, "rows": case_rows, "norms": case_norms, "ce_bwd": case_ce_bwd,
-         "nf4": case_nf4}
+         "nf4": case_nf4, "ce_gemm": case_ce_gemm}
 
 
 def main(argv=None):

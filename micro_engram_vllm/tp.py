@@ -17,28 +17,35 @@ import torch.nn.functional as F
 from micro_engram.module import check_loaded
 
 
+def _masked_rows(shard, ids, start):
+    """Rows of `ids` that fall in this rank's shard [start, start + len), zeros for the others."""
+    n, width = shard.shape
+    if n == 0:  # more ranks than rows: this rank owns none of this table
+        return shard.new_zeros(*ids.shape, width)
+    local = ids.long() - start
+    owned = ((local >= 0) & (local < n)).unsqueeze(-1)
+    return F.embedding(local.clamp(0, n - 1), shard) * owned.to(shard.dtype)
+
+
 def tp_lookup(all_reduce):
     """A MicroEngram.row_lookup_fn: masked local lookup, then `all_reduce` (sum over TP)."""
 
     def lookup(engram, idx):
         _rank, world, starts, _pers = engram.row_info
         tables = engram.__dict__.get("row_views") or engram.row_shards  # UVA views when offloaded
-        parts = []
-        for shard, i, start in zip(tables, idx, starts):
-            n = shard.shape[0]
-            if n == 0:  # more ranks than rows: this rank owns none of this table
-                parts.append(shard.new_zeros(*i.shape, shard.shape[1]))
-                continue
-            local = i.long() - start
-            mine = (local >= 0) & (local < n)
-            rows = F.embedding(local.clamp(0, n - 1), shard)
-            parts.append(rows * mine.unsqueeze(-1).to(rows.dtype))
-        out = torch.cat(parts, dim=-1)
-        if world > 1:
-            out = all_reduce(out)
-        return list(out.split(engram.engram_dim, dim=-1))
+        mem = torch.cat([_masked_rows(t, ids, a) for t, ids, a in zip(tables, idx, starts)], dim=-1)
+        if world > 1:  # every row has exactly one owner: the sum is exact in any dtype
+            mem = all_reduce(mem)
+        return list(mem.split(engram.engram_dim, dim=-1))
 
     return lookup
+
+
+def _check_hash_seed(engram, sd, where):
+    saved = sd.get("mults")
+    if saved is not None and not torch.equal(saved.to(engram.mults.device).long(), engram.mults.long()):
+        raise ValueError(f"[micro_engram] {where}: the saved hash multipliers differ from this engram's "
+                         f"seed; the seed is wrong for these weights")
 
 
 def load_rows(engram, sd, where, complete=True):
@@ -48,33 +55,31 @@ def load_rows(engram, sd, where, complete=True):
     one); everything else loads as usual (delta scales converted by the module's hook).
     complete=False: `sd` may be part of the engram (weights streamed from a checkpoint), so
     nothing is reported missing. Returns the set of table indices loaded."""
-    sd = dict(sd)
+    rest = {k: v for k, v in sd.items() if not k.startswith("tables.")}
+    tables = {k: v for k, v in sd.items() if k.startswith("tables.")}
     _rank, _world, starts, _pers = engram.row_info
+    known = {f"tables.{k}.weight": k for k in range(len(engram.row_shards))}
+    unknown = [name for name in tables if name not in known]
+    if unknown:
+        raise ValueError(f"[micro_engram] {where}: tables this engram does not have: {unknown[:5]}")
     loaded = set()
-    for k, shard in enumerate(engram.row_shards):
-        t = sd.pop(f"tables.{k}.weight", None)
-        if t is None:
-            continue
+    for name, full in tables.items():
+        k = known[name]
+        shard = engram.row_shards[k]
         want = (engram.table_rows[k], engram.engram_dim)
-        if tuple(t.shape) != want:
-            raise ValueError(f"[micro_engram] {where}: tables.{k}.weight is {tuple(t.shape)}, this engram "
-                             f"needs {want}")
+        if tuple(full.shape) != want:
+            raise ValueError(f"[micro_engram] {where}: {name} is {tuple(full.shape)}, this engram needs {want}")
         with torch.no_grad():
-            shard.copy_(t[starts[k]:starts[k] + shard.shape[0]])
+            shard.copy_(full[starts[k]:starts[k] + shard.shape[0]])
         loaded.add(k)
-    extra = [k for k in sd if k.startswith("tables.")]
-    if extra:
-        raise ValueError(f"[micro_engram] {where}: tables this engram does not have: {extra[:5]}")
     if complete:
-        missing = [k for k in range(len(engram.row_shards)) if k not in loaded]
-        if missing:
-            raise ValueError(f"[micro_engram] {where}: missing tables {missing}")
-        check_loaded(engram, sd, where)
-    elif sd:
-        if "mults" in sd and not torch.equal(sd["mults"].to(engram.mults.device).long(), engram.mults.long()):
-            raise ValueError(f"[micro_engram] {where}: the saved hash multipliers differ from this engram's "
-                             f"seed; the seed is wrong for these weights")
-        res = engram.load_state_dict(sd, strict=False)
+        absent = sorted(set(range(len(engram.row_shards))) - loaded)
+        if absent:
+            raise ValueError(f"[micro_engram] {where}: missing tables {absent}")
+        check_loaded(engram, rest, where)
+    elif rest:
+        _check_hash_seed(engram, rest, where)
+        res = engram.load_state_dict(rest, strict=False)
         if res.unexpected_keys:
             raise ValueError(f"[micro_engram] {where}: unexpected engram tensors {res.unexpected_keys[:10]}")
     return loaded

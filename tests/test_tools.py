@@ -195,38 +195,48 @@ def _word(i):
     return next(k for k, v in _VOCAB.items() if v == i)
 
 
+def _prompt_logprobs(ids, boost):
+    """vLLM-style prompt_logprobs: assistant-ish words ("aa...", "<end>") get probability `boost`,
+    every other word 0.1; the first position has none."""
+    def entry(i):
+        word = _word(i)
+        p = boost if word.startswith("aa") or word == "<end>" else 0.1
+        return {str(i): {"logprob": math.log(p), "rank": 1, "decoded_token": word}}
+
+    return [None] + [entry(i) for i in ids[1:]]
+
+
 class _Fake(BaseHTTPRequestHandler):
-    boost = 0.9  # probability of assistant-ish words ("aa...", "<end>"); others 0.1
+    """A stand-in vLLM server: /tokenize and /v1/completions with prompt log-probs."""
+
+    boost = 0.9
 
     def log_message(self, *a):
         pass
 
-    def _send(self, obj):
-        data = json.dumps(obj).encode()
+    def _reply(self, payload):
+        body = json.dumps(payload).encode()
         self.send_response(200)
-        self.send_header("Content-Type", "application/json")
-        self.send_header("Content-Length", str(len(data)))
+        for key, value in (("Content-Type", "application/json"), ("Content-Length", str(len(body)))):
+            self.send_header(key, value)
         self.end_headers()
-        self.wfile.write(data)
+        self.wfile.write(body)
 
     def do_GET(self):
-        self._send({"data": [{"id": "fake"}]})
+        self._reply({"data": [{"id": "fake"}]})
 
     def do_POST(self):
-        req = json.loads(self.rfile.read(int(self.headers["Content-Length"])))
+        size = int(self.headers["Content-Length"])
+        req = json.loads(self.rfile.read(size))
         if self.path == "/tokenize":
             text = req.get("prompt")
-            if text is None:
+            if text is None:  # chat: a simple role-tagged rendering
                 text = "".join(f"<{m['role']}>{m['content']}<end>" for m in req["messages"]) + "<assistant>"
-            return self._send({"tokens": _tok(text)})
-        p = req["prompt"]
-        ids = p if isinstance(p, list) else _tok(p)
-        lps = [None]
-        for i in ids[1:]:
-            w = _word(i)
-            pr = type(self).boost if (w.startswith("aa") or w == "<end>") else 0.1
-            lps.append({str(i): {"logprob": math.log(pr), "rank": 1, "decoded_token": w}})
-        self._send({"choices": [{"text": "", "prompt_token_ids": ids, "prompt_logprobs": lps}]})
+            self._reply({"tokens": _tok(text)})
+            return
+        ids = req["prompt"] if isinstance(req["prompt"], list) else _tok(req["prompt"])
+        choice = {"text": "", "prompt_token_ids": ids, "prompt_logprobs": _prompt_logprobs(ids, type(self).boost)}
+        self._reply({"choices": [choice]})
 
 
 @pytest.fixture
