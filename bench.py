@@ -187,7 +187,8 @@ def count_launches(trainer, micro):
             "attn_bwd_dq_kernel", "attn_bwd_tc_kernel", "attn_delta_kernel", "doc_end_from_start_kernel",
             "attn_tiles_kernel", "attn_bwd_sdp_kernel", "attn_bwd_acc_kernel",
             "gemm_pair_kernel", "nf4_dequant_kernel", "nf4_quantize_kernel", "p2p_allreduce_mean_kernel",
-            "layer_gather_kernel", "p2p_gather_kernel", "p2p_sum_slots_kernel")
+            "layer_gather_kernel", "p2p_gather_kernel", "p2p_sum_slots_kernel", "row_push_kernel",
+            "row_accumulate_kernel", "rows_serve_kernel", "rows_collect_kernel", "adam_rows_kernel")
     pat = re.compile(r"\b(" + "|".join(ours) + r")\b")
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         trainer.train_step(micro)

@@ -589,20 +589,31 @@ __global__ void __launch_bounds__(256) rows_collect_kernel(FetchArgs a, int64_t 
 // Sum of squares of the touched rows' accumulated gradients (every row lives on exactly one
 // rank, so the sum over ranks is the global table norm^2): the first min(count, cap) slots of
 // each compact accumulator (holes are zero). counts are read on the device.
-__global__ void touched_sqnorm_kernel(const int64_t* __restrict__ acc_ptrs,
-                                      const int64_t* __restrict__ cnt_ptrs, const int64_t* __restrict__ caps,
-                                      int n_tables, int dim, float* __restrict__ out) {
+__global__ void __launch_bounds__(256) touched_sqnorm_kernel(const int64_t* __restrict__ acc_ptrs,
+                                                              const int64_t* __restrict__ cnt_ptrs,
+                                                              const int64_t* __restrict__ caps, int n_tables, int dim,
+                                                              float* __restrict__ out) {
+  // the used slots of a table are one contiguous [cnt, dim] block: a flat float4 reduction with
+  // four loads in flight per thread
   __shared__ float scratch[64];
   float local_sum = 0.f;
-  const int lane = threadIdx.x & 31;
-  const int warps_total = gridDim.x * (blockDim.x >> 5);
-  const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   for (int k = 0; k < n_tables; ++k) {
-    const int cnt = (int)min((int64_t)*reinterpret_cast<const int*>(cnt_ptrs[k]), caps[k]);
-    const float* acc = reinterpret_cast<const float*>(acc_ptrs[k]);
-    for (int r = wid; r < cnt; r += warps_total) {
-      const float* a = acc + (int64_t)r * dim;
-      for (int j = lane; j < dim; j += 32) local_sum += a[j] * a[j];
+    const int64_t cnt = min((int64_t)*reinterpret_cast<const int*>(cnt_ptrs[k]), caps[k]);
+    const float4* acc = reinterpret_cast<const float4*>(acc_ptrs[k]);
+    const int64_t n4 = cnt * dim / 4;
+    int64_t i = t0;
+    for (; i + 3 * stride < n4; i += 4 * stride) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = acc[i + u * stride];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) local_sum += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
+    }
+    for (; i < n4; i += stride) {
+      const float4 v = acc[i];
+      local_sum += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
     }
   }
   const float s = block_sum(local_sum, scratch);
@@ -1515,7 +1526,8 @@ void engram_touched_sqnorm(torch::Tensor acc_ptrs, torch::Tensor cnt_ptrs, torch
                            torch::Tensor sq) {
   const at::cuda::CUDAGuard guard(sq.device());
   const int nt = (int)acc_ptrs.numel();
-  touched_sqnorm_kernel<<<sm_count() * 2, 512, 0, at::cuda::getCurrentCUDAStream()>>>(
+  TORCH_CHECK(dim % 4 == 0, "engram_touched_sqnorm: dim must be a multiple of 4");
+  touched_sqnorm_kernel<<<sm_count() * 4, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       acc_ptrs.data_ptr<int64_t>(), cnt_ptrs.data_ptr<int64_t>(), caps.data_ptr<int64_t>(), nt, (int)dim,
       sq.data_ptr<float>());
 }

@@ -19,9 +19,11 @@ reference  the reference's MicroEngram with micro_engram_sharding: rows (unique 
            exchanged with all_to_all over NCCL) and its RowTables optimizer, from baseline/_ref
 
 Timing: CUDA events around K steps after W warm-up steps, barrier + synchronize on both sides,
-max over ranks. The NVLink roofline figure counts the row bytes that must cross NVLink each
-step (every lookup's 128-byte row in, every gradient row back as fp32, (world-1)/world of them
-remote) against the measured 770 GB/s per direction.
+max over ranks. The roofline is the slower of the tensor-core time of the six projection GEMMs
+(key and value: forward, input gradient, weight gradient) at the measured bf16 peak and the
+NVLink time of the bytes that must cross it per GPU (each remote lookup's 128-byte bf16 row in,
+its bf16 gradient back with an 8-byte header; (world-1)/world of the lookups are remote) at the
+measured 770 GB/s per direction; frac_of_roofline = roofline / measured step.
 """
 import argparse
 import json
@@ -232,15 +234,28 @@ def main():
     ms, rank, world = got
     lookups = ROWS_PER_GPU * SEQ * len(TABLES) * HEADS
     remote = (world - 1) / world
-    nvlink_bytes = lookups * remote * (EDIM * 2 + EDIM * 4)  # bf16 row in, fp32 gradient back
+    # bytes that must cross NVLink per GPU: every remote lookup's bf16 row in (written by its owner)
+    # and its bf16 gradient back (plus an 8-byte header per entry)
+    nvlink_bytes = lookups * remote * (EDIM * 2 + EDIM * 2 + 8)
+    # tensor-core work: key and value projections forward, their input gradient and weight gradient
+    tokens, mem = ROWS_PER_GPU * SEQ, len(TABLES) * HEADS * EDIM
+    flops = 3 * 2 * (2 * tokens * mem * DMODEL)
+    from micro_engram_fork_b200.utils.kernel_bench import peaks
+
+    peak = peaks()
+    link_ms = nvlink_bytes / (NVLINK_GBS * 1e9) * 1e3
+    tc_ms = flops / (peak["bf16_tflops"] * 1e12) * 1e3
+    roof_ms = max(link_ms, tc_ms)
     if rank == 0:
         print(json.dumps({
             "impl": args.impl, "metric": "engram module fwd+bwd+update step (config 2)", "ms_per_step": round(ms, 3),
             "tokens_per_s": round(ROWS_PER_GPU * SEQ * world / (ms / 1e3), 1), "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "lookups_per_gpu": lookups,
-            "nvlink_bytes_per_gpu": int(nvlink_bytes),
-            "nvlink_roofline_ms": round(nvlink_bytes / (NVLINK_GBS * 1e9) * 1e3, 3),
-            "frac_of_nvlink_roofline": round(nvlink_bytes / (NVLINK_GBS * 1e9) * 1e3 / ms, 4) if world > 1 else None,
+            "nvlink_bytes_per_gpu": int(nvlink_bytes), "nvlink_roofline_ms": round(link_ms, 3),
+            "gemm_flops_per_gpu": flops, "tensor_roofline_ms": round(tc_ms, 3),
+            "frac_of_roofline": round(roof_ms / ms, 4),
+            "roofline": f"max(GEMM FLOPs at {peak['bf16_tflops']} TFLOP/s ({peak['source']}), NVLink bytes at "
+                        f"{NVLINK_GBS} GB/s per direction)",
             "config": {"tables": TABLES, "heads": HEADS, "dim": EDIM, "tokens_per_gpu": ROWS_PER_GPU * SEQ,
                        "d_model": DMODEL, "data": "synthetic Zipf(1.1) ids, docs 256-4096, hidden N(0,1) bf16"}}),
               flush=True)

@@ -64,25 +64,43 @@ def _prompts(n, length, vocab=262144, seed=0):
     return [np.searchsorted(cdf, rng.random(length)).astype(np.int64).tolist() for _ in range(n)]
 
 
+def _plugin_root(impl):
+    return os.path.join(ROOT, "baseline", "_ref") if impl == "reference" else ROOT
+
+
 def run(args):
-    os.environ.setdefault("VLLM_USE_V2_MODEL_RUNNER", "1")
-    os.environ.setdefault("VLLM_WORKER_MULTIPROC_METHOD", "fork")
-    if args.impl == "reference":
-        ref = os.path.join(ROOT, "baseline", "_ref")
-        if not os.path.isfile(os.path.join(ref, "micro_engram_vllm", "__init__.py")):
-            print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not installed"}))
-            return
-        sys.path.insert(0, ref)
-    else:
-        sys.path.insert(0, ROOT)
+    """Build the model folder, then serve it in a child process whose import path holds only the
+    chosen plugin (vLLM's worker processes find plugins through their import path, so the two
+    arms must never share one)."""
+    import subprocess
+
+    plugin = _plugin_root(args.impl)
+    if not os.path.isfile(os.path.join(plugin, "micro_engram_vllm", "__init__.py")):
+        print(json.dumps({"impl": args.impl, "unavailable": "baseline/_ref is not installed"}))
+        return
+    if args.impl == "ours":  # the vllm.general_plugins entry point of this repository (in-tree metadata)
+        subprocess.run([sys.executable, "setup.py", "-q", "egg_info"], cwd=ROOT, check=True, capture_output=True)
+    folder = _model_folder(tempfile.mkdtemp(prefix="me_serve_"))
+    env = dict(os.environ, PYTHONPATH=plugin, VLLM_USE_V2_MODEL_RUNNER="1")
+    env.setdefault("VLLM_WORKER_MULTIPROC_METHOD", "fork")
+    child = [sys.executable, os.path.abspath(__file__), "--child", folder, "--impl", args.impl, "--tp", str(args.tp),
+             "--requests", str(args.requests), "--prompt", str(args.prompt), "--gen", str(args.gen)]
+    subprocess.run(child, env=env, cwd=tempfile.gettempdir(), check=True)
+
+
+def serve(args):
+    """The timed serving run (child process: only the arm's plugin is importable)."""
+    plugin = _plugin_root(args.impl)
     import micro_engram_vllm
     import torch
     from vllm import LLM, SamplingParams
 
-    assert os.path.abspath(micro_engram_vllm.__file__).startswith(ref if args.impl == "reference" else ROOT)
+    where = os.path.abspath(micro_engram_vllm.__file__)
+    if not where.startswith(os.path.abspath(plugin) + os.sep) or (args.impl == "reference" and where.startswith(
+            os.path.join(ROOT, "micro_engram_vllm"))):
+        raise SystemExit(f"serve_bench: the {args.impl} arm imported the plugin from {where}")
     micro_engram_vllm.register()
-    tmp = _model_folder(tempfile.mkdtemp(prefix="me_serve_"))
-    llm = LLM(model=tmp, skip_tokenizer_init=True, dtype="bfloat16", load_format="dummy", enforce_eager=True,
+    llm = LLM(model=args.child, skip_tokenizer_init=True, dtype="bfloat16", load_format="dummy", enforce_eager=True,
               tensor_parallel_size=args.tp, distributed_executor_backend="mp" if args.tp > 1 else None,
               max_model_len=args.prompt + args.gen + 16, max_num_seqs=args.requests,
               max_num_batched_tokens=max(8192, args.prompt), gpu_memory_utilization=0.85)
@@ -104,7 +122,7 @@ def run(args):
         "impl": args.impl, "metric": "vLLM TP decode tok/s (config 5)", "value": round(decode_tps, 1),
         "unit": "tokens/s", "tp": args.tp, "prefill_ttft_s": round(times["ttft"], 3),
         "full_s": round(times["full"], 3), "higher_is_better": True, "dtype": "bf16",
-        "data": "synthetic Zipf(1.1) prompts, random (dummy) weights",
+        "data": "synthetic Zipf(1.1) prompts, random (dummy) weights", "plugin": where,
         "config": {"model": "31B-class Gemma-style hybrid decoder + engrams at layers 0 and 29",
                    "requests": args.requests, "prompt_tokens": args.prompt, "gen_tokens": args.gen,
                    "tables": TABLES, "cuda_graphs": False,
@@ -118,7 +136,12 @@ def main():
     ap.add_argument("--requests", type=int, default=64)
     ap.add_argument("--prompt", type=int, default=2048)
     ap.add_argument("--gen", type=int, default=256)
-    run(ap.parse_args())
+    ap.add_argument("--child", default="", help=argparse.SUPPRESS)  # internal: serve this model folder
+    args = ap.parse_args()
+    if args.child:
+        serve(args)
+    else:
+        run(args)
 
 
 if __name__ == "__main__":
