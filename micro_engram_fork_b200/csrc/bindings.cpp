@@ -101,9 +101,9 @@ torch::Tensor gemm_tn_f32(torch::Tensor At, torch::Tensor Bt);
 void gemm_carry_copy(int64_t device, int64_t segs, int64_t nsegs, int64_t begin16, int64_t end16);
 void layer_gather(torch::Tensor segs, int64_t begin16, int64_t end16);
 void gemm_f32_scatter(torch::Tensor A, torch::Tensor W, torch::Tensor recv_ptrs, int64_t rows_per_rank,
-                      int64_t slot, int64_t slot_elems);
+                      int64_t slot, int64_t slot_elems, bool b_kmajor);
 void p2p_gather(torch::Tensor bases, int64_t rank, int64_t call, int64_t stage_off, int64_t half_bytes, int64_t n16,
-                torch::Tensor out, double timeout_s, torch::Tensor status);
+                torch::Tensor out, double timeout_s, torch::Tensor status, bool poison);
 void p2p_sum_slots(torch::Tensor bases, int64_t rank, int64_t call, int64_t recv_off, int64_t slot_elems,
                    torch::Tensor out, double timeout_s, torch::Tensor status);
 std::vector<torch::Tensor> gemm_ce(torch::Tensor H, torch::Tensor E, torch::Tensor labels, int64_t lab_start,
@@ -170,8 +170,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_tn_f32", &gemm_tn_f32);
   m.def("gemm_carry_copy", &gemm_carry_copy);
   m.def("layer_gather", &layer_gather);
-  m.def("gemm_f32_scatter", &gemm_f32_scatter);
-  m.def("p2p_gather", &p2p_gather);
+  m.def("gemm_f32_scatter", &gemm_f32_scatter, py::arg("A"), py::arg("W"), py::arg("recv_ptrs"),
+        py::arg("rows_per_rank"), py::arg("slot"), py::arg("slot_elems"), py::arg("b_kmajor") = false);
+  m.def("p2p_gather", &p2p_gather, py::arg("bases"), py::arg("rank"), py::arg("call"), py::arg("stage_off"),
+        py::arg("half_bytes"), py::arg("n16"), py::arg("out"), py::arg("timeout_s"), py::arg("status"),
+        py::arg("poison") = false);
   m.def("p2p_sum_slots", &p2p_sum_slots);
   m.def("gemm_ce", &gemm_ce);
   m.def("gemm_status", &gemm_status);

@@ -35,21 +35,28 @@ torch::Tensor gemm(torch::Tensor A, torch::Tensor W, bool b_kmajor, c10::optiona
   return D;
 }
 
-// dH rows scattered to their owners: rows [r * rows_per_rank, (r + 1) * rows_per_rank) of
-// A . W (fp32, W [K, N] read N-major) are stored into rank r's receive buffer recv_ptrs[r], in
-// slot `slot` (slots of slot_elems floats; rows of N floats). The caller signals the peers after
-// this launch (p2p_sum_slots) so the owners can sum their slots.
+// Rows scattered to their owners (the GEMM half of a fused GEMM -> reduce-scatter): rows
+// [r * rows_per_rank, (r + 1) * rows_per_rank) of the fp32 product are stored into rank r's
+// receive buffer recv_ptrs[r], in slot `slot` (slots of slot_elems floats; rows of N floats).
+// The product is A . W with W [K, N] read N-major (the LM head's dH), or A . W^T with W [N, K]
+// (b_kmajor: a row-parallel linear's partial). M may stop short of world * rows_per_rank: the
+// missing rows are not stored. A product of one partial wave of tiles is split along K so that
+// small-M calls (decode) keep every SM busy. The caller signals the peers after this launch
+// (p2p_sum_slots) so the owners can sum their slots.
 void gemm_f32_scatter(torch::Tensor A, torch::Tensor W, torch::Tensor recv_ptrs, int64_t rows_per_rank,
-                      int64_t slot, int64_t slot_elems) {
+                      int64_t slot, int64_t slot_elems, bool b_kmajor) {
   check_operand(A, "A");
   check_operand(W, "W");
   TORCH_CHECK(recv_ptrs.is_cuda() && recv_ptrs.scalar_type() == torch::kInt64, "gemm_f32_scatter: recv_ptrs");
   const at::cuda::CUDAGuard guard(A.device());
-  const int M = (int)A.size(0), K = (int)A.size(1), N = (int)W.size(1);
-  TORCH_CHECK(W.size(0) == K && N % 8 == 0 && K % 8 == 0, "gemm_f32_scatter: W must be [K, N], N % 8 == 0");
-  TORCH_CHECK(rows_per_rank > 0 && M == rows_per_rank * recv_ptrs.numel(), "gemm_f32_scatter: M != world * rows");
-  TORCH_CHECK(slot_elems >= rows_per_rank * N, "gemm_f32_scatter: slots too small");
+  const int M = (int)A.size(0), K = (int)A.size(1);
+  const int N = (int)(b_kmajor ? W.size(0) : W.size(1));
+  TORCH_CHECK((b_kmajor ? W.size(1) : W.size(0)) == K && N % 8 == 0 && K % 8 == 0,
+              "gemm_f32_scatter: inner dimensions differ, or N or K not a multiple of 8");
+  TORCH_CHECK(rows_per_rank > 0 && M <= rows_per_rank * recv_ptrs.numel(), "gemm_f32_scatter: M > world * rows");
+  TORCH_CHECK(slot_elems >= rows_per_rank * N && slot_elems % 4 == 0, "gemm_f32_scatter: slots too small");
   if (M == 0 || N == 0) return;
+  TORCH_CHECK(K > 0, "gemm_f32_scatter: K == 0");
   const int dev = A.get_device();
   GemmArgs a = base_args(M, N, K, (N + BN - 1) / BN, dev);
   a.ldd = N;
@@ -57,9 +64,16 @@ void gemm_f32_scatter(torch::Tensor A, torch::Tensor W, torch::Tensor recv_ptrs,
   a.peer_rows = (int)rows_per_rank;
   a.peer_slot = (int)slot;
   a.peer_slot_elems = slot_elems;
+  a.split_one_wave = 1;
+  auto stream = at::cuda::getCurrentCUDAStream();
   const CUtensorMap ta = make_tmap(A.data_ptr(), M, K, A.stride(0), BK, BM);
-  const CUtensorMap tb = make_tmap(W.data_ptr(), K, N, W.stride(0), 64, BK);
-  launch<EPI_F32, true>(ta, tb, a, dev, at::cuda::getCurrentCUDAStream());
+  if (b_kmajor) {
+    const CUtensorMap tb = make_tmap(W.data_ptr(), N, K, W.stride(0), BK, BN / 2);
+    launch<EPI_F32, false>(ta, tb, a, dev, stream);
+  } else {
+    const CUtensorMap tb = make_tmap(W.data_ptr(), K, N, W.stride(0), 64, BK);
+    launch<EPI_F32, true>(ta, tb, a, dev, stream);
+  }
 }
 
 // out[M, N] (fp32) = A[M, K] . W, with W [K, N] read N-major (the LM head's dH = P . E).

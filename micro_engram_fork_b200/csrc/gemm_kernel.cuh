@@ -120,6 +120,7 @@ struct GemmArgs {
   // to finish a 32-row slice (counted in `cnt`, which starts at zero) sums the splits in split
   // order and stores the result, so the tail is as deterministic as the rest of the GEMM.
   int dp_tiles, tail_units, splits;
+  int split_one_wave;   // host only: also split a single partial wave (small-M F32 products)
   float* ws;
   int* cnt;
   // side copy carried by warp 6: units [gbegin16, gend16) of the segment table gsegs
@@ -751,7 +752,8 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, 
   a.splits = 1;
   torch::Tensor ws, cnt;
   const int rem = ntiles % nclusters;
-  if ((EPI == EPI_STORE || EPI == EPI_F32) && ntiles > nclusters && rem > 0 && 2 * rem <= nclusters) {
+  if ((EPI == EPI_STORE || EPI == EPI_F32) && (ntiles > nclusters || a.split_one_wave) && rem > 0 &&
+      2 * rem <= nclusters) {
     // the last partial wave would leave most SMs idle: split its tiles along K instead
     const int splits = std::min(nclusters / rem, std::max(1, nk / 4));
     if (splits >= 2) {

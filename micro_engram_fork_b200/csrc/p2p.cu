@@ -118,24 +118,42 @@ ME_DEVICE bool flags_barrier(const int64_t* __restrict__ bases, int world, int r
 }
 
 // out[r * n16 ...] = rank r's stage (n16 16-byte units at stage_off + parity * half) for every r.
+// poison: when a wait ran out (here, or in an earlier kernel of this rank: status[0] set), every
+// byte of out becomes 0xFF (NaN in fp32 and bf16) instead of stale data, so a consumer that does
+// not read the status cannot silently use another call's values.
 __global__ void __launch_bounds__(256) p2p_gather_kernel(const int64_t* __restrict__ bases, int world, int rank,
                                                          uint32_t call, int64_t stage_off, int64_t half_bytes,
                                                          int64_t n16, uint4* __restrict__ out, uint64_t timeout_ns,
-                                                         int* status) {
-  if (!flags_barrier(bases, world, rank, call, timeout_ns, status)) return;
-  const int64_t off = stage_off + (int64_t)(call & 1u) * half_bytes;
+                                                         int* status, bool poison) {
+  const bool ok = flags_barrier(bases, world, rank, call, timeout_ns, status);
   const int64_t total = n16 * world;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if (!ok || (poison && *reinterpret_cast<volatile int*>(status) != 0)) {
+    if (poison)
+      for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride)
+        out[i] = make_uint4(~0u, ~0u, ~0u, ~0u);
+    return;
+  }
+  const int64_t off = stage_off + (int64_t)(call & 1u) * half_bytes;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
     const int r = (int)(i / n16);
     out[i] = __ldcg(reinterpret_cast<const uint4*>(bases[r] + off) + (i - (int64_t)r * n16));
   }
 }
 
 // out[i] = sum over slots s of this rank's recv[parity][s][i] (fp32), after every peer signalled
-// that its scattered stores into those slots are done.
+// that its scattered stores into those slots are done. OutT float4 (fp32 out) or uint2 (four
+// bf16, rounded to nearest even: the reduce half of a row-parallel linear's all-reduce).
+ME_DEVICE void put4(float4* out, int64_t i, const float4& v) { out[i] = v; }
+ME_DEVICE void put4(uint2* out, int64_t i, const float4& v) {
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+  out[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+}
+
+template <typename OutT>
 __global__ void __launch_bounds__(256) p2p_sum_slots_kernel(const int64_t* __restrict__ bases, int world, int rank,
                                                             uint32_t call, int64_t recv_off, int64_t slot_elems,
-                                                            int64_t n4, float4* __restrict__ out, uint64_t timeout_ns,
+                                                            int64_t n4, OutT* __restrict__ out, uint64_t timeout_ns,
                                                             int* status) {
   if (!flags_barrier(bases, world, rank, call, timeout_ns, status)) return;
   const float* recv = reinterpret_cast<const float*>(bases[rank] + recv_off) +
@@ -146,7 +164,7 @@ __global__ void __launch_bounds__(256) p2p_sum_slots_kernel(const int64_t* __res
       const float4 v = __ldcg(reinterpret_cast<const float4*>(recv + (int64_t)sl * slot_elems) + i);
       acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
     }
-    out[i] = acc;
+    put4(out, i, acc);
   }
 }
 
@@ -182,7 +200,7 @@ int grid_for(int64_t units, int dev) {
 
 // Gather every rank's staged bytes (n16 16-byte units each) into out [world * n16 * 16 bytes].
 void p2p_gather(torch::Tensor bases, int64_t rank, int64_t call, int64_t stage_off, int64_t half_bytes, int64_t n16,
-                torch::Tensor out, double timeout_s, torch::Tensor status) {
+                torch::Tensor out, double timeout_s, torch::Tensor status, bool poison) {
   const int world = (int)bases.numel();
   TORCH_CHECK(world >= 1 && world <= MAX_RANKS && out.is_cuda() && out.nbytes() >= (size_t)(world * n16 * 16),
               "p2p_gather: bad arguments");
@@ -191,23 +209,33 @@ void p2p_gather(torch::Tensor bases, int64_t rank, int64_t call, int64_t stage_o
   const at::cuda::CUDAGuard guard(out.device());
   p2p_gather_kernel<<<grid_for(world * n16, out.get_device()), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       bases.data_ptr<int64_t>(), world, (int)rank, (uint32_t)call, stage_off, half_bytes, n16,
-      reinterpret_cast<uint4*>(out.data_ptr()), (uint64_t)(timeout_s * 1e9), status.data_ptr<int>());
+      reinterpret_cast<uint4*>(out.data_ptr()), (uint64_t)(timeout_s * 1e9), status.data_ptr<int>(), poison);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-// out[n] (fp32) = sum of this rank's `world` receive slots of the parity of `call`.
+// out[n] (fp32, or bf16 rounded from the fp32 sum) = sum of this rank's `world` receive slots
+// of the parity of `call`.
 void p2p_sum_slots(torch::Tensor bases, int64_t rank, int64_t call, int64_t recv_off, int64_t slot_elems,
                    torch::Tensor out, double timeout_s, torch::Tensor status) {
   const int world = (int)bases.numel();
-  TORCH_CHECK(world >= 1 && world <= MAX_RANKS && out.is_cuda() && out.scalar_type() == torch::kFloat32 &&
+  const bool f32 = out.scalar_type() == torch::kFloat32;
+  TORCH_CHECK(world >= 1 && world <= MAX_RANKS && out.is_cuda() && (f32 || out.scalar_type() == torch::kBFloat16) &&
                   out.is_contiguous() && out.numel() % 4 == 0 && out.numel() <= slot_elems,
               "p2p_sum_slots: bad arguments");
-  TORCH_CHECK(recv_off % 16 == 0 && slot_elems % 4 == 0, "p2p_sum_slots: 16-byte alignment");
+  TORCH_CHECK(recv_off % 16 == 0 && slot_elems % 4 == 0 && reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
+              "p2p_sum_slots: 16-byte alignment");
   const at::cuda::CUDAGuard guard(out.device());
   const int64_t n4 = out.numel() / 4;
-  p2p_sum_slots_kernel<<<grid_for(n4, out.get_device()), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      bases.data_ptr<int64_t>(), world, (int)rank, (uint32_t)call, recv_off, slot_elems, n4,
-      reinterpret_cast<float4*>(out.data_ptr()), (uint64_t)(timeout_s * 1e9), status.data_ptr<int>());
+  const int grid = grid_for(n4, out.get_device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (f32)
+    p2p_sum_slots_kernel<float4><<<grid, 256, 0, stream>>>(
+        bases.data_ptr<int64_t>(), world, (int)rank, (uint32_t)call, recv_off, slot_elems, n4,
+        reinterpret_cast<float4*>(out.data_ptr()), (uint64_t)(timeout_s * 1e9), status.data_ptr<int>());
+  else
+    p2p_sum_slots_kernel<uint2><<<grid, 256, 0, stream>>>(
+        bases.data_ptr<int64_t>(), world, (int)rank, (uint32_t)call, recv_off, slot_elems, n4,
+        reinterpret_cast<uint2*>(out.data_ptr()), (uint64_t)(timeout_s * 1e9), status.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -8,7 +8,8 @@ Registration failure on an unusual torch build falls back to the plain callable,
 warning, so the kernel keeps working outside compiled graphs. Reference counterpart:
 micro_engram/train/vendor/op_registry.py:40-67 (the same decorator contract).
 
-Ops registered here are the serving path's: the history fill, the n-gram hash, and the
+Ops registered here are the serving path's: the history fill, the n-gram hash, the fused
+row-parallel linear of tensor-parallel serving (GEMM -> reduce-scatter -> all-gather), and the
 whole engram injection (hash -> row gather -> key/value projections -> gate -> residual),
 which runs as one op so a compiled decoder layer sees a single node per engram.
 """
@@ -101,3 +102,28 @@ def serve_inject(hidden: torch.Tensor, hist: torch.Tensor, canon: torch.Tensor, 
 def _(hidden, hist, canon, mults, orders, rows, pad_id, w_ptrs, per, world, dim, src_dtype, key_w, value_w,
       q_scale, k_scale, keep, sqrt_gate, status):
     return torch.empty_like(hidden)
+
+
+# Fused row-parallel linears (parallel/tp_linear.py) by handle: the op carries an int, the
+# object (its peer buffers and call counter) stays on the host.
+_TP_LINEARS: list = []
+
+
+def add_tp_linear(obj) -> int:
+    """Make a TPRowLinear callable through tp_row_linear; returns its handle."""
+    _TP_LINEARS.append(obj)
+    return len(_TP_LINEARS) - 1
+
+
+@register_kernel_op("tp_row_linear")
+def tp_row_linear(x: torch.Tensor, weight: torch.Tensor, handle: int) -> torch.Tensor:
+    """x [M, K_local] . weight[N, K_local]^T summed over the tensor-parallel ranks, on every rank:
+    the GEMM's epilogue reduce-scatters its fp32 partial over NVLink, then a slot sum and an
+    all-gather. Collective (every rank calls it in the same order); eager only, since the call
+    counter that pairs the ranks' buffers lives in the host object."""
+    return _TP_LINEARS[handle](x, weight)
+
+
+@tp_row_linear.register_fake
+def _(x, weight, handle):
+    return x.new_empty((x.shape[0], weight.shape[0]))

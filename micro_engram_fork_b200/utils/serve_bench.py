@@ -13,7 +13,9 @@ model (an assembled model folder), so no weight file is read.
 
 ours       this repository's plugin (micro_engram_vllm): one fused custom op per engram layer
            reads each row from the TP rank that owns it over NVLink (no all-reduce), projects it
-           on the tcgen05 GEMM and applies the gate
+           on the tcgen05 GEMM and applies the gate; with --fused-tp the base model's o_proj and
+           down_proj also run as the fused GEMM -> reduce-scatter -> all-gather op
+           (parallel/tp_linear.py) instead of a library GEMM and vLLM's all-reduce
 reference  the reference's plugin from baseline/_ref (masked local lookup + all-reduce)
 
 Workload: `requests` prompts of `prompt` Zipf(1.1) token ids, `gen` greedy tokens each
@@ -82,9 +84,13 @@ def run(args):
         subprocess.run([sys.executable, "setup.py", "-q", "egg_info"], cwd=ROOT, check=True, capture_output=True)
     folder = _model_folder(tempfile.mkdtemp(prefix="me_serve_"))
     env = dict(os.environ, PYTHONPATH=plugin, VLLM_USE_V2_MODEL_RUNNER="1")
+    if args.fused_tp and args.impl == "ours":
+        env["MICRO_ENGRAM_FUSED_TP"] = "1"
     env.setdefault("VLLM_WORKER_MULTIPROC_METHOD", "fork")
     child = [sys.executable, os.path.abspath(__file__), "--child", folder, "--impl", args.impl, "--tp", str(args.tp),
              "--requests", str(args.requests), "--prompt", str(args.prompt), "--gen", str(args.gen)]
+    if args.fused_tp and args.impl == "ours":
+        child.append("--fused-tp")
     subprocess.run(child, env=env, cwd=tempfile.gettempdir(), check=True)
 
 
@@ -122,6 +128,7 @@ def serve(args):
         "impl": args.impl, "metric": "vLLM TP decode tok/s (config 5)", "value": round(decode_tps, 1),
         "unit": "tokens/s", "tp": args.tp, "prefill_ttft_s": round(times["ttft"], 3),
         "full_s": round(times["full"], 3), "higher_is_better": True, "dtype": "bf16",
+        "fused_tp_linears": bool(args.fused_tp and args.impl == "ours"),
         "data": "synthetic Zipf(1.1) prompts, random (dummy) weights", "plugin": where,
         "config": {"model": "31B-class Gemma-style hybrid decoder + engrams at layers 0 and 29",
                    "requests": args.requests, "prompt_tokens": args.prompt, "gen_tokens": args.gen,
@@ -136,6 +143,8 @@ def main():
     ap.add_argument("--requests", type=int, default=64)
     ap.add_argument("--prompt", type=int, default=2048)
     ap.add_argument("--gen", type=int, default=256)
+    ap.add_argument("--fused-tp", action="store_true",
+                    help="ours: o_proj / down_proj GEMM + all-reduce as the fused peer-memory op")
     ap.add_argument("--child", default="", help=argparse.SUPPRESS)  # internal: serve this model folder
     args = ap.parse_args()
     if args.child:

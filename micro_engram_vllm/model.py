@@ -130,6 +130,77 @@ def _uva_views(shards):
     return [get_accelerator_view_from_cpu_tensor(p.data) for p in shards]
 
 
+def fused_tp_wanted(vllm_config, environ=None):
+    """Replace the row-parallel linears' GEMM + all-reduce with the fused peer-memory op?
+    additional_config {"micro_engram_fused_tp": true} or MICRO_ENGRAM_FUSED_TP=1; off by default."""
+    environ = os.environ if environ is None else environ
+    extra = getattr(vllm_config, "additional_config", None)
+    if isinstance(extra, dict) and "micro_engram_fused_tp" in extra:
+        return bool(extra["micro_engram_fused_tp"])
+    return environ.get("MICRO_ENGRAM_FUSED_TP", "0") == "1"
+
+
+def _fusable(lin):
+    """A plain bf16 row-parallel linear whose output vLLM all-reduces."""
+    w = getattr(lin, "weight", None)
+    return (getattr(lin, "input_is_parallel", False) and getattr(lin, "reduce_results", False)
+            and getattr(lin, "bias", None) is None and w is not None and w.dim() == 2 and w.dtype == torch.bfloat16
+            and w.shape[0] % 8 == 0 and w.shape[1] % 8 == 0)
+
+
+def _route_row_parallel(lin, handle, rows):
+    """lin.forward -> the fused op for bf16 inputs of at most `rows` rows (else vLLM's own path)."""
+    from micro_engram_fork_b200.ops.registry import tp_row_linear
+
+    plain = lin.forward
+
+    def forward(input_):
+        if input_.dim() != 2 or input_.dtype != torch.bfloat16 or input_.shape[0] > rows:
+            return plain(input_)
+        y = tp_row_linear(input_.contiguous(), lin.weight, handle)
+        return (y, None) if lin.return_bias else y
+
+    lin.forward = forward
+
+
+def fuse_row_parallel(model, vllm_config):
+    """Route every decoder layer's o_proj and down_proj through one shared TPRowLinear (the GEMM's
+    epilogue reduce-scatters over NVLink; no NCCL all-reduce). Needs TP > 1 and eager execution:
+    the host-side call counter that pairs the ranks' buffers would be frozen by a CUDA graph.
+    Returns the number of linears routed."""
+    tp_size = get_tensor_model_parallel_world_size()
+    if tp_size == 1 or not fused_tp_wanted(vllm_config):
+        return 0
+    if not getattr(vllm_config.model_config, "enforce_eager", False):
+        logger.warning("[micro_engram] micro_engram_fused_tp needs enforce_eager=True (CUDA graphs would freeze "
+                       "its call counter); vLLM's all-reduce is kept")
+        return 0
+    from micro_engram_fork_b200.ops.registry import add_tp_linear
+    from micro_engram_fork_b200.parallel.tp_linear import TPRowLinear
+
+    rows = vllm_config.scheduler_config.max_num_batched_tokens
+    lins = []
+    for layer in model.model.layers:
+        if isinstance(layer, PPMissingLayer):
+            continue
+        pair = (getattr(getattr(layer, "self_attn", None), "o_proj", None),
+                getattr(getattr(layer, "mlp", None), "down_proj", None))
+        lins += [lin for lin in pair if lin is not None and _fusable(lin)]
+    if not lins:
+        return 0
+    n_out = {lin.weight.shape[0] for lin in lins}
+    if len(n_out) != 1:
+        raise ValueError(f"[micro_engram] micro_engram_fused_tp: row-parallel outputs differ {sorted(n_out)}")
+    shared = TPRowLinear(rows, n_out.pop(), lins[0].weight.device, group=get_tp_group().cpu_group)
+    handle = add_tp_linear(shared)
+    model.__dict__["micro_engram_tp_linear"] = shared
+    for lin in lins:
+        _route_row_parallel(lin, handle, rows)
+    logger.info("[micro_engram] %d row-parallel linears fused with their all-reduce (GEMM epilogue "
+                "reduce-scatter over NVLink, %d rows max)", len(lins), rows)
+    return len(lins)
+
+
 def _dummy_rows(engram, seed):
     """load_format="dummy" (random weights for benchmarking) never calls load_weights, so the
     row shards, allocated empty, get N(0, 0.02) rows here instead of whatever memory held."""
@@ -196,6 +267,7 @@ def _with_canon(spec, sd):
 class EngramGemma4ForCausalLM(Gemma4ForCausalLM):
     def __init__(self, *, vllm_config: VllmConfig, prefix: str = ""):
         super().__init__(vllm_config=vllm_config, prefix=prefix)
+        fuse_row_parallel(self, vllm_config)
         self.micro_engram_slots = []
         self.micro_engram_separate = False
         self.micro_engram_conf = None

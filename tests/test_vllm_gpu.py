@@ -67,7 +67,7 @@ def _hf_logprobs(hf, eng, ids):
     return plain, withe
 
 
-def _serve(folder, prompt, n_new, tp=1):
+def _serve(folder, prompt, n_new, tp=1, fused=False):
     os.environ["VLLM_ENABLE_V1_MULTIPROCESSING"] = "0"
     os.environ["VLLM_USE_V2_MODEL_RUNNER"] = "1"
     if tp > 1:
@@ -80,7 +80,8 @@ def _serve(folder, prompt, n_new, tp=1):
     extra = {"tensor_parallel_size": tp, "distributed_executor_backend": "mp"} if tp > 1 else {}
     llm = LLM(model=folder, skip_tokenizer_init=True, dtype="bfloat16", enforce_eager=True, max_model_len=256,
               gpu_memory_utilization=0.2, max_num_seqs=4,
-              additional_config={"micro_engram": os.path.join(folder, "engram_config.json")}, **extra)
+              additional_config={"micro_engram": os.path.join(folder, "engram_config.json"),
+                                 "micro_engram_fused_tp": fused}, **extra)
     sp = SamplingParams(max_tokens=n_new, temperature=0.0, prompt_logprobs=0, logprobs=0, detokenize=False)
     out = llm.generate([{"prompt_token_ids": prompt}], sp)[0]
     prompt_lp = [None] + [next(iter(d.values())).logprob for d in out.prompt_logprobs[1:]]
@@ -89,16 +90,17 @@ def _serve(folder, prompt, n_new, tp=1):
     return prompt_lp, gen, gen_lp
 
 
-def _main(folder, tp):
+def _main(folder, tp, fused):
     torch.manual_seed(3)
     prompt = torch.randint(3, V, (40,)).tolist()
-    prompt_lp, gen, gen_lp = _serve(folder, prompt, 8, tp)
+    prompt_lp, gen, gen_lp = _serve(folder, prompt, 8, tp, fused)
     with open(os.path.join(folder, "served.json"), "w") as f:
         json.dump({"prompt": prompt, "prompt_lp": prompt_lp, "gen": gen, "gen_lp": gen_lp}, f)
 
 
-@pytest.mark.parametrize("tp", [1, 2])
-def test_vllm_serves_engram_like_hf(tmp_path, tp):
+@pytest.mark.parametrize("tp,fused", [(1, False), (2, False), (2, True)])
+def test_vllm_serves_engram_like_hf(tmp_path, tp, fused):
+    """fused: the row-parallel linears' GEMM + all-reduce replaced by the fused peer-memory op."""
     pytest.importorskip("vllm")
     if torch.cuda.device_count() < tp:
         pytest.skip(f"needs {tp} GPUs")
@@ -109,8 +111,10 @@ def test_vllm_serves_engram_like_hf(tmp_path, tp):
     hf, eng = _build(folder)
     env = dict(os.environ, PYTHONPATH=os.pathsep.join([os.path.dirname(os.path.dirname(__file__)),
                                                        os.environ.get("PYTHONPATH", "")]))
-    r = subprocess.run([sys.executable, __file__, folder, str(tp)], env=env, capture_output=True, text=True,
-                       timeout=900)
+    r = subprocess.run([sys.executable, __file__, folder, str(tp), str(int(fused))], env=env, capture_output=True,
+                       text=True, timeout=900)
+    if fused:
+        assert "row-parallel linears fused" in r.stdout + r.stderr, "the fused op was not switched on"
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-6000:]
     with open(os.path.join(folder, "served.json")) as f:
         s = json.load(f)
@@ -134,4 +138,4 @@ def test_vllm_serves_engram_like_hf(tmp_path, tp):
 
 
 if __name__ == "__main__":
-    _main(sys.argv[1], int(sys.argv[2]) if len(sys.argv) > 2 else 1)
+    _main(sys.argv[1], int(sys.argv[2]) if len(sys.argv) > 2 else 1, len(sys.argv) > 3 and sys.argv[3] == "1")
