@@ -196,21 +196,19 @@ class MicroEngram(nn.Module):
         """(q scale, k scale) in fp32: 1 + delta, with the delta made fp32 first."""
         return 1 + self.q_scale.float(), 1 + self.k_scale.float()
 
+    def _shift_scales(self, sd, prefix, offset):
+        """Module deltas <-> stored scales: a state dict holds 1 + delta in fp32 (in bf16 a small
+        delta would round away), the module holds the delta itself."""
+        for key in [prefix + n for n in self.DELTA_SCALES if prefix + n in sd]:
+            sd[key] = sd[key].detach().float() + offset
+
     def _save_to_state_dict(self, destination, prefix, keep_vars):
         super()._save_to_state_dict(destination, prefix, keep_vars)
-        for name in self.DELTA_SCALES:
-            key = prefix + name
-            if key in destination:
-                destination[key] = destination[key].detach().float() + 1
+        self._shift_scales(destination, prefix, 1.0)
 
-    def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
-                              error_msgs):
-        for name in self.DELTA_SCALES:
-            key = prefix + name
-            if key in state_dict:
-                state_dict[key] = state_dict[key].float() - 1
-        super()._load_from_state_dict(state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
-                                      error_msgs)
+    def _load_from_state_dict(self, state_dict, prefix, *rest):
+        self._shift_scales(state_dict, prefix, -1.0)
+        super()._load_from_state_dict(state_dict, prefix, *rest)
 
     # ------------------------------------------------------------------ hashing
     def _consts(self, device):

@@ -75,16 +75,21 @@ def messages_of(obj, ds):
 
 
 # ============================================================================ tokenizing
+_JINJA_TAGS = ("{%", "{{")
+
+
 def load_template(value):
-    """A chat template from chat_template_jinja: a file path or the template text itself."""
+    """chat_template_jinja as template text. The key names a template file or holds the template
+    itself; a value that opens no file and carries no Jinja tag is a missing file."""
     if not value:
         return None
-    if os.path.isfile(value):
+    try:
         with open(value, encoding="utf-8") as f:
             return f.read()
-    if "{%" in value or "{{" in value:
-        return value
-    raise FileNotFoundError(f"chat_template_jinja: no such file {value}")
+    except OSError:  # no such file, a folder, or template text too long to be a path
+        if any(tag in value for tag in _JINJA_TAGS):
+            return value
+        raise FileNotFoundError(f"chat_template_jinja: no such file {value}") from None
 
 
 def _turn_end(text, start, end, eot):
@@ -301,16 +306,17 @@ def tokenize_all(cfg, tokenizer, tok_path):
 
 
 def read_axolotl_prepared(path):
-    """Samples from an Axolotl prepared dataset (input_ids; labels -100 mark untrained tokens)."""
+    """Samples from an Axolotl prepared dataset: a datasets.save_to_disk folder (a Dataset, or a
+    DatasetDict whose "train" split is used) with input_ids and labels, where a label of -100
+    marks a token that is not trained."""
     from datasets import load_from_disk
 
-    ds = load_from_disk(path)
-    if hasattr(ds, "keys") and "train" in ds:
-        ds = ds["train"]
-    cols = ds.select_columns(["input_ids", "labels"])
-    items = [(r["input_ids"], np.asarray(r["labels"]) != IGNORE) for r in cols]
-    LOG.warning(f"[micro_engram] {len(items):,} samples from the Axolotl prepared dataset {path}")
-    return Samples.from_list(items)
+    loaded = load_from_disk(path)
+    split = loaded["train"] if isinstance(loaded, dict) and "train" in loaded else loaded  # DatasetDict is a dict
+    ids = split["input_ids"]
+    trained = [np.not_equal(np.asarray(lab), IGNORE) for lab in split["labels"]]
+    LOG.warning(f"[micro_engram] {len(ids):,} samples from the Axolotl prepared dataset {path}")
+    return Samples.from_list(list(zip(ids, trained)))
 
 
 def prepare(cfg, tokenizer, tok_path, rank=0, barrier=None):

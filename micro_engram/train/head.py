@@ -292,11 +292,13 @@ class _FusedVocabCE(torch.autograd.Function):
 
 
 def reference_loss_sum(hidden, labels, weight, softcap=None):
-    """Plain full-logit loss sum (tests)."""
-    z = (hidden.to(weight.dtype) @ weight.t()).float()
+    """Summed token cross-entropy over the whole vocabulary, the plain way (the tests' oracle for
+    the vocab-parallel loss): fp32 logits hidden . weight^T, the optional softcap
+    cap * tanh(z / cap), then log-sum-exp minus the target logit, over tokens whose label is not
+    IGNORE."""
+    logits = torch.mm(hidden.to(weight.dtype), weight.t()).float()
     if softcap:
-        z = torch.tanh(z / softcap) * softcap
-    valid = labels != IGNORE
-    lse = torch.logsumexp(z, dim=-1)
-    tgt = z.gather(1, labels.clamp_min(0)[:, None]).squeeze(1)
-    return torch.where(valid, lse - tgt, torch.zeros_like(lse)).sum()
+        logits = softcap * torch.tanh(logits / softcap)
+    keep = labels.ne(IGNORE)
+    picked = torch.take_along_dim(logits, labels.masked_fill(~keep, 0).unsqueeze(1), dim=1).squeeze(1)
+    return ((torch.logsumexp(logits, dim=1) - picked) * keep).sum()

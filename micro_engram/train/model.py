@@ -121,19 +121,19 @@ def grad_from_layer(text, first_layer, enabled):
     if not enabled or first_layer is None:
         yield
         return
-    layer = text.layers[first_layer]
+    before = torch.is_grad_enabled()
 
-    def grad_on(*_):
+    def switch_on(_module, _args, _output):  # returns nothing, so the layer's output stands
         torch.set_grad_enabled(True)
 
-    h = layer.register_forward_hook(grad_on, prepend=True)
-    prev = torch.is_grad_enabled()
+    # forward hooks run in registration order: prepended, this one runs ahead of the engram's
+    hook = text.layers[first_layer].register_forward_hook(switch_on, prepend=True)
     torch.set_grad_enabled(False)
     try:
         yield
     finally:
-        h.remove()
-        torch.set_grad_enabled(prev)
+        torch.set_grad_enabled(before)
+        hook.remove()
 
 
 def checkpointing(model, text, cfg, no_grad_upto):

@@ -27,32 +27,27 @@ NAMESPACE = "micro_engram_b200"
 _warned = False
 
 
-class _PlainOp:
-    """The surface of a registered op (call, register_fake) for when registration fails."""
-
-    def __init__(self, fn: Callable):
-        self._fn = fn
-
-    def __call__(self, *args, **kwargs):
-        return self._fn(*args, **kwargs)
-
-    def register_fake(self, fn: Callable) -> Callable:
-        return fn
+def _unregistered(fn: Callable) -> Callable:
+    """The surface of a registered op (call, register_fake) on the bare function itself."""
+    fn.register_fake = lambda fake: fake
+    return fn
 
 
 def register_kernel_op(name: str, mutates_args: Sequence[str] = ()) -> Callable:
-    """Decorator: register `fn` as torch.ops.micro_engram_b200.<name> (or return a plain shim)."""
+    """Decorator: register `fn` as torch.ops.micro_engram_b200.<name>; if this torch build
+    refuses, keep `fn` callable as it is and say so once."""
+    qualname = f"{NAMESPACE}::{name}"
 
     def deco(fn: Callable):
         global _warned
         try:
-            return torch.library.custom_op(f"{NAMESPACE}::{name}", mutates_args=tuple(mutates_args))(fn)
+            return torch.library.custom_op(qualname, mutates_args=tuple(mutates_args))(fn)
         except Exception as exc:  # noqa: BLE001 - any registration failure keeps the kernel usable
             if not _warned:
                 _warned = True
-                LOG.warning("custom op %s::%s not registered (%s: %s); it runs as a plain call",
-                            NAMESPACE, name, type(exc).__name__, exc)
-            return _PlainOp(fn)
+                LOG.warning("%s not registered (%s: %s): it runs as a plain call that torch.compile traces into",
+                            qualname, type(exc).__name__, exc)
+            return _unregistered(fn)
 
     return deco
 

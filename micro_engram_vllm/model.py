@@ -70,23 +70,26 @@ def _check_weights_exist(conf, path):
                              f"{where} (relative paths start at the config's folder)")
 
 
+def _read_json(path):
+    with open(path) as f:
+        return json.load(f)
+
+
 def select_engram(additional_config, model_dir, environ=None):
-    """The engram to serve, or None for plain Gemma 4."""
+    """The engram to serve, or None for plain Gemma 4: a config named by --additional-config or
+    MICRO_ENGRAM_CONFIG (a file, or a folder holding one; weights in their own files), else a
+    config beside the model (an assembled folder; weights inside the checkpoint)."""
     environ = os.environ if environ is None else environ
     chosen = _chosen_path(additional_config, environ)
-    if chosen:
-        path = os.path.join(chosen, CONFIG_NAME) if os.path.isdir(chosen) else chosen
-        if not os.path.isfile(path):
-            raise ValueError(f"[micro_engram] engram config not found: {path}")
-        with open(path) as f:
-            conf = json.load(f)
-        _check_weights_exist(conf, path)
-        return EngramSelection(conf, path, True)
-    beside = os.path.join(model_dir, CONFIG_NAME)
-    if os.path.isfile(beside):
-        with open(beside) as f:
-            return EngramSelection(json.load(f), beside, False)
-    return None
+    if not chosen:
+        beside = os.path.join(model_dir, CONFIG_NAME)
+        return EngramSelection(_read_json(beside), beside, separate=False) if os.path.isfile(beside) else None
+    path = os.path.join(chosen, CONFIG_NAME) if os.path.isdir(chosen) else chosen
+    if not os.path.isfile(path):
+        raise ValueError(f"[micro_engram] engram config not found: {path}")
+    conf = _read_json(path)
+    _check_weights_exist(conf, path)
+    return EngramSelection(conf, path, separate=True)
 
 
 def resolve_engram(additional_config, model_dir, environ=None):

@@ -8,7 +8,7 @@ from unittest import mock
 import torch
 import torch.nn as nn
 
-from test_vllm_tp import fake_vllm
+from test_vllm_tp import vllm_faked
 
 
 class _RowLinear(nn.Module):
@@ -42,7 +42,7 @@ def _config(extra=None, eager=True):
 
 
 def test_switch_and_routing():
-    with mock.patch.dict(sys.modules, fake_vllm()):
+    with vllm_faked():
         sys.modules.pop("micro_engram_vllm.model", None)
         from micro_engram_vllm import model as M
         from micro_engram_fork_b200.ops.registry import add_tp_linear

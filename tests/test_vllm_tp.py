@@ -5,6 +5,7 @@ vLLM itself cannot run here, so the plugin is imported against a minimal fake of
 modules it uses (`fake_vllm`): a decoder layer that is a tanh(Linear), a causal-LM shell with
 a name-checking weight loader, and the TP helpers backed by the test's process group. 3 ranks
 with 31-row tables give an uneven row split (11/11/9); world 1 is the degenerate case."""
+import contextlib
 import json
 import logging
 import os
@@ -124,6 +125,26 @@ def fake_vllm():
     return {name: module(name, **members) for name, members in tree.items()}
 
 
+@contextlib.contextmanager
+def vllm_faked():
+    """The fake vLLM modules in sys.modules for the duration; afterwards the real entries (or
+    none) come back and the plugin modules that bound the fakes are dropped. Everything else
+    imported meanwhile stays imported: dropping it too (mock.patch.dict(sys.modules) would) makes
+    the next import re-run modules that register torch libraries, which torch refuses."""
+    fakes = fake_vllm()
+    saved = {name: sys.modules.get(name) for name in fakes}
+    sys.modules.update(fakes)
+    try:
+        yield
+    finally:
+        for name, mod in saved.items():
+            if mod is None:
+                sys.modules.pop(name, None)
+            else:
+                sys.modules[name] = mod
+        sys.modules.pop("micro_engram_vllm.model", None)
+
+
 def serving_config(conf_path=None, model_dir="/nonexistent", **extra):
     additional = {"micro_engram": conf_path} if conf_path else {}
     additional.update(extra)
@@ -212,7 +233,7 @@ def _layer_matches(model, full, ids, h):
 def _model_checks(rank, world, tmp):
     from micro_engram.rows import row_range
 
-    with mock.patch.dict(sys.modules, fake_vllm()):
+    with vllm_faked():
         sys.modules.pop("micro_engram_vllm.model", None)
         from micro_engram_vllm.model import EngramGemma4ForCausalLM
 
