@@ -380,12 +380,18 @@ class Trainer:
                 g.copy_(part.view_as(g))
 
     # ================================================================== the run
+    def _publish_config(self, rows_dir):
+        """Rank 0 writes the run's engram config into output_dir: with no weights while the run
+        trains, pointing at the saved row folder once it is done."""
+        if self.rank != 0:
+            return
+        os.makedirs(self.cfg.output_dir, exist_ok=True)
+        write_config(build_config(self.base_conf, self.slots, lambda _slot: rows_dir), self.cfg.output_dir)
+
     def train(self):
         cfg = self.cfg
         self._maybe_resume()
-        if self.rank == 0:
-            os.makedirs(cfg.output_dir, exist_ok=True)
-            write_config(build_config(self.base_conf, self.slots, lambda s: None), cfg.output_dir)
+        self._publish_config(None)
         self.reporter.open()
         snapshot_at = cfg.micro_engram_memory_snapshot
         if snapshot_at and self.device.type == "cuda":
@@ -414,8 +420,8 @@ class Trainer:
         if not cfg.save_steps or self.global_step % cfg.save_steps:
             self.save_checkpoint()
         self.rows.save(os.path.join(cfg.output_dir, ROWS_DIR))
+        self._publish_config(ROWS_DIR)
         if self.rank == 0:
-            write_config(build_config(self.base_conf, self.slots, lambda s: ROWS_DIR), cfg.output_dir)
             self.log0(f"[micro_engram] done: {cfg.output_dir}/{ROWS_DIR} holds the engram; serve it with "
                       f"--additional-config '{{\"micro_engram\": \"{cfg.output_dir}/{CONFIG_NAME}\"}}'")
 
@@ -443,13 +449,13 @@ def _fail_fast():
     import sys
     import traceback
 
-    rank = os.environ.get("RANK", "?")
-    print(f"\n[micro_engram] rank {rank} FAILED:", file=sys.stderr, flush=True)
-    traceback.print_exc()
+    who = f"[micro_engram] rank {os.environ.get('RANK', '?')}"
+    lines = [f"\n{who} FAILED:\n{traceback.format_exc()}"]
     if torch.cuda.is_available() and torch.cuda.is_initialized():
         dev = torch.cuda.current_device()
-        print(f"[micro_engram] rank {rank}: {torch.cuda.memory_allocated(dev) / 2 ** 30:.2f} GiB allocated, "
-              f"{torch.cuda.memory_reserved(dev) / 2 ** 30:.2f} GiB reserved", file=sys.stderr, flush=True)
+        gib = [torch.cuda.memory_allocated(dev) / 2 ** 30, torch.cuda.memory_reserved(dev) / 2 ** 30]
+        lines.append(f"{who}: {gib[0]:.2f} GiB allocated, {gib[1]:.2f} GiB reserved\n")
+    sys.stderr.write("".join(lines))
     sys.stderr.flush()
     os._exit(1)
 
