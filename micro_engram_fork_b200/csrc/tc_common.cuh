@@ -23,9 +23,19 @@ namespace tc {
 // matches, so a thread that has made no runtime call yet (autograd's worker thread on its first
 // backward op, for one) can get here with no current context; bind the current device's
 // primary context first.
+// The driver function is looked up through the runtime (cudaGetDriverEntryPoint), as the
+// tensor-map encoder is, so the extension does not link libcuda and imports on a machine
+// without a driver.
 inline void bind_primary_context() {
+  using CtxGetCurrent = CUresult (*)(CUcontext*);
+  static CtxGetCurrent get_current = [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) != cudaSuccess) fn = nullptr;
+    return reinterpret_cast<CtxGetCurrent>(fn);
+  }();
   CUcontext cur = nullptr;
-  if (cuCtxGetCurrent(&cur) != CUDA_SUCCESS || cur == nullptr) {
+  if (get_current == nullptr || get_current(&cur) != CUDA_SUCCESS || cur == nullptr) {
     int dev = 0;
     cudaGetDevice(&dev);
     cudaSetDevice(dev);

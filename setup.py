@@ -35,7 +35,6 @@ setup(
         sources=SOURCES,
         include_dirs=[os.path.join(HERE, CSRC)],
         extra_compile_args={"cxx": CXX, "nvcc": NVCC},
-        libraries=["cuda"],
     )],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
     entry_points={"vllm.general_plugins": ["micro_engram = micro_engram_vllm:register"]},
