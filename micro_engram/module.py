@@ -182,14 +182,15 @@ class MicroEngram(nn.Module):
         return list(self.parameters()) + list(self.row_shards or [])
 
     def lookup(self, idx):
-        """Table rows for the hashed ids `idx` (one tensor per table)."""
-        if self.row_shards is not None:
-            if self.row_lookup_fn is not None:
-                return self.row_lookup_fn(self, idx)
+        """Table rows for the hashed ids `idx` (one tensor per table): the module's own tables,
+        or, when row-sharded, the installed lookup (vLLM's TP path) or the row exchange."""
+        if self.row_shards is None:
+            return [tab(i) for tab, i in zip(self.tables, idx)]
+        if self.row_lookup_fn is None:
             from .rows import row_lookup
 
             return row_lookup(self, idx)
-        return [tab(i) for tab, i in zip(self.tables, idx)]
+        return self.row_lookup_fn(self, idx)
 
     # ------------------------------------------------------------------ delta scales
     def norm_scales(self):

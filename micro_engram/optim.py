@@ -21,6 +21,11 @@ import torch
 from micro_engram_fork_b200.ops import use_native
 
 
+def _nonzero_rows(g):
+    """Indices of the rows of g (first dimension) that hold any non-zero value."""
+    return g.reshape(g.shape[0], -1).ne(0).any(dim=1).nonzero().squeeze(1)
+
+
 def _local(t):
     to_local = getattr(t, "to_local", None)
     return to_local() if to_local is not None else t
@@ -232,15 +237,15 @@ class LazyAdamW(torch.optim.Optimizer):
             if not group["lazy"]:
                 raise ValueError("sparse row gradients need lazy=True")
             rows, g = sparse
-            keep = (g != 0).flatten(1).any(dim=1)
-            rows, g = rows[keep], g[keep]
+            live = _nonzero_rows(g)
+            rows, g = rows[live], g[live]
             if rows.numel() == 0:
                 return
             pw = P.index_select(0, rows).float()
             m, v = M.index_select(0, rows).float(), V.index_select(0, rows).float()
         elif group["lazy"] and P.dim() >= 2:
             G = _local(p.grad)
-            rows = (G != 0).flatten(1).any(dim=1).nonzero().squeeze(1)
+            rows = _nonzero_rows(G)
             if rows.numel() == 0:
                 return
             pw, g = P.index_select(0, rows).float(), G.index_select(0, rows).float()

@@ -127,10 +127,10 @@ def with_stops(tagged, stops, cancel):
 
 
 def parse_stops(body):
-    stop = body.get("stop")
-    if not stop:
-        return []
-    return [stop] if isinstance(stop, str) else [s for s in stop if s]
+    """The request's stop strings as a list: OpenAI accepts one string or a list (empty entries
+    mean nothing)."""
+    stop = body.get("stop") or []
+    return list(filter(None, [stop] if isinstance(stop, str) else stop))
 
 
 def flat_content(content):

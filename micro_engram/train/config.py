@@ -80,10 +80,11 @@ class FsdpConfig(BaseModel):
 
     @model_validator(mode="before")
     @classmethod
-    def _drop_ignored(cls, data):
-        if isinstance(data, dict):
-            return {k: v for k, v in data.items() if k not in IGNORED_FSDP_KEYS}
-        return data
+    def _without_axolotl_only(cls, data):
+        """Axolotl FSDP keys with no meaning here are dropped before the strict check."""
+        if not isinstance(data, dict):
+            return data
+        return {k: data[k] for k in data.keys() - IGNORED_FSDP_KEYS}
 
 
 class TrainConfig(MicroEngramArgs):
@@ -178,9 +179,9 @@ class TrainConfig(MicroEngramArgs):
 
     @property
     def large_head_policy(self):
-        if self.large_head_attention:
-            return self.large_head_attention
-        return "auto" if self.flash_attn_d512 else "sdpa"
+        """The hd-512 attention route: large_head_attention when set, else flash_attn_d512's
+        legacy meaning (True: auto, unset or False: sdpa)."""
+        return self.large_head_attention or ("auto" if self.flash_attn_d512 else "sdpa")
 
     def get(self, key, default=None):
         v = getattr(self, key, default)

@@ -71,10 +71,10 @@ def load_base(cfg, rank, local_rank, device):
 
 
 def text_model(model):
-    """(name, the text decoder stack's owner)."""
-    name, _ = find_text_layers(model)
-    parent = name.rsplit(".", 1)[0] if "." in name else ""
-    return parent, (model.get_submodule(parent) if parent else model)
+    """(name, the text decoder stack's owner): the module one level above the layer list."""
+    layers_name, _ = find_text_layers(model)
+    parent, _, _ = layers_name.rpartition(".")
+    return parent, model.get_submodule(parent) if parent else model
 
 
 def hybrid_attention(text, cfg):
