@@ -339,7 +339,7 @@ __global__ void __launch_bounds__(256) row_push_kernel(const __nv_bfloat16* __re
     const int64_t e = base + lane;
     int k = 0, owner = a.me, local = 0, slot = -1;
     int64_t n = 0;
-    const bool valid = e < events;
+    bool valid = e < events;
     if (valid) {
       k = (int)(e / N);
       n = e - (int64_t)k * N;
@@ -347,6 +347,13 @@ __global__ void __launch_bounds__(256) row_push_kernel(const __nv_bfloat16* __re
       const int64_t pk = a.per[k];
       owner = (int)(row / pk);
       local = (int)(row - (int64_t)owner * pk);
+#ifdef ME_BOUNDS_CHECK
+      if (row < 0 || owner >= a.world) {  // a row id outside every shard: dropped, reported
+        report(a.status, ME_ERR_BOUNDS, k);
+        valid = false;
+        owner = a.me;
+      }
+#endif
     }
     // entries for other owners: one counter atomic per owner per warp, then each lane's place
     const bool remote = valid && owner != a.me;
@@ -437,9 +444,17 @@ __global__ void __launch_bounds__(256) row_accumulate_kernel(RowTablesArgs a, fl
       if (sub == 0) {
         const int2 h = __ldcg(hdr + i);
         k = h.x;
-        const int t = a.me * a.n_tables + k;
-        s = claim_slot(reinterpret_cast<int*>(a.pos_ptrs[t]), reinterpret_cast<int*>(a.cnt_ptrs[t]),
-                       reinterpret_cast<int*>(a.list_ptrs[t]), a.caps[k], h.y, a.status, k);
+#ifdef ME_BOUNDS_CHECK
+        if (k < 0 || k >= a.n_tables || h.y < 0 || h.y >= a.per[k]) {  // a corrupt inbox entry
+          report(a.status, ME_ERR_BOUNDS, 600 + src);
+          k = 0;  // s stays 0: the entry is dropped
+        } else
+#endif
+        {
+          const int t = a.me * a.n_tables + k;
+          s = claim_slot(reinterpret_cast<int*>(a.pos_ptrs[t]), reinterpret_cast<int*>(a.cnt_ptrs[t]),
+                         reinterpret_cast<int*>(a.list_ptrs[t]), a.caps[k], h.y, a.status, k);
+        }
       }
       s = __shfl_sync(gmask, s, 0, 8);
       k = __shfl_sync(gmask, k, 0, 8);
@@ -521,7 +536,13 @@ __global__ void __launch_bounds__(256) rows_serve_kernel(FetchArgs a, int ntok_m
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int64_t w0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   for (int r = 0; !failed && r < a.world; ++r) {
-    const int n = ntok[r];
+    int n = ntok[r];
+#ifdef ME_BOUNDS_CHECK
+    if (n < 0 || n > a.cap_tok) {  // a token count beyond the requester's lookup list
+      if (threadIdx.x == 0) report(a.status, ME_ERR_BOUNDS, 700 + r);
+      n = 0;
+    }
+#endif
     const int64_t events = (int64_t)n * a.n_tables;
     const uint8_t* req = reinterpret_cast<const uint8_t*>(a.fbases[r]);
     const int64_t* ridx = reinterpret_cast<const int64_t*>(req + kFIdx);
@@ -536,7 +557,10 @@ __global__ void __launch_bounds__(256) rows_serve_kernel(FetchArgs a, int ntok_m
         t = (int)(e - (int64_t)k * n);
         const int64_t row = __ldcg(ridx + (int64_t)k * a.cap_tok + t);
         const int64_t pk = a.per[k];
-        if (row / pk == a.me) local = row - (int64_t)a.me * pk;
+#ifdef ME_BOUNDS_CHECK
+        if (row < 0 || row / pk >= a.world) report(a.status, ME_ERR_BOUNDS, 800 + k);  // no owner serves it
+#endif
+        if (row >= 0 && row / pk == a.me) local = row - (int64_t)a.me * pk;
       }
       unsigned own = __ballot_sync(0xffffffffu, local >= 0);
       while (own) {  // four owned events at a time, 8 lanes each
