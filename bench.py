@@ -35,7 +35,7 @@ METRIC = "train tokens/s (31B-class, seq 8192)"
 MODEL = "31B-class Gemma-style hybrid decoder (60L, d5376, FFN 21504, 32q heads, sliding hd256x16kv / global hd512x4kv 5:1, V=262144), stage-1 engram"
 SEQ, MBS, GA = 8192, 1, 3
 TABLES = {2: 1572864, 3: 4194304, 4: 4194304}
-BASELINE_VALUE = None  # the reference publishes no tokens/s figure
+BASELINE_VALUE = None  # the reference publishes no tokens/s figure, so vs_baseline is null
 
 
 def base_config_31b():

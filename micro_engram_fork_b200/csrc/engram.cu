@@ -579,7 +579,7 @@ __global__ void __launch_bounds__(256) rows_serve_kernel(FetchArgs a, int ntok_m
           uint4* dst = recv + ((int64_t)tt * a.n_tables + kk) * chunks;
           for (int c = sub; c < chunks; c += 8) dst[c] = src[c];
         }
-        for (int q = 0; q < 4 && own; ++q) own &= own - 1;  // the four handled this round
+        for (int q = 0; q < 4 && own; ++q) own &= own - 1;  // the four handled in this pass
       }
     }
   }
