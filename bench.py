@@ -29,7 +29,6 @@ import re
 import subprocess
 import sys
 import tempfile
-import time
 
 METRIC = "train tokens/s (31B-class, seq 8192)"
 MODEL = "31B-class Gemma-style hybrid decoder (60L, d5376, FFN 21504, 32q heads, sliding hd256x16kv / global hd512x4kv 5:1, V=262144), stage-1 engram"

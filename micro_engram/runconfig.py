@@ -20,7 +20,7 @@ import json
 import logging
 import os
 from collections.abc import Mapping
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 import torch
 

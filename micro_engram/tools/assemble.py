@@ -17,7 +17,6 @@ import json
 import os
 import re
 import shutil
-import sys
 
 from micro_engram.weights import CONFIG_NAME, base_mismatch, engram_specs, load_engram_weights
 

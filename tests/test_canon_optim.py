@@ -3,7 +3,6 @@
 Oracles: an independently written hash, torch.optim.AdamW, and analytic properties
 (untouched rows bit-identical, bias-corrected second moment = 1 under a constant gradient,
 unbiased stochastic rounding)."""
-import os
 
 import pytest
 import torch

@@ -1,7 +1,6 @@
 """Our Gemma-4-style decoder == HF transformers' Gemma4ForCausalLM (the oracle), on CPU fp32:
 weights saved by HF load through our safetensors loader; logits match for one document and
 for packed documents (HF isolates them via position_ids on the eager path with a mask)."""
-import os
 import tempfile
 
 import pytest

@@ -68,7 +68,6 @@ def _worker(rank, world, port, q):
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     try:
         from micro_engram_fork_b200.models import gemma as G
-        from micro_engram_fork_b200.ops.attention import doc_starts
         from micro_engram_fork_b200.parallel import sharded_base as SB
 
         dev = torch.device("cuda", rank)
