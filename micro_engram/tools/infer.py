@@ -14,196 +14,205 @@ import glob
 import json
 import os
 import re
+from collections import ChainMap
 
 import torch
 
 from micro_engram.module import MicroEngram, check_loaded, engram_from_spec, find_text_layers, layer_device_dtype
 from micro_engram.weights import CONFIG_NAME, base_mismatch, engram_specs, resolve_weights_path
-from micro_engram.weights import load_engram_weights as load_engram_file
+from micro_engram.weights import load_engram_weights as read_engram_source
 
-_LAYER_KEY = re.compile(r"layers\.(\d+)\.micro_engram\.")
+_ENGRAM_KEY = re.compile(r"layers\.(\d+)\.micro_engram\.(.+)$")
+DEFAULTS = {"layer": 0, "table_size": 65_536, "engram_dim": 128, "num_heads": 4, "gate": "scalar", "seed": 0}
+_FROM_CONFIG = ("layer", "table_size", "table_sizes", "engram_dim", "num_heads", "gate", "seed")
+_PASSED_THROUGH = ("pad_id", "model_dim", "token_merge", "canon_path")
 
 
-def first(*values):
-    for v in values:
-        if v is not None:
-            return v
-    return None
+def _present(d):
+    """The entries of d that say something (None means: not given here)."""
+    return {k: v for k, v in d.items() if v is not None}
+
+
+# ------------------------------------------------------------------ where the engram comes from
+def _model_folder_tensors(model_path):
+    """(local-name state dict, layer) of the engram inside a model folder's own shards:
+    safetensors first, .bin only when those hold none."""
+    from safetensors import safe_open
+
+    def shards():
+        for fn in sorted(glob.glob(os.path.join(model_path, "*.safetensors"))):
+            with safe_open(fn, framework="pt", device="cpu") as fh:
+                yield from ((k, fh.get_tensor(k)) for k in fh.keys() if "micro_engram." in k)
+
+    def bins():
+        for fn in sorted(glob.glob(os.path.join(model_path, "*.bin"))):
+            yield from ((k, v) for k, v in torch.load(fn, map_location="cpu").items() if "micro_engram." in k)
+
+    for source in (shards, bins):
+        found, layer = {}, None
+        for key, tensor in source():
+            m = _ENGRAM_KEY.search(key)
+            if m:
+                layer = int(m.group(1))
+            found[key.split("micro_engram.", 1)[1]] = tensor
+        if found:
+            return found, layer
+    return {}, None
 
 
 def load_engram_weights(model_path, engram_pt=None):
-    """(engram state dict with local names, layer seen in the key names or None)."""
-    if engram_pt:
-        return load_engram_file(engram_pt), None
-    sd, layer = {}, None
-
-    def take(key, val):
-        nonlocal layer
-        m = _LAYER_KEY.search(key)
-        if m:
-            layer = int(m.group(1))
-        sd[key.split("micro_engram.", 1)[1]] = val
-
-    from safetensors import safe_open
-
-    for fn in sorted(glob.glob(os.path.join(model_path, "*.safetensors"))):
-        with safe_open(fn, framework="pt", device="cpu") as fh:
-            for k in fh.keys():
-                if "micro_engram." in k:
-                    take(k, fh.get_tensor(k))
-    if not sd:
-        for fn in sorted(glob.glob(os.path.join(model_path, "*.bin"))):
-            for k, v in torch.load(fn, map_location="cpu").items():
-                if "micro_engram." in k:
-                    take(k, v)
-    return sd, layer
+    """(engram state dict with local names, layer named by the keys or None)."""
+    return (read_engram_source(engram_pt), None) if engram_pt else _model_folder_tensors(model_path)
 
 
-def _read_conf(args):
+def _config_of(args):
+    """(engram config dict, its path): --engram-config, else the one beside the model, else {}."""
     path = args.engram_config or os.path.join(args.model, CONFIG_NAME)
-    if os.path.isfile(path):
-        with open(path) as f:
-            return json.load(f), path
-    if args.engram_config:
-        raise SystemExit(f"--engram-config file not found: {args.engram_config}")
-    return {}, path
+    if not os.path.isfile(path):
+        if args.engram_config:
+            raise SystemExit(f"--engram-config file not found: {args.engram_config}")
+        return {}, path
+    with open(path) as f:
+        return json.load(f), path
 
 
 def shape_settings(sd, orders):
-    """What the saved tensors say about the engram's layout."""
-    n_tables = sum(1 for k in sd if k.startswith("tables.") and k.endswith(".weight"))
-    t0 = sd.get("tables.0.weight")
-    rows = [int(sd[f"tables.{k}.weight"].shape[0]) for k in range(n_tables) if f"tables.{k}.weight" in sd]
-    heads = n_tables // len(orders) if n_tables else None
-    gate = ("ple" if "up.weight" in sd else "scalar_sqrt" if "q_scale" in sd else "scalar" if "value.weight" in sd
-            else None)
-    return {"table_size": int(t0.shape[0]) if t0 is not None else None,
-            "table_sizes": ({n: rows[i * heads] for i, n in enumerate(orders)}
-                            if rows and heads and len(set(rows)) > 1 else None),
-            "engram_dim": int(t0.shape[1]) if t0 is not None else None, "num_heads": heads, "gate": gate}
+    """What the saved tensors say about the engram's layout (None where they say nothing)."""
+    gate = "ple" if "up.weight" in sd else "scalar_sqrt" if "q_scale" in sd else "scalar" if "value.weight" in sd \
+        else None
+    tables = [sd[f"tables.{k}.weight"] for k in range(len(sd)) if f"tables.{k}.weight" in sd]
+    if not tables:
+        return {"table_size": None, "table_sizes": None, "engram_dim": None, "num_heads": None, "gate": gate}
+    heads = len(tables) // len(orders)
+    rows = [int(t.shape[0]) for t in tables]
+    per_order = {n: rows[i * heads] for i, n in enumerate(orders)} if heads and len(set(rows)) > 1 else None
+    return {"table_size": rows[0], "table_sizes": per_order, "engram_dim": int(tables[0].shape[1]),
+            "num_heads": heads or None, "gate": gate}
 
 
 def resolve_settings(args, sd, layer_from_key):
-    conf, path = _read_conf(args)
+    """One engram's settings, each key from the first layer that gives it: flags, the engram
+    config, the saved tensors, DEFAULTS."""
+    conf, path = _config_of(args)
     orders = tuple(conf.get("orders", (2, 3)))
-    shp = shape_settings(sd, orders)
-    s = {"layer": first(args.layer, conf.get("layer"), layer_from_key, 0),
-         "table_size": first(args.table_size, conf.get("table_size"), shp["table_size"], 65_536),
-         "table_sizes": None if args.table_size else first(conf.get("table_sizes"), shp["table_sizes"]),
-         "engram_dim": first(args.dim, conf.get("engram_dim"), shp["engram_dim"], 128),
-         "num_heads": first(args.heads, conf.get("num_heads"), shp["num_heads"], 4),
-         "orders": orders, "pad_id": conf.get("pad_id"), "model_dim": conf.get("model_dim"),
-         "token_merge": conf.get("token_merge"), "canon_path": conf.get("canon_path"),
-         "gate": first(getattr(args, "gate", None), conf.get("gate"), shp["gate"], "scalar"),
-         "seed": first(conf.get("seed"), 0)}
+    flags = _present({"layer": args.layer, "table_size": args.table_size, "engram_dim": args.dim,
+                      "num_heads": args.heads, "gate": getattr(args, "gate", None)})
+    seen = _present({**shape_settings(sd, orders), "layer": layer_from_key})
+    chain = ChainMap(flags, _present({k: conf.get(k) for k in _FROM_CONFIG}), seen, DEFAULTS)
+    settings = {k: chain.get(k) for k in (*DEFAULTS, "table_sizes")}
+    if args.table_size:  # an explicit size is one size for every order
+        settings["table_sizes"] = None
+    settings.update({"orders": orders}, **{k: conf.get(k) for k in _PASSED_THROUGH})
     if conf:
         print(f"[engram] settings: {path} (explicit flags override it)")
-    elif shp["table_size"] is not None:
+    elif "table_size" in seen:
         print("[engram] no engram config: settings read from the saved tensors (orders 2 and 3 assumed)")
     else:
         print("[engram] no config and no tensors to read: defaults")
-    print("[engram] using: " + str({k: v for k, v in s.items() if k not in ("pad_id", "model_dim", "canon_path")}))
-    return s
-
-
-class EngramRunner:
-    """Attaches engram(s) to an HF model and keeps the token history of one generation.
-
-    EngramRunner(model, engram, layer) or EngramRunner(model, [(engram, layer), ...])."""
-
-    def __init__(self, model, engrams, layer_idx=None):
-        self.model = model
-        self.engrams = [(engrams, layer_idx)] if layer_idx is not None else list(engrams)
-        self.engram = self.engrams[0][0]
-        self.hist = None
-        self.enabled = True
-        _, layers = find_text_layers(model)
-        model.register_forward_pre_hook(self._grab, with_kwargs=True)
-        for engram, layer in self.engrams:
-            target = layers[layer]
-            device, dtype = layer_device_dtype(target)
-            engram.to(device=device, dtype=dtype)
-            target.add_module("micro_engram", engram)
-            target.register_forward_hook(self._hook(engram))
-
-    def reset(self):
-        self.hist = None
-
-    def _grab(self, _mod, args, kwargs):
-        ids = kwargs.get("input_ids")
-        if ids is None and args:
-            ids = args[0]
-        if ids is not None:
-            self.hist = ids if self.hist is None else torch.cat([self.hist, ids.to(self.hist.device)], dim=1)
-
-    def _hook(self, engram):
-        def inject(_mod, _args, output):
-            if not self.enabled or self.hist is None:
-                return output
-            hidden = output[0] if isinstance(output, tuple) else output
-            new = self.forward(engram, hidden)
-            return (new,) + tuple(output[1:]) if isinstance(output, tuple) else new
-        return inject
-
-    @torch.no_grad()
-    def forward(self, engram, hidden):
-        T = hidden.shape[1]
-        tail = self.hist[:, -(T + max(engram.orders) - 1):]  # all that T new positions' n-grams reach
-        idx = [i[:, -T:] for i in engram.hash_ids(tail.to(hidden.device))]
-        return engram.inject(hidden, idx)
+    shown = {k: v for k, v in settings.items() if k not in ("pad_id", "model_dim", "canon_path")}
+    print(f"[engram] using: {shown}")
+    return settings
 
 
 def plan_engrams(args):
-    """[(settings, state dict)] per engram, read before the model load so bad paths fail fast."""
-    explicit = args.engram_pt
+    """[(settings, state dict)] per engram, read before the model loads so a bad path fails fast."""
+    given_pt = args.engram_pt
     if not args.engram_pt and args.engram_config:
         with open(args.engram_config) as f:
             args.engram_pt = resolve_weights_path(json.load(f), args.engram_config)
-    conf, conf_path = _read_conf(args)
-    if conf:
-        msg = base_mismatch(conf, args.model)
-        if msg:
-            print(f"[engram] WARNING: {msg}")
-    if len(conf.get("engrams") or []) > 1:
-        plans = []
-        for spec in engram_specs(conf, conf_path):
-            src = explicit or spec["weights"] or args.model
-            sd = load_engram_file(src, layer=spec["layer"])
-            if not any(k.startswith("tables.") for k in sd):
-                raise SystemExit(f"no engram weights for layer {spec['layer']} in {src}")
-            spec["model_dim"] = conf.get("model_dim")
-            print(f"[engram] layer {spec['layer']}: {spec['gate']} gate, {spec['num_heads']} heads, seed "
-                  f"{spec['seed']}, from {src}")
-            plans.append((spec, sd))
-        return plans
-    sd, layer = load_engram_weights(args.model, args.engram_pt)
-    if not sd:
-        raise SystemExit("no micro_engram weights found (wrong path, or they were not saved)")
-    return [(resolve_settings(args, sd, layer), sd)]
+    conf, conf_path = _config_of(args)
+    note = base_mismatch(conf, args.model) if conf else None
+    if note:
+        print(f"[engram] WARNING: {note}")
+    if len(conf.get("engrams") or []) <= 1:
+        sd, layer = load_engram_weights(args.model, args.engram_pt)
+        if not sd:
+            raise SystemExit("no micro_engram weights found (wrong path, or they were not saved)")
+        return [(resolve_settings(args, sd, layer), sd)]
+    plans = []
+    for spec in engram_specs(conf, conf_path):  # several engrams: each from its own weights, by layer
+        where = given_pt or spec["weights"] or args.model
+        sd = read_engram_source(where, layer=spec["layer"])
+        if not any(k.startswith("tables.") for k in sd):
+            raise SystemExit(f"no engram weights for layer {spec['layer']} in {where}")
+        spec["model_dim"] = conf.get("model_dim")
+        print(f"[engram] layer {spec['layer']}: {spec['gate']} gate, {spec['num_heads']} heads, seed "
+              f"{spec['seed']}, from {where}")
+        plans.append((spec, sd))
+    return plans
+
+
+# ------------------------------------------------------------------ the generation session
+class EngramSession:
+    """Engrams attached to one HF model, plus the token history of the generation in flight.
+
+    A pre-hook on the model appends every call's input_ids to the history (prefill, then one
+    token per decode step); a hook after each engram's layer adds the engram's gated memory,
+    hashing only the tail of the history that the call's new positions' n-grams reach."""
+
+    def __init__(self, model, attached):
+        self.model, self.attached = model, list(attached)  # [(engram, layer)]
+        self.history, self.enabled = None, True
+        _, layers = find_text_layers(model)
+        model.register_forward_pre_hook(self._see_inputs, with_kwargs=True)
+        for engram, layer in self.attached:
+            block = layers[layer]
+            device, dtype = layer_device_dtype(block)
+            block.add_module("micro_engram", engram.to(device=device, dtype=dtype))
+            block.register_forward_hook(self._after_layer(engram))
+
+    def new_sequence(self):
+        self.history = None
+
+    def _see_inputs(self, _mod, args, kwargs):
+        ids = kwargs.get("input_ids")
+        if ids is None:
+            ids = args[0] if args else None
+        if ids is None:
+            return
+        self.history = ids if self.history is None else torch.cat([self.history, ids.to(self.history.device)], 1)
+
+    def _after_layer(self, engram):
+        def add_memory(_mod, _args, output):
+            if not self.enabled or self.history is None:
+                return output
+            if isinstance(output, tuple):
+                return (self.with_memory(engram, output[0]),) + tuple(output[1:])
+            return self.with_memory(engram, output)
+
+        return add_memory
+
+    @torch.no_grad()
+    def with_memory(self, engram, hidden):
+        """hidden [B, T, d] of the newest T positions + the engram's gated memory."""
+        T = hidden.shape[1]
+        reach = self.history[:, -(T + max(engram.orders) - 1):].to(hidden.device)
+        return engram.inject(hidden, [i[:, -T:] for i in engram.hash_ids(reach)])
 
 
 def attach_planned(plans, model):
+    """Build every planned engram for `model`, check it against its tensors, attach them."""
     text_cfg = getattr(model.config, "text_config", model.config)
-    pairs = []
+    pad = getattr(text_cfg, "pad_token_id", None)
+    attached = []
     for s, sd in plans:
         if s.get("model_dim") and s["model_dim"] != text_cfg.hidden_size:
             raise SystemExit(f"the config says model_dim {s['model_dim']}, the model has hidden_size "
                              f"{text_cfg.hidden_size}")
         canon = None
-        if "canon" not in sd and s.get("token_merge"):
+        if s.get("token_merge") and "canon" not in sd:
             path = s.get("canon_path")
-            if not path or not os.path.isfile(path):
+            if not (path and os.path.isfile(path)):
                 raise SystemExit(f"training merged tokens but the weights have no 'canon' and the canon file is "
                                  f"missing ({path}); copy it and fix canon_path in {CONFIG_NAME}")
             canon = torch.load(path, map_location="cpu")
-        engram = engram_from_spec(s, text_cfg.hidden_size, text_cfg.vocab_size,
-                                  first(getattr(text_cfg, "pad_token_id", None), 0), canon)
+        engram = engram_from_spec(s, text_cfg.hidden_size, text_cfg.vocab_size, 0 if pad is None else pad, canon)
         check_loaded(engram, sd, f"layer {s['layer']} weights")
-        out = engram.up if engram.gate == "ple" else engram.value
+        out_w = (engram.up if engram.gate == "ple" else engram.value).weight
         print(f"[engram] layer {s['layer']}: {len(sd)} tensors, output-weight magnitude "
-              f"{out.weight.float().abs().mean().item():.6f} ({engram.gate} gate; 0 = untrained or not loaded)")
-        pairs.append((engram, s["layer"]))
-    return EngramRunner(model, pairs)
+              f"{out_w.float().abs().mean().item():.6f} ({engram.gate} gate; 0 = untrained or not loaded)")
+        attached.append((engram, s["layer"]))
+    return EngramSession(model, attached)
 
 
 def add_engram_args(ap):
@@ -218,12 +227,21 @@ def add_engram_args(ap):
 
 
 def load_model(args):
+    """(model, tokenizer, EngramSession) for the engram(s) `args` name."""
     from transformers import AutoModelForCausalLM, AutoTokenizer
 
     plans = plan_engrams(args)
     tok = AutoTokenizer.from_pretrained(args.model)
     model = AutoModelForCausalLM.from_pretrained(args.model, dtype=torch.bfloat16, device_map="auto").eval()
     return model, tok, attach_planned(plans, model)
+
+
+def _prompt_ids(tok, prompt, raw):
+    if raw or not getattr(tok, "chat_template", None):
+        return tok(prompt, return_tensors="pt").input_ids
+    ids = tok.apply_chat_template([{"role": "user", "content": prompt}], add_generation_prompt=True,
+                                  return_tensors="pt")
+    return ids if torch.is_tensor(ids) else ids["input_ids"]
 
 
 def main(argv=None):
@@ -236,22 +254,15 @@ def main(argv=None):
     ap.add_argument("--temperature", type=float, default=0.8)
     ap.add_argument("--top-p", type=float, default=0.95)
     args = ap.parse_args(argv)
-    model, tok, runner = load_model(args)
-    runner.enabled = not args.no_engram
-    print(f"[engram] enabled: {runner.enabled}")
-    if args.raw or not getattr(tok, "chat_template", None):
-        ids = tok(args.prompt, return_tensors="pt").input_ids
-    else:
-        ids = tok.apply_chat_template([{"role": "user", "content": args.prompt}], add_generation_prompt=True,
-                                      return_tensors="pt")
-        if not torch.is_tensor(ids):
-            ids = ids["input_ids"]
-    ids = ids.to(next(model.parameters()).device)
-    runner.reset()
+    model, tok, session = load_model(args)
+    session.enabled = not args.no_engram
+    print(f"[engram] enabled: {session.enabled}")
+    ids = _prompt_ids(tok, args.prompt, args.raw).to(next(model.parameters()).device)
+    session.new_sequence()
+    sample = args.temperature > 0
     with torch.no_grad():
-        out = model.generate(input_ids=ids, max_new_tokens=args.max_new_tokens, do_sample=args.temperature > 0,
-                             temperature=args.temperature if args.temperature > 0 else None, top_p=args.top_p,
-                             use_cache=True)
+        out = model.generate(input_ids=ids, max_new_tokens=args.max_new_tokens, do_sample=sample,
+                             temperature=args.temperature if sample else None, top_p=args.top_p, use_cache=True)
     print("\n--- output ---")
     print(tok.decode(out[0, ids.shape[1]:], skip_special_tokens=True))
 

@@ -205,7 +205,7 @@ class Server:
         from transformers import StoppingCriteriaList, TextIteratorStreamer
 
         self.runner.enabled = engram_on
-        self.runner.reset()
+        self.runner.new_sequence()
         if body.get("seed") is not None:
             torch.manual_seed(int(body["seed"]))
         streamer = TextIteratorStreamer(self.tok, skip_prompt=True, skip_special_tokens=skip_special)

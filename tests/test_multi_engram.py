@@ -114,12 +114,12 @@ def test_inference_loads_the_trained_engrams(multi):
         want = trained(h, ids)
         torch.testing.assert_close(served(h, ids), want, atol=1e-5, rtol=0)
         # prefill 25 tokens, then decode one at a time through the runner's history rule
-        runner = infer.EngramRunner.__new__(infer.EngramRunner)
-        runner.hist, runner.enabled = None, True
+        session = infer.EngramSession.__new__(infer.EngramSession)
+        session.history, session.enabled = None, True
         outs = []
         for a, b in [(0, 25)] + [(t, t + 1) for t in range(25, 40)]:
-            runner._grab(None, (), {"input_ids": ids[:, a:b]})
-            outs.append(runner.forward(served, h[:, a:b]))
+            session._see_inputs(None, (), {"input_ids": ids[:, a:b]})
+            outs.append(session.with_memory(served, h[:, a:b]))
         torch.testing.assert_close(torch.cat(outs, 1), want, atol=1e-5, rtol=0)
 
 
