@@ -325,3 +325,37 @@ def test_server_stream_transforms():
     assert "".join(t for k, t in out if k == "content") == "abc " and c.cancelled
     assert ("reasoning", "STOP inside") in out
     assert parse_stops({"stop": "x"}) == ["x"] and parse_stops({"stop": ["a", ""]}) == ["a"]
+
+
+def test_infer_settings_layering(tmp_path, capsys):
+    """Each setting comes from the first source that gives it: flag, engram config, the saved
+    tensors, the defaults; an explicit --table-size drops per-order sizes."""
+    import json
+    import types
+
+    import torch
+
+    from micro_engram.tools import infer
+
+    sd = {f"tables.{k}.weight": torch.zeros(rows, 16) for k, rows in enumerate([100, 100, 300, 300])}
+    sd["q_scale"] = torch.zeros(8)
+    sd["value.weight"] = torch.zeros(8, 32)
+
+    def args(**kw):
+        base = {"model": str(tmp_path), "engram_config": None, "layer": None, "table_size": None, "dim": None,
+                "heads": None, "gate": None}
+        return types.SimpleNamespace(**{**base, **kw})
+
+    s = infer.resolve_settings(args(), sd, 5)  # no config: the tensors, then the defaults
+    assert (s["layer"], s["table_size"], s["engram_dim"], s["num_heads"], s["gate"]) == (5, 100, 16, 2, "scalar_sqrt")
+    assert s["table_sizes"] == {2: 100, 3: 300} and s["seed"] == 0 and s["orders"] == (2, 3)
+    conf = {"layer": 7, "engram_dim": 16, "gate": "scalar", "seed": 70049, "orders": [2, 3], "table_sizes": {"2": 9}}
+    path = tmp_path / "micro_engram_config.json"
+    path.write_text(json.dumps(conf))
+    s = infer.resolve_settings(args(heads=4), sd, 5)  # config over tensors, flags over both
+    assert (s["layer"], s["gate"], s["seed"], s["num_heads"], s["table_sizes"]) == (7, "scalar", 70049, 4, {"2": 9})
+    s = infer.resolve_settings(args(table_size=64, layer=1), sd, 5)
+    assert (s["table_size"], s["table_sizes"], s["layer"]) == (64, None, 1)
+    assert infer.shape_settings({}, (2, 3)) == {"table_size": None, "table_sizes": None, "engram_dim": None,
+                                                "num_heads": None, "gate": None}
+    assert "settings:" in capsys.readouterr().out
