@@ -4,7 +4,7 @@ events (warm-up, synchronize on both sides) and reported against the measured ro
 figures otherwise). Also the workload that the committed ncu summaries in profiles/ capture.
 
   python -m micro_engram_fork_b200.utils.kernel_bench [--case all|gemm|attn_fwd|attn_bwd|gate|ce|qkv|geglu|rows|
-                                                       norms|ce_bwd|nf4|ce_gemm] [--iters N] [--small]
+                                                       norms|ce_bwd|nf4|ce_gemm|tp] [--iters N] [--small]
 """
 import argparse
 import json
@@ -348,9 +348,54 @@ def case_nf4(C, dev, it, pk):
                 ms, pk)
 
 
+def case_tp(C, dev, it, pk):
+    """The fused row-parallel linear's three kernels (scatter GEMM, slot sum, gather) for two
+    ranks emulated on this GPU (every flag published beforehand, as in its GPU test), against
+    the plain bf16 GEMM of one rank: the device time of the op without NVLink, and the host time
+    of issuing it, to tell a launch-bound call from a GPU-bound one. o_proj at TP = 2."""
+    import time
+
+    world, N, K, flags = 2, 5376, 8192, 256
+    r = {}
+    for M in (64, 8192):
+        rows = -(-M // world)
+        slot, half = rows * N, (rows * N * 2 + 15) // 16 * 16
+        xs = [torch.randn(M, K, device=dev).to(torch.bfloat16) for _ in range(world)]
+        ws = [(torch.randn(N, K, device=dev) * K ** -0.5).to(torch.bfloat16) for _ in range(world)]
+        rb = [torch.zeros(flags + 2 * world * slot * 4, dtype=torch.uint8, device=dev) for _ in range(world)]
+        gb = [torch.zeros(flags + 2 * half, dtype=torch.uint8, device=dev) for _ in range(world)]
+        for b in rb + gb:
+            b[:flags].view(torch.int32)[:world] = 1 << 30  # every wait is already satisfied
+        rbases = torch.tensor([b.data_ptr() for b in rb], dtype=torch.int64, device=dev)
+        gbases = torch.tensor([b.data_ptr() for b in gb], dtype=torch.int64, device=dev)
+        recv = torch.tensor([b.data_ptr() + flags for b in rb], dtype=torch.int64, device=dev)
+        stages = [b[flags:flags + rows * N * 2].view(torch.bfloat16).view(rows, N) for b in gb]
+        status = torch.zeros(2, dtype=torch.int32, device=dev)
+        out = torch.empty(world * rows, N, dtype=torch.bfloat16, device=dev)
+
+        def one_rank(rk=0):
+            C.gemm_f32_scatter(xs[rk], ws[rk], recv, rows, rk, slot, True)
+            C.p2p_sum_slots(rbases, rk, 2, flags, slot, stages[rk], 5.0, status)
+            C.p2p_gather(gbases, rk, 2, flags, half, rows * N * 2 // 16, out, 5.0, status, True)
+
+        ms = _time(one_rank, it)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(it):
+            one_rank()
+        host_us = (time.perf_counter() - t0) / it * 1e6
+        torch.cuda.synchronize()
+        gemm_ms = _time(lambda: C.gemm(xs[0], ws[0], True, None), it)
+        flops = 2 * M * N * K
+        r[f"M {M}"] = {"fused_ms": round(ms, 4), "host_us_per_call": round(host_us, 1),
+                       "plain_gemm_ms": round(gemm_ms, 4), "fused_frac_of_peak": round(flops / ms / 1e9 / pk["bf16_tflops"], 3),
+                       "status": status.tolist()}
+    return r
+
+
 CASES = {"gemm": case_gemm, "attn_fwd": case_attn_fwd, "attn_bwd": case_attn_bwd, "gate": case_gate, "ce": case_ce,
          "qkv": case_qkv, "geglu": case_geglu, "rows": case_rows, "norms": case_norms, "ce_bwd": case_ce_bwd,
-         "nf4": case_nf4, "ce_gemm": case_ce_gemm}
+         "nf4": case_nf4, "ce_gemm": case_ce_gemm, "tp": case_tp}
 
 
 def main(argv=None):
