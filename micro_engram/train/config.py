@@ -202,6 +202,10 @@ _CONFIG_ERRORS = (
      "no gradient, so reentrant checkpointing would drop the engram's)"),
     (lambda c: c.micro_engram_sharding not in (None, "rows"),
      "micro_engram_sharding: tables are always row-sharded here; use rows or leave it out"),
+    (lambda c: c.lr_scheduler == "warmup_stable_decay" and not c.micro_engram_lr_epoch_decay
+     and "num_decay_steps" not in (c.lr_scheduler_kwargs or {}),
+     "lr_scheduler: warmup_stable_decay needs lr_scheduler_kwargs.num_decay_steps (the length of its final "
+     "decay)"),
 )
 
 

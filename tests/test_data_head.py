@@ -168,3 +168,41 @@ def test_packing_order_is_pinned():
     bins = pack(lens, 512, 11)
     assert hashlib.sha256(json.dumps(bins).encode()).hexdigest()[:16] == "a9436382b82cb5d7"
     assert sorted(i for b in bins for i in b) == [i for i in range(500) if 0 < lens[i] <= 512]
+
+
+def test_every_lr_schedule():
+    """Each lr_scheduler value (and the epoch decay) builds and follows its curve over 10 steps
+    with 2 warmup steps; warmup_stable_decay without its decay length is refused at load."""
+    import types
+
+    import pytest
+    import torch
+
+    from micro_engram.train.config import TrainConfig
+    from micro_engram.train.loop import Trainer
+
+    def lrs(**kw):
+        base = dict(base_model="x", datasets=[{"path": "d.jsonl", "type": "completion"}], output_dir="o",
+                    learning_rate=1.0, warmup_steps=2)
+        cfg = TrainConfig(**{**base, **kw})
+        opt = torch.optim.SGD([torch.nn.Parameter(torch.zeros(1))], lr=1.0)
+        sched = Trainer._make_scheduler(types.SimpleNamespace(cfg=cfg, dense_opt=opt, total_steps=10))
+        out = []
+        for _ in range(10):
+            out.append(round(opt.param_groups[0]["lr"], 3))
+            opt.step()
+            sched.step()
+        return out
+
+    assert lrs(lr_scheduler="constant") == [1.0] * 10  # never warms up
+    assert lrs(lr_scheduler="constant_with_warmup") == [0.0, 0.5] + [1.0] * 8
+    assert lrs(lr_scheduler="linear") == [0.0, 0.5, 1.0, 0.875, 0.75, 0.625, 0.5, 0.375, 0.25, 0.125]
+    cos = lrs(lr_scheduler="cosine")
+    assert cos[:3] == [0.0, 0.5, 1.0] and cos[6] == 0.5 and cos[-1] < 0.05
+    assert lrs(lr_scheduler="cosine", cosine_min_lr_ratio=0.1)[-1] > cos[-1]
+    assert lrs(lr_scheduler="warmup_stable_decay", lr_scheduler_kwargs={"num_decay_steps": 4})[:7] == \
+        [0.0, 0.5, 1.0, 1.0, 1.0, 1.0, 1.0]
+    assert lrs(micro_engram_lr_epoch_decay=0.5, num_epochs=2) == [0.0, 0.5, 1.0, 1.0, 1.0] + [0.5] * 5
+    with pytest.raises(ValueError, match="num_decay_steps"):
+        TrainConfig(base_model="x", datasets=[{"path": "d.jsonl", "type": "completion"}], output_dir="o",
+                    lr_scheduler="warmup_stable_decay")
