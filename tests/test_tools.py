@@ -359,3 +359,34 @@ def test_infer_settings_layering(tmp_path, capsys):
     assert infer.shape_settings({}, (2, 3)) == {"table_size": None, "table_sizes": None, "engram_dim": None,
                                                 "num_heads": None, "gate": None}
     assert "settings:" in capsys.readouterr().out
+
+
+def test_base_fingerprint_and_mismatch(tmp_path):
+    """The base fingerprint names a folder's text weights (embedding and the first, middle and
+    last layers' projections): the same weights give the same fingerprint, changed weights or
+    an engram config recorded on another base give a warning, no record gives none."""
+    import torch
+    from safetensors.torch import save_file
+
+    from micro_engram.weights import base_fingerprint, base_mismatch
+
+    def folder(name, scale, engram_scale=1.0):
+        d = tmp_path / name
+        d.mkdir()
+        g = torch.Generator().manual_seed(1)
+        ts = {"model.embed_tokens.weight": torch.randn(32, 8, generator=g) * scale}
+        for i in range(3):
+            for proj in ("self_attn.q_proj", "mlp.down_proj"):
+                ts[f"model.layers.{i}.{proj}.weight"] = torch.randn(8, 8, generator=g)
+        ts["model.layers.1.micro_engram.tables.0.weight"] = torch.randn(4, 8, generator=g) * engram_scale
+        save_file(ts, str(d / "model.safetensors"))
+        return str(d)
+
+    a, same, other = folder("a", 1.0), folder("same", 1.0, engram_scale=3.0), folder("other", 2.0)
+    fa = base_fingerprint(a)
+    assert fa is not None and len(fa) == 16 and base_fingerprint(other) != fa
+    assert base_fingerprint(same) == fa  # an assembled engram inside the folder is not part of the base
+    assert base_fingerprint(str(tmp_path / "missing")) is None
+    assert base_mismatch({"base_fingerprint": fa}, same) is None
+    assert "other base weights" in base_mismatch({"base_fingerprint": fa, "base_model": "a"}, other)
+    assert base_mismatch({}, other) is None

@@ -308,4 +308,8 @@ def test_trainer_full_run(assets):
     with open(os.path.join(out, "train_log.jsonl")) as f:
         lines = [json.loads(x) for x in f]
     assert lines and all("loss" in x and "table_grad_norm" in x for x in lines)
+    keys = {"loss", "ppl", "grad_norm", "table_grad_norm", "learning_rate", "dense_lr", "epoch", "step", "s_per_step",
+            "trained_tokens_per_s"}  # the documented JSONL keys (memory keys are CUDA-only)
+    assert all(keys <= set(x) for x in lines), keys - set(lines[0])
+    assert [x["step"] for x in lines] == sorted(x["step"] for x in lines)
     assert any(k.startswith("engram_L1/") for k in lines[-1])
