@@ -6,9 +6,12 @@
 // blk.L.engram_kv.mengram_{tables, key, value, down, up} and blk.L.engram_gate.mengram_{q,k}_scale.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <string>
+#include <thread>
+#include <vector>
 
 #include "engram_runtime.h"
 #include "runtime.h"
@@ -418,6 +421,59 @@ int me_rt_hist_load(me_rt_hist* h, int32_t seq, const void* buf, size_t size) {
 }
 
 // ------------------------------------------------------------------ injection (CPU, fp32)
+}  // extern "C"
+
+namespace {
+
+// One position: gather its rows, then the gate and the residual add into x (fp32 weights, double
+// accumulation). Positions are independent, so any split over threads gives the same bits.
+void inject_position(const Engram& e, int64_t d, const int32_t* rows, float* x, float kp, std::vector<float>& mem,
+                     std::vector<float>& h, std::vector<float>& a, std::vector<float>& b) {
+  const int64_t md = e.mem_dim();
+  for (uint32_t k = 0; k < e.n_tables; ++k) gather_row(e, rows[k], mem.data() + (size_t)k * e.dim);
+  rms(x, d, h.data());
+  if (e.gate == ME_RT_GATE_PLE) {
+    matvec(e.down_f, md, d, h.data(), a.data());  // down: [mem_dim, d]
+    for (int64_t i = 0; i < md; ++i) {
+      const float z = a[i];
+      const float g = 0.5f * z * (1.0f + std::tanh(0.7978845608028654f * (z + 0.044715f * z * z * z)));
+      a[i] = g * mem[i];
+    }
+    matvec(e.up_f, d, md, a.data(), b.data());  // up: [d, mem_dim]
+    for (int64_t j = 0; j < d; ++j) x[j] += b[j] * kp;
+    return;
+  }
+  matvec(e.key_f, d, md, mem.data(), a.data());
+  rms(a.data(), d, a.data());
+  double s = 0;
+  for (int64_t j = 0; j < d; ++j) {
+    const double qh = e.qs_f.empty() ? h[j] : h[j] * e.qs_f[j];
+    const double kk = e.ks_f.empty() ? a[j] : a[j] * e.ks_f[j];
+    s += qh * kk;
+  }
+  float sc = (float)(s / std::sqrt((double)d));
+  if (e.gate == ME_RT_GATE_SCALAR_SQRT) {
+    const float sg = sc > 0 ? 1.f : (sc < 0 ? -1.f : 0.f);
+    sc = sg * std::sqrt(std::max(std::fabs(sc), 1e-6f));
+  }
+  const float alpha = 1.0f / (1.0f + std::exp(-sc));
+  matvec(e.value_f, d, md, mem.data(), b.data());
+  for (int64_t j = 0; j < d; ++j) x[j] += alpha * b[j] * kp;
+}
+
+// Worker threads for n positions: ME_RT_THREADS, else the machine's hardware threads, with at
+// least 4 positions per thread (a decode step of one token stays on the calling thread).
+int64_t worker_count(int64_t n) {
+  int64_t want = 0;
+  if (const char* env = std::getenv("ME_RT_THREADS")) want = std::atoll(env);
+  if (want <= 0) want = std::max(1u, std::thread::hardware_concurrency());
+  return std::max<int64_t>(1, std::min<int64_t>(want, n / 4));
+}
+
+}  // namespace
+
+extern "C" {
+
 int me_rt_inject_cpu(const me_rt* crt, int32_t ei, float* hidden, const int32_t* rows, const float* keep, int64_t n) {
   me_rt* rt = const_cast<me_rt*>(crt);  // lazily made fp32 copies only
   if (!rt || ei < 0 || ei >= (int32_t)rt->engrams.size() || (n > 0 && (!hidden || !rows)))
@@ -425,7 +481,6 @@ int me_rt_inject_cpu(const me_rt* crt, int32_t ei, float* hidden, const int32_t*
   Engram& e = rt->engrams[ei];
   if (!tensors_ready(e, rt->n_embd)) return fail(ME_RT_ERR_STATE, "engram tensors are not bound");
   const int64_t d = rt->n_embd, md = e.mem_dim();
-  std::vector<float> mem(md), h(d), a(std::max(d, md)), b(std::max(d, md));
   if (e.gate == ME_RT_GATE_PLE) {
     ensure_f32(e.down, &e.down_f);
     ensure_f32(e.up, &e.up_f);
@@ -435,43 +490,23 @@ int me_rt_inject_cpu(const me_rt* crt, int32_t ei, float* hidden, const int32_t*
     ensure_f32(e.q_scale, &e.qs_f);
     ensure_f32(e.k_scale, &e.ks_f);
   }
-  for (int64_t t = 0; t < n; ++t) {
-    for (uint32_t k = 0; k < e.n_tables; ++k) {
-      const int64_t r = rows[t * e.n_tables + k];
-      if (r < 0 || (uint64_t)r >= e.total_rows) return fail(ME_RT_ERR_ARG, "row index out of range");
-      gather_row(e, r, mem.data() + (size_t)k * e.dim);
-    }
-    float* x = hidden + t * d;
-    rms(x, d, h.data());
-    const float kp = keep ? keep[t] : 1.0f;
-    if (e.gate == ME_RT_GATE_PLE) {
-      matvec(e.down_f, md, d, h.data(), a.data());  // down: [mem_dim, d]
-      for (int64_t i = 0; i < md; ++i) {
-        const float z = a[i];
-        const float g = 0.5f * z * (1.0f + std::tanh(0.7978845608028654f * (z + 0.044715f * z * z * z)));
-        a[i] = g * mem[i];
-      }
-      matvec(e.up_f, d, md, a.data(), b.data());  // up: [d, mem_dim]
-      for (int64_t j = 0; j < d; ++j) x[j] += b[j] * kp;
-    } else {
-      matvec(e.key_f, d, md, mem.data(), a.data());
-      rms(a.data(), d, a.data());
-      double s = 0;
-      for (int64_t j = 0; j < d; ++j) {
-        const double qh = e.qs_f.empty() ? h[j] : h[j] * e.qs_f[j];
-        const double kk = e.ks_f.empty() ? a[j] : a[j] * e.ks_f[j];
-        s += qh * kk;
-      }
-      float sc = (float)(s / std::sqrt((double)d));
-      if (e.gate == ME_RT_GATE_SCALAR_SQRT) {
-        const float sg = sc > 0 ? 1.f : (sc < 0 ? -1.f : 0.f);
-        sc = sg * std::sqrt(std::max(std::fabs(sc), 1e-6f));
-      }
-      const float alpha = 1.0f / (1.0f + std::exp(-sc));
-      matvec(e.value_f, d, md, mem.data(), b.data());
-      for (int64_t j = 0; j < d; ++j) x[j] += alpha * b[j] * kp;
-    }
+  for (int64_t i = 0; i < n * (int64_t)e.n_tables; ++i)  // checked up front: the workers cannot fail
+    if (rows[i] < 0 || (uint64_t)rows[i] >= e.total_rows) return fail(ME_RT_ERR_ARG, "row index out of range");
+  auto run = [&](int64_t t0, int64_t t1) {
+    std::vector<float> mem(md), h(d), a(std::max(d, md)), b(std::max(d, md));
+    for (int64_t t = t0; t < t1; ++t)
+      inject_position(e, d, rows + t * e.n_tables, hidden + t * d, keep ? keep[t] : 1.0f, mem, h, a, b);
+  };
+  const int64_t workers = worker_count(n);
+  if (workers == 1) {
+    run(0, n);
+    return ME_RT_OK;
   }
+  std::vector<std::thread> pool;
+  const int64_t per = (n + workers - 1) / workers;
+  for (int64_t t0 = per; t0 < n; t0 += per) pool.emplace_back(run, t0, std::min(n, t0 + per));
+  run(0, std::min(n, per));
+  for (auto& th : pool) th.join();
   return ME_RT_OK;
 }
 

@@ -130,6 +130,11 @@ def test_runtime_matches_module(tmp_path, gate, orders, sizes, dtype):
     ref = oracle.inject(h, oracle.hash_prev(hist)).detach().numpy()
     got = rt.inject_cpu(0, h.numpy(), rows)
     np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-4 * np.abs(ref).max())
+    os.environ["ME_RT_THREADS"] = "1"  # the positions split over threads above, on one thread here
+    try:
+        assert np.array_equal(rt.inject_cpu(0, h.numpy(), rows), got)
+    finally:
+        del os.environ["ME_RT_THREADS"]
     keep = np.ones(40, np.float32)
     keep[3] = 0
     got_k = rt.inject_cpu(0, h.numpy(), rows, keep)
