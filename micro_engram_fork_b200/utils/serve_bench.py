@@ -99,7 +99,12 @@ def serve(args):
     plugin = _plugin_root(args.impl)
     import micro_engram_vllm
     import torch
-    from vllm import LLM, SamplingParams
+
+    try:
+        from vllm import LLM, SamplingParams
+    except ImportError as exc:
+        print(json.dumps({"impl": args.impl, "unavailable": f"vllm is not importable ({exc})"}))
+        return
 
     where = os.path.abspath(micro_engram_vllm.__file__)
     if not where.startswith(os.path.abspath(plugin) + os.sep) or (args.impl == "reference" and where.startswith(
