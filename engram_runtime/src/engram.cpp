@@ -168,6 +168,14 @@ void gather_row(const Engram& e, int64_t row, float* out) {
     std::memcpy(out, reinterpret_cast<const float*>(t->data) + row * e.dim, e.dim * 4);
     return;
   }
+  if (t->type == me::GGML_BF16) {  // bf16 is the top half of an fp32
+    const uint16_t* src = reinterpret_cast<const uint16_t*>(t->data) + row * e.dim;
+    for (uint32_t i = 0; i < e.dim; ++i) {
+      const uint32_t bits = (uint32_t)src[i] << 16;
+      std::memcpy(out + i, &bits, 4);
+    }
+    return;
+  }
   me::Tensor v = *t;
   v.data = t->data + (size_t)row * e.dim * 2;
   v.ne = {(int64_t)e.dim};
