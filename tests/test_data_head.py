@@ -206,3 +206,19 @@ def test_every_lr_schedule():
     with pytest.raises(ValueError, match="num_decay_steps"):
         TrainConfig(base_model="x", datasets=[{"path": "d.jsonl", "type": "completion"}], output_dir="o",
                     lr_scheduler="warmup_stable_decay")
+
+
+def test_example_configs_load():
+    """The example YAMLs in examples/ pass the config rules and the engram request rules."""
+    import glob
+    import os
+
+    from micro_engram.runconfig import engram_requests
+    from micro_engram.train.config import load_config
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    paths = sorted(glob.glob(os.path.join(root, "examples", "*.yaml")))
+    assert paths
+    for path in paths:
+        reqs = engram_requests(load_config(path))
+        assert reqs and all(r.spec["layer"] >= 0 for r in reqs), path
